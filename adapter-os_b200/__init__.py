@@ -1,0 +1,493 @@
+"""adapter-os B200 backend: host-side mirror of the reference's kernel API.
+
+The compute lives in ``libaoscuda.so`` (hand-written sm_100a CUDA behind the C
+ABI in include/aos_cuda.h).  This module binds it with ctypes and mirrors the
+names and behaviour of the reference's Rust surface:
+
+* ``RouterRing`` / ``IoBuffers`` — crates/adapteros-lora-kernel-api/src/lib.rs:58-246
+* ``route_batch`` — Router::route_with_adapter_info (crates/adapteros-lora-router/src/router.rs:1517-1952),
+  batched one decision per token
+* ``CudaKernels`` — a ``FusedKernels`` implementation (lib.rs:308-716)
+
+There is no CPU fallback: importing works anywhere, but every compute call
+raises ``AosError`` when the library or an sm_100 device is missing.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libaoscuda.so")
+_lib = None
+
+MAX_K = 8
+Q15_DENOM = np.float32(32767.0)
+MODULES = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+
+STATUS = {0: "OK", -1: "INVALID", -2: "CUDA", -3: "NOMEM", -4: "NONFINITE", -5: "NOT_FOUND",
+          -6: "TIMEOUT", -7: "NO_DEVICE", -8: "STATE"}
+
+
+class AosError(RuntimeError):
+    """adapteros_core::AosError equivalent carrying the C status code."""
+
+    def __init__(self, code, msg):
+        super().__init__(f"{STATUS.get(code, code)}: {msg}")
+        self.code = code
+
+
+class RouterRingC(C.Structure):
+    """aos_router_ring: the 40-byte RouterRing device layout (ring_buffer.rs:44-58)."""
+
+    _fields_ = [("top_k", C.c_uint32), ("position", C.c_uint32),
+                ("indices", C.c_uint16 * 8), ("gates_q15", C.c_int16 * 8)]
+
+
+RING_DTYPE = np.dtype([("top_k", "<u4"), ("position", "<u4"), ("indices", "<u2", (8,)),
+                       ("gates_q15", "<i2", (8,))])
+
+
+class RouterParams(C.Structure):
+    _fields_ = [("k", C.c_uint32), ("tau", C.c_float), ("eps", C.c_float), ("routing_bias", C.c_float)]
+
+
+class ModelConfig(C.Structure):
+    _fields_ = [
+        ("hidden", C.c_uint32), ("n_heads", C.c_uint32), ("n_kv_heads", C.c_uint32),
+        ("head_dim", C.c_uint32), ("intermediate", C.c_uint32), ("vocab", C.c_uint32),
+        ("n_layers", C.c_uint32), ("rms_eps", C.c_float), ("rope_theta", C.c_float),
+        ("rope_mlx_as_written", C.c_uint32), ("max_batch", C.c_uint32),
+        ("kv_block_size", C.c_uint32), ("kv_num_blocks", C.c_uint32), ("max_seq_len", C.c_uint32),
+        ("lora_rank_capacity", C.c_uint32), ("lora_max_adapters", C.c_uint32),
+        ("lora_module_mask", C.c_uint32), ("device", C.c_int32),
+    ]
+
+
+class Metrics(C.Structure):
+    _fields_ = [
+        ("steps", C.c_uint64), ("tokens", C.c_uint64), ("route_calls", C.c_uint64),
+        ("base_weight_bytes", C.c_uint64), ("arena_bytes", C.c_uint64),
+        ("arena_used_rank_cols", C.c_uint64), ("kv_pool_bytes", C.c_uint64),
+        ("adapters_loaded", C.c_uint32), ("kv_blocks_used", C.c_uint32),
+        ("kv_blocks_total", C.c_uint32), ("sequences", C.c_uint32), ("last_step_ms", C.c_float),
+    ]
+
+
+class DeterminismReport(C.Structure):
+    _fields_ = [
+        ("backend", C.c_char * 32), ("device_name", C.c_char * 64), ("sm_major", C.c_uint32),
+        ("sm_minor", C.c_uint32), ("fast_math", C.c_uint32), ("float_atomics", C.c_uint32),
+        ("fixed_reduction_order", C.c_uint32), ("kernel_build_id", C.c_char * 64),
+    ]
+
+
+def lib():
+    """Load libaoscuda.so (built in-tree); raise AosError if it is missing."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise AosError(-7, f"{LIB_PATH} is not built (run adapter-os_b200/build.py); "
+                               "there is no CPU fallback")
+        L = C.CDLL(LIB_PATH)
+        vp, u32, u64, i32, f32 = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int32, C.c_float
+        sig = {
+            "aos_version": (C.c_char_p, []),
+            "aos_device_count": (C.c_int, []),
+            "aos_last_error": (C.c_char_p, [vp]),
+            "aos_route_batch": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, vp, vp, vp, vp]),
+            "aos_route_batch_dev": (C.c_int, [vp, vp, vp, vp, vp, u32, u32, vp, vp, vp, vp, vp]),
+            "aos_lora_op_f32": (C.c_int, [vp, u32, u32, u32, vp, vp, vp, u32, u32, vp, vp, vp]),
+            "aos_lora_op_f32_dev": (C.c_int, [vp, u32, u32, u32, vp, vp, vp, u32, u32, vp, vp, vp, vp]),
+            "aos_init": (vp, [vp]),
+            "aos_destroy": (None, [vp]),
+            "aos_device_name": (C.c_char_p, [vp]),
+            "aos_stream": (vp, [vp]),
+            "aos_load_weight": (C.c_int, [vp, C.c_int, u32, C.c_int, vp, u64, C.c_int]),
+            "aos_adapter_new": (C.c_int, [vp, C.c_uint16, u32, f32]),
+            "aos_adapter_set_module": (C.c_int, [vp, C.c_uint16, u32, C.c_int, vp, vp, C.c_int]),
+            "aos_adapter_unload": (C.c_int, [vp, C.c_uint16]),
+            "aos_adapter_is_loaded": (C.c_int, [vp, C.c_uint16]),
+            "aos_kv_alloc": (C.c_int, [vp, u64, u32]),
+            "aos_kv_free": (C.c_int, [vp, u64]),
+            "aos_kv_set_len": (C.c_int, [vp, u64, u32]),
+            "aos_kv_get_len": (C.c_int, [vp, u64, vp]),
+            "aos_kv_write": (C.c_int, [vp, u64, u32, u32, u32, vp, vp, C.c_int]),
+            "aos_kv_read": (C.c_int, [vp, u64, u32, u32, u32, vp, vp]),
+            "aos_kv_fill_synthetic": (C.c_int, [vp, u64, f32]),
+            "aos_kv_clear_all": (C.c_int, [vp]),
+            "aos_kv_memory_bytes": (u64, [vp]),
+            "aos_run_step_batch": (C.c_int, [vp, vp, vp, vp, u32, vp, vp]),
+            "aos_run_step_batch_dev": (C.c_int, [vp, vp, vp, vp, u32, vp, vp, vp]),
+            "aos_layer_step_dev": (C.c_int, [vp, u32, vp, vp, u32, vp, C.c_int, vp]),
+            "aos_get_metrics": (C.c_int, [vp, vp]),
+            "aos_health_check": (C.c_int, [vp]),
+            "aos_attest_determinism": (C.c_int, [vp, vp]),
+        }
+        for name, (res, args) in sig.items():
+            if not hasattr(L, name):
+                continue  # tests/test_capi_symbols.py reports missing exports
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error(ctx=None) -> str:
+    m = lib().aos_last_error(ctx)
+    return m.decode() if m else ""
+
+
+def check(rc, ctx=None):
+    if rc != 0:
+        raise AosError(rc, last_error(ctx))
+    return rc
+
+
+def device_count() -> int:
+    try:
+        return int(lib().aos_device_count())
+    except AosError:
+        return 0
+
+
+def _p(a):
+    """Pointer of a numpy array or torch tensor (None -> NULL)."""
+    if a is None:
+        return None
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    return a.ctypes.data
+
+
+def _params(k, tau, eps, routing_bias):
+    return RouterParams(int(k), float(tau), float(eps), float(routing_bias))
+
+
+# ------------------------------------------------------------------ RouterRing / IoBuffers
+class RouterRing:
+    """RouterRing (kernel-api/src/lib.rs:58-193): fixed [u16; 8] indices,
+    [i16; 8] Q15 gates, k <= 8; unused entries zero-filled.  ``set`` follows
+    RouterRing::set's release-build policy (length mismatch or out-of-range
+    index -> zero-filled, k = 0)."""
+
+    def __init__(self, k=0):
+        self.indices = np.zeros(8, np.uint16)
+        self.gates_q15 = np.zeros(8, np.int16)
+        self.position = 0
+        self.k = min(int(k), 8)
+        self.dropout_seed = 0
+        self.dropout_rate = 0.0
+
+    def set(self, indices, gates, max_adapter=0xFFFF):
+        if len(indices) != len(gates) or any(int(i) >= max_adapter for i in indices):
+            self.indices[:] = 0
+            self.gates_q15[:] = 0
+            self.k = 0
+            return
+        k = min(len(indices), 8)
+        self.indices[:] = 0
+        self.gates_q15[:] = 0
+        self.indices[:k] = np.asarray(indices[:k], np.uint16)
+        self.gates_q15[:k] = np.asarray(gates[:k], np.int16)
+        self.k = k
+
+    def active_indices(self):
+        return self.indices[: self.k]
+
+    def active_gates(self):
+        return self.gates_q15[: self.k]
+
+    def to_record(self):
+        r = np.zeros(1, RING_DTYPE)
+        r[0]["top_k"], r[0]["position"] = self.k, self.position
+        r[0]["indices"], r[0]["gates_q15"] = self.indices, self.gates_q15
+        return r[0]
+
+    @staticmethod
+    def from_record(rec):
+        r = RouterRing(int(rec["top_k"]))
+        r.indices[:] = rec["indices"]
+        r.gates_q15[:] = rec["gates_q15"]
+        r.position = int(rec["position"])
+        return r
+
+
+class IoBuffers:
+    """IoBuffers (kernel-api/src/lib.rs:221-246) for one sequence."""
+
+    def __init__(self, vocab_size):
+        self.input_ids = []
+        self.output_logits = np.zeros(vocab_size, np.float32)
+        self.position = 0
+        self.attention_entropy = None
+        self.activations = None
+        self.session_id = None
+
+
+# ------------------------------------------------------------------ router
+def route_batch(priors, stable_ids=None, k=4, tau=1.0, eps=0.02, routing_bias=1.0,
+                version_weights=None, allowed=None, positions=None, raise_on_nonfinite=True):
+    """Batched router on the GPU (host arrays in, host arrays out).
+
+    Returns (rings [T] RING_DTYPE, entropy [T] f32, status [T] i32).  A
+    non-finite prior raises AosError(NONFINITE) like validate_router_inputs
+    (router.rs:611-625) unless raise_on_nonfinite is False."""
+    pr = np.ascontiguousarray(priors, dtype=np.float32)
+    if pr.ndim == 1:
+        pr = pr[None, :]
+    T, N = pr.shape
+    sid = np.ascontiguousarray(np.arange(N) if stable_ids is None else stable_ids, dtype=np.uint64)
+    vw = None if version_weights is None else np.ascontiguousarray(version_weights, np.float32)
+    al = None if allowed is None else np.ascontiguousarray(allowed, np.uint8)
+    pos = None if positions is None else np.ascontiguousarray(positions, np.uint32)
+    rings = np.zeros(T, RING_DTYPE)
+    ent = np.zeros(T, np.float32)
+    st = np.zeros(T, np.int32)
+    p = _params(k, tau, eps, routing_bias)
+    rc = lib().aos_route_batch(_p(pr), _p(sid), _p(vw), _p(al), _p(pos), T, N, C.byref(p), _p(rings),
+                               _p(ent), _p(st))
+    if rc != 0 and not (rc == -4 and not raise_on_nonfinite):
+        raise AosError(rc, last_error())
+    return rings, ent, st
+
+
+def route_batch_dev(priors, stable_ids, rings_out, k=4, tau=1.0, eps=0.02, routing_bias=1.0,
+                    version_weights=None, allowed=None, positions=None, entropy=None, status=None,
+                    stream=None):
+    """Device form: every array is a torch CUDA tensor; enqueued on ``stream``."""
+    T, N = priors.shape
+    p = _params(k, tau, eps, routing_bias)
+    check(lib().aos_route_batch_dev(_p(priors), _p(stable_ids), _p(version_weights), _p(allowed),
+                                    _p(positions), T, N, C.byref(p), _p(rings_out), _p(entropy),
+                                    _p(status), stream))
+
+
+# ------------------------------------------------------------------ fp32 LoRA op
+def lora_op_f32(x, W, A, B, rings, alpha=None):
+    """fp32 base + K-sparse LoRA on the GPU (host arrays); see aos_lora_op_f32."""
+    x = np.ascontiguousarray(x, np.float32)
+    W = np.ascontiguousarray(W, np.float32)
+    A = np.ascontiguousarray(A, np.float32)
+    B = np.ascontiguousarray(B, np.float32)
+    rings = np.ascontiguousarray(rings, RING_DTYPE)
+    T, ind = x.shape
+    outd = W.shape[0]
+    n_ad, rank, _ = A.shape
+    al = None if alpha is None else np.ascontiguousarray(alpha, np.float32)
+    y = np.zeros((T, outd), np.float32)
+    check(lib().aos_lora_op_f32(_p(x), T, ind, outd, _p(W), _p(A), _p(B), n_ad, rank, _p(al),
+                                _p(rings), _p(y)))
+    return y
+
+
+def lora_op_f32_dev(x, W, A, B, rings, y, alpha=None, stream=None):
+    T, ind = x.shape
+    outd = W.shape[0]
+    n_ad, rank, _ = A.shape
+    check(lib().aos_lora_op_f32_dev(_p(x), T, ind, outd, _p(W), _p(A), _p(B), n_ad, rank, _p(alpha),
+                                    _p(rings), _p(y), stream))
+
+
+# ------------------------------------------------------------------ FusedKernels
+MOD_INDEX = {name: i for i, name in enumerate(MODULES)}
+W_EMBED, W_LM_HEAD, W_FINAL_NORM, W_ATTN_NORM, W_MLP_NORM, W_PROJ = range(6)
+
+
+class CudaKernels:
+    """``FusedKernels`` implementation over libaoscuda (kernel-api/src/lib.rs:308-716).
+
+    Method names follow the trait: ``load``-time weights go through
+    ``load_weight``/``load_host_model``; ``load_adapter_with_metadata``,
+    ``unload_adapter``, ``run_step`` (one sequence, one RouterRing), the batched
+    ``run_step_batch`` (one ring per token), the KV-cache methods and
+    ``get_metrics``/``health_check``/``attest_determinism``."""
+
+    def __init__(self, hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab, n_layers,
+                 rms_eps=1e-5, rope_theta=1e6, rope_mlx_as_written=False, max_batch=64,
+                 kv_block_size=16, kv_num_blocks=1024, max_seq_len=4096, lora_rank_capacity=1024,
+                 lora_max_adapters=128, lora_modules=MODULES, device=0):
+        mask = 0
+        for m in lora_modules:
+            mask |= 1 << MOD_INDEX[m]
+        self.cfg = ModelConfig(hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab, n_layers,
+                               rms_eps, rope_theta, int(bool(rope_mlx_as_written)), max_batch,
+                               kv_block_size, kv_num_blocks, max_seq_len, lora_rank_capacity,
+                               lora_max_adapters, mask, device)
+        L = lib()
+        self._L = L
+        self.ctx = L.aos_init(C.byref(self.cfg))
+        if not self.ctx:
+            raise AosError(-2, last_error())
+        self.vocab, self.hidden, self.n_layers = vocab, hidden, n_layers
+        self.n_kv_heads, self.head_dim = n_kv_heads, head_dim
+        self._sessions = {}
+
+    def close(self):
+        if getattr(self, "ctx", None):
+            self._L.aos_destroy(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc):
+        if rc != 0:
+            raise AosError(rc, last_error(self.ctx))
+        return rc
+
+    # -- identity -------------------------------------------------------
+    def device_name(self) -> str:
+        return self._L.aos_device_name(self.ctx).decode()
+
+    def stream(self):
+        return self._L.aos_stream(self.ctx)
+
+    def attest_determinism(self) -> dict:
+        r = DeterminismReport()
+        self._check(self._L.aos_attest_determinism(self.ctx, C.byref(r)))
+        return {"backend": r.backend.decode(), "device": r.device_name.decode(),
+                "sm": (r.sm_major, r.sm_minor), "fast_math": bool(r.fast_math),
+                "float_atomics": bool(r.float_atomics),
+                "fixed_reduction_order": bool(r.fixed_reduction_order),
+                "build": r.kernel_build_id.decode()}
+
+    def get_metrics(self) -> dict:
+        m = Metrics()
+        self._check(self._L.aos_get_metrics(self.ctx, C.byref(m)))
+        return {f: getattr(m, f) for f, _ in Metrics._fields_}
+
+    def health_check(self):
+        return self._check(self._L.aos_health_check(self.ctx))
+
+    # -- weights (FusedKernels::load) ------------------------------------
+    def load_weight(self, kind, data, layer=0, module=0, on_device=False):
+        n = data.numel() if hasattr(data, "numel") else data.size
+        self._check(self._L.aos_load_weight(self.ctx, kind, layer, module, _p(data), n, int(on_device)))
+
+    def load_host_model(self, m):
+        """Load a model given as per-layer/module bf16 (uint16) arrays (oracle.HostModel layout)."""
+        if m.embed is not None:
+            self.load_weight(W_EMBED, m.embed)
+            self.load_weight(W_LM_HEAD, m.lm_head)
+            self.load_weight(W_FINAL_NORM, m.final_norm)
+        for l in range(m.n_layers):
+            self.load_weight(W_ATTN_NORM, m.attn_norm[l], layer=l)
+            self.load_weight(W_MLP_NORM, m.mlp_norm[l], layer=l)
+            for mod in range(7):
+                self.load_weight(W_PROJ, m.w[mod][l], layer=l, module=mod)
+
+    # -- hot-swap (load_adapter_with_metadata / unload_adapter) ----------
+    def load_adapter_with_metadata(self, adapter_id, rank, alpha, modules):
+        """modules: {(layer, module_index_or_name): (A [rank, in], B [out, rank])} bf16 bits."""
+        self._check(self._L.aos_adapter_new(self.ctx, adapter_id, rank, float(alpha)))
+        for (layer, mod), (A, B) in modules.items():
+            mi = MOD_INDEX[mod] if isinstance(mod, str) else int(mod)
+            dev = hasattr(A, "data_ptr") and A.is_cuda
+            A = A if hasattr(A, "data_ptr") else np.ascontiguousarray(A, np.uint16)
+            B = B if hasattr(B, "data_ptr") else np.ascontiguousarray(B, np.uint16)
+            self._check(self._L.aos_adapter_set_module(self.ctx, adapter_id, layer, mi, _p(A), _p(B), int(dev)))
+
+    def unload_adapter(self, adapter_id):
+        self._check(self._L.aos_adapter_unload(self.ctx, adapter_id))
+
+    def detach_adapter(self, adapter_id):
+        self.unload_adapter(adapter_id)
+
+    def is_loaded(self, adapter_id) -> bool:
+        return bool(self._L.aos_adapter_is_loaded(self.ctx, adapter_id))
+
+    # -- KV cache --------------------------------------------------------
+    def supports_kv_cache(self):
+        return True
+
+    def kv_alloc(self, seq_id, max_tokens):
+        self._check(self._L.aos_kv_alloc(self.ctx, seq_id, max_tokens))
+
+    def kv_free(self, seq_id):
+        self._check(self._L.aos_kv_free(self.ctx, seq_id))
+
+    def kv_set_len(self, seq_id, n):
+        self._check(self._L.aos_kv_set_len(self.ctx, seq_id, n))
+
+    def kv_len(self, seq_id):
+        v = C.c_uint32()
+        self._check(self._L.aos_kv_get_len(self.ctx, seq_id, C.byref(v)))
+        return v.value
+
+    def kv_write(self, seq_id, layer, pos0, k, v):
+        k = np.ascontiguousarray(k, np.uint16)
+        v = np.ascontiguousarray(v, np.uint16)
+        self._check(self._L.aos_kv_write(self.ctx, seq_id, layer, pos0, k.shape[0], _p(k), _p(v), 0))
+
+    def kv_read(self, seq_id, layer, pos0, n):
+        k = np.zeros((n, self.n_kv_heads, self.head_dim), np.uint16)
+        v = np.zeros_like(k)
+        self._check(self._L.aos_kv_read(self.ctx, seq_id, layer, pos0, n, _p(k), _p(v)))
+        return k, v
+
+    def kv_fill_synthetic(self, seed=0, std=1.0):
+        self._check(self._L.aos_kv_fill_synthetic(self.ctx, seed, float(std)))
+
+    def clear_session_cache(self, session_id):
+        sid = self._sessions.pop(session_id, None)
+        if sid is not None:
+            self.kv_free(sid)
+
+    def clear_all_caches(self):
+        self._check(self._L.aos_kv_clear_all(self.ctx))
+        self._sessions.clear()
+
+    def cache_memory_bytes(self):
+        return int(self._L.aos_kv_memory_bytes(self.ctx))
+
+    # -- the step --------------------------------------------------------
+    def run_step_batch(self, rings, token_ids, seq_ids, want_logits=True, want_hidden=False):
+        """One decode token per entry (host arrays); returns (logits [T,V] f32, hidden [T,H] bf16 bits)."""
+        rings = np.ascontiguousarray(rings, RING_DTYPE)
+        tok = np.ascontiguousarray(token_ids, np.uint32)
+        sid = np.ascontiguousarray(seq_ids, np.uint64)
+        T = len(tok)
+        logits = np.zeros((T, self.vocab), np.float32) if want_logits else None
+        hidden = np.zeros((T, self.hidden), np.uint16) if want_hidden else None
+        self._check(self._L.aos_run_step_batch(self.ctx, _p(rings), _p(tok), _p(sid), T, _p(logits), _p(hidden)))
+        return logits, hidden
+
+    def run_step_batch_dev(self, rings, token_ids, seq_ids, logits=None, hidden=None, stream=None):
+        """Device form: rings/token_ids/logits/hidden are torch CUDA tensors; seq_ids a host array."""
+        sid = np.ascontiguousarray(seq_ids, np.uint64)
+        self._check(self._L.aos_run_step_batch_dev(self.ctx, _p(rings), _p(token_ids), _p(sid), len(sid),
+                                                  _p(logits), _p(hidden), stream))
+
+    def layer_step_dev(self, layer, rings, seq_ids, hidden, advance=False, stream=None):
+        sid = np.ascontiguousarray(seq_ids, np.uint64)
+        self._check(self._L.aos_layer_step_dev(self.ctx, layer, _p(rings), _p(sid), len(sid), _p(hidden),
+                                              int(advance), stream))
+
+    def run_step(self, ring: RouterRing, io: IoBuffers):
+        """FusedKernels::run_step for one sequence: every id in io.input_ids is
+        decoded in turn at io.position; output_logits gets the last token's
+        logits and io.position advances by len(input_ids)
+        (mlx-ffi/src/backend.rs:1212-1310)."""
+        if not io.input_ids:
+            raise AosError(-1, "Input token IDs cannot be empty")
+        key = io.session_id
+        if key not in self._sessions:
+            sid = len(self._sessions) + (1 << 62)
+            self.kv_alloc(sid, int(self.cfg.max_seq_len))
+            self._sessions[key] = sid
+        sid = self._sessions[key]
+        self.kv_set_len(sid, io.position)
+        rec = np.zeros(1, RING_DTYPE)
+        rec[0] = ring.to_record()
+        logits = None
+        for tok in io.input_ids:
+            logits, _ = self.run_step_batch(rec, [tok], [sid])
+        io.output_logits[: self.vocab] = logits[0][: len(io.output_logits)]
+        io.position += len(io.input_ids)

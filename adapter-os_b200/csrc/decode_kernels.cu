@@ -1,0 +1,159 @@
+// decode_kernels.cu — the small per-step kernels around the GEMMs:
+// embedding gather, RMSNorm, the LoRA routing prep (touched rank slabs), and
+// synthetic KV fill.  All reductions use a fixed order.
+
+#include "common.cuh"
+
+namespace aos {
+namespace {
+
+// Embedding lookup (mlx_cpp_wrapper_real.cpp:3424-3430 mx::take); ids outside
+// the vocabulary give a zero row (metal/src/kernels/adapteros_kernels.metal:195-234).
+__global__ void embed_kernel(const uint16_t* __restrict__ table, const uint32_t* __restrict__ ids, int T, int H,
+                             int V, uint16_t* __restrict__ out) {
+    const int t = blockIdx.x;
+    if (t >= T) return;
+    const uint32_t id = ids[t];
+    const uint4* src = reinterpret_cast<const uint4*>(table + (size_t)id * H);
+    uint4* dst = reinterpret_cast<uint4*>(out + (size_t)t * H);
+    for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = id < (uint32_t)V ? src[i] : make_uint4(0, 0, 0, 0);
+}
+
+// RMSNorm (mlx_cpp_wrapper_real.cpp:3384-3390): y = x * (w / sqrt(mean(x^2) + eps)).
+// One CTA (256 threads) per token; fixed-order tree reduction; bf16 in/out.
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
+                                                      int T, int H, float eps, uint16_t* __restrict__ y) {
+    const int t = blockIdx.x;
+    if (t >= T) return;
+    const uint16_t* xt = x + (size_t)t * H;
+    float ss = 0.0f;
+    for (int i = threadIdx.x * 8; i < H; i += 256 * 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(xt + i);
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float a = __uint_as_float(u[j] << 16), b = __uint_as_float(u[j] & 0xffff0000u);
+            ss = fmaf(a, a, ss);
+            ss = fmaf(b, b, ss);
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    __shared__ float part[8];
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int i = 0; i < 8; ++i) tot += part[i];
+    const float denom = sqrtf(tot / (float)H + eps);
+    for (int i = threadIdx.x * 8; i < H; i += 256 * 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(xt + i);
+        const uint4 ww = *reinterpret_cast<const uint4*>(w + i);
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+        const uint32_t g[4] = {ww.x, ww.y, ww.z, ww.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float a = __uint_as_float(u[j] << 16), b = __uint_as_float(u[j] & 0xffff0000u);
+            const float wa = __uint_as_float(g[j] << 16), wb = __uint_as_float(g[j] & 0xffff0000u);
+            const float ra = a * __fdiv_rn(wa, denom), rb = b * __fdiv_rn(wb, denom);
+            o[j] = (uint32_t)f2bf(ra) | ((uint32_t)f2bf(rb) << 16);
+        }
+        *reinterpret_cast<uint4*>(y + (size_t)t * H + i) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// Routing prep for the LoRA GEMMs: mark every 16-column rank slab of the
+// arena that holds a column of an adapter selected (q15 > 0) by any token,
+// then compact the marks in ascending slab order.  One CTA of 1024 threads.
+__global__ void __launch_bounds__(1024) lora_prep_kernel(const aos_router_ring* __restrict__ rings, int T,
+                                                         const int* __restrict__ col_off, const int* __restrict__ rank,
+                                                         int max_adapters, int n_slab_total, int* __restrict__ slabs,
+                                                         int* __restrict__ n_slabs) {
+    extern __shared__ int marks[];  // [n_slab_total]
+    __shared__ int warp_sums[32];
+    for (int i = threadIdx.x; i < n_slab_total; i += blockDim.x) marks[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < T * AOS_MAX_K; i += blockDim.x) {
+        const aos_router_ring& r = rings[i / AOS_MAX_K];
+        const int s = i % AOS_MAX_K;
+        if (s >= (int)r.top_k || r.gates_q15[s] <= 0) continue;
+        const int a = r.indices[s];
+        if (a >= max_adapters) continue;
+        const int c0 = col_off[a], rk = rank[a];
+        if (c0 < 0 || rk <= 0) continue;
+        for (int sl = c0 / 16; sl <= (c0 + rk - 1) / 16; ++sl) marks[sl] = 1;  // benign same-value race
+    }
+    __syncthreads();
+    // ordered compaction: chunked exclusive scan over marks
+    int running = 0;
+    for (int base = 0; base < n_slab_total; base += blockDim.x) {
+        const int i = base + threadIdx.x;
+        const int m = i < n_slab_total ? marks[i] : 0;
+        const unsigned bal = __ballot_sync(0xffffffffu, m);
+        const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+        if (lane == 0) warp_sums[w] = __popc(bal);
+        __syncthreads();
+        int before = running;
+        for (int j = 0; j < w; ++j) before += warp_sums[j];
+        before += __popc(bal & ((1u << lane) - 1u));
+        if (m) slabs[before] = i;
+        int tot = 0;
+        for (int j = 0; j < (int)(blockDim.x >> 5); ++j) tot += warp_sums[j];
+        __syncthreads();
+        running += tot;
+    }
+    if (threadIdx.x == 0) *n_slabs = running;
+}
+
+// SplitMix64-based synthetic bf16 fill ~N(0, std) (Box-Muller), seeded and
+// position-independent so any page can be regenerated.
+__device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+
+__global__ void fill_normal_bf16(uint16_t* __restrict__ p, size_t n, uint64_t seed, float std) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < (n + 1) / 2; i += (size_t)gridDim.x * blockDim.x) {
+        const uint64_t r = splitmix64(seed ^ (i * 0xD1B54A32D192ED03ull));
+        const float u1 = ((float)(r >> 40) + 0.5f) * (1.0f / 16777216.0f);
+        const float u2 = (float)((r >> 16) & 0xFFFFFF) * (1.0f / 16777216.0f);
+        const float rad = sqrtf(-2.0f * logf(u1)) * std;
+        float s, c;
+        sincospif(2.0f * u2, &s, &c);
+        p[2 * i] = f2bf(rad * c);
+        if (2 * i + 1 < n) p[2 * i + 1] = f2bf(rad * s);
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_embed(const uint16_t* table, const uint32_t* ids, int T, int H, int V, uint16_t* out,
+                         cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    embed_kernel<<<T, 128, 0, s>>>(table, ids, T, H, V, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* w, int T, int H, float eps, uint16_t* y,
+                           cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    rmsnorm_kernel<<<T, 256, 0, s>>>(x, w, T, H, eps, y);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_lora_prep(const aos_router_ring* rings, int T, const int* col_off, const int* rank,
+                             int max_adapters, int n_slab_total, int* slabs, int* n_slabs, cudaStream_t s) {
+    lora_prep_kernel<<<1, 1024, (size_t)n_slab_total * sizeof(int), s>>>(rings, T, col_off, rank, max_adapters,
+                                                                        n_slab_total, slabs, n_slabs);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fill_normal(uint16_t* p, size_t n, uint64_t seed, float std, cudaStream_t s) {
+    if (!n) return cudaSuccess;
+    fill_normal_bf16<<<148 * 8, 256, 0, s>>>(p, n, seed, std);
+    return cudaGetLastError();
+}
+
+}  // namespace aos

@@ -1,0 +1,1036 @@
+// runtime.cu — the backend context behind the C ABI: base weights, the LoRA
+// adapter arena, the paged KV cache, per-batch-size step plans (prebuilt TMA
+// descriptors + a captured CUDA graph) and the decode step itself.
+//
+// This is the B200 counterpart of a FusedKernels backend
+// (crates/adapteros-lora-kernel-api/src/lib.rs:308-716): load() -> aos_init +
+// aos_load_weight; load_adapter_with_metadata()/unload_adapter() ->
+// aos_adapter_*; run_step() -> aos_run_step_batch; KV-cache methods ->
+// aos_kv_*; get_metrics()/health_check()/attest_determinism().
+//
+// Arena layout (per layer and LoRA module, allocated once at init):
+//   A_cat  [R][in]          bf16  lora_A rows of every adapter, adapter a at rows [off_a, off_a + r_a)
+//   B_slab [R/16][out][16]  bf16  lora_B columns grouped in 16-column slabs
+// where R is the arena's rank capacity.  Column ranges are handed out in
+// 8-column units (ranks 8, 16, 32, 64 ... share slabs only in the rank-8 case),
+// so one decode step streams exactly the slabs its tokens selected.
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "tc_gemm.cuh"
+
+namespace aos {
+cudaError_t launch_embed(const uint16_t*, const uint32_t*, int, int, int, uint16_t*, cudaStream_t);
+cudaError_t launch_rmsnorm(const uint16_t*, const uint16_t*, int, int, float, uint16_t*, cudaStream_t);
+cudaError_t launch_lora_prep(const aos_router_ring*, int, const int*, const int*, int, int, int*, int*, cudaStream_t);
+cudaError_t launch_fill_normal(uint16_t*, size_t, uint64_t, float, cudaStream_t);
+cudaError_t launch_attention(const CUtensorMap&, const CUtensorMap&, const uint16_t*, const int*, const int*, float*,
+                             float*, int, int, int, int, int, int, int, int*, uint16_t*, cudaStream_t);
+int attn_max_chunks(int max_seq_len);
+cudaError_t attn_configure();
+}  // namespace aos
+
+using namespace aos;
+
+namespace {
+
+constexpr int kGroupQKV = 0, kGroupO = 1, kGroupGU = 2, kGroupD = 3;
+
+struct AdapterEntry {
+    int off = -1;
+    int rank = 0;
+    float alpha = 0.f;
+};
+
+struct Sequence {
+    std::vector<int> blocks;
+    uint32_t len = 0;
+    uint32_t cap = 0;
+};
+
+struct LayerPlan {
+    TcParams shrink[4];  // per group
+    TcParams gemm[4];
+    int shrink_grid[4], gemm_grid[4];
+};
+
+struct StepPlan {
+    int T = 0, T_pad = 0;
+    std::vector<LayerPlan> layers;
+    TcParams lm_head;
+    int lm_grid = 0;
+    void* logits_dst = nullptr;
+    cudaGraphExec_t graph = nullptr;
+    void* graph_logits = nullptr;
+    bool graph_valid = false;
+};
+
+}  // namespace
+
+struct aos_ctx {
+    aos_model_config cfg{};
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    std::string dev_name;
+    uint32_t QD = 0, KVD = 0, G = 0;
+    uint32_t module_mask = 0;
+
+    // base weights
+    uint16_t *embed = nullptr, *lm_head = nullptr, *final_norm = nullptr;
+    std::vector<uint16_t*> attn_norm, mlp_norm, w_qkv, w_o, w_gate, w_up, w_down;
+    std::vector<uint8_t> loaded;  // bookkeeping of loaded tensors
+    uint64_t base_bytes = 0;
+
+    // arena
+    int R = 0;
+    std::vector<uint16_t*> A[AOS_NUM_MODULES], B[AOS_NUM_MODULES];  // [layer]
+    int *d_col_owner = nullptr, *d_col_off = nullptr, *d_rank = nullptr;
+    float* d_scale = nullptr;
+    std::vector<int> col_owner;  // host mirror, 8-column units
+    std::unordered_map<uint16_t, AdapterEntry> adapters;
+    uint64_t arena_bytes = 0;
+
+    // KV cache
+    uint16_t *k_pool = nullptr, *v_pool = nullptr;
+    std::vector<int> free_blocks;
+    std::unordered_map<uint64_t, Sequence> seqs;
+    int max_blocks = 0;
+    CUtensorMap tm_k{}, tm_v{};
+
+    // scratch
+    int T_cap = 0;
+    uint16_t *d_hidden = nullptr, *d_normed = nullptr, *d_q = nullptr, *d_attn = nullptr, *d_act = nullptr;
+    uint16_t* d_hm[AOS_NUM_MODULES] = {};
+    int *d_slabs = nullptr, *d_n_slabs = nullptr;
+    int *d_block_tables = nullptr, *d_ctx_lens = nullptr;
+    int *h_block_tables = nullptr, *h_ctx_lens = nullptr;  // pinned staging
+    aos_router_ring* d_rings = nullptr;
+    uint32_t* d_tokens = nullptr;
+    float* d_logits = nullptr;
+    float *d_rope = nullptr;
+    float *d_attn_part = nullptr, *d_attn_ml = nullptr;
+    int attn_chunks = 0;
+    float* d_ws = nullptr;
+    size_t ws_bytes = 0;
+    int* d_counters = nullptr;
+    int* d_err = nullptr;
+    std::map<int, std::unique_ptr<StepPlan>> plans;
+
+    // metrics
+    aos_metrics m{};
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+
+    int fail(int code, const std::string& msg) {
+        err = msg;
+        return code;
+    }
+};
+
+namespace {
+
+#define CTX_CUDA(ctx, expr)                                                                  \
+    do {                                                                                     \
+        cudaError_t _e = (expr);                                                             \
+        if (_e != cudaSuccess)                                                               \
+            return (ctx)->fail(AOS_ERR_CUDA, std::string(#expr ": ") + cudaGetErrorString(_e)); \
+    } while (0)
+
+uint32_t mod_out(const aos_ctx* c, int m) {
+    const uint32_t H = c->cfg.hidden, I = c->cfg.intermediate;
+    const uint32_t outs[7] = {c->QD, c->KVD, c->KVD, H, I, I, H};
+    return outs[m];
+}
+uint32_t mod_in(const aos_ctx* c, int m) {
+    const uint32_t H = c->cfg.hidden, I = c->cfg.intermediate;
+    const uint32_t ins[7] = {H, H, H, c->QD, H, H, I};
+    return ins[m];
+}
+
+template <class T>
+cudaError_t dalloc(T** p, size_t n_elems, uint64_t* counter = nullptr) {
+    cudaError_t e = cudaMalloc((void**)p, n_elems * sizeof(T) + 256);
+    if (e == cudaSuccess) {
+        e = cudaMemset(*p, 0, n_elems * sizeof(T));
+        if (counter) *counter += n_elems * sizeof(T);
+    }
+    return e;
+}
+
+int splits_for(int tiles, int kb) {
+    const int sms = tc_num_sms();
+    int s = tiles > 0 ? sms / tiles : 1;
+    s = std::max(1, std::min(s, kb / 2));
+    return std::min(s, 16);
+}
+
+// Build the TcParams of every GEMM of one layer for a padded batch T_pad.
+int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
+    const uint32_t H = c->cfg.hidden, I = c->cfg.intermediate;
+    const int T_pad = std::max(32, ((T + 15) / 16) * 16);
+    const int smem_budget = 227 * 1024;
+    int rc;
+    auto x_map = [&](CUtensorMap* m, const uint16_t* buf, uint32_t K) {
+        return tc_encode_2d(m, buf, K, (uint64_t)c->T_cap, (uint64_t)K * 2, 64, (uint32_t)T_pad, 128);
+    };
+    auto w_map = [&](CUtensorMap* m, const uint16_t* w, uint32_t rows, uint32_t K) {
+        return tc_encode_2d(m, w, K, rows, (uint64_t)K * 2, 64, 128, 128);
+    };
+    auto a_map = [&](CUtensorMap* m, int mod) {
+        const uint32_t K = mod_in(c, mod);
+        return tc_encode_2d(m, c->A[mod][layer], K, (uint64_t)c->R, (uint64_t)K * 2, 64, 16, 128);
+    };
+    auto b_map = [&](CUtensorMap* m, int mod) {
+        const uint32_t out = mod_out(c, mod);
+        return tc_encode_3d(m, c->B[mod][layer], 16, out, (uint64_t)c->R / 16, 32, (uint64_t)out * 32, 16, 128, 1, 32);
+    };
+    auto h_map = [&](CUtensorMap* m, int mod) {
+        return tc_encode_2d(m, c->d_hm[mod], (uint64_t)c->R, (uint64_t)c->T_cap, (uint64_t)c->R * 2, 16,
+                            (uint32_t)T_pad, 32);
+    };
+    auto common = [&](TcParams& p) {
+        std::memset(&p, 0, sizeof(p));
+        p.T = T;
+        p.slabs = c->d_slabs;
+        p.n_slabs = c->d_n_slabs;
+        p.ws = c->d_ws;
+        p.counters = c->d_counters;
+        p.err = c->d_err;
+        p.R = c->R;
+        p.col_owner = c->d_col_owner;
+        p.adapter_scale = c->d_scale;
+        p.rings = c->d_rings;
+        p.max_adapters = (int)c->cfg.lora_max_adapters;
+        p.layer = layer;
+    };
+    const bool lora[4] = {(c->module_mask & 0x7u) != 0, (c->module_mask & 0x8u) != 0, (c->module_mask & 0x30u) != 0,
+                          (c->module_mask & 0x40u) != 0};
+    const int groups_mods[4][3] = {{AOS_MOD_Q, AOS_MOD_K, AOS_MOD_V}, {AOS_MOD_O, -1, -1},
+                                   {AOS_MOD_GATE, AOS_MOD_UP, -1}, {AOS_MOD_DOWN, -1, -1}};
+    const uint16_t* group_x[4] = {c->d_normed, c->d_attn, c->d_normed, c->d_act};
+    const uint32_t group_k[4] = {H, c->QD, H, I};
+
+    for (int g = 0; g < 4; ++g) {
+        // ---------------- shrink: hm = gate * (A_cat x) for every module of the group
+        TcParams& s = lp.shrink[g];
+        common(s);
+        lp.shrink_grid[g] = 0;
+        if (lora[g]) {
+            s.mode = TC_SHRINK_HM;
+            s.shrink = 1;
+            s.n_sub = 1;
+            s.kb = (int)(group_k[g] / 64);
+            int nseg = 0;
+            for (int j = 0; j < 3; ++j) {
+                const int mod = groups_mods[g][j];
+                if (mod < 0) continue;
+                if ((rc = a_map(&s.tm_w[nseg], mod))) return rc;
+                s.out[nseg] = c->d_hm[mod];
+                s.seg_module[nseg] = mod;
+                ++nseg;
+            }
+            s.n_seg = nseg;
+            if ((rc = x_map(&s.tm_x, group_x[g], group_k[g]))) return rc;
+            const int max_tiles = nseg * (c->R / 128 + 1);
+            s.splits = splits_for(max_tiles, s.kb);
+            if ((rc = tc_prepare(s, smem_budget))) return rc;
+            lp.shrink_grid[g] = std::min(max_tiles * s.splits, tc_num_sms());
+        }
+        // ---------------- base GEMM + fused LoRA expand + epilogue
+        TcParams& p = lp.gemm[g];
+        common(p);
+        p.lora = lora[g] ? 1 : 0;
+        p.kb = (int)(group_k[g] / 64);
+        if ((rc = x_map(&p.tm_x, group_x[g], group_k[g]))) return rc;
+        int tiles = 0;
+        if (g == kGroupQKV) {
+            p.mode = TC_QKV_ROPE;
+            p.n_sub = 1;
+            p.n_seg = 3;
+            const uint32_t rows_total = c->QD + 2 * c->KVD;
+            const uint32_t r0[3] = {0, c->QD, c->QD + c->KVD};
+            const uint32_t nr[3] = {c->QD, c->KVD, c->KVD};
+            for (int j = 0; j < 3; ++j) {
+                if ((rc = w_map(&p.tm_w[j], c->w_qkv[layer], rows_total, H))) return rc;
+                p.seg_wrow0[j] = (int)r0[j];
+                p.seg_tiles[j] = (int)(nr[j] / 128);
+                p.seg_rows[j] = (int)nr[j];
+                p.seg_module[j] = groups_mods[g][j];
+                p.seg_out0[j] = 0;
+                if (p.lora) {
+                    if ((rc = b_map(&p.tm_lb[j], groups_mods[g][j]))) return rc;
+                    if ((rc = h_map(&p.tm_lh[j], groups_mods[g][j]))) return rc;
+                }
+                tiles += p.seg_tiles[j];
+            }
+            p.out[0] = c->d_q;
+            p.ld_out = (int)c->QD;
+            p.rope = c->d_rope;
+            p.k_pool = c->k_pool;
+            p.v_pool = c->v_pool;
+            p.block_tables = c->d_block_tables;
+            p.ctx_lens = c->d_ctx_lens;
+            p.max_blocks = c->max_blocks;
+            p.num_blocks = (int)c->cfg.kv_num_blocks;
+            p.nkv = (int)c->cfg.n_kv_heads;
+        } else if (g == kGroupGU) {
+            p.mode = TC_SWIGLU;
+            p.n_sub = 2;
+            p.n_seg = 1;
+            if ((rc = w_map(&p.tm_w[0], c->w_gate[layer], I, H))) return rc;
+            if ((rc = w_map(&p.tm_w[1], c->w_up[layer], I, H))) return rc;
+            if (p.lora) {
+                if ((rc = b_map(&p.tm_lb[0], AOS_MOD_GATE))) return rc;
+                if ((rc = b_map(&p.tm_lb[1], AOS_MOD_UP))) return rc;
+                if ((rc = h_map(&p.tm_lh[0], AOS_MOD_GATE))) return rc;
+                if ((rc = h_map(&p.tm_lh[1], AOS_MOD_UP))) return rc;
+            }
+            p.seg_tiles[0] = (int)((I + 127) / 128);
+            p.seg_rows[0] = (int)I;
+            p.seg_module[0] = AOS_MOD_GATE;
+            p.out[0] = c->d_act;
+            p.ld_out = (int)I;
+            tiles = p.seg_tiles[0];
+        } else {
+            const int mod = g == kGroupO ? AOS_MOD_O : AOS_MOD_DOWN;
+            p.mode = TC_RESID_BF16;
+            p.n_sub = 1;
+            p.n_seg = 1;
+            if ((rc = w_map(&p.tm_w[0], g == kGroupO ? c->w_o[layer] : c->w_down[layer], H, group_k[g]))) return rc;
+            if (p.lora) {
+                if ((rc = b_map(&p.tm_lb[0], mod))) return rc;
+                if ((rc = h_map(&p.tm_lh[0], mod))) return rc;
+            }
+            p.seg_tiles[0] = (int)((H + 127) / 128);
+            p.seg_rows[0] = (int)H;
+            p.seg_module[0] = mod;
+            p.resid = c->d_hidden;
+            p.ld_out = (int)H;
+            tiles = p.seg_tiles[0];
+        }
+        p.splits = splits_for(tiles, p.kb);
+        if ((rc = tc_prepare(p, smem_budget))) return rc;
+        lp.gemm_grid[g] = std::min(tiles * p.splits, tc_num_sms());
+    }
+    return AOS_OK;
+}
+
+size_t ws_need(const TcParams& p, int tiles) {
+    return p.splits > 1 ? (size_t)tiles * p.splits * p.n_sub * p.T_pad * 128 * 4 : 0;
+}
+
+int get_plan(aos_ctx* c, int T, StepPlan** out) {
+    const int T_pad = std::max(32, ((T + 15) / 16) * 16);
+    auto it = c->plans.find(T);
+    if (it != c->plans.end()) {
+        *out = it->second.get();
+        return AOS_OK;
+    }
+    auto plan = std::make_unique<StepPlan>();
+    plan->T = T;
+    plan->T_pad = T_pad;
+    plan->layers.resize(c->cfg.n_layers);
+    for (uint32_t l = 0; l < c->cfg.n_layers; ++l) {
+        int rc = build_layer_plan(c, (int)l, T, plan->layers[l]);
+        if (rc) return c->fail(rc, "building the GEMM plan failed (tensor map encode)");
+    }
+    // lm_head: logits = normed . lm_head^T (f32 out)
+    TcParams& p = plan->lm_head;
+    std::memset(&p, 0, sizeof(p));
+    p.T = T;
+    p.mode = TC_STORE_F32;
+    p.n_sub = 1;
+    p.n_seg = 1;
+    p.kb = (int)(c->cfg.hidden / 64);
+    p.err = c->d_err;
+    p.ws = c->d_ws;
+    p.counters = c->d_counters;
+    const uint32_t V = c->cfg.vocab;
+    int rc = tc_encode_2d(&p.tm_w[0], c->lm_head, c->cfg.hidden, V, (uint64_t)c->cfg.hidden * 2, 64, 128, 128);
+    rc |= tc_encode_2d(&p.tm_x, c->d_normed, c->cfg.hidden, (uint64_t)c->T_cap, (uint64_t)c->cfg.hidden * 2, 64,
+                       (uint32_t)T_pad, 128);
+    if (rc) return c->fail(AOS_ERR_CUDA, "lm_head tensor map encode failed");
+    p.seg_tiles[0] = (int)((V + 127) / 128);
+    p.seg_rows[0] = (int)V;
+    p.out[0] = c->d_logits;
+    p.ld_out = (int)V;
+    p.splits = 1;
+    if ((rc = tc_prepare(p, 227 * 1024))) return c->fail(rc, "lm_head plan");
+    plan->lm_grid = std::min(p.seg_tiles[0], tc_num_sms());
+    // workspace for split-K partials
+    size_t need = 0;
+    for (auto& lp : plan->layers)
+        for (int g = 0; g < 4; ++g) {
+            int tiles = 0;
+            for (int j = 0; j < lp.gemm[g].n_seg; ++j) tiles += lp.gemm[g].seg_tiles[j];
+            need = std::max(need, ws_need(lp.gemm[g], tiles));
+            need = std::max(need, ws_need(lp.shrink[g], lp.shrink[g].n_seg * (c->R / 128 + 1)));
+        }
+    if (need > c->ws_bytes) {
+        if (c->d_ws) cudaFree(c->d_ws);
+        c->d_ws = nullptr;
+        c->ws_bytes = 0;
+        CTX_CUDA(c, cudaMalloc((void**)&c->d_ws, need));
+        c->ws_bytes = need;
+        // all cached plans point at the workspace: refresh them
+        for (auto& kv : c->plans)
+            for (auto& lp : kv.second->layers)
+                for (int g = 0; g < 4; ++g) lp.gemm[g].ws = lp.shrink[g].ws = c->d_ws;
+        for (auto& kv : c->plans) kv.second->graph_valid = false;
+        for (auto& lp : plan->layers)
+            for (int g = 0; g < 4; ++g) lp.gemm[g].ws = lp.shrink[g].ws = c->d_ws;
+    }
+    *out = plan.get();
+    c->plans[T] = std::move(plan);
+    return AOS_OK;
+}
+
+#define LAUNCH(ctx, expr)                                                                       \
+    do {                                                                                        \
+        cudaError_t _e = (expr);                                                                \
+        if (_e != cudaSuccess)                                                                  \
+            return (ctx)->fail(AOS_ERR_CUDA, std::string("launch " #expr ": ") + cudaGetErrorString(_e)); \
+    } while (0)
+
+// Enqueue one decoder layer on `s` (hidden state in ctx->d_hidden).
+int enqueue_layer(aos_ctx* c, const StepPlan& plan, int layer, cudaStream_t s) {
+    const LayerPlan& lp = plan.layers[layer];
+    const int T = plan.T;
+    const uint32_t H = c->cfg.hidden;
+    LAUNCH(c, launch_rmsnorm(c->d_hidden, c->attn_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
+    if (lp.shrink_grid[kGroupQKV]) LAUNCH(c, tc_launch(lp.shrink[kGroupQKV], lp.shrink_grid[kGroupQKV], s));
+    LAUNCH(c, tc_launch(lp.gemm[kGroupQKV], lp.gemm_grid[kGroupQKV], s));
+    LAUNCH(c, launch_attention(c->tm_k, c->tm_v, c->d_q, c->d_block_tables, c->d_ctx_lens, c->d_attn_part, c->d_attn_ml, T,
+                               (int)c->cfg.n_heads, (int)c->cfg.n_kv_heads, layer, (int)c->cfg.kv_num_blocks,
+                               c->max_blocks, c->attn_chunks, c->d_err, c->d_attn, s));
+    if (lp.shrink_grid[kGroupO]) LAUNCH(c, tc_launch(lp.shrink[kGroupO], lp.shrink_grid[kGroupO], s));
+    LAUNCH(c, tc_launch(lp.gemm[kGroupO], lp.gemm_grid[kGroupO], s));
+    LAUNCH(c, launch_rmsnorm(c->d_hidden, c->mlp_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
+    if (lp.shrink_grid[kGroupGU]) LAUNCH(c, tc_launch(lp.shrink[kGroupGU], lp.shrink_grid[kGroupGU], s));
+    LAUNCH(c, tc_launch(lp.gemm[kGroupGU], lp.gemm_grid[kGroupGU], s));
+    if (lp.shrink_grid[kGroupD]) LAUNCH(c, tc_launch(lp.shrink[kGroupD], lp.shrink_grid[kGroupD], s));
+    LAUNCH(c, tc_launch(lp.gemm[kGroupD], lp.gemm_grid[kGroupD], s));
+    return AOS_OK;
+}
+
+// Device part of a decode step: routing prep, embedding, layers, final norm, lm_head.
+int enqueue_step(aos_ctx* c, StepPlan& plan, bool with_logits, cudaStream_t s) {
+    const int T = plan.T;
+    LAUNCH(c, launch_lora_prep(c->d_rings, T, c->d_col_off, c->d_rank, (int)c->cfg.lora_max_adapters, c->R / 16,
+                               c->d_slabs, c->d_n_slabs, s));
+    LAUNCH(c, launch_embed(c->embed, c->d_tokens, T, (int)c->cfg.hidden, (int)c->cfg.vocab, c->d_hidden, s));
+    for (uint32_t l = 0; l < c->cfg.n_layers; ++l) {
+        int rc = enqueue_layer(c, plan, (int)l, s);
+        if (rc) return rc;
+    }
+    if (with_logits) {
+        LAUNCH(c, launch_rmsnorm(c->d_hidden, c->final_norm, T, (int)c->cfg.hidden, c->cfg.rms_eps, c->d_normed, s));
+        LAUNCH(c, tc_launch(plan.lm_head, plan.lm_grid, s));
+    }
+    return AOS_OK;
+}
+
+bool use_graphs() {
+    const char* e = getenv("AOS_NO_GRAPH");
+    return !(e && e[0] == '1');
+}
+
+int run_step_device(aos_ctx* c, int T, bool with_logits, cudaStream_t s) {
+    StepPlan* plan = nullptr;
+    int rc = get_plan(c, T, &plan);
+    if (rc) return rc;
+    if (!use_graphs()) return enqueue_step(c, *plan, with_logits, s);
+    if (!plan->graph_valid || (plan->graph_logits != (void*)(with_logits ? c->d_logits : nullptr))) {
+        if (plan->graph) cudaGraphExecDestroy(plan->graph);
+        plan->graph = nullptr;
+        cudaGraph_t g;
+        CTX_CUDA(c, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        rc = enqueue_step(c, *plan, with_logits, s);
+        cudaError_t e = cudaStreamEndCapture(s, &g);
+        if (rc) return rc;
+        if (e != cudaSuccess) return c->fail(AOS_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+        e = cudaGraphInstantiate(&plan->graph, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) return c->fail(AOS_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+        plan->graph_valid = true;
+        plan->graph_logits = with_logits ? c->d_logits : nullptr;
+    }
+    CTX_CUDA(c, cudaGraphLaunch(plan->graph, s));
+    return AOS_OK;
+}
+
+// Resolve sequences to page tables and positions for a step (host side).
+int stage_sequences(aos_ctx* c, const uint64_t* seq_ids, uint32_t T) {
+    if (T > (uint32_t)c->cfg.max_batch) return c->fail(AOS_ERR_INVALID, "T exceeds max_batch");
+    for (uint32_t t = 0; t < T; ++t) {
+        auto it = c->seqs.find(seq_ids[t]);
+        if (it == c->seqs.end()) return c->fail(AOS_ERR_NOT_FOUND, "unknown sequence id " + std::to_string(seq_ids[t]));
+        Sequence& sq = it->second;
+        if (sq.len >= sq.cap) return c->fail(AOS_ERR_NOMEM, "sequence " + std::to_string(seq_ids[t]) + " is full");
+        for (uint32_t u = 0; u < t; ++u)
+            if (seq_ids[u] == seq_ids[t]) return c->fail(AOS_ERR_INVALID, "a sequence appears twice in one step");
+        int* row = c->h_block_tables + (size_t)t * c->max_blocks;
+        std::fill(row, row + c->max_blocks, 0);
+        std::copy(sq.blocks.begin(), sq.blocks.end(), row);
+        c->h_ctx_lens[t] = (int)sq.len;
+    }
+    return AOS_OK;
+}
+
+int upload_tables(aos_ctx* c, uint32_t T, cudaStream_t s) {
+    CTX_CUDA(c, cudaMemcpyAsync(c->d_block_tables, c->h_block_tables, (size_t)T * c->max_blocks * 4,
+                                cudaMemcpyHostToDevice, s));
+    CTX_CUDA(c, cudaMemcpyAsync(c->d_ctx_lens, c->h_ctx_lens, (size_t)T * 4, cudaMemcpyHostToDevice, s));
+    return AOS_OK;
+}
+
+void advance(aos_ctx* c, const uint64_t* seq_ids, uint32_t T) {
+    for (uint32_t t = 0; t < T; ++t) c->seqs[seq_ids[t]].len += 1;
+    c->m.steps += 1;
+    c->m.tokens += T;
+}
+
+int check_device_error(aos_ctx* c) {
+    int e = 0;
+    CTX_CUDA(c, cudaMemcpy(&e, c->d_err, 4, cudaMemcpyDeviceToHost));
+    if (e) return c->fail(e, "a bounded device-side wait timed out (the kernel returned early)");
+    return AOS_OK;
+}
+
+}  // namespace
+
+// ============================================================================ C ABI
+extern "C" {
+
+const char* aos_last_error(const aos_ctx* ctx) { return ctx ? ctx->err.c_str() : global_error(); }
+
+aos_ctx* aos_init(const aos_model_config* cfg) {
+    if (!cfg) {
+        set_global_error("aos_init: cfg is NULL");
+        return nullptr;
+    }
+    const aos_model_config& k = *cfg;
+    if (k.head_dim != 128 || k.n_heads == 0 || k.n_kv_heads == 0 || k.n_heads % k.n_kv_heads ||
+        k.n_heads / k.n_kv_heads > 16 || k.hidden % 128 || k.intermediate % 128 || k.n_layers == 0 ||
+        k.kv_block_size != 16 || k.max_batch == 0 || k.max_batch > 256 || k.vocab == 0 || k.kv_num_blocks == 0 ||
+        k.max_seq_len == 0 || k.lora_rank_capacity % 16 || k.lora_max_adapters > 65535) {
+        set_global_error("aos_init: unsupported config (head_dim 128, hidden/intermediate % 128, KV block 16, "
+                         "max_batch <= 256, rank capacity % 16, GQA group <= 16)");
+        return nullptr;
+    }
+    if (require_device(k.device)) return nullptr;
+    if (cudaSetDevice(k.device) != cudaSuccess) {
+        set_global_error("aos_init: cudaSetDevice failed");
+        return nullptr;
+    }
+    auto c = std::make_unique<aos_ctx>();
+    c->cfg = k;
+    c->device = k.device;
+    c->QD = k.n_heads * k.head_dim;
+    c->KVD = k.n_kv_heads * k.head_dim;
+    c->G = k.n_heads / k.n_kv_heads;
+    uint32_t mask = k.lora_module_mask ? k.lora_module_mask : 0x7Fu;
+    // a fused GEMM group shares one LoRA flag
+    if (mask & 0x7u) mask |= 0x7u;
+    if (mask & 0x30u) mask |= 0x30u;
+    if (k.lora_rank_capacity == 0 || k.lora_max_adapters == 0) mask = 0;
+    c->module_mask = mask;
+    c->R = mask ? (int)k.lora_rank_capacity : 16;
+    c->T_cap = std::max(32, (int)((k.max_batch + 15) / 16) * 16);
+    c->max_blocks = (int)((k.max_seq_len + 15) / 16);
+    cudaDeviceProp prop;
+    cudaGetDeviceProperties(&prop, k.device);
+    c->dev_name = prop.name;
+    auto fail_init = [&](const char* what, cudaError_t e) -> aos_ctx* {
+        set_global_error(std::string("aos_init: ") + what + ": " + cudaGetErrorString(e));
+        return nullptr;
+    };
+    cudaError_t e;
+#define INIT_CHECK(expr, what)                 \
+    if ((e = (expr)) != cudaSuccess) return fail_init(what, e);
+    INIT_CHECK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream");
+    const uint32_t L = k.n_layers, H = k.hidden, I = k.intermediate, V = k.vocab;
+    // base weights
+    INIT_CHECK(dalloc(&c->embed, (size_t)V * H, &c->base_bytes), "embed");
+    INIT_CHECK(dalloc(&c->lm_head, (size_t)V * H, &c->base_bytes), "lm_head");
+    INIT_CHECK(dalloc(&c->final_norm, (size_t)H, &c->base_bytes), "final_norm");
+    c->attn_norm.resize(L);
+    c->mlp_norm.resize(L);
+    c->w_qkv.resize(L);
+    c->w_o.resize(L);
+    c->w_gate.resize(L);
+    c->w_up.resize(L);
+    c->w_down.resize(L);
+    for (uint32_t l = 0; l < L; ++l) {
+        INIT_CHECK(dalloc(&c->attn_norm[l], H, &c->base_bytes), "norm");
+        INIT_CHECK(dalloc(&c->mlp_norm[l], H, &c->base_bytes), "norm");
+        INIT_CHECK(dalloc(&c->w_qkv[l], (size_t)(c->QD + 2 * c->KVD) * H, &c->base_bytes), "w_qkv");
+        INIT_CHECK(dalloc(&c->w_o[l], (size_t)H * c->QD, &c->base_bytes), "w_o");
+        INIT_CHECK(dalloc(&c->w_gate[l], (size_t)I * H, &c->base_bytes), "w_gate");
+        INIT_CHECK(dalloc(&c->w_up[l], (size_t)I * H, &c->base_bytes), "w_up");
+        INIT_CHECK(dalloc(&c->w_down[l], (size_t)H * I, &c->base_bytes), "w_down");
+    }
+    // arena
+    for (int m = 0; m < AOS_NUM_MODULES; ++m) {
+        c->A[m].assign(L, nullptr);
+        c->B[m].assign(L, nullptr);
+        if (!(mask & (1u << m))) continue;
+        for (uint32_t l = 0; l < L; ++l) {
+            INIT_CHECK(dalloc(&c->A[m][l], (size_t)c->R * mod_in(c.get(), m), &c->arena_bytes), "arena A");
+            INIT_CHECK(dalloc(&c->B[m][l], (size_t)c->R * mod_out(c.get(), m), &c->arena_bytes), "arena B");
+        }
+    }
+    INIT_CHECK(dalloc(&c->d_col_owner, (size_t)c->R), "col_owner");
+    INIT_CHECK(cudaMemset(c->d_col_owner, 0xFF, (size_t)c->R * 4), "col_owner");
+    const uint32_t NA = std::max(1u, k.lora_max_adapters);
+    INIT_CHECK(dalloc(&c->d_col_off, NA), "col_off");
+    INIT_CHECK(cudaMemset(c->d_col_off, 0xFF, (size_t)NA * 4), "col_off");
+    INIT_CHECK(dalloc(&c->d_rank, NA), "rank");
+    INIT_CHECK(dalloc(&c->d_scale, NA), "scale");
+    c->col_owner.assign(c->R / 8, -1);
+    // KV cache
+    const size_t kv_elems = (size_t)L * k.kv_num_blocks * k.n_kv_heads * 16 * 128;
+    INIT_CHECK(dalloc(&c->k_pool, kv_elems), "k_pool");
+    INIT_CHECK(dalloc(&c->v_pool, kv_elems), "v_pool");
+    for (int b = (int)k.kv_num_blocks - 1; b >= 0; --b) c->free_blocks.push_back(b);
+    const uint64_t kv_rows = (uint64_t)L * k.kv_num_blocks * k.n_kv_heads * 16;
+    if (tc_encode_2d(&c->tm_k, c->k_pool, 128, kv_rows, 256, 64, 16, 128) ||
+        tc_encode_2d(&c->tm_v, c->v_pool, 128, kv_rows, 256, 64, 16, 128)) {
+        set_global_error("aos_init: KV tensor map encode failed");
+        return nullptr;
+    }
+    // scratch
+    const size_t TC = (size_t)c->T_cap;
+    INIT_CHECK(dalloc(&c->d_hidden, TC * H), "hidden");
+    INIT_CHECK(dalloc(&c->d_normed, TC * H), "normed");
+    INIT_CHECK(dalloc(&c->d_q, TC * c->QD), "q");
+    INIT_CHECK(dalloc(&c->d_attn, TC * c->QD), "attn");
+    INIT_CHECK(dalloc(&c->d_act, TC * I), "act");
+    for (int m = 0; m < AOS_NUM_MODULES; ++m) INIT_CHECK(dalloc(&c->d_hm[m], TC * c->R), "hm");
+    INIT_CHECK(dalloc(&c->d_slabs, (size_t)c->R / 16 + 1), "slabs");
+    INIT_CHECK(dalloc(&c->d_n_slabs, 1), "n_slabs");
+    INIT_CHECK(dalloc(&c->d_block_tables, TC * c->max_blocks), "block tables");
+    INIT_CHECK(dalloc(&c->d_ctx_lens, TC), "ctx lens");
+    INIT_CHECK(cudaMallocHost((void**)&c->h_block_tables, TC * c->max_blocks * 4), "pinned tables");
+    INIT_CHECK(cudaMallocHost((void**)&c->h_ctx_lens, TC * 4), "pinned lens");
+    INIT_CHECK(dalloc(&c->d_rings, TC), "rings");
+    INIT_CHECK(dalloc(&c->d_tokens, TC), "tokens");
+    INIT_CHECK(dalloc(&c->d_logits, TC * V), "logits");
+    c->attn_chunks = attn_max_chunks((int)k.max_seq_len);
+    INIT_CHECK(dalloc(&c->d_attn_part, TC * k.n_kv_heads * c->attn_chunks * c->G * 128), "attn part");
+    INIT_CHECK(dalloc(&c->d_attn_ml, TC * k.n_kv_heads * c->attn_chunks * c->G * 2), "attn ml");
+    INIT_CHECK(dalloc(&c->d_counters, 1 << 16), "counters");
+    INIT_CHECK(dalloc(&c->d_err, 1), "err");
+    // RoPE table, angles as the reference computes them (mlx_cpp_wrapper_real.cpp:3249-3268)
+    {
+        const uint32_t half = 64, P = k.max_seq_len + 1;
+        std::vector<float> inv(half), tab((size_t)P * half * 2);
+        for (uint32_t i = 0; i < half; ++i) {
+            const float ex = k.rope_mlx_as_written ? (-2.0f * (float)i / 128.0f) : (2.0f * (float)i / 128.0f);
+            inv[i] = 1.0f / std::pow(k.rope_theta, ex);
+        }
+        for (uint32_t p = 0; p < P; ++p)
+            for (uint32_t i = 0; i < half; ++i) {
+                const float ang = (float)p * inv[i];
+                tab[((size_t)p * half + i) * 2] = std::cos(ang);
+                tab[((size_t)p * half + i) * 2 + 1] = std::sin(ang);
+            }
+        INIT_CHECK(cudaMalloc((void**)&c->d_rope, tab.size() * 4), "rope");
+        INIT_CHECK(cudaMemcpy(c->d_rope, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice), "rope");
+    }
+    INIT_CHECK(tc_configure(), "GEMM smem attribute");
+    INIT_CHECK(attn_configure(), "attention smem attribute");
+    INIT_CHECK(cudaEventCreate(&c->ev0), "event");
+    INIT_CHECK(cudaEventCreate(&c->ev1), "event");
+    INIT_CHECK(cudaDeviceSynchronize(), "init sync");
+#undef INIT_CHECK
+    c->m.base_weight_bytes = c->base_bytes;
+    c->m.arena_bytes = c->arena_bytes;
+    c->m.kv_pool_bytes = kv_elems * 4;
+    c->m.kv_blocks_total = k.kv_num_blocks;
+    return c.release();
+}
+
+void aos_destroy(aos_ctx* c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    for (auto& kv : c->plans)
+        if (kv.second->graph) cudaGraphExecDestroy(kv.second->graph);
+    auto f = [](void* p) {
+        if (p) cudaFree(p);
+    };
+    f(c->embed); f(c->lm_head); f(c->final_norm);
+    for (auto* p : c->attn_norm) f(p);
+    for (auto* p : c->mlp_norm) f(p);
+    for (auto* p : c->w_qkv) f(p);
+    for (auto* p : c->w_o) f(p);
+    for (auto* p : c->w_gate) f(p);
+    for (auto* p : c->w_up) f(p);
+    for (auto* p : c->w_down) f(p);
+    for (int m = 0; m < AOS_NUM_MODULES; ++m) {
+        for (auto* p : c->A[m]) f(p);
+        for (auto* p : c->B[m]) f(p);
+        f(c->d_hm[m]);
+    }
+    f(c->d_col_owner); f(c->d_col_off); f(c->d_rank); f(c->d_scale);
+    f(c->k_pool); f(c->v_pool);
+    f(c->d_hidden); f(c->d_normed); f(c->d_q); f(c->d_attn); f(c->d_act);
+    f(c->d_slabs); f(c->d_n_slabs); f(c->d_block_tables); f(c->d_ctx_lens);
+    f(c->d_rings); f(c->d_tokens); f(c->d_logits); f(c->d_rope);
+    f(c->d_attn_part); f(c->d_attn_ml); f(c->d_ws); f(c->d_counters); f(c->d_err);
+    if (c->h_block_tables) cudaFreeHost(c->h_block_tables);
+    if (c->h_ctx_lens) cudaFreeHost(c->h_ctx_lens);
+    if (c->ev0) cudaEventDestroy(c->ev0);
+    if (c->ev1) cudaEventDestroy(c->ev1);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+const char* aos_device_name(const aos_ctx* c) { return c ? c->dev_name.c_str() : ""; }
+void* aos_stream(aos_ctx* c) { return c ? (void*)c->stream : nullptr; }
+
+int aos_load_weight(aos_ctx* c, aos_weight_kind kind, uint32_t layer, aos_module module, const uint16_t* data,
+                    uint64_t n, int src_on_device) {
+    if (!c || !data) return AOS_ERR_INVALID;
+    const uint32_t H = c->cfg.hidden, V = c->cfg.vocab;
+    uint16_t* dst = nullptr;
+    uint64_t want = 0;
+    if (kind != AOS_W_EMBED && kind != AOS_W_LM_HEAD && kind != AOS_W_FINAL_NORM && layer >= c->cfg.n_layers)
+        return c->fail(AOS_ERR_INVALID, "layer out of range");
+    switch (kind) {
+        case AOS_W_EMBED: dst = c->embed; want = (uint64_t)V * H; break;
+        case AOS_W_LM_HEAD: dst = c->lm_head; want = (uint64_t)V * H; break;
+        case AOS_W_FINAL_NORM: dst = c->final_norm; want = H; break;
+        case AOS_W_ATTN_NORM: dst = c->attn_norm[layer]; want = H; break;
+        case AOS_W_MLP_NORM: dst = c->mlp_norm[layer]; want = H; break;
+        case AOS_W_PROJ: {
+            if ((int)module < 0 || (int)module >= AOS_NUM_MODULES) return c->fail(AOS_ERR_INVALID, "bad module");
+            want = (uint64_t)mod_out(c, module) * mod_in(c, module);
+            switch (module) {
+                case AOS_MOD_Q: dst = c->w_qkv[layer]; break;
+                case AOS_MOD_K: dst = c->w_qkv[layer] + (size_t)c->QD * H; break;
+                case AOS_MOD_V: dst = c->w_qkv[layer] + (size_t)(c->QD + c->KVD) * H; break;
+                case AOS_MOD_O: dst = c->w_o[layer]; break;
+                case AOS_MOD_GATE: dst = c->w_gate[layer]; break;
+                case AOS_MOD_UP: dst = c->w_up[layer]; break;
+                case AOS_MOD_DOWN: dst = c->w_down[layer]; break;
+            }
+            break;
+        }
+        default: return c->fail(AOS_ERR_INVALID, "bad weight kind");
+    }
+    if (n != want) return c->fail(AOS_ERR_INVALID, "weight size mismatch: got " + std::to_string(n) + ", want " + std::to_string(want));
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    CTX_CUDA(c, cudaMemcpy(dst, data, n * 2, src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
+    return AOS_OK;
+}
+
+// ------------------------------------------------------------------ adapters
+int aos_adapter_new(aos_ctx* c, uint16_t id, uint32_t rank, float alpha) {
+    if (!c) return AOS_ERR_INVALID;
+    if (!c->module_mask) return c->fail(AOS_ERR_STATE, "this context has no LoRA arena");
+    if (id >= c->cfg.lora_max_adapters) return c->fail(AOS_ERR_INVALID, "adapter id >= lora_max_adapters");
+    if (rank < 8 || rank > 256 || rank % 8) return c->fail(AOS_ERR_INVALID, "rank must be a multiple of 8 in [8, 256]");
+    if (!std::isfinite(alpha)) return c->fail(AOS_ERR_INVALID, "alpha must be finite");
+    if (c->adapters.count(id)) return c->fail(AOS_ERR_INVALID, "adapter id already loaded");
+    // first fit over 8-column units; ranks >= 16 start on a slab boundary
+    const int units = (int)rank / 8, align = rank >= 16 ? 2 : 1, n_units = (int)c->col_owner.size();
+    int start = -1;
+    for (int u = 0; u + units <= n_units; u += align) {
+        bool free_run = true;
+        for (int j = 0; j < units; ++j)
+            if (c->col_owner[u + j] >= 0) { free_run = false; break; }
+        if (free_run) { start = u; break; }
+    }
+    if (start < 0) return c->fail(AOS_ERR_NOMEM, "adapter arena full");
+    const int off = start * 8;
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    // zero the adapter's rows/columns in every layer and module
+    for (int m = 0; m < AOS_NUM_MODULES; ++m) {
+        if (!(c->module_mask & (1u << m))) continue;
+        const uint32_t in = mod_in(c, m), out = mod_out(c, m);
+        for (uint32_t l = 0; l < c->cfg.n_layers; ++l) {
+            CTX_CUDA(c, cudaMemset(c->A[m][l] + (size_t)off * in, 0, (size_t)rank * in * 2));
+            for (int col = off; col < off + (int)rank;) {
+                const int slab = col / 16, c0 = col % 16, w = std::min(16 - c0, off + (int)rank - col);
+                CTX_CUDA(c, cudaMemset2D(c->B[m][l] + (size_t)slab * out * 16 + c0, 32, 0, (size_t)w * 2, out));
+                col += w;
+            }
+        }
+    }
+    for (int j = 0; j < units; ++j) c->col_owner[start + j] = id;
+    std::vector<int> owner((size_t)rank, (int)id);
+    CTX_CUDA(c, cudaMemcpy(c->d_col_owner + off, owner.data(), rank * 4, cudaMemcpyHostToDevice));
+    const int irank = (int)rank;
+    const float scale = alpha / (float)rank;
+    CTX_CUDA(c, cudaMemcpy(c->d_col_off + id, &off, 4, cudaMemcpyHostToDevice));
+    CTX_CUDA(c, cudaMemcpy(c->d_rank + id, &irank, 4, cudaMemcpyHostToDevice));
+    CTX_CUDA(c, cudaMemcpy(c->d_scale + id, &scale, 4, cudaMemcpyHostToDevice));
+    c->adapters[id] = AdapterEntry{off, (int)rank, alpha};
+    c->m.adapters_loaded = (uint32_t)c->adapters.size();
+    c->m.arena_used_rank_cols += rank;
+    return AOS_OK;
+}
+
+int aos_adapter_set_module(aos_ctx* c, uint16_t id, uint32_t layer, aos_module module, const uint16_t* A,
+                           const uint16_t* B, int src_on_device) {
+    if (!c || !A || !B) return AOS_ERR_INVALID;
+    auto it = c->adapters.find(id);
+    if (it == c->adapters.end()) return c->fail(AOS_ERR_NOT_FOUND, "adapter not loaded");
+    if (layer >= c->cfg.n_layers || (int)module < 0 || (int)module >= AOS_NUM_MODULES)
+        return c->fail(AOS_ERR_INVALID, "layer or module out of range");
+    if (!(c->module_mask & (1u << module))) return c->fail(AOS_ERR_INVALID, "module not enabled for LoRA in this context");
+    const int off = it->second.off, rank = it->second.rank;
+    const uint32_t in = mod_in(c, module), out = mod_out(c, module);
+    const cudaMemcpyKind kind = src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    CTX_CUDA(c, cudaMemcpy(c->A[module][layer] + (size_t)off * in, A, (size_t)rank * in * 2, kind));
+    for (int col = off; col < off + rank;) {
+        const int slab = col / 16, c0 = col % 16, w = std::min(16 - c0, off + rank - col);
+        CTX_CUDA(c, cudaMemcpy2D(c->B[module][layer] + (size_t)slab * out * 16 + c0, 32, B + (col - off), (size_t)rank * 2,
+                                 (size_t)w * 2, out, kind));
+        col += w;
+    }
+    return AOS_OK;
+}
+
+int aos_adapter_unload(aos_ctx* c, uint16_t id) {
+    if (!c) return AOS_ERR_INVALID;
+    auto it = c->adapters.find(id);
+    if (it == c->adapters.end()) return c->fail(AOS_ERR_NOT_FOUND, "adapter not loaded");
+    const int off = it->second.off, rank = it->second.rank;
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    CTX_CUDA(c, cudaStreamSynchronize(c->stream));  // no step may still read the columns
+    for (int j = 0; j < rank / 8; ++j) c->col_owner[off / 8 + j] = -1;
+    CTX_CUDA(c, cudaMemset(c->d_col_owner + off, 0xFF, (size_t)rank * 4));
+    const int neg = -1, zero = 0;
+    CTX_CUDA(c, cudaMemcpy(c->d_col_off + id, &neg, 4, cudaMemcpyHostToDevice));
+    CTX_CUDA(c, cudaMemcpy(c->d_rank + id, &zero, 4, cudaMemcpyHostToDevice));
+    c->m.arena_used_rank_cols -= rank;
+    c->adapters.erase(it);
+    c->m.adapters_loaded = (uint32_t)c->adapters.size();
+    return AOS_OK;
+}
+
+int aos_adapter_is_loaded(const aos_ctx* c, uint16_t id) { return c && c->adapters.count(id) ? 1 : 0; }
+
+// ------------------------------------------------------------------ KV cache
+int aos_kv_alloc(aos_ctx* c, uint64_t seq_id, uint32_t max_tokens) {
+    if (!c) return AOS_ERR_INVALID;
+    if (c->seqs.count(seq_id)) return c->fail(AOS_ERR_INVALID, "sequence already allocated");
+    if (max_tokens == 0 || max_tokens > c->cfg.max_seq_len) return c->fail(AOS_ERR_INVALID, "max_tokens out of range");
+    const size_t need = (max_tokens + 15) / 16;
+    if (need > c->free_blocks.size()) return c->fail(AOS_ERR_NOMEM, "KV pool exhausted");
+    Sequence s;
+    s.cap = max_tokens;
+    for (size_t i = 0; i < need; ++i) {
+        s.blocks.push_back(c->free_blocks.back());
+        c->free_blocks.pop_back();
+    }
+    c->seqs[seq_id] = std::move(s);
+    c->m.sequences = (uint32_t)c->seqs.size();
+    c->m.kv_blocks_used = c->cfg.kv_num_blocks - (uint32_t)c->free_blocks.size();
+    return AOS_OK;
+}
+
+int aos_kv_free(aos_ctx* c, uint64_t seq_id) {
+    if (!c) return AOS_ERR_INVALID;
+    auto it = c->seqs.find(seq_id);
+    if (it == c->seqs.end()) return c->fail(AOS_ERR_NOT_FOUND, "unknown sequence");
+    for (int b : it->second.blocks) c->free_blocks.push_back(b);
+    c->seqs.erase(it);
+    c->m.sequences = (uint32_t)c->seqs.size();
+    c->m.kv_blocks_used = c->cfg.kv_num_blocks - (uint32_t)c->free_blocks.size();
+    return AOS_OK;
+}
+
+int aos_kv_set_len(aos_ctx* c, uint64_t seq_id, uint32_t len) {
+    if (!c) return AOS_ERR_INVALID;
+    auto it = c->seqs.find(seq_id);
+    if (it == c->seqs.end()) return c->fail(AOS_ERR_NOT_FOUND, "unknown sequence");
+    if (len > it->second.cap) return c->fail(AOS_ERR_INVALID, "len beyond the sequence's capacity");
+    it->second.len = len;
+    return AOS_OK;
+}
+
+int aos_kv_get_len(const aos_ctx* c, uint64_t seq_id, uint32_t* len) {
+    if (!c || !len) return AOS_ERR_INVALID;
+    auto it = c->seqs.find(seq_id);
+    if (it == c->seqs.end()) return AOS_ERR_NOT_FOUND;
+    *len = it->second.len;
+    return AOS_OK;
+}
+
+static int kv_copy(aos_ctx* c, uint64_t seq_id, uint32_t layer, uint32_t pos0, uint32_t n, const uint16_t* k_src,
+                   const uint16_t* v_src, uint16_t* k_dst, uint16_t* v_dst, int src_on_device) {
+    auto it = c->seqs.find(seq_id);
+    if (it == c->seqs.end()) return c->fail(AOS_ERR_NOT_FOUND, "unknown sequence");
+    if (layer >= c->cfg.n_layers || pos0 + n > it->second.cap) return c->fail(AOS_ERR_INVALID, "KV range out of bounds");
+    const uint32_t nkv = c->cfg.n_kv_heads;
+    const bool write = k_src != nullptr;
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    // Runs of positions inside one page: per head the page rows are contiguous
+    // (256 B each), the caller's rows are strided by n_kv_heads * 256 B.
+    for (uint32_t i = 0; i < n;) {
+        const uint32_t pos = pos0 + i;
+        const uint32_t run = std::min(n - i, 16 - pos % 16);
+        const int blk = it->second.blocks[pos / 16];
+        for (uint32_t h = 0; h < nkv; ++h) {
+            const size_t idx = ((((size_t)layer * c->cfg.kv_num_blocks + blk) * nkv + h) * 16 + pos % 16) * 128;
+            const size_t src = ((size_t)i * nkv + h) * 128;
+            const size_t pitch = (size_t)nkv * 256;
+            if (write) {
+                const cudaMemcpyKind kd = src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+                CTX_CUDA(c, cudaMemcpy2D(c->k_pool + idx, 256, k_src + src, pitch, 256, run, kd));
+                CTX_CUDA(c, cudaMemcpy2D(c->v_pool + idx, 256, v_src + src, pitch, 256, run, kd));
+            } else {
+                CTX_CUDA(c, cudaMemcpy2D(k_dst + src, pitch, c->k_pool + idx, 256, 256, run, cudaMemcpyDeviceToHost));
+                CTX_CUDA(c, cudaMemcpy2D(v_dst + src, pitch, c->v_pool + idx, 256, 256, run, cudaMemcpyDeviceToHost));
+            }
+        }
+        i += run;
+    }
+    return AOS_OK;
+}
+
+int aos_kv_write(aos_ctx* c, uint64_t seq_id, uint32_t layer, uint32_t pos0, uint32_t n, const uint16_t* k,
+                 const uint16_t* v, int src_on_device) {
+    if (!c || !k || !v) return AOS_ERR_INVALID;
+    return kv_copy(c, seq_id, layer, pos0, n, k, v, nullptr, nullptr, src_on_device);
+}
+
+int aos_kv_read(aos_ctx* c, uint64_t seq_id, uint32_t layer, uint32_t pos0, uint32_t n, uint16_t* k, uint16_t* v) {
+    if (!c || !k || !v) return AOS_ERR_INVALID;
+    CTX_CUDA(c, cudaStreamSynchronize(c->stream));
+    return kv_copy(c, seq_id, layer, pos0, n, nullptr, nullptr, k, v, 0);
+}
+
+int aos_kv_fill_synthetic(aos_ctx* c, uint64_t seed, float std) {
+    if (!c) return AOS_ERR_INVALID;
+    const size_t n = (size_t)c->cfg.n_layers * c->cfg.kv_num_blocks * c->cfg.n_kv_heads * 16 * 128;
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    LAUNCH(c, launch_fill_normal(c->k_pool, n, seed, std, c->stream));
+    LAUNCH(c, launch_fill_normal(c->v_pool, n, seed ^ 0x5bd1e995ull, std, c->stream));
+    CTX_CUDA(c, cudaStreamSynchronize(c->stream));
+    return AOS_OK;
+}
+
+int aos_kv_clear_all(aos_ctx* c) {
+    if (!c) return AOS_ERR_INVALID;
+    std::vector<uint64_t> ids;
+    for (auto& kv : c->seqs) ids.push_back(kv.first);
+    for (auto id : ids) aos_kv_free(c, id);
+    return AOS_OK;
+}
+
+uint64_t aos_kv_memory_bytes(const aos_ctx* c) {
+    return c ? (uint64_t)c->cfg.n_layers * c->cfg.kv_num_blocks * c->cfg.n_kv_heads * 16 * 128 * 2 * 2 : 0;
+}
+
+// ------------------------------------------------------------------ the step
+int aos_run_step_batch_dev(aos_ctx* c, const aos_router_ring* rings, const uint32_t* token_ids, const uint64_t* seq_ids,
+                           uint32_t T, float* logits, uint16_t* hidden_out, void* stream) {
+    if (!c || !rings || !token_ids || !seq_ids || T == 0) return AOS_ERR_INVALID;
+    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    int rc = stage_sequences(c, seq_ids, T);
+    if (rc) return rc;
+    if ((rc = upload_tables(c, T, s))) return rc;
+    if (rings != c->d_rings)
+        CTX_CUDA(c, cudaMemcpyAsync(c->d_rings, rings, (size_t)T * sizeof(aos_router_ring), cudaMemcpyDeviceToDevice, s));
+    if (token_ids != c->d_tokens)
+        CTX_CUDA(c, cudaMemcpyAsync(c->d_tokens, token_ids, (size_t)T * 4, cudaMemcpyDeviceToDevice, s));
+    if ((rc = run_step_device(c, (int)T, true, s))) return rc;
+    if (logits && logits != c->d_logits)
+        CTX_CUDA(c, cudaMemcpyAsync(logits, c->d_logits, (size_t)T * c->cfg.vocab * 4, cudaMemcpyDeviceToDevice, s));
+    if (hidden_out)
+        CTX_CUDA(c, cudaMemcpyAsync(hidden_out, c->d_hidden, (size_t)T * c->cfg.hidden * 2, cudaMemcpyDeviceToDevice, s));
+    advance(c, seq_ids, T);
+    return AOS_OK;
+}
+
+int aos_run_step_batch(aos_ctx* c, const aos_router_ring* rings, const uint32_t* token_ids, const uint64_t* seq_ids,
+                       uint32_t T, float* logits, uint16_t* hidden_out) {
+    if (!c || !rings || !token_ids || !seq_ids || T == 0) return AOS_ERR_INVALID;
+    if (T > c->cfg.max_batch) return c->fail(AOS_ERR_INVALID, "T exceeds max_batch");
+    cudaStream_t s = c->stream;
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    CTX_CUDA(c, cudaMemcpyAsync(c->d_rings, rings, (size_t)T * sizeof(aos_router_ring), cudaMemcpyHostToDevice, s));
+    CTX_CUDA(c, cudaMemcpyAsync(c->d_tokens, token_ids, (size_t)T * 4, cudaMemcpyHostToDevice, s));
+    CTX_CUDA(c, cudaEventRecord(c->ev0, s));
+    int rc = aos_run_step_batch_dev(c, c->d_rings, c->d_tokens, seq_ids, T, c->d_logits, nullptr, s);
+    if (rc) return rc;
+    CTX_CUDA(c, cudaEventRecord(c->ev1, s));
+    if (logits) CTX_CUDA(c, cudaMemcpyAsync(logits, c->d_logits, (size_t)T * c->cfg.vocab * 4, cudaMemcpyDeviceToHost, s));
+    if (hidden_out)
+        CTX_CUDA(c, cudaMemcpyAsync(hidden_out, c->d_hidden, (size_t)T * c->cfg.hidden * 2, cudaMemcpyDeviceToHost, s));
+    CTX_CUDA(c, cudaStreamSynchronize(s));
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, c->ev0, c->ev1);
+    c->m.last_step_ms = ms;
+    return check_device_error(c);
+}
+
+int aos_layer_step_dev(aos_ctx* c, uint32_t layer, const aos_router_ring* rings, const uint64_t* seq_ids, uint32_t T,
+                       uint16_t* hidden, int adv, void* stream) {
+    if (!c || !rings || !seq_ids || !hidden || T == 0) return AOS_ERR_INVALID;
+    if (layer >= c->cfg.n_layers) return c->fail(AOS_ERR_INVALID, "layer out of range");
+    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    int rc = stage_sequences(c, seq_ids, T);
+    if (rc) return rc;
+    if ((rc = upload_tables(c, T, s))) return rc;
+    StepPlan* plan = nullptr;
+    if ((rc = get_plan(c, (int)T, &plan))) return rc;
+    if (rings != c->d_rings)
+        CTX_CUDA(c, cudaMemcpyAsync(c->d_rings, rings, (size_t)T * sizeof(aos_router_ring), cudaMemcpyDeviceToDevice, s));
+    CTX_CUDA(c, cudaMemcpyAsync(c->d_hidden, hidden, (size_t)T * c->cfg.hidden * 2, cudaMemcpyDeviceToDevice, s));
+    LAUNCH(c, launch_lora_prep(c->d_rings, (int)T, c->d_col_off, c->d_rank, (int)c->cfg.lora_max_adapters, c->R / 16,
+                               c->d_slabs, c->d_n_slabs, s));
+    if ((rc = enqueue_layer(c, *plan, (int)layer, s))) return rc;
+    CTX_CUDA(c, cudaMemcpyAsync(hidden, c->d_hidden, (size_t)T * c->cfg.hidden * 2, cudaMemcpyDeviceToDevice, s));
+    if (adv) advance(c, seq_ids, T);
+    return AOS_OK;
+}
+
+// ------------------------------------------------------------------ metrics etc.
+int aos_get_metrics(const aos_ctx* c, aos_metrics* out) {
+    if (!c || !out) return AOS_ERR_INVALID;
+    *out = c->m;
+    return AOS_OK;
+}
+
+int aos_health_check(aos_ctx* c) {
+    if (!c) return AOS_ERR_INVALID;
+    cudaError_t e = cudaStreamQuery(c->stream);
+    if (e != cudaSuccess && e != cudaErrorNotReady) return c->fail(AOS_ERR_CUDA, cudaGetErrorString(e));
+    return check_device_error(c);
+}
+
+int aos_attest_determinism(const aos_ctx* c, aos_determinism_report* out) {
+    if (!c || !out) return AOS_ERR_INVALID;
+    std::memset(out, 0, sizeof(*out));
+    std::snprintf(out->backend, sizeof(out->backend), "cuda-sm100a");
+    std::snprintf(out->device_name, sizeof(out->device_name), "%s", c->dev_name.c_str());
+    cudaDeviceProp p;
+    cudaGetDeviceProperties(&p, c->device);
+    out->sm_major = (uint32_t)p.major;
+    out->sm_minor = (uint32_t)p.minor;
+    out->fast_math = 0;
+    out->float_atomics = 0;
+    out->fixed_reduction_order = 1;
+    std::snprintf(out->kernel_build_id, sizeof(out->kernel_build_id), "%s", aos_version());
+    return AOS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,645 @@
+// tc_gemm.cu — tcgen05/TMEM/TMA weight-streaming GEMM with the LoRA expand
+// fused into the same accumulator, and the decoder's epilogues.
+//
+// Per 128-row output tile (MMA M = weight rows, N = decode tokens, "swap-AB"):
+//   base steps : TMA W[128 x 64] + X[T x 64] (SWIZZLE_128B) -> 4 MMAs (K=16)
+//   LoRA steps : TMA lora_B slabs [128 x 16] + gated H slabs [T x 16]
+//                (SWIZZLE_32B), four slabs per step -> 4 MMAs (K=16)
+// so the tile's accumulator ends as  W x + sum_a B_a (g_a * scale_a * A_a x)
+// (mlx_cpp_wrapper_real.cpp:3372-3419) without ever materialising the LoRA
+// delta.  The shrink GEMM (H = A_cat x) is the same kernel with lora_A rows
+// gathered slab by slab and the TC_SHRINK_HM epilogue.
+//
+// Roles (192 threads, one CTA per SM, persistent over work units):
+//   warp 0      : TMA producer (one elected lane)
+//   warp 1      : TMEM allocator + MMA issuer (one elected lane)
+//   warps 2..5  : epilogue, TMEM lane quarter = warp % 4
+// Work unit = (segment, tile, split); splits > 1 write fp32 partials and the
+// last-arriving CTA of a tile reduces them in split order (fixed order, so the
+// result is bit-identical run to run; no float atomics).
+//
+// Every mbarrier wait is bounded (kSpinLimitCycles): on timeout the kernel
+// records AOS_ERR_TIMEOUT in p.err, drains its own TMA copies and MMAs, frees
+// TMEM and returns.
+
+#include <algorithm>
+#include <cstring>
+
+#include "tc_gemm.cuh"
+
+namespace aos {
+namespace {
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait; false on timeout or when another role already failed.
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
+    if (mbar_try(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try(bar, parity)) {
+        if (*(volatile int*)err != 0) return false;
+        if (clock64() - t0 > kSpinLimitCycles) {
+            atomicCAS(err, 0, AOS_ERR_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
+// Time-bounded wait that ignores the error word: used only to drain this
+// CTA's own copies / MMAs before it exits on an error path.
+__device__ __noinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
+    const long long t0 = clock64();
+    while (!mbar_try(bar, parity))
+        if (clock64() - t0 > kSpinLimitCycles) return false;
+    return true;
+}
+__device__ __forceinline__ void tma_2d(const CUtensorMap* m, uint32_t dst, uint32_t bar, int x, int y,
+                                       uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ void tma_3d(const CUtensorMap* m, uint32_t dst, uint32_t bar, int x, int y, int z,
+                                       uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y), "r"(z), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void umma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+          "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+          "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+          "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Barrier over the 4 epilogue warps that also ORs a predicate, so a failed
+// (timed-out) wait in any thread makes every epilogue thread leave together.
+__device__ __forceinline__ bool epi_bar_any(bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)pred)
+        : "memory");
+    return r != 0;
+}
+
+// Shared-memory matrix descriptors (tcgen05 "version 1"), K-major operands.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)(1024u >> 4) << 32) |
+           ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
+}
+__device__ __forceinline__ uint64_t desc_sw32(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)(256u >> 4) << 32) |
+           ((uint64_t)1u << 46) | ((uint64_t)6u << 61);
+}
+// kind::f16 instruction descriptor: D f32, A/B bf16, both K-major, M=128.
+__device__ __forceinline__ uint32_t idesc_bf16(int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+// ---------------------------------------------------------------- work units
+struct Unit {
+    int seg, tile, tile_global, split, step0, step1;
+};
+
+struct Sched {
+    int n_slabs, lora_steps, total_steps, units;
+    int tiles[kTcMaxSets];
+};
+
+__device__ __forceinline__ Sched make_sched(const TcParams& p) {
+    Sched s;
+    s.n_slabs = (p.lora || p.shrink) ? __ldg(p.n_slabs) : 0;
+    s.lora_steps = p.lora ? cdiv(s.n_slabs, kSlabsPerStep) : 0;
+    s.total_steps = p.kb + s.lora_steps;
+    s.units = 0;
+    for (int g = 0; g < kTcMaxSets; ++g) {
+        s.tiles[g] = g < p.n_seg ? (p.shrink ? cdiv(s.n_slabs, kShrinkSlabsPerTile) : p.seg_tiles[g]) : 0;
+        s.units += s.tiles[g] * p.splits;
+    }
+    return s;
+}
+
+__device__ __forceinline__ Unit unit_of(const TcParams& p, const Sched& s, int u) {
+    Unit r;
+    int tile_u = u / p.splits;
+    r.split = u % p.splits;
+    int base = 0;
+    r.seg = 0;
+    while (r.seg < p.n_seg - 1 && tile_u >= s.tiles[r.seg]) {
+        tile_u -= s.tiles[r.seg];
+        base += s.tiles[r.seg];
+        ++r.seg;
+    }
+    r.tile = tile_u;
+    r.tile_global = base + tile_u;
+    r.step0 = (int)((long long)r.split * s.total_steps / p.splits);
+    r.step1 = (int)((long long)(r.split + 1) * s.total_steps / p.splits);
+    return r;
+}
+
+// ---------------------------------------------------------------- epilogue
+struct EpiSmem {
+    float* xbuf;                // [128][33] exchange buffer (RoPE)
+    const aos_router_ring* rings;  // shared copy of the rings (HM)
+};
+
+__device__ __forceinline__ float gate_coef(const TcParams& p, const aos_router_ring& ring, int owner) {
+    // sum over slots naming this adapter with q15 > 0 (mlx-ffi/src/backend.rs:405-418)
+    float c = 0.0f;
+    const int k = min((int)ring.top_k, AOS_MAX_K);
+    for (int s = 0; s < k; ++s)
+        if ((int)ring.indices[s] == owner && ring.gates_q15[s] > 0) {
+            const float blend = __fdiv_rn((float)ring.gates_q15[s], AOS_Q15_DENOM);
+            c += blend * __ldg(p.adapter_scale + owner);
+        }
+    return c;
+}
+
+// Apply the epilogue to tokens [t0, t0+32) of one tile row.  v[sub][j] holds
+// the fp32 accumulator for token t0 + j.  Must be called uniformly by all
+// 128 epilogue threads (RoPE uses a named barrier).
+__device__ void epilogue_chunk(const TcParams& p, const EpiSmem& es, const Unit& u, const Sched& sc, int row,
+                               int t0, float (&v)[2][32]) {
+    const int seg = u.seg;
+    const int col = p.seg_out0[seg] + u.tile * kTcBM + row;
+    if (p.mode != TC_SHRINK_HM && p.mode != TC_QKV_ROPE && u.tile * kTcBM + row >= p.seg_rows[seg]) return;
+    switch (p.mode) {
+        case TC_STORE_BF16: {
+            uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]);
+            for (int j = 0; j < 32 && t0 + j < p.T; ++j) o[(size_t)(t0 + j) * p.ld_out + col] = f2bf(v[0][j]);
+            break;
+        }
+        case TC_STORE_F32: {
+            float* o = reinterpret_cast<float*>(p.out[seg]);
+            for (int j = 0; j < 32 && t0 + j < p.T; ++j) o[(size_t)(t0 + j) * p.ld_out + col] = v[0][j];
+            break;
+        }
+        case TC_RESID_BF16: {
+            for (int j = 0; j < 32 && t0 + j < p.T; ++j) {
+                uint16_t* h = p.resid + (size_t)(t0 + j) * p.ld_out + col;
+                *h = f2bf(bf2f(*h) + v[0][j]);
+            }
+            break;
+        }
+        case TC_SWIGLU: {
+            uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]);
+            for (int j = 0; j < 32 && t0 + j < p.T; ++j) {
+                const float g = v[0][j], up = v[1][j];
+                const float sg = 1.0f / (1.0f + expf(-g));  // gate * sigmoid(gate) * up (:3522)
+                o[(size_t)(t0 + j) * p.ld_out + col] = f2bf((g * sg) * up);
+            }
+            break;
+        }
+        case TC_QKV_ROPE: {
+            const int module = p.seg_module[seg];
+            if (module != AOS_MOD_V) {
+                // half-split RoPE (mlx_cpp_wrapper_real.cpp:3270-3280): pair (d, d+64)
+                for (int j = 0; j < 32; ++j) es.xbuf[row * 33 + j] = v[0][j];
+                epi_bar();
+                const int half = kTcBM / 2, i = row & (half - 1);
+                const int partner = row ^ half;
+                for (int j = 0; j < 32; ++j) {
+                    const int t = t0 + j;
+                    if (t >= p.T) break;
+                    const int pos = __ldg(p.ctx_lens + t);
+                    const float2 cs = *reinterpret_cast<const float2*>(p.rope + ((size_t)pos * half + i) * 2);
+                    const float x = v[0][j], y = es.xbuf[partner * 33 + j];
+                    v[0][j] = row < half ? (x * cs.x - y * cs.y) : (y * cs.y + x * cs.x);
+                }
+                epi_bar();
+            }
+            if (module == AOS_MOD_Q) {
+                uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]);
+                for (int j = 0; j < 32 && t0 + j < p.T; ++j) o[(size_t)(t0 + j) * p.ld_out + col] = f2bf(v[0][j]);
+            } else {
+                uint16_t* pool = module == AOS_MOD_K ? p.k_pool : p.v_pool;
+                const int kvh = u.tile;  // one tile per kv head (head_dim == 128)
+                for (int j = 0; j < 32 && t0 + j < p.T; ++j) {
+                    const int t = t0 + j;
+                    const int pos = __ldg(p.ctx_lens + t);
+                    const int blk = __ldg(p.block_tables + (size_t)t * p.max_blocks + (pos >> 4));
+                    const size_t idx = ((((size_t)p.layer * p.num_blocks + blk) * p.nkv + kvh) * 16 + (pos & 15)) * 128 + row;
+                    pool[idx] = f2bf(v[0][j]);
+                }
+            }
+            break;
+        }
+        case TC_SHRINK_HM: {
+            const int slot = u.tile * kShrinkSlabsPerTile + (row >> 4);
+            if (slot >= sc.n_slabs) break;
+            const int c = __ldg(p.slabs + slot) * kSlab + (row & 15);
+            const int owner = __ldg(p.col_owner + c);
+            uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]);
+            for (int j = 0; j < 32 && t0 + j < p.T; ++j) {
+                const int t = t0 + j;
+                const float coef = owner >= 0 ? gate_coef(p, es.rings[t], owner) : 0.0f;
+                o[(size_t)t * p.R + c] = f2bf(v[0][j] * coef);
+            }
+            break;
+        }
+        default:
+            break;
+    }
+}
+
+// ---------------------------------------------------------------- the kernel
+__global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 1024-align the dynamic region (SWIZZLE_128B atoms).
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int NS = p.n_stages;
+    uint8_t* stages = smem;
+    uint8_t* tail = smem + (size_t)NS * p.stage_bytes;
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(tail);
+    uint64_t* empty_bar = full_bar + NS;
+    uint64_t* tfull_bar = empty_bar + NS;   // [2]
+    uint64_t* tempty_bar = tfull_bar + 2;   // [2]
+    uint64_t* drain_bar = tempty_bar + 2;   // [1]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+    int* flag = reinterpret_cast<int*>(tmem_slot + 1);
+    float* xbuf = reinterpret_cast<float*>(tail + 512);
+    aos_router_ring* rings_s = reinterpret_cast<aos_router_ring*>(tail + 512 + 128 * 33 * 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const Sched sc = make_sched(p);
+    const int cols_per_acc = p.n_sub * p.T_pad;
+    const int acc_stages = (2 * cols_per_acc <= 512) ? 2 : 1;
+    int tmem_cols = 32;
+    while (tmem_cols < acc_stages * cols_per_acc) tmem_cols <<= 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(smem_u32(&full_bar[s]), 1);
+            mbar_init(smem_u32(&empty_bar[s]), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(smem_u32(&tfull_bar[a]), 1);
+            mbar_init(smem_u32(&tempty_bar[a]), 4);
+        }
+        mbar_init(smem_u32(drain_bar), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(tmem_cols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    if (p.mode == TC_SHRINK_HM && warp >= 2) {
+        const int n_words = p.T * (int)(sizeof(aos_router_ring) / 4);
+        for (int i = threadIdx.x - 64; i < n_words; i += 128)
+            reinterpret_cast<uint32_t*>(rings_s)[i] = reinterpret_cast<const uint32_t*>(p.rings)[i];
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t idesc = idesc_bf16(p.T_pad);
+
+    if (warp == 0) {
+        // ============================ TMA producer ============================
+        if (lane == 0) {
+            const uint64_t pol_w = policy_evict_first();
+            const uint64_t pol_x = policy_evict_last();
+            uint32_t last_phase[16];
+            uint32_t used_mask = 0;
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int uidx = blockIdx.x; uidx < sc.units && ok; uidx += gridDim.x) {
+                const Unit u = unit_of(p, sc, uidx);
+                for (int step = u.step0; step < u.step1; ++step) {
+                    if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, p.err)) { ok = false; break; }
+                    const uint32_t fb = smem_u32(&full_bar[stage]);
+                    const uint32_t sbase = smem_u32(stages + (size_t)stage * p.stage_bytes);
+                    const uint32_t act = sbase + p.act_off;
+                    if (step < p.kb) {
+                        const int kx = step * kTcBK;
+                        if (p.shrink) {
+                            const int first = u.tile * kShrinkSlabsPerTile;
+                            const int nv = min(kShrinkSlabsPerTile, sc.n_slabs - first);
+                            mbar_expect_tx(fb, (uint32_t)(nv * kSlab * 128 + p.T_pad * 128));
+                            for (int q = 0; q < nv; ++q)
+                                tma_2d(&p.tm_w[u.seg], sbase + q * (kSlab * 128), fb, kx,
+                                       __ldg(p.slabs + first + q) * kSlab, pol_w);
+                        } else {
+                            mbar_expect_tx(fb, (uint32_t)(p.n_sub * kTcBM * 128 + p.T_pad * 128));
+                            for (int sub = 0; sub < p.n_sub; ++sub)
+                                tma_2d(&p.tm_w[u.seg * p.n_sub + sub], sbase + sub * (kTcBM * 128), fb, kx,
+                                       p.seg_wrow0[u.seg] + u.tile * kTcBM, pol_w);
+                        }
+                        tma_2d(&p.tm_x, act, fb, kx, 0, pol_x);
+                    } else {
+                        const int g0 = (step - p.kb) * kSlabsPerStep;
+                        const int nv = min(kSlabsPerStep, sc.n_slabs - g0);
+                        mbar_expect_tx(fb, (uint32_t)(p.n_sub * nv * (kTcBM * 32 + p.T_pad * 32)));
+                        for (int sub = 0; sub < p.n_sub; ++sub) {
+                            const int set = u.seg * p.n_sub + sub;
+                            for (int q = 0; q < nv; ++q) {
+                                const int slab = __ldg(p.slabs + g0 + q);
+                                tma_3d(&p.tm_lb[set], sbase + sub * (kTcBM * 128) + q * (kTcBM * 32), fb, 0,
+                                       u.tile * kTcBM, slab, pol_w);
+                                tma_2d(&p.tm_lh[set], act + (sub * kSlabsPerStep + q) * (p.T_pad * 32), fb,
+                                       slab * kSlab, 0, pol_x);
+                            }
+                        }
+                    }
+                    last_phase[stage] = phase;
+                    used_mask |= 1u << stage;
+                    if (++stage == NS) { stage = 0; phase ^= 1u; }
+                }
+            }
+            // Drain: every issued copy must land before the CTA may exit.
+            for (int s = 0; s < NS; ++s)
+                if (used_mask & (1u << s)) mbar_wait_drain(smem_u32(&full_bar[s]), last_phase[s]);
+        }
+    } else if (warp == 1) {
+        // ============================ MMA issuer ==============================
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int it = 0;
+            bool ok = true;
+            bool issued_any = false;
+            for (int uidx = blockIdx.x; uidx < sc.units && ok; uidx += gridDim.x, ++it) {
+                const Unit u = unit_of(p, sc, uidx);
+                const int acc = it % acc_stages;
+                const uint32_t tphase = (uint32_t)((it / acc_stages) & 1);
+                if (!mbar_wait(smem_u32(&tempty_bar[acc]), tphase ^ 1u, p.err)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d0 = tmem_base + (uint32_t)(acc * cols_per_acc);
+                bool first = true;
+                for (int step = u.step0; step < u.step1; ++step) {
+                    if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t sbase = smem_u32(stages + (size_t)stage * p.stage_bytes);
+                    const uint32_t act = sbase + p.act_off;
+                    if (step < p.kb) {
+                        for (int sub = 0; sub < p.n_sub; ++sub) {
+                            const uint32_t a0 = sbase + sub * (kTcBM * 128);
+#pragma unroll
+                            for (int kk = 0; kk < kTcBK / 16; ++kk)
+                                umma_bf16(d0 + sub * p.T_pad, desc_sw128(a0 + kk * 32), desc_sw128(act + kk * 32), idesc,
+                                          (first && kk == 0) ? 0u : 1u);
+                        }
+                    } else {
+                        const int g0 = (step - p.kb) * kSlabsPerStep;
+                        const int nv = min(kSlabsPerStep, sc.n_slabs - g0);
+                        for (int sub = 0; sub < p.n_sub; ++sub)
+                            for (int q = 0; q < nv; ++q)
+                                umma_bf16(d0 + sub * p.T_pad, desc_sw32(sbase + sub * (kTcBM * 128) + q * (kTcBM * 32)),
+                                          desc_sw32(act + (sub * kSlabsPerStep + q) * (p.T_pad * 32)), idesc,
+                                          (first && q == 0) ? 0u : 1u);
+                    }
+                    issued_any = true;
+                    umma_commit(smem_u32(&empty_bar[stage]));  // frees the stage when these MMAs finish
+                    first = false;
+                    if (++stage == NS) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                umma_commit(smem_u32(&tfull_bar[acc]));
+            }
+            if (!ok && issued_any) {
+                umma_commit(smem_u32(drain_bar));
+                mbar_wait_drain(smem_u32(drain_bar), 0);
+            }
+        }
+    } else {
+        // ============================ epilogue ================================
+        const int q = warp & 3;
+        const int row = q * 32 + lane;
+        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+        EpiSmem es{xbuf, rings_s};
+        int it = 0;
+        for (int uidx = blockIdx.x; uidx < sc.units; uidx += gridDim.x, ++it) {
+            const Unit u = unit_of(p, sc, uidx);
+            const int acc = it % acc_stages;
+            const uint32_t tphase = (uint32_t)((it / acc_stages) & 1);
+            const bool ok = mbar_wait(smem_u32(&tfull_bar[acc]), tphase, p.err);
+            if (epi_bar_any(!ok)) break;
+            tc_fence_after();
+            const uint32_t t_acc = tmem_base + lane_off + (uint32_t)(acc * cols_per_acc);
+            float v[2][32];
+            if (p.splits == 1) {
+                for (int t0 = 0; t0 < p.T_pad; t0 += 32) {
+                    for (int sub = 0; sub < p.n_sub; ++sub) tmem_ld32(t_acc + sub * p.T_pad + t0, v[sub]);
+                    epilogue_chunk(p, es, u, sc, row, t0, v);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
+            } else {
+                // partial -> workspace [tile][split][sub][t][row]
+                const size_t tile_stride = (size_t)p.n_sub * p.T_pad * kTcBM;
+                float* wsu = p.ws + ((size_t)u.tile_global * p.splits + u.split) * tile_stride;
+                for (int t0 = 0; t0 < p.T_pad; t0 += 32)
+                    for (int sub = 0; sub < p.n_sub; ++sub) {
+                        tmem_ld32(t_acc + sub * p.T_pad + t0, v[sub]);
+                        for (int j = 0; j < 32; ++j) wsu[((size_t)sub * p.T_pad + t0 + j) * kTcBM + row] = v[sub][j];
+                    }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
+                __threadfence();
+                epi_bar();
+                if (threadIdx.x == 64) {
+                    const int old = atomicAdd(p.counters + u.tile_global, 1);
+                    *flag = (old == p.splits - 1);
+                }
+                epi_bar();
+                const bool last = *flag != 0;
+                epi_bar();  // everyone has read the flag before it can be rewritten
+                if (!last) continue;
+                __threadfence();
+                const float* wst = p.ws + (size_t)u.tile_global * p.splits * tile_stride;
+                for (int t0 = 0; t0 < p.T_pad; t0 += 32) {
+                    for (int sub = 0; sub < p.n_sub; ++sub)
+                        for (int j = 0; j < 32; ++j) {
+                            float s = 0.0f;
+                            for (int sp = 0; sp < p.splits; ++sp)
+                                s += __ldcg(wst + (size_t)sp * tile_stride + ((size_t)sub * p.T_pad + t0 + j) * kTcBM + row);
+                            v[sub][j] = s;
+                        }
+                    epilogue_chunk(p, es, u, sc, row, t0, v);
+                }
+                if (threadIdx.x == 64) p.counters[u.tile_global] = 0;  // self-reset for the next launch
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols));
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    }
+    return fn;
+}
+
+CUtensorMapSwizzle swz(int bytes) {
+    switch (bytes) {
+        case 128: return CU_TENSOR_MAP_SWIZZLE_128B;
+        case 64: return CU_TENSOR_MAP_SWIZZLE_64B;
+        case 32: return CU_TENSOR_MAP_SWIZZLE_32B;
+        default: return CU_TENSOR_MAP_SWIZZLE_NONE;
+    }
+}
+
+}  // namespace
+
+int tc_encode_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                 uint32_t box_inner, uint32_t box_outer, int swizzle_bytes) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return AOS_ERR_CUDA;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15) || ((box_inner * 2) & 15)) return AOS_ERR_INVALID;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swz(swizzle_bytes), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? AOS_OK : AOS_ERR_CUDA;
+}
+
+int tc_encode_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1_bytes,
+                 uint64_t stride2_bytes, uint32_t b0, uint32_t b1, uint32_t b2, int swizzle_bytes) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return AOS_ERR_CUDA;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (stride1_bytes & 15) || (stride2_bytes & 15)) return AOS_ERR_INVALID;
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+    cuuint32_t box[3] = {b0, b1, b2};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swz(swizzle_bytes), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? AOS_OK : AOS_ERR_CUDA;
+}
+
+size_t tc_tail_bytes(const TcParams& p) {
+    return 512 + 128 * 33 * 4 + (size_t)p.T_pad * sizeof(aos_router_ring);
+}
+
+size_t tc_smem_bytes(const TcParams& p) {
+    return 1024 + (size_t)p.n_stages * p.stage_bytes + tc_tail_bytes(p);
+}
+
+int tc_prepare(TcParams& p, int smem_budget) {
+    if (p.T <= 0 || p.T > 256 || p.n_sub < 1 || p.n_sub > 2 || p.n_seg < 1 || p.n_seg > kTcMaxSets ||
+        p.n_seg * p.n_sub > kTcMaxSets || p.splits < 1 || p.kb < 1)
+        return AOS_ERR_INVALID;
+    p.T_pad = ((p.T + 15) / 16) * 16;
+    if (p.T_pad < 32) p.T_pad = 32;  // epilogue works in 32-token chunks
+    const uint32_t w_bytes = (uint32_t)p.n_sub * kTcBM * 128;
+    const uint32_t act_base = (uint32_t)p.T_pad * 128;
+    const uint32_t act_lora = (uint32_t)p.n_sub * kSlabsPerStep * p.T_pad * 32;
+    const uint32_t act = std::max(act_base, p.lora ? act_lora : 0u);
+    p.act_off = w_bytes;
+    p.stage_bytes = (w_bytes + act + 1023) & ~1023u;
+    const size_t fixed = 1024 + tc_tail_bytes(p);
+    int ns = (int)((smem_budget - (int)fixed) / (int)p.stage_bytes);
+    ns = std::min(ns, 8);
+    if (ns < 2) return AOS_ERR_INVALID;
+    p.n_stages = ns;
+    if (2 * p.splits > p.kb + 1 && p.splits > 1) p.splits = std::max(1, p.kb / 2);
+    return AOS_OK;
+}
+
+int tc_num_sms() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+// Opt the kernel in to the full 227 KB of shared memory (once per device,
+// outside any stream capture).
+cudaError_t tc_configure() {
+    return cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+}
+
+cudaError_t tc_launch(const TcParams& p, int grid, cudaStream_t stream) {
+    const size_t smem = tc_smem_bytes(p);
+    if (smem > 227 * 1024) return cudaErrorInvalidValue;
+    tc_gemm_kernel<<<grid, kTcThreads, smem, stream>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace aos

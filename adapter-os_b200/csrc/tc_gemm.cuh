@@ -1,0 +1,80 @@
+// tc_gemm.cuh — parameters of the tcgen05 weight-streaming GEMM (tc_gemm.cu).
+//
+// D[rows, tokens] = W[rows, K] . X[tokens, K]^T  (+ sum over touched LoRA rank
+// slabs of  B_slab[rows, 16] . Hm[tokens, slab cols]^T), i.e. the base
+// projection y = x W^T of mlx_cpp_wrapper_real.cpp:3372-3381 fused with the
+// LoRA expand of :3394-3419, computed "swap-AB": weight rows are the MMA's M
+// (128 per tile) and the decode tokens are its N (<= 256).
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace aos {
+
+enum TcMode : int {
+    TC_STORE_BF16 = 0,  // out[t][col] = bf16(acc)
+    TC_RESID_BF16 = 1,  // resid[t][col] = bf16(resid + acc)          (o / down + residual)
+    TC_STORE_F32 = 2,   // out[t][col] = acc                           (lm_head logits)
+    TC_QKV_ROPE = 3,    // q -> out (RoPE), k -> paged K (RoPE), v -> paged V
+    TC_SWIGLU = 4,      // out[t][col] = bf16(silu(acc0) * acc1)        (n_sub = 2)
+    TC_SHRINK_HM = 5    // hm[t][slab col] = bf16(acc * gate(t, owner(col)))
+};
+
+constexpr int kTcMaxSets = 3;    // operand sets = segments x sub-tiles
+constexpr int kTcThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kTcBM = 128;       // weight rows per tile
+constexpr int kTcBK = 64;        // K elements per base step (128 B, one SW128 row)
+constexpr int kSlab = 16;        // LoRA rank columns per slab (one K=16 MMA)
+constexpr int kSlabsPerStep = 4;
+constexpr int kShrinkSlabsPerTile = kTcBM / kSlab;  // 8
+
+struct TcParams {
+    CUtensorMap tm_w[kTcMaxSets];   // base weights [rows, K] (or lora_A [R, K] for shrink), SW128
+    CUtensorMap tm_x;               // activations [T, K], SW128
+    CUtensorMap tm_lb[kTcMaxSets];  // lora_B slabs [R/16][rows][16], SW32
+    CUtensorMap tm_lh[kTcMaxSets];  // gated shrink output [T, R], SW32
+    int mode, n_sub, n_seg, T, T_pad, kb, splits, n_stages, lora, shrink;
+    int seg_tiles[kTcMaxSets];      // tiles per segment (ignored for shrink: from n_slabs)
+    int seg_wrow0[kTcMaxSets];      // first W row of the segment
+    int seg_out0[kTcMaxSets];       // first output feature of the segment
+    int seg_rows[kTcMaxSets];       // valid output rows of the segment
+    int seg_module[kTcMaxSets];
+    uint32_t stage_bytes, act_off;  // bytes per pipeline stage; offset of the activation region
+    const int* slabs;               // touched slab list (ascending)
+    const int* n_slabs;             // its length
+    // epilogue
+    void* out[kTcMaxSets];
+    int ld_out;
+    uint16_t* resid;
+    const float* rope;  // [max_pos][hd/2][2] cos/sin
+    uint16_t* k_pool;
+    uint16_t* v_pool;
+    const int* block_tables;
+    const int* ctx_lens;
+    int max_blocks, num_blocks, nkv, layer;
+    int R;                          // arena rank capacity (columns of hm)
+    const int* col_owner;           // [R] adapter id owning the column, -1 if free
+    const float* adapter_scale;     // [max_adapters] alpha / rank
+    const aos_router_ring* rings;   // [T]
+    int max_adapters;
+    float* ws;                      // split-K partials
+    int* counters;                  // per tile, self-resetting
+    int* err;                       // device error word (0 = ok)
+};
+
+// Host helpers (tc_gemm.cu).
+int tc_encode_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                 uint32_t box_inner, uint32_t box_outer, int swizzle_bytes);
+int tc_encode_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                 uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1, uint32_t b2,
+                 int swizzle_bytes);
+// Fills stage sizes; returns 0 or an aos_status.
+int tc_prepare(TcParams& p, int smem_budget);
+cudaError_t tc_launch(const TcParams& p, int grid, cudaStream_t stream);
+cudaError_t tc_configure();
+size_t tc_smem_bytes(const TcParams& p);
+int tc_num_sms();
+
+}  // namespace aos

@@ -1,0 +1,250 @@
+/*
+ * aos_cuda.h — C ABI of the B200 (sm_100a) backend for adapter-os's per-token
+ * hot path: batched K-sparse router, fused base + gathered-LoRA projections,
+ * SwiGLU MLP and paged-KV decode attention.
+ *
+ * The ABI is what a `FusedKernels` implementation
+ * (crates/adapteros-lora-kernel-api/src/lib.rs:308-716) calls through a thin
+ * extern "C" FFI crate; conventions follow the MLX C wrapper
+ * (crates/adapteros-lora-mlx-ffi/wrapper.h): opaque handles, int status codes
+ * and a per-handle last-error string.
+ *
+ * Rules shared by every entry point:
+ *   - Status: 0 = AOS_OK, negative = error (see aos_status); the message is in
+ *     aos_last_error(ctx) (or aos_last_error(NULL) for context-free calls).
+ *   - There is no CPU fallback: with no usable sm_100 device every compute
+ *     entry point fails with AOS_ERR_NO_DEVICE.
+ *   - `_dev` entry points take device pointers and enqueue on `stream` (a
+ *     cudaStream_t, NULL = the context's stream); the others take host
+ *     pointers and return when the result is in host memory.
+ *   - A context is single-threaded (the Rust side serialises calls with
+ *     &mut self, lib.rs:371); distinct contexts may be used concurrently.
+ */
+#ifndef AOS_CUDA_H
+#define AOS_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AOS_MAX_K 8             /* adapteros-core/src/defaults.rs:37 MAX_K */
+#define AOS_Q15_DENOM 32767.0f  /* adapteros-lora-router/src/quantization.rs:22 */
+#define AOS_NUM_MODULES 7
+
+typedef enum aos_status {
+    AOS_OK = 0,
+    AOS_ERR_INVALID = -1,    /* AosError::Validation: bad argument or shape        */
+    AOS_ERR_CUDA = -2,       /* AosError::Kernel: a CUDA call or kernel failed      */
+    AOS_ERR_NOMEM = -3,      /* arena / KV pool / device allocation exhausted      */
+    AOS_ERR_NONFINITE = -4,  /* AosError::DeterminismViolation: NaN/Inf router input */
+    AOS_ERR_NOT_FOUND = -5,  /* unknown adapter id / sequence id                  */
+    AOS_ERR_TIMEOUT = -6,    /* a bounded device-side wait ran out                */
+    AOS_ERR_NO_DEVICE = -7,  /* no sm_100 device: there is no CPU fallback         */
+    AOS_ERR_STATE = -8       /* call out of order (e.g. step before weights load)  */
+} aos_status;
+
+/* Module ids, in the order of MLXLoraLayer (mlx_cpp_wrapper_real.cpp:1248-1256). */
+typedef enum aos_module {
+    AOS_MOD_Q = 0, AOS_MOD_K = 1, AOS_MOD_V = 2, AOS_MOD_O = 3,
+    AOS_MOD_GATE = 4, AOS_MOD_UP = 5, AOS_MOD_DOWN = 6
+} aos_module;
+
+/* Base-weight kinds for aos_load_weight. */
+typedef enum aos_weight_kind {
+    AOS_W_EMBED = 0,      /* [vocab, hidden]                                     */
+    AOS_W_LM_HEAD = 1,    /* [vocab, hidden]                                     */
+    AOS_W_FINAL_NORM = 2, /* [hidden]                                            */
+    AOS_W_ATTN_NORM = 3,  /* [hidden] per layer (input_layernorm)                */
+    AOS_W_MLP_NORM = 4,   /* [hidden] per layer (post_attention_layernorm)       */
+    AOS_W_PROJ = 5        /* [out, in] per layer and module (q..down, nn.Linear) */
+} aos_weight_kind;
+
+/* RouterRing device layout, 40 bytes
+ * (kernel-mtl/src/ring_buffer.rs:44-58; kernel-api/src/lib.rs:58-75).
+ * Unused entries are zero-filled (RouterRing::set, lib.rs:188-192). */
+typedef struct aos_router_ring {
+    uint32_t top_k;
+    uint32_t position;
+    uint16_t indices[AOS_MAX_K];
+    int16_t gates_q15[AOS_MAX_K];
+} aos_router_ring;
+
+/* Router parameters; sanitised like Router::new_with_weights
+ * (router.rs:397-400 via sanitize_k/eps/tau, :127-187) and set_routing_bias
+ * (:556-561).  Features are empty, so feature scores are 0 (router.rs:985-988). */
+typedef struct aos_router_params {
+    uint32_t k;          /* 0 -> 1, > 8 -> 8                                   */
+    float tau;           /* non-finite or <= 0 -> 1.0                          */
+    float eps;           /* non-finite or outside [0,1] -> 0.02                */
+    float routing_bias;  /* non-finite or <= 0 -> 1.0                          */
+} aos_router_params;
+
+/* Decoder shape and resource sizing for a context. */
+typedef struct aos_model_config {
+    uint32_t hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab, n_layers;
+    float rms_eps;
+    float rope_theta;
+    uint32_t rope_mlx_as_written; /* 1: inv_freq = 1/theta^(-2i/hd) as MLX code writes it */
+    uint32_t max_batch;           /* tokens per decode step (<= 256)                      */
+    uint32_t kv_block_size;       /* tokens per KV page; must be 16                        */
+    uint32_t kv_num_blocks;       /* KV pages per layer in the pool                        */
+    uint32_t max_seq_len;         /* longest sequence (tokens)                             */
+    uint32_t lora_rank_capacity;  /* rank columns in the adapter arena (multiple of 16)    */
+    uint32_t lora_max_adapters;   /* adapter ids are < this (<= 65535)                     */
+    uint32_t lora_module_mask;    /* bit m: module m may carry LoRA (0 = all seven)        */
+    int32_t device;               /* CUDA ordinal                                          */
+} aos_model_config;
+
+typedef struct aos_metrics {           /* BackendMetrics (kernel-api/src/lib.rs:28-39) */
+    uint64_t steps, tokens, route_calls;
+    uint64_t base_weight_bytes, arena_bytes, arena_used_rank_cols, kv_pool_bytes;
+    uint32_t adapters_loaded, kv_blocks_used, kv_blocks_total, sequences;
+    float last_step_ms;
+} aos_metrics;
+
+typedef struct aos_determinism_report { /* attestation.rs:130-460 (subset)            */
+    char backend[32];
+    char device_name[64];
+    uint32_t sm_major, sm_minor;
+    uint32_t fast_math;             /* 0: built without fast-math                     */
+    uint32_t float_atomics;         /* 0: no floating-point atomics on any path       */
+    uint32_t fixed_reduction_order; /* 1: every split reduction has a fixed order     */
+    char kernel_build_id[64];
+} aos_determinism_report;
+
+typedef struct aos_ctx aos_ctx;
+
+/* ---- library ------------------------------------------------------------ */
+const char* aos_version(void);
+/* Number of sm_100 devices visible (0 when none). */
+int aos_device_count(void);
+/* Last error of a context, or of context-free calls when ctx is NULL
+ * (mlx_get_last_error, wrapper.h:199-200). */
+const char* aos_last_error(const aos_ctx* ctx);
+
+/* ---- batched router (crates/adapteros-lora-router/src/router.rs:1567-1952) ----
+ * One RouterRing per token: scores = ((prior + 0) - 0) * bias * clamp(vw,0,2),
+ * total-order sort DESC with stable_id ASC tie-break (:234-264), top-K,
+ * f64 Kahan softmax (:1340-1411), entropy floor eps/K and f32 renormalise
+ * (:1818-1842), Q15 round-half-away (quantization.rs:172-175), canonical order
+ * (q15 DESC, score DESC, stable_id ASC, idx ASC; :1310-1325).  Bit-exact with
+ * the reference.  priors: [T, N]; stable_ids: [N]; version_weights: [N] or
+ * NULL; allowed: [N] (0/1) or NULL; positions: [T] or NULL (ring.position);
+ * entropy: [T] or NULL; status: [T] or NULL (0 or AOS_ERR_NONFINITE).  A
+ * token whose inputs are non-finite gets an empty ring and the call returns
+ * AOS_ERR_NONFINITE.  N <= 4096. */
+int aos_route_batch(const float* priors, const uint64_t* stable_ids, const float* version_weights,
+                    const uint8_t* allowed, const uint32_t* positions, uint32_t T, uint32_t N,
+                    const aos_router_params* params, aos_router_ring* rings, float* entropy,
+                    int32_t* status);
+/* Device-pointer form; enqueued on `stream`, no host synchronisation.
+ * Per-token errors are only reported through `status`. */
+int aos_route_batch_dev(const float* priors, const uint64_t* stable_ids,
+                        const float* version_weights, const uint8_t* allowed,
+                        const uint32_t* positions, uint32_t T, uint32_t N,
+                        const aos_router_params* params, aos_router_ring* rings, float* entropy,
+                        int32_t* status, void* stream);
+
+/* ---- fp32 LoRA op (config 1) ---------------------------------------------
+ * y[t] = W x[t] + sum over ring slots with q15 > 0 of
+ *        (q15/32767 * (B_a (A_a x[t]))) * (alpha_a / rank)
+ * (kernel_testing.rs:220-257 cpu_lora_forward; liquid.rs:222-250 blend loop;
+ *  gate dequant mlx-ffi/src/backend.rs:405-418).  x: [T, in]; W: [out, in];
+ * A: [n_adapters, rank, in]; B: [n_adapters, out, rank]; alpha: [n_adapters]
+ * or NULL (alpha = rank); rings: [T]; y: [T, out].  rank <= 64, in % 4 == 0. */
+int aos_lora_op_f32(const float* x, uint32_t T, uint32_t in_dim, uint32_t out_dim,
+                    const float* W, const float* A, const float* B, uint32_t n_adapters,
+                    uint32_t rank, const float* alpha, const aos_router_ring* rings, float* y);
+int aos_lora_op_f32_dev(const float* x, uint32_t T, uint32_t in_dim, uint32_t out_dim,
+                        const float* W, const float* A, const float* B, uint32_t n_adapters,
+                        uint32_t rank, const float* alpha, const aos_router_ring* rings, float* y,
+                        void* stream);
+
+/* ---- context: FusedKernels::load + hot-swap arena + KV cache ------------- */
+/* Create a backend on cfg->device; allocates the KV pool, adapter arena and
+ * step scratch up front (kernel-mtl/src/lib.rs:1476-1537 load). */
+aos_ctx* aos_init(const aos_model_config* cfg);
+void aos_destroy(aos_ctx* ctx);
+/* FusedKernels::device_name (lib.rs:374). */
+const char* aos_device_name(const aos_ctx* ctx);
+/* The context's CUDA stream (cudaStream_t). */
+void* aos_stream(aos_ctx* ctx);
+
+/* Load one bf16 base tensor (the plan's safetensors entries,
+ * kernel-mtl/src/lib.rs:660-1135).  layer is ignored for EMBED/LM_HEAD/
+ * FINAL_NORM; module is used only for AOS_W_PROJ.  data holds the tensor in
+ * row-major [out, in] (nn.Linear) order; src_on_device = 1 if it is a device
+ * pointer.  n_elems must match the configured shape. */
+int aos_load_weight(aos_ctx* ctx, aos_weight_kind kind, uint32_t layer, aos_module module,
+                    const uint16_t* data, uint64_t n_elems, int src_on_device);
+
+/* Adapter arena (FusedKernels::load_adapter_with_metadata / unload_adapter,
+ * lib.rs:388-432; MLX mlx_lora_adapter_new / _set_module, wrapper.h:383-397).
+ * aos_adapter_new reserves `rank` arena columns for id (rank % 8 == 0,
+ * 8 <= rank <= 256); scale = alpha / rank.  Modules that are never set stay
+ * zero (contribute nothing). */
+int aos_adapter_new(aos_ctx* ctx, uint16_t id, uint32_t rank, float alpha);
+/* A: [rank, in] (lora_A), B: [out, rank] (lora_B), bf16, for one layer/module. */
+int aos_adapter_set_module(aos_ctx* ctx, uint16_t id, uint32_t layer, aos_module module,
+                           const uint16_t* A, const uint16_t* B, int src_on_device);
+int aos_adapter_unload(aos_ctx* ctx, uint16_t id);
+/* 1 if id is resident, else 0. */
+int aos_adapter_is_loaded(const aos_ctx* ctx, uint16_t id);
+
+/* Paged KV cache (replaces the first-fit contiguous allocator of
+ * crates/adapteros-lora-worker/src/kvcache.rs:112-524 with 16-token pages). */
+int aos_kv_alloc(aos_ctx* ctx, uint64_t seq_id, uint32_t max_tokens);
+int aos_kv_free(aos_ctx* ctx, uint64_t seq_id);
+/* Declare `len` tokens already cached for seq (their K/V written by
+ * aos_kv_write or aos_kv_fill_synthetic). */
+int aos_kv_set_len(aos_ctx* ctx, uint64_t seq_id, uint32_t len);
+int aos_kv_get_len(const aos_ctx* ctx, uint64_t seq_id, uint32_t* len);
+/* Write K/V rows [n_tokens, n_kv_heads, head_dim] bf16 for positions
+ * pos0..pos0+n_tokens-1 of one layer. */
+int aos_kv_write(aos_ctx* ctx, uint64_t seq_id, uint32_t layer, uint32_t pos0, uint32_t n_tokens,
+                 const uint16_t* k, const uint16_t* v, int src_on_device);
+int aos_kv_read(aos_ctx* ctx, uint64_t seq_id, uint32_t layer, uint32_t pos0, uint32_t n_tokens,
+                uint16_t* k, uint16_t* v);
+/* Fill every page of the pool with seeded synthetic bf16 values ~N(0, std). */
+int aos_kv_fill_synthetic(aos_ctx* ctx, uint64_t seed, float std);
+/* FusedKernels::clear_all_caches / cache_memory_bytes (lib.rs:536-554). */
+int aos_kv_clear_all(aos_ctx* ctx);
+uint64_t aos_kv_memory_bytes(const aos_ctx* ctx);
+
+/* ---- the step (FusedKernels::run_step, batched; lib.rs:371) --------------
+ * One decode token per entry: rings[t] selects the adapters for token t,
+ * token_ids[t] is its input id and seq_ids[t] its sequence (each at most once
+ * per call).  Runs embedding -> n_layers x [RMSNorm -> q/k/v + LoRA -> RoPE ->
+ * paged-KV append -> GQA attention -> o + LoRA -> residual -> RMSNorm ->
+ * gate/up + LoRA -> SwiGLU -> down + LoRA -> residual] -> final RMSNorm ->
+ * lm_head (mlx_cpp_wrapper_real.cpp:3338-3559) and advances each sequence
+ * by one token (IoBuffers.position += 1, mlx-ffi/src/backend.rs:1292).
+ * logits: [T, vocab] f32 or NULL; hidden_out: [T, hidden] bf16 (the final
+ * hidden state before the final norm) or NULL. */
+int aos_run_step_batch(aos_ctx* ctx, const aos_router_ring* rings, const uint32_t* token_ids,
+                       const uint64_t* seq_ids, uint32_t T, float* logits, uint16_t* hidden_out);
+/* Device-pointer form (rings, token_ids, logits, hidden_out on the device;
+ * seq_ids stays a host array because it drives the page tables). */
+int aos_run_step_batch_dev(aos_ctx* ctx, const aos_router_ring* rings, const uint32_t* token_ids,
+                           const uint64_t* seq_ids, uint32_t T, float* logits,
+                           uint16_t* hidden_out, void* stream);
+/* One decoder layer on a caller-provided hidden state (config 2): hidden is
+ * [T, hidden] bf16 on the device, updated in place; sequences advance only
+ * if advance != 0. */
+int aos_layer_step_dev(aos_ctx* ctx, uint32_t layer, const aos_router_ring* rings,
+                       const uint64_t* seq_ids, uint32_t T, uint16_t* hidden, int advance,
+                       void* stream);
+
+/* ---- metrics / health / attestation (lib.rs:383, 559-593) ---------------- */
+int aos_get_metrics(const aos_ctx* ctx, aos_metrics* out);
+/* 0 = healthy; otherwise the first device error seen (e.g. AOS_ERR_TIMEOUT). */
+int aos_health_check(aos_ctx* ctx);
+int aos_attest_determinism(const aos_ctx* ctx, aos_determinism_report* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AOS_CUDA_H */
