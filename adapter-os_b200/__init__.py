@@ -76,6 +76,14 @@ class Metrics(C.Structure):
     ]
 
 
+KERNEL_CLASSES = ("gemm", "shrink", "attention", "rmsnorm", "prep", "embed", "lm_head", "other")
+
+
+class Profile(C.Structure):
+    _fields_ = [("launches", C.c_uint64 * 8), ("ms", C.c_double * 8), ("steps", C.c_uint64),
+                ("last_touched_slabs", C.c_uint32)]
+
+
 class DeterminismReport(C.Structure):
     _fields_ = [
         ("backend", C.c_char * 32), ("device_name", C.c_char * 64), ("sm_major", C.c_uint32),
@@ -123,6 +131,8 @@ def lib():
             "aos_run_step_batch_dev": (C.c_int, [vp, vp, vp, vp, u32, vp, vp, vp]),
             "aos_layer_step_dev": (C.c_int, [vp, u32, vp, vp, u32, vp, C.c_int, vp]),
             "aos_get_metrics": (C.c_int, [vp, vp]),
+            "aos_profile_enable": (C.c_int, [vp, C.c_int]),
+            "aos_profile_read": (C.c_int, [vp, vp, C.c_int]),
             "aos_health_check": (C.c_int, [vp]),
             "aos_attest_determinism": (C.c_int, [vp, vp]),
         }
@@ -365,6 +375,17 @@ class CudaKernels:
 
     def health_check(self):
         return self._check(self._L.aos_health_check(self.ctx))
+
+    def profile_enable(self, on=True):
+        """Per-kernel-class CUDA-event timing of every launch (steps run without graphs)."""
+        self._check(self._L.aos_profile_enable(self.ctx, int(bool(on))))
+
+    def profile_read(self, reset=True) -> dict:
+        p = Profile()
+        self._check(self._L.aos_profile_read(self.ctx, C.byref(p), int(bool(reset))))
+        return {"steps": p.steps, "touched_slabs": p.last_touched_slabs,
+                "ms": {k: p.ms[i] for i, k in enumerate(KERNEL_CLASSES)},
+                "launches": {k: p.launches[i] for i, k in enumerate(KERNEL_CLASSES)}}
 
     # -- weights (FusedKernels::load) ------------------------------------
     def load_weight(self, kind, data, layer=0, module=0, on_device=False):

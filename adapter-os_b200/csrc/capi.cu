@@ -51,12 +51,34 @@ int require_device(int device) {
 
 namespace {
 
-// RAII device buffer for the host-pointer convenience entry points.
+// Device staging buffer for the host-pointer entry points: grow-only and
+// cached per thread and device, so steady-state calls never allocate.
 struct DevBuf {
     void* p = nullptr;
-    cudaError_t alloc(size_t n) { return n ? cudaMalloc(&p, n) : cudaSuccess; }
-    ~DevBuf() {
-        if (p) cudaFree(p);
+    int slot;
+    explicit DevBuf(int s) : slot(s) {}
+    cudaError_t alloc(size_t n) {
+        struct Cache {
+            void* ptr[16] = {};
+            size_t cap[16] = {};
+            int dev[16] = {};
+        };
+        thread_local Cache cache;
+        if (!n) return cudaSuccess;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cache.ptr[slot] && (cache.cap[slot] < n || cache.dev[slot] != dev)) {
+            cudaFree(cache.ptr[slot]);
+            cache.ptr[slot] = nullptr;
+        }
+        if (!cache.ptr[slot]) {
+            cudaError_t e = cudaMalloc(&cache.ptr[slot], n);
+            if (e != cudaSuccess) return e;
+            cache.cap[slot] = n;
+            cache.dev[slot] = dev;
+        }
+        p = cache.ptr[slot];
+        return cudaSuccess;
     }
 };
 
@@ -121,7 +143,7 @@ int aos_route_batch(const float* priors, const uint64_t* stable_ids, const float
     if (rc) return rc;
     if ((rc = require_device())) return rc;
     if (T == 0) return AOS_OK;
-    DevBuf dp, ds, dv, da, dpos, dr, de, dst;
+    DevBuf dp(0), ds(1), dv(2), da(3), dpos(4), dr(5), de(6), dst(7);
     AOS_RETURN_IF_CUDA(dp.alloc((size_t)T * N * 4), set_global_error);
     AOS_RETURN_IF_CUDA(ds.alloc((size_t)N * 8), set_global_error);
     AOS_RETURN_IF_CUDA(dr.alloc((size_t)T * sizeof(aos_router_ring)), set_global_error);
@@ -195,7 +217,7 @@ int aos_lora_op_f32(const float* x, uint32_t T, uint32_t in_dim, uint32_t out_di
     int rc = require_device();
     if (rc) return rc;
     if (T == 0) return AOS_OK;
-    DevBuf dx, dw, da, db, dal, dr, dy;
+    DevBuf dx(8), dw(9), da(10), db(11), dal(12), dr(13), dy(14);
     const size_t nx = (size_t)T * in_dim * 4, nw = (size_t)out_dim * in_dim * 4;
     const size_t na = (size_t)n_adapters * rank * in_dim * 4, nb = (size_t)n_adapters * out_dim * rank * 4;
     AOS_RETURN_IF_CUDA(dx.alloc(nx), set_global_error);

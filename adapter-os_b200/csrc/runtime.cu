@@ -128,6 +128,11 @@ struct aos_ctx {
 
     // metrics
     aos_metrics m{};
+    bool prof_on = false;
+    std::vector<cudaEvent_t> prof_ev;
+    std::vector<int> prof_cls;
+    size_t prof_used = 0;
+    aos_profile prof{};
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
 
     int fail(int code, const std::string& msg) {
@@ -401,42 +406,80 @@ int get_plan(aos_ctx* c, int T, StepPlan** out) {
             return (ctx)->fail(AOS_ERR_CUDA, std::string("launch " #expr ": ") + cudaGetErrorString(_e)); \
     } while (0)
 
+// Per-kernel-class device timing (aos_profile_enable): each launch is
+// bracketed by two CUDA events taken from a pool; aos_profile_read sums them.
+int prof_begin(aos_ctx* c, int cls, cudaStream_t s);
+void prof_end(aos_ctx* c, int slot, cudaStream_t s);
+
+#define PLAUNCH(ctx, cls, s, expr)                 \
+    do {                                           \
+        const int _slot = prof_begin(ctx, cls, s); \
+        LAUNCH(ctx, expr);                         \
+        prof_end(ctx, _slot, s);                   \
+    } while (0)
+
 // Enqueue one decoder layer on `s` (hidden state in ctx->d_hidden).
 int enqueue_layer(aos_ctx* c, const StepPlan& plan, int layer, cudaStream_t s) {
     const LayerPlan& lp = plan.layers[layer];
     const int T = plan.T;
     const uint32_t H = c->cfg.hidden;
-    LAUNCH(c, launch_rmsnorm(c->d_hidden, c->attn_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
-    if (lp.shrink_grid[kGroupQKV]) LAUNCH(c, tc_launch(lp.shrink[kGroupQKV], lp.shrink_grid[kGroupQKV], s));
-    LAUNCH(c, tc_launch(lp.gemm[kGroupQKV], lp.gemm_grid[kGroupQKV], s));
-    LAUNCH(c, launch_attention(c->tm_k, c->tm_v, c->d_q, c->d_block_tables, c->d_ctx_lens, c->d_attn_part, c->d_attn_ml, T,
-                               (int)c->cfg.n_heads, (int)c->cfg.n_kv_heads, layer, (int)c->cfg.kv_num_blocks,
-                               c->max_blocks, c->attn_chunks, c->d_err, c->d_attn, s));
-    if (lp.shrink_grid[kGroupO]) LAUNCH(c, tc_launch(lp.shrink[kGroupO], lp.shrink_grid[kGroupO], s));
-    LAUNCH(c, tc_launch(lp.gemm[kGroupO], lp.gemm_grid[kGroupO], s));
-    LAUNCH(c, launch_rmsnorm(c->d_hidden, c->mlp_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
-    if (lp.shrink_grid[kGroupGU]) LAUNCH(c, tc_launch(lp.shrink[kGroupGU], lp.shrink_grid[kGroupGU], s));
-    LAUNCH(c, tc_launch(lp.gemm[kGroupGU], lp.gemm_grid[kGroupGU], s));
-    if (lp.shrink_grid[kGroupD]) LAUNCH(c, tc_launch(lp.shrink[kGroupD], lp.shrink_grid[kGroupD], s));
-    LAUNCH(c, tc_launch(lp.gemm[kGroupD], lp.gemm_grid[kGroupD], s));
+    PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(c->d_hidden, c->attn_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
+    if (lp.shrink_grid[kGroupQKV])
+        PLAUNCH(c, AOS_K_SHRINK, s, tc_launch(lp.shrink[kGroupQKV], lp.shrink_grid[kGroupQKV], s));
+    PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupQKV], lp.gemm_grid[kGroupQKV], s));
+    PLAUNCH(c, AOS_K_ATTN, s,
+            launch_attention(c->tm_k, c->tm_v, c->d_q, c->d_block_tables, c->d_ctx_lens, c->d_attn_part, c->d_attn_ml, T,
+                             (int)c->cfg.n_heads, (int)c->cfg.n_kv_heads, layer, (int)c->cfg.kv_num_blocks, c->max_blocks,
+                             c->attn_chunks, c->d_err, c->d_attn, s));
+    if (lp.shrink_grid[kGroupO]) PLAUNCH(c, AOS_K_SHRINK, s, tc_launch(lp.shrink[kGroupO], lp.shrink_grid[kGroupO], s));
+    PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupO], lp.gemm_grid[kGroupO], s));
+    PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(c->d_hidden, c->mlp_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
+    if (lp.shrink_grid[kGroupGU])
+        PLAUNCH(c, AOS_K_SHRINK, s, tc_launch(lp.shrink[kGroupGU], lp.shrink_grid[kGroupGU], s));
+    PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupGU], lp.gemm_grid[kGroupGU], s));
+    if (lp.shrink_grid[kGroupD]) PLAUNCH(c, AOS_K_SHRINK, s, tc_launch(lp.shrink[kGroupD], lp.shrink_grid[kGroupD], s));
+    PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupD], lp.gemm_grid[kGroupD], s));
     return AOS_OK;
 }
 
 // Device part of a decode step: routing prep, embedding, layers, final norm, lm_head.
 int enqueue_step(aos_ctx* c, StepPlan& plan, bool with_logits, cudaStream_t s) {
     const int T = plan.T;
-    LAUNCH(c, launch_lora_prep(c->d_rings, T, c->d_col_off, c->d_rank, (int)c->cfg.lora_max_adapters, c->R / 16,
-                               c->d_slabs, c->d_n_slabs, s));
-    LAUNCH(c, launch_embed(c->embed, c->d_tokens, T, (int)c->cfg.hidden, (int)c->cfg.vocab, c->d_hidden, s));
+    PLAUNCH(c, AOS_K_PREP, s,
+            launch_lora_prep(c->d_rings, T, c->d_col_off, c->d_rank, (int)c->cfg.lora_max_adapters, c->R / 16, c->d_slabs,
+                             c->d_n_slabs, s));
+    PLAUNCH(c, AOS_K_EMBED, s, launch_embed(c->embed, c->d_tokens, T, (int)c->cfg.hidden, (int)c->cfg.vocab, c->d_hidden, s));
     for (uint32_t l = 0; l < c->cfg.n_layers; ++l) {
         int rc = enqueue_layer(c, plan, (int)l, s);
         if (rc) return rc;
     }
     if (with_logits) {
-        LAUNCH(c, launch_rmsnorm(c->d_hidden, c->final_norm, T, (int)c->cfg.hidden, c->cfg.rms_eps, c->d_normed, s));
-        LAUNCH(c, tc_launch(plan.lm_head, plan.lm_grid, s));
+        PLAUNCH(c, AOS_K_NORM, s,
+                launch_rmsnorm(c->d_hidden, c->final_norm, T, (int)c->cfg.hidden, c->cfg.rms_eps, c->d_normed, s));
+        PLAUNCH(c, AOS_K_LM_HEAD, s, tc_launch(plan.lm_head, plan.lm_grid, s));
     }
     return AOS_OK;
+}
+
+int prof_begin(aos_ctx* c, int cls, cudaStream_t s) {
+    if (!c->prof_on) return -1;
+    if (c->prof_used + 2 > c->prof_ev.size()) {
+        for (int i = 0; i < 64; ++i) {
+            cudaEvent_t e;
+            if (cudaEventCreate(&e) != cudaSuccess) return -1;
+            c->prof_ev.push_back(e);
+        }
+        c->prof_cls.resize(c->prof_ev.size() / 2);
+    }
+    const int slot = (int)c->prof_used;
+    c->prof_used += 2;
+    c->prof_cls[slot / 2] = cls;
+    cudaEventRecord(c->prof_ev[slot], s);
+    return slot;
+}
+
+void prof_end(aos_ctx* c, int slot, cudaStream_t s) {
+    if (slot >= 0) cudaEventRecord(c->prof_ev[slot + 1], s);
 }
 
 bool use_graphs() {
@@ -448,6 +491,23 @@ int run_step_device(aos_ctx* c, int T, bool with_logits, cudaStream_t s) {
     StepPlan* plan = nullptr;
     int rc = get_plan(c, T, &plan);
     if (rc) return rc;
+    if (c->prof_on) {  // instrumented, graph-less step; times are collected after the step
+        rc = enqueue_step(c, *plan, with_logits, s);
+        if (rc) return rc;
+        CTX_CUDA(c, cudaStreamSynchronize(s));
+        for (size_t i = 0; i + 1 < c->prof_used; i += 2) {
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, c->prof_ev[i], c->prof_ev[i + 1]);
+            c->prof.ms[c->prof_cls[i / 2]] += ms;
+            c->prof.launches[c->prof_cls[i / 2]] += 1;
+        }
+        c->prof_used = 0;
+        c->prof.steps += 1;
+        int ns = 0;
+        CTX_CUDA(c, cudaMemcpy(&ns, c->d_n_slabs, 4, cudaMemcpyDeviceToHost));
+        c->prof.last_touched_slabs = (uint32_t)ns;
+        return AOS_OK;
+    }
     if (!use_graphs()) return enqueue_step(c, *plan, with_logits, s);
     if (!plan->graph_valid || (plan->graph_logits != (void*)(with_logits ? c->d_logits : nullptr))) {
         if (plan->graph) cudaGraphExecDestroy(plan->graph);
@@ -692,6 +752,7 @@ void aos_destroy(aos_ctx* c) {
     if (c->h_ctx_lens) cudaFreeHost(c->h_ctx_lens);
     if (c->ev0) cudaEventDestroy(c->ev0);
     if (c->ev1) cudaEventDestroy(c->ev1);
+    for (auto e : c->prof_ev) cudaEventDestroy(e);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
 }
@@ -1004,6 +1065,19 @@ int aos_layer_step_dev(aos_ctx* c, uint32_t layer, const aos_router_ring* rings,
 }
 
 // ------------------------------------------------------------------ metrics etc.
+int aos_profile_enable(aos_ctx* c, int enable) {
+    if (!c) return AOS_ERR_INVALID;
+    c->prof_on = enable != 0;
+    return AOS_OK;
+}
+
+int aos_profile_read(aos_ctx* c, aos_profile* out, int reset) {
+    if (!c || !out) return AOS_ERR_INVALID;
+    *out = c->prof;
+    if (reset) c->prof = aos_profile{};
+    return AOS_OK;
+}
+
 int aos_get_metrics(const aos_ctx* c, aos_metrics* out) {
     if (!c || !out) return AOS_ERR_INVALID;
     *out = c->m;

@@ -238,6 +238,32 @@ int aos_layer_step_dev(aos_ctx* ctx, uint32_t layer, const aos_router_ring* ring
                        const uint64_t* seq_ids, uint32_t T, uint16_t* hidden, int advance,
                        void* stream);
 
+/* ---- per-kernel device timing (replaces Metal counter sampling,
+ * crates/adapteros-lora-kernel-prof/src/lib.rs:1-21) ------------------------
+ * While enabled, steps run without CUDA graphs and every launch is bracketed
+ * by CUDA events on its stream; aos_profile_read sums the device time per
+ * kernel class. */
+typedef enum aos_kernel_class {
+    AOS_K_GEMM = 0,    /* base projection + fused LoRA expand (tcgen05)      */
+    AOS_K_SHRINK = 1,  /* LoRA shrink H = gate * (A x) (tcgen05)             */
+    AOS_K_ATTN = 2,    /* paged decode attention + chunk combine             */
+    AOS_K_NORM = 3,    /* RMSNorm                                            */
+    AOS_K_PREP = 4,    /* routing prep (touched rank slabs)                  */
+    AOS_K_EMBED = 5,   /* embedding gather                                   */
+    AOS_K_LM_HEAD = 6, /* lm_head GEMM (tcgen05)                             */
+    AOS_K_NUM_CLASSES = 8
+} aos_kernel_class;
+
+typedef struct aos_profile {
+    uint64_t launches[AOS_K_NUM_CLASSES];
+    double ms[AOS_K_NUM_CLASSES];
+    uint64_t steps;
+    uint32_t last_touched_slabs; /* rank slabs the last step streamed        */
+} aos_profile;
+
+int aos_profile_enable(aos_ctx* ctx, int enable);
+int aos_profile_read(aos_ctx* ctx, aos_profile* out, int reset);
+
 /* ---- metrics / health / attestation (lib.rs:383, 559-593) ---------------- */
 int aos_get_metrics(const aos_ctx* ctx, aos_metrics* out);
 /* 0 = healthy; otherwise the first device error seen (e.g. AOS_ERR_TIMEOUT). */

@@ -195,11 +195,15 @@ def liquid_blend_f32(x, As, Bs, alphas, coeffs, out_dim):
 def f32_to_bf16_bits(a: np.ndarray) -> np.ndarray:
     """Round-to-nearest-even f32 -> bf16 bit patterns (uint16)."""
     a = np.ascontiguousarray(a, dtype=np.float32)
-    u = a.view(np.uint32).astype(np.uint64)
-    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    u = a.view(np.uint32)
+    finite = np.isfinite(a)
+    if finite.all():
+        # |x| < inf: adding at most 0x8000 cannot carry out of 32 bits
+        return ((u + (0x7FFF + ((u >> 16) & 1))) >> 16).astype(np.uint16)
+    r = ((u + (0x7FFF + ((u >> 16) & 1))) >> 16).astype(np.uint16)
+    r[~finite] = (u[~finite] >> 16).astype(np.uint16)
     nan = np.isnan(a)
-    if nan.any():
-        r[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    r[nan] |= 0x40
     return r
 
 
@@ -336,9 +340,9 @@ class HostKV:
         self.k_pool = np.zeros(shape, np.uint16) if k_pool is None else k_pool
         self.v_pool = np.zeros(shape, np.uint16) if v_pool is None else v_pool
         self.num_blocks, self.block_size = num_blocks, block_size
-        self.block_tables = np.ascontiguousarray(block_tables, dtype=np.int32)
+        self.block_tables = np.array(block_tables, dtype=np.int32, copy=True)
         self.max_blocks = self.block_tables.shape[1]
-        self.ctx_lens = np.ascontiguousarray(ctx_lens, dtype=np.int32)
+        self.ctx_lens = np.array(ctx_lens, dtype=np.int32, copy=True)
 
     def _struct(self):
         s = OracleKV()

@@ -41,7 +41,7 @@ class Setup:
         mb = (max_seq + 15) // 16
         self.nb = T * mb
         bt = np.arange(T * mb, dtype=np.int32).reshape(T, mb)
-        self.kv = O.HostKV(self.m, self.nb, 16, bt, self.ctx_lens)
+        self.kv = O.HostKV(self.m, self.nb, 16, bt, self.ctx_lens.copy())  # own copy: tests advance it
         # cached K/V ~ N(0, 1)
         for t, n in enumerate(ctx_lens):
             for l in range(L):
