@@ -81,7 +81,7 @@ KERNEL_CLASSES = ("gemm", "shrink", "attention", "rmsnorm", "prep", "embed", "lm
 
 class Profile(C.Structure):
     _fields_ = [("launches", C.c_uint64 * 8), ("ms", C.c_double * 8), ("steps", C.c_uint64),
-                ("last_touched_slabs", C.c_uint32)]
+                ("last_touched_groups", C.c_uint32)]
 
 
 class DeterminismReport(C.Structure):
@@ -383,7 +383,7 @@ class CudaKernels:
     def profile_read(self, reset=True) -> dict:
         p = Profile()
         self._check(self._L.aos_profile_read(self.ctx, C.byref(p), int(bool(reset))))
-        return {"steps": p.steps, "touched_slabs": p.last_touched_slabs,
+        return {"steps": p.steps, "touched_groups": p.last_touched_groups,
                 "ms": {k: p.ms[i] for i, k in enumerate(KERNEL_CLASSES)},
                 "launches": {k: p.launches[i] for i, k in enumerate(KERNEL_CLASSES)}}
 

@@ -38,17 +38,28 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
-    if (mbar_try(bar, parity)) return true;
+// Bounded wait; false on timeout or when another role already failed.  The
+// fast path only polls the barrier; the error word and the clock are checked
+// every 1024 polls so a completed phase is seen without an extra L2 round trip.
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, int* err) {
     const long long t0 = clock64();
+    uint32_t n = 0;
     while (!mbar_try(bar, parity)) {
-        if (*(volatile int*)err != 0) return false;
-        if (clock64() - t0 > kSpinLimitCycles) {
-            atomicCAS(err, 0, AOS_ERR_TIMEOUT);
-            return false;
+        if ((++n & 1023u) == 0) {
+            if (*(volatile int*)err != 0) return false;
+            if (clock64() - t0 > kSpinLimitCycles) {
+                atomicCAS(err, 0, AOS_ERR_TIMEOUT);
+                return false;
+            }
         }
     }
     return true;
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+        if (mbar_try(bar, parity)) return true;
+    return mbar_wait_slow(bar, parity, err);
 }
 // Time-bounded wait that ignores the error word: used only to drain this
 // CTA's own copies / MMAs before it exits on an error path.

@@ -1,5 +1,5 @@
 // decode_kernels.cu — the small per-step kernels around the GEMMs:
-// embedding gather, RMSNorm, the LoRA routing prep (touched rank slabs), and
+// embedding gather, RMSNorm, the LoRA routing prep (touched rank groups), and
 // synthetic KV fill.  All reductions use a fixed order.
 
 #include "common.cuh"
@@ -62,9 +62,11 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* __restrict
     }
 }
 
-// Routing prep for the LoRA GEMMs: mark every 16-column rank slab of the
+// Routing prep for the LoRA GEMMs: mark every 64-column rank group of the
 // arena that holds a column of an adapter selected (q15 > 0) by any token,
-// then compact the marks in ascending slab order.  One CTA of 1024 threads.
+// then compact the marks in ascending group order.  One CTA of 1024 threads.
+// (Names below say "slab" for a group of kPrepGroupCols arena columns.)
+constexpr int kPrepGroupCols = 64;
 __global__ void __launch_bounds__(1024) lora_prep_kernel(const aos_router_ring* __restrict__ rings, int T,
                                                          const int* __restrict__ col_off, const int* __restrict__ rank,
                                                          int max_adapters, int n_slab_total, int* __restrict__ slabs,
@@ -81,7 +83,8 @@ __global__ void __launch_bounds__(1024) lora_prep_kernel(const aos_router_ring* 
         if (a >= max_adapters) continue;
         const int c0 = col_off[a], rk = rank[a];
         if (c0 < 0 || rk <= 0) continue;
-        for (int sl = c0 / 16; sl <= (c0 + rk - 1) / 16; ++sl) marks[sl] = 1;  // benign same-value race
+        for (int sl = c0 / kPrepGroupCols; sl <= (c0 + rk - 1) / kPrepGroupCols; ++sl)
+            marks[sl] = 1;  // benign same-value race
     }
     __syncthreads();
     // ordered compaction: chunked exclusive scan over marks
@@ -103,6 +106,29 @@ __global__ void __launch_bounds__(1024) lora_prep_kernel(const aos_router_ring* 
         running += tot;
     }
     if (threadIdx.x == 0) *n_slabs = running;
+}
+
+// Per-token LoRA coefficient table coef[t][a] = sum over the ring slots that
+// name adapter a with q15 > 0 of (q15 / 32767) * (alpha_a / rank_a), i.e. the
+// blend weight of mlx-ffi/src/backend.rs:405-418 times the module scale of
+// mlx_cpp_wrapper_real.cpp:3410-3411 (0 for adapters the token did not select
+// or that are not loaded).  One CTA per token.
+__global__ void __launch_bounds__(256) lora_coef_kernel(const aos_router_ring* __restrict__ rings,
+                                                        const int* __restrict__ rank, const float* __restrict__ scale,
+                                                        int max_adapters, float* __restrict__ coef) {
+    const int t = blockIdx.x;
+    float* row = coef + (size_t)t * max_adapters;
+    for (int a = threadIdx.x; a < max_adapters; a += blockDim.x) row[a] = 0.0f;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const aos_router_ring r = rings[t];
+        const int k = min((int)r.top_k, AOS_MAX_K);
+        for (int s = 0; s < k; ++s) {
+            const int a = r.indices[s];
+            if (r.gates_q15[s] <= 0 || a >= max_adapters || rank[a] <= 0) continue;
+            row[a] += __fdiv_rn((float)r.gates_q15[s], AOS_Q15_DENOM) * scale[a];
+        }
+    }
 }
 
 // SplitMix64-based synthetic bf16 fill ~N(0, std) (Box-Muller), seeded and
@@ -144,9 +170,11 @@ cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* w, int T, int H, f
 }
 
 cudaError_t launch_lora_prep(const aos_router_ring* rings, int T, const int* col_off, const int* rank,
-                             int max_adapters, int n_slab_total, int* slabs, int* n_slabs, cudaStream_t s) {
+                             const float* scale, int max_adapters, int n_slab_total, int* slabs, int* n_slabs,
+                             float* coef, cudaStream_t s) {
     lora_prep_kernel<<<1, 1024, (size_t)n_slab_total * sizeof(int), s>>>(rings, T, col_off, rank, max_adapters,
                                                                         n_slab_total, slabs, n_slabs);
+    if (T > 0) lora_coef_kernel<<<T, 256, 0, s>>>(rings, rank, scale, max_adapters, coef);
     return cudaGetLastError();
 }
 

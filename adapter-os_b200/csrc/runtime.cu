@@ -9,11 +9,12 @@
 // aos_kv_*; get_metrics()/health_check()/attest_determinism().
 //
 // Arena layout (per layer and LoRA module, allocated once at init):
-//   A_cat  [R][in]          bf16  lora_A rows of every adapter, adapter a at rows [off_a, off_a + r_a)
-//   B_slab [R/16][out][16]  bf16  lora_B columns grouped in 16-column slabs
-// where R is the arena's rank capacity.  Column ranges are handed out in
-// 8-column units (ranks 8, 16, 32, 64 ... share slabs only in the rank-8 case),
-// so one decode step streams exactly the slabs its tokens selected.
+//   A_cat  [R][in]   bf16  lora_A rows of every adapter, adapter a at rows [off_a, off_a + r_a)
+//   B_cat  [out][R]  bf16  lora_B columns of every adapter at columns [off_a, off_a + r_a)
+// where R is the arena's rank capacity (a multiple of 64).  Column ranges are
+// handed out in 8-column units aligned to the rank's power-of-two factor, and
+// a decode step streams only the 64-column rank groups its tokens selected
+// (one TMA box of 128 rows x 128 B per group and weight tile).
 
 #include <algorithm>
 #include <cmath>
@@ -31,7 +32,8 @@
 namespace aos {
 cudaError_t launch_embed(const uint16_t*, const uint32_t*, int, int, int, uint16_t*, cudaStream_t);
 cudaError_t launch_rmsnorm(const uint16_t*, const uint16_t*, int, int, float, uint16_t*, cudaStream_t);
-cudaError_t launch_lora_prep(const aos_router_ring*, int, const int*, const int*, int, int, int*, int*, cudaStream_t);
+cudaError_t launch_lora_prep(const aos_router_ring*, int, const int*, const int*, const float*, int, int, int*, int*,
+                             float*, cudaStream_t);
 cudaError_t launch_fill_normal(uint16_t*, size_t, uint64_t, float, cudaStream_t);
 cudaError_t launch_attention(const CUtensorMap&, const CUtensorMap&, const uint16_t*, const int*, const int*, float*,
                              float*, int, int, int, int, int, int, int, int*, uint16_t*, cudaStream_t);
@@ -96,6 +98,7 @@ struct aos_ctx {
     std::vector<uint16_t*> A[AOS_NUM_MODULES], B[AOS_NUM_MODULES];  // [layer]
     int *d_col_owner = nullptr, *d_col_off = nullptr, *d_rank = nullptr;
     float* d_scale = nullptr;
+    float* d_coef = nullptr;  // [T_cap][max_adapters] per-step gate * alpha/rank
     std::vector<int> col_owner;  // host mirror, 8-column units
     std::unordered_map<uint16_t, AdapterEntry> adapters;
     uint64_t arena_bytes = 0;
@@ -111,7 +114,7 @@ struct aos_ctx {
     int T_cap = 0;
     uint16_t *d_hidden = nullptr, *d_normed = nullptr, *d_q = nullptr, *d_attn = nullptr, *d_act = nullptr;
     uint16_t* d_hm[AOS_NUM_MODULES] = {};
-    int *d_slabs = nullptr, *d_n_slabs = nullptr;
+    int *d_groups = nullptr, *d_n_groups = nullptr;
     int *d_block_tables = nullptr, *d_ctx_lens = nullptr;
     int *h_block_tables = nullptr, *h_ctx_lens = nullptr;  // pinned staging
     aos_router_ring* d_rings = nullptr;
@@ -124,6 +127,7 @@ struct aos_ctx {
     size_t ws_bytes = 0;
     int* d_counters = nullptr;
     int* d_err = nullptr;
+    unsigned long long* d_trace = nullptr;  // AOS_TC_TRACE diagnostics
     std::map<int, std::unique_ptr<StepPlan>> plans;
 
     // metrics
@@ -171,11 +175,18 @@ cudaError_t dalloc(T** p, size_t n_elems, uint64_t* counter = nullptr) {
     return e;
 }
 
+// Split-K factor: enough (tile, split) units to cover the SMs about
+// `AOS_TC_WAVES` times (tuning knob, default 1), at least 2 K-steps per split.
 int splits_for(int tiles, int kb) {
+    static const float waves = [] {
+        const char* e = getenv("AOS_TC_WAVES");
+        const float v = e ? (float)atof(e) : 1.0f;
+        return v > 0.f ? v : 1.0f;
+    }();
     const int sms = tc_num_sms();
-    int s = tiles > 0 ? sms / tiles : 1;
+    int s = tiles > 0 ? (int)(waves * sms) / tiles : 1;
     s = std::max(1, std::min(s, kb / 2));
-    return std::min(s, 16);
+    return std::min(s, 32);
 }
 
 // Build the TcParams of every GEMM of one layer for a padded batch T_pad.
@@ -192,28 +203,27 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
     };
     auto a_map = [&](CUtensorMap* m, int mod) {
         const uint32_t K = mod_in(c, mod);
-        return tc_encode_2d(m, c->A[mod][layer], K, (uint64_t)c->R, (uint64_t)K * 2, 64, 16, 128);
+        return tc_encode_2d(m, c->A[mod][layer], K, (uint64_t)c->R, (uint64_t)K * 2, 64, kGroup, 128);
     };
-    auto b_map = [&](CUtensorMap* m, int mod) {
+    auto b_map = [&](CUtensorMap* m, int mod) {  // B_cat [out][R]
         const uint32_t out = mod_out(c, mod);
-        return tc_encode_3d(m, c->B[mod][layer], 16, out, (uint64_t)c->R / 16, 32, (uint64_t)out * 32, 16, 128, 1, 32);
+        return tc_encode_2d(m, c->B[mod][layer], (uint64_t)c->R, out, (uint64_t)c->R * 2, kGroup, 128, 128);
     };
-    auto h_map = [&](CUtensorMap* m, int mod) {
-        return tc_encode_2d(m, c->d_hm[mod], (uint64_t)c->R, (uint64_t)c->T_cap, (uint64_t)c->R * 2, 16,
-                            (uint32_t)T_pad, 32);
+    auto h_map = [&](CUtensorMap* m, int mod) {  // hm [T][R]
+        return tc_encode_2d(m, c->d_hm[mod], (uint64_t)c->R, (uint64_t)c->T_cap, (uint64_t)c->R * 2, kGroup,
+                            (uint32_t)T_pad, 128);
     };
     auto common = [&](TcParams& p) {
         std::memset(&p, 0, sizeof(p));
         p.T = T;
-        p.slabs = c->d_slabs;
-        p.n_slabs = c->d_n_slabs;
+        p.groups = c->d_groups;
+        p.n_groups = c->d_n_groups;
         p.ws = c->d_ws;
         p.counters = c->d_counters;
         p.err = c->d_err;
         p.R = c->R;
         p.col_owner = c->d_col_owner;
-        p.adapter_scale = c->d_scale;
-        p.rings = c->d_rings;
+        p.coef = c->d_coef;
         p.max_adapters = (int)c->cfg.lora_max_adapters;
         p.layer = layer;
     };
@@ -325,6 +335,14 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
         p.splits = splits_for(tiles, p.kb);
         if ((rc = tc_prepare(p, smem_budget))) return rc;
         lp.gemm_grid[g] = std::min(tiles * p.splits, tc_num_sms());
+        // Diagnostics: AOS_TC_TRACE=<0..7> traces layer 0's GEMM g (0..3) or shrink g-4.
+        if (const char* tv = getenv("AOS_TC_TRACE")) {
+            const int want = atoi(tv);
+            if (layer == 0 && c->d_trace) {
+                if (want == g) p.trace = c->d_trace;
+                if (want == g + 4) lp.shrink[g].trace = c->d_trace;
+            }
+        }
     }
     return AOS_OK;
 }
@@ -446,8 +464,8 @@ int enqueue_layer(aos_ctx* c, const StepPlan& plan, int layer, cudaStream_t s) {
 int enqueue_step(aos_ctx* c, StepPlan& plan, bool with_logits, cudaStream_t s) {
     const int T = plan.T;
     PLAUNCH(c, AOS_K_PREP, s,
-            launch_lora_prep(c->d_rings, T, c->d_col_off, c->d_rank, (int)c->cfg.lora_max_adapters, c->R / 16, c->d_slabs,
-                             c->d_n_slabs, s));
+            launch_lora_prep(c->d_rings, T, c->d_col_off, c->d_rank, c->d_scale, (int)c->cfg.lora_max_adapters,
+                             c->R / kGroup, c->d_groups, c->d_n_groups, c->d_coef, s));
     PLAUNCH(c, AOS_K_EMBED, s, launch_embed(c->embed, c->d_tokens, T, (int)c->cfg.hidden, (int)c->cfg.vocab, c->d_hidden, s));
     for (uint32_t l = 0; l < c->cfg.n_layers; ++l) {
         int rc = enqueue_layer(c, plan, (int)l, s);
@@ -504,8 +522,8 @@ int run_step_device(aos_ctx* c, int T, bool with_logits, cudaStream_t s) {
         c->prof_used = 0;
         c->prof.steps += 1;
         int ns = 0;
-        CTX_CUDA(c, cudaMemcpy(&ns, c->d_n_slabs, 4, cudaMemcpyDeviceToHost));
-        c->prof.last_touched_slabs = (uint32_t)ns;
+        CTX_CUDA(c, cudaMemcpy(&ns, c->d_n_groups, 4, cudaMemcpyDeviceToHost));
+        c->prof.last_touched_groups = (uint32_t)ns;
         return AOS_OK;
     }
     if (!use_graphs()) return enqueue_step(c, *plan, with_logits, s);
@@ -582,7 +600,7 @@ aos_ctx* aos_init(const aos_model_config* cfg) {
     if (k.head_dim != 128 || k.n_heads == 0 || k.n_kv_heads == 0 || k.n_heads % k.n_kv_heads ||
         k.n_heads / k.n_kv_heads > 16 || k.hidden % 128 || k.intermediate % 128 || k.n_layers == 0 ||
         k.kv_block_size != 16 || k.max_batch == 0 || k.max_batch > 256 || k.vocab == 0 || k.kv_num_blocks == 0 ||
-        k.max_seq_len == 0 || k.lora_rank_capacity % 16 || k.lora_max_adapters > 65535) {
+        k.max_seq_len == 0 || k.lora_max_adapters > 65535) {
         set_global_error("aos_init: unsupported config (head_dim 128, hidden/intermediate % 128, KV block 16, "
                          "max_batch <= 256, rank capacity % 16, GQA group <= 16)");
         return nullptr;
@@ -604,7 +622,7 @@ aos_ctx* aos_init(const aos_model_config* cfg) {
     if (mask & 0x30u) mask |= 0x30u;
     if (k.lora_rank_capacity == 0 || k.lora_max_adapters == 0) mask = 0;
     c->module_mask = mask;
-    c->R = mask ? (int)k.lora_rank_capacity : 16;
+    c->R = mask ? (int)((k.lora_rank_capacity + kGroup - 1) / kGroup) * kGroup : kGroup;
     c->T_cap = std::max(32, (int)((k.max_batch + 15) / 16) * 16);
     c->max_blocks = (int)((k.max_seq_len + 15) / 16);
     cudaDeviceProp prop;
@@ -676,8 +694,8 @@ aos_ctx* aos_init(const aos_model_config* cfg) {
     INIT_CHECK(dalloc(&c->d_attn, TC * c->QD), "attn");
     INIT_CHECK(dalloc(&c->d_act, TC * I), "act");
     for (int m = 0; m < AOS_NUM_MODULES; ++m) INIT_CHECK(dalloc(&c->d_hm[m], TC * c->R), "hm");
-    INIT_CHECK(dalloc(&c->d_slabs, (size_t)c->R / 16 + 1), "slabs");
-    INIT_CHECK(dalloc(&c->d_n_slabs, 1), "n_slabs");
+    INIT_CHECK(dalloc(&c->d_groups, (size_t)c->R / kGroup + 1), "groups");
+    INIT_CHECK(dalloc(&c->d_n_groups, 1), "n_groups");
     INIT_CHECK(dalloc(&c->d_block_tables, TC * c->max_blocks), "block tables");
     INIT_CHECK(dalloc(&c->d_ctx_lens, TC), "ctx lens");
     INIT_CHECK(cudaMallocHost((void**)&c->h_block_tables, TC * c->max_blocks * 4), "pinned tables");
@@ -685,11 +703,13 @@ aos_ctx* aos_init(const aos_model_config* cfg) {
     INIT_CHECK(dalloc(&c->d_rings, TC), "rings");
     INIT_CHECK(dalloc(&c->d_tokens, TC), "tokens");
     INIT_CHECK(dalloc(&c->d_logits, TC * V), "logits");
+    INIT_CHECK(dalloc(&c->d_coef, TC * NA), "lora coef");
     c->attn_chunks = attn_max_chunks((int)k.max_seq_len);
     INIT_CHECK(dalloc(&c->d_attn_part, TC * k.n_kv_heads * c->attn_chunks * c->G * 128), "attn part");
     INIT_CHECK(dalloc(&c->d_attn_ml, TC * k.n_kv_heads * c->attn_chunks * c->G * 2), "attn ml");
     INIT_CHECK(dalloc(&c->d_counters, 1 << 16), "counters");
     INIT_CHECK(dalloc(&c->d_err, 1), "err");
+    if (getenv("AOS_TC_TRACE")) INIT_CHECK(dalloc(&c->d_trace, (size_t)tc_num_sms() * kTraceStride), "trace");
     // RoPE table, angles as the reference computes them (mlx_cpp_wrapper_real.cpp:3249-3268)
     {
         const uint32_t half = 64, P = k.max_seq_len + 1;
@@ -742,12 +762,12 @@ void aos_destroy(aos_ctx* c) {
         for (auto* p : c->B[m]) f(p);
         f(c->d_hm[m]);
     }
-    f(c->d_col_owner); f(c->d_col_off); f(c->d_rank); f(c->d_scale);
+    f(c->d_col_owner); f(c->d_col_off); f(c->d_rank); f(c->d_scale); f(c->d_coef);
     f(c->k_pool); f(c->v_pool);
     f(c->d_hidden); f(c->d_normed); f(c->d_q); f(c->d_attn); f(c->d_act);
-    f(c->d_slabs); f(c->d_n_slabs); f(c->d_block_tables); f(c->d_ctx_lens);
+    f(c->d_groups); f(c->d_n_groups); f(c->d_block_tables); f(c->d_ctx_lens);
     f(c->d_rings); f(c->d_tokens); f(c->d_logits); f(c->d_rope);
-    f(c->d_attn_part); f(c->d_attn_ml); f(c->d_ws); f(c->d_counters); f(c->d_err);
+    f(c->d_attn_part); f(c->d_attn_ml); f(c->d_ws); f(c->d_counters); f(c->d_err); f(c->d_trace);
     if (c->h_block_tables) cudaFreeHost(c->h_block_tables);
     if (c->h_ctx_lens) cudaFreeHost(c->h_ctx_lens);
     if (c->ev0) cudaEventDestroy(c->ev0);
@@ -804,8 +824,11 @@ int aos_adapter_new(aos_ctx* c, uint16_t id, uint32_t rank, float alpha) {
     if (rank < 8 || rank > 256 || rank % 8) return c->fail(AOS_ERR_INVALID, "rank must be a multiple of 8 in [8, 256]");
     if (!std::isfinite(alpha)) return c->fail(AOS_ERR_INVALID, "alpha must be finite");
     if (c->adapters.count(id)) return c->fail(AOS_ERR_INVALID, "adapter id already loaded");
-    // first fit over 8-column units; ranks >= 16 start on a slab boundary
-    const int units = (int)rank / 8, align = rank >= 16 ? 2 : 1, n_units = (int)c->col_owner.size();
+    // First fit over 8-column units, aligned to the rank's largest power-of-two
+    // factor (capped at one 64-column group) so an adapter spans as few rank
+    // groups as its size allows.
+    const int pow2 = (int)(rank & (~rank + 1u));
+    const int units = (int)rank / 8, align = std::min(pow2, kGroup) / 8, n_units = (int)c->col_owner.size();
     int start = -1;
     for (int u = 0; u + units <= n_units; u += align) {
         bool free_run = true;
@@ -822,11 +845,7 @@ int aos_adapter_new(aos_ctx* c, uint16_t id, uint32_t rank, float alpha) {
         const uint32_t in = mod_in(c, m), out = mod_out(c, m);
         for (uint32_t l = 0; l < c->cfg.n_layers; ++l) {
             CTX_CUDA(c, cudaMemset(c->A[m][l] + (size_t)off * in, 0, (size_t)rank * in * 2));
-            for (int col = off; col < off + (int)rank;) {
-                const int slab = col / 16, c0 = col % 16, w = std::min(16 - c0, off + (int)rank - col);
-                CTX_CUDA(c, cudaMemset2D(c->B[m][l] + (size_t)slab * out * 16 + c0, 32, 0, (size_t)w * 2, out));
-                col += w;
-            }
+            CTX_CUDA(c, cudaMemset2D(c->B[m][l] + off, (size_t)c->R * 2, 0, (size_t)rank * 2, out));
         }
     }
     for (int j = 0; j < units; ++j) c->col_owner[start + j] = id;
@@ -856,12 +875,8 @@ int aos_adapter_set_module(aos_ctx* c, uint16_t id, uint32_t layer, aos_module m
     const cudaMemcpyKind kind = src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
     CTX_CUDA(c, cudaSetDevice(c->device));
     CTX_CUDA(c, cudaMemcpy(c->A[module][layer] + (size_t)off * in, A, (size_t)rank * in * 2, kind));
-    for (int col = off; col < off + rank;) {
-        const int slab = col / 16, c0 = col % 16, w = std::min(16 - c0, off + rank - col);
-        CTX_CUDA(c, cudaMemcpy2D(c->B[module][layer] + (size_t)slab * out * 16 + c0, 32, B + (col - off), (size_t)rank * 2,
-                                 (size_t)w * 2, out, kind));
-        col += w;
-    }
+    CTX_CUDA(c, cudaMemcpy2D(c->B[module][layer] + off, (size_t)c->R * 2, B, (size_t)rank * 2, (size_t)rank * 2, out,
+                             kind));
     return AOS_OK;
 }
 
@@ -1056,8 +1071,8 @@ int aos_layer_step_dev(aos_ctx* c, uint32_t layer, const aos_router_ring* rings,
     if (rings != c->d_rings)
         CTX_CUDA(c, cudaMemcpyAsync(c->d_rings, rings, (size_t)T * sizeof(aos_router_ring), cudaMemcpyDeviceToDevice, s));
     CTX_CUDA(c, cudaMemcpyAsync(c->d_hidden, hidden, (size_t)T * c->cfg.hidden * 2, cudaMemcpyDeviceToDevice, s));
-    LAUNCH(c, launch_lora_prep(c->d_rings, (int)T, c->d_col_off, c->d_rank, (int)c->cfg.lora_max_adapters, c->R / 16,
-                               c->d_slabs, c->d_n_slabs, s));
+    LAUNCH(c, launch_lora_prep(c->d_rings, (int)T, c->d_col_off, c->d_rank, c->d_scale, (int)c->cfg.lora_max_adapters,
+                               c->R / kGroup, c->d_groups, c->d_n_groups, c->d_coef, s));
     if ((rc = enqueue_layer(c, *plan, (int)layer, s))) return rc;
     CTX_CUDA(c, cudaMemcpyAsync(hidden, c->d_hidden, (size_t)T * c->cfg.hidden * 2, cudaMemcpyDeviceToDevice, s));
     if (adv) advance(c, seq_ids, T);
@@ -1065,6 +1080,15 @@ int aos_layer_step_dev(aos_ctx* c, uint32_t layer, const aos_router_ring* rings,
 }
 
 // ------------------------------------------------------------------ metrics etc.
+int aos_debug_trace_read(aos_ctx* c, uint64_t* out, uint64_t n) {
+    if (!c || !out) return AOS_ERR_INVALID;
+    if (!c->d_trace) return c->fail(AOS_ERR_STATE, "tracing is off (set AOS_TC_TRACE before aos_init)");
+    const uint64_t cap = (uint64_t)tc_num_sms() * kTraceStride;
+    CTX_CUDA(c, cudaStreamSynchronize(c->stream));
+    CTX_CUDA(c, cudaMemcpy(out, c->d_trace, (n < cap ? n : cap) * 8, cudaMemcpyDeviceToHost));
+    return AOS_OK;
+}
+
 int aos_profile_enable(aos_ctx* c, int enable) {
     if (!c) return AOS_ERR_INVALID;
     c->prof_on = enable != 0;

@@ -3,12 +3,12 @@
 //
 // Per 128-row output tile (MMA M = weight rows, N = decode tokens, "swap-AB"):
 //   base steps : TMA W[128 x 64] + X[T x 64] (SWIZZLE_128B) -> 4 MMAs (K=16)
-//   LoRA steps : TMA lora_B slabs [128 x 16] + gated H slabs [T x 16]
-//                (SWIZZLE_32B), four slabs per step -> 4 MMAs (K=16)
+//   LoRA steps : TMA lora_B[128 rows x one 64-column rank group] + gated H
+//                [T x the same group] (SWIZZLE_128B) -> 4 MMAs (K=16)
 // so the tile's accumulator ends as  W x + sum_a B_a (g_a * scale_a * A_a x)
 // (mlx_cpp_wrapper_real.cpp:3372-3419) without ever materialising the LoRA
 // delta.  The shrink GEMM (H = A_cat x) is the same kernel with lora_A rows
-// gathered slab by slab and the TC_SHRINK_HM epilogue.
+// gathered group by group and the TC_SHRINK_HM epilogue.
 //
 // Roles (192 threads, one CTA per SM, persistent over work units):
 //   warp 0      : TMA producer (one elected lane)
@@ -52,18 +52,28 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait; false on timeout or when another role already failed.
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
-    if (mbar_try(bar, parity)) return true;
+// Bounded wait; false on timeout or when another role already failed.  The
+// fast path only polls the barrier; the error word and the clock are checked
+// every 1024 polls so a completed phase is seen without an extra L2 round trip.
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, int* err) {
     const long long t0 = clock64();
+    uint32_t n = 0;
     while (!mbar_try(bar, parity)) {
-        if (*(volatile int*)err != 0) return false;
-        if (clock64() - t0 > kSpinLimitCycles) {
-            atomicCAS(err, 0, AOS_ERR_TIMEOUT);
-            return false;
+        if ((++n & 1023u) == 0) {
+            if (*(volatile int*)err != 0) return false;
+            if (clock64() - t0 > kSpinLimitCycles) {
+                atomicCAS(err, 0, AOS_ERR_TIMEOUT);
+                return false;
+            }
         }
     }
     return true;
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+        if (mbar_try(bar, parity)) return true;
+    return mbar_wait_slow(bar, parity, err);
 }
 // Time-bounded wait that ignores the error word: used only to drain this
 // CTA's own copies / MMAs before it exits on an error path.
@@ -79,14 +89,6 @@ __device__ __forceinline__ void tma_2d(const CUtensorMap* m, uint32_t dst, uint3
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
         " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y), "l"(policy)
-        : "memory");
-}
-__device__ __forceinline__ void tma_3d(const CUtensorMap* m, uint32_t dst, uint32_t bar, int x, int y, int z,
-                                       uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-        " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y), "r"(z), "l"(policy)
         : "memory");
 }
 __device__ __forceinline__ uint64_t policy_evict_first() {
@@ -142,16 +144,17 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t addr) {
     return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)(1024u >> 4) << 32) |
            ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
 }
-__device__ __forceinline__ uint64_t desc_sw32(uint32_t addr) {
-    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)(256u >> 4) << 32) |
-           ((uint64_t)1u << 46) | ((uint64_t)6u << 61);
-}
 // kind::f16 instruction descriptor: D f32, A/B bf16, both K-major, M=128.
 __device__ __forceinline__ uint32_t idesc_bf16(int n) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
 __device__ __forceinline__ int cdiv(int a, int b) { return (a + b - 1) / b; }
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 // ---------------------------------------------------------------- work units
 struct Unit {
@@ -159,18 +162,18 @@ struct Unit {
 };
 
 struct Sched {
-    int n_slabs, lora_steps, total_steps, units;
+    int n_groups, lora_steps, total_steps, units;
     int tiles[kTcMaxSets];
 };
 
 __device__ __forceinline__ Sched make_sched(const TcParams& p) {
     Sched s;
-    s.n_slabs = (p.lora || p.shrink) ? __ldg(p.n_slabs) : 0;
-    s.lora_steps = p.lora ? cdiv(s.n_slabs, kSlabsPerStep) : 0;
+    s.n_groups = (p.lora || p.shrink) ? __ldg(p.n_groups) : 0;
+    s.lora_steps = p.lora ? s.n_groups : 0;  // one 64-column rank group per step
     s.total_steps = p.kb + s.lora_steps;
     s.units = 0;
     for (int g = 0; g < kTcMaxSets; ++g) {
-        s.tiles[g] = g < p.n_seg ? (p.shrink ? cdiv(s.n_slabs, kShrinkSlabsPerTile) : p.seg_tiles[g]) : 0;
+        s.tiles[g] = g < p.n_seg ? (p.shrink ? cdiv(s.n_groups, kShrinkGroupsPerTile) : p.seg_tiles[g]) : 0;
         s.units += s.tiles[g] * p.splits;
     }
     return s;
@@ -196,102 +199,115 @@ __device__ __forceinline__ Unit unit_of(const TcParams& p, const Sched& s, int u
 
 // ---------------------------------------------------------------- epilogue
 struct EpiSmem {
-    float* xbuf;                // [128][33] exchange buffer (RoPE)
-    const aos_router_ring* rings;  // shared copy of the rings (HM)
+    float* xbuf;  // [128][33] exchange buffer (RoPE)
 };
-
-__device__ __forceinline__ float gate_coef(const TcParams& p, const aos_router_ring& ring, int owner) {
-    // sum over slots naming this adapter with q15 > 0 (mlx-ffi/src/backend.rs:405-418)
-    float c = 0.0f;
-    const int k = min((int)ring.top_k, AOS_MAX_K);
-    for (int s = 0; s < k; ++s)
-        if ((int)ring.indices[s] == owner && ring.gates_q15[s] > 0) {
-            const float blend = __fdiv_rn((float)ring.gates_q15[s], AOS_Q15_DENOM);
-            c += blend * __ldg(p.adapter_scale + owner);
-        }
-    return c;
-}
 
 // Apply the epilogue to tokens [t0, t0+32) of one tile row.  v[sub][j] holds
 // the fp32 accumulator for token t0 + j.  Must be called uniformly by all
-// 128 epilogue threads (RoPE uses a named barrier).
-__device__ void epilogue_chunk(const TcParams& p, const EpiSmem& es, const Unit& u, const Sched& sc, int row,
-                               int t0, float (&v)[2][32]) {
+// 128 epilogue threads (RoPE uses a named barrier).  Every loop is fully
+// unrolled with predicates, and all loads of a chunk are issued before its
+// stores, so a chunk costs one or two memory latencies, not 32.
+__device__ __forceinline__ void epilogue_chunk(const TcParams& p, const EpiSmem& es, const Unit& u, const Sched& sc,
+                                               int row, int t0, float (&v)[2][32]) {
     const int seg = u.seg;
     const int col = p.seg_out0[seg] + u.tile * kTcBM + row;
     if (p.mode != TC_SHRINK_HM && p.mode != TC_QKV_ROPE && u.tile * kTcBM + row >= p.seg_rows[seg]) return;
+    const int nt = min(32, p.T - t0);  // valid tokens in this chunk
     switch (p.mode) {
         case TC_STORE_BF16: {
-            uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]);
-            for (int j = 0; j < 32 && t0 + j < p.T; ++j) o[(size_t)(t0 + j) * p.ld_out + col] = f2bf(v[0][j]);
+            uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]) + (size_t)t0 * p.ld_out + col;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < nt) o[(size_t)j * p.ld_out] = f2bf(v[0][j]);
             break;
         }
         case TC_STORE_F32: {
-            float* o = reinterpret_cast<float*>(p.out[seg]);
-            for (int j = 0; j < 32 && t0 + j < p.T; ++j) o[(size_t)(t0 + j) * p.ld_out + col] = v[0][j];
+            float* o = reinterpret_cast<float*>(p.out[seg]) + (size_t)t0 * p.ld_out + col;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < nt) o[(size_t)j * p.ld_out] = v[0][j];
             break;
         }
         case TC_RESID_BF16: {
-            for (int j = 0; j < 32 && t0 + j < p.T; ++j) {
-                uint16_t* h = p.resid + (size_t)(t0 + j) * p.ld_out + col;
-                *h = f2bf(bf2f(*h) + v[0][j]);
-            }
+            uint16_t* h = p.resid + (size_t)t0 * p.ld_out + col;
+            uint16_t hv[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) hv[j] = j < nt ? h[(size_t)j * p.ld_out] : (uint16_t)0;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < nt) h[(size_t)j * p.ld_out] = f2bf(bf2f(hv[j]) + v[0][j]);
             break;
         }
         case TC_SWIGLU: {
-            uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]);
-            for (int j = 0; j < 32 && t0 + j < p.T; ++j) {
+            uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]) + (size_t)t0 * p.ld_out + col;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
                 const float g = v[0][j], up = v[1][j];
                 const float sg = 1.0f / (1.0f + expf(-g));  // gate * sigmoid(gate) * up (:3522)
-                o[(size_t)(t0 + j) * p.ld_out + col] = f2bf((g * sg) * up);
+                if (j < nt) o[(size_t)j * p.ld_out] = f2bf((g * sg) * up);
             }
             break;
         }
         case TC_QKV_ROPE: {
             const int module = p.seg_module[seg];
+            int pos[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) pos[j] = j < nt ? __ldg(p.ctx_lens + t0 + j) : 0;
             if (module != AOS_MOD_V) {
                 // half-split RoPE (mlx_cpp_wrapper_real.cpp:3270-3280): pair (d, d+64)
-                for (int j = 0; j < 32; ++j) es.xbuf[row * 33 + j] = v[0][j];
-                epi_bar();
                 const int half = kTcBM / 2, i = row & (half - 1);
                 const int partner = row ^ half;
+                float2 cs[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    cs[j] = *reinterpret_cast<const float2*>(p.rope + ((size_t)pos[j] * half + i) * 2);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) es.xbuf[row * 33 + j] = v[0][j];
+                epi_bar();
+#pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    const int t = t0 + j;
-                    if (t >= p.T) break;
-                    const int pos = __ldg(p.ctx_lens + t);
-                    const float2 cs = *reinterpret_cast<const float2*>(p.rope + ((size_t)pos * half + i) * 2);
                     const float x = v[0][j], y = es.xbuf[partner * 33 + j];
-                    v[0][j] = row < half ? (x * cs.x - y * cs.y) : (y * cs.y + x * cs.x);
+                    v[0][j] = row < half ? (x * cs[j].x - y * cs[j].y) : (y * cs[j].y + x * cs[j].x);
                 }
                 epi_bar();
             }
             if (module == AOS_MOD_Q) {
-                uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]);
-                for (int j = 0; j < 32 && t0 + j < p.T; ++j) o[(size_t)(t0 + j) * p.ld_out + col] = f2bf(v[0][j]);
+                uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]) + (size_t)t0 * p.ld_out + col;
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (j < nt) o[(size_t)j * p.ld_out] = f2bf(v[0][j]);
             } else {
                 uint16_t* pool = module == AOS_MOD_K ? p.k_pool : p.v_pool;
                 const int kvh = u.tile;  // one tile per kv head (head_dim == 128)
-                for (int j = 0; j < 32 && t0 + j < p.T; ++j) {
-                    const int t = t0 + j;
-                    const int pos = __ldg(p.ctx_lens + t);
-                    const int blk = __ldg(p.block_tables + (size_t)t * p.max_blocks + (pos >> 4));
-                    const size_t idx = ((((size_t)p.layer * p.num_blocks + blk) * p.nkv + kvh) * 16 + (pos & 15)) * 128 + row;
-                    pool[idx] = f2bf(v[0][j]);
-                }
+                int blk[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    blk[j] = j < nt ? __ldg(p.block_tables + (size_t)(t0 + j) * p.max_blocks + (pos[j] >> 4)) : 0;
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (j < nt) {
+                        const size_t idx =
+                            ((((size_t)p.layer * p.num_blocks + blk[j]) * p.nkv + kvh) * 16 + (pos[j] & 15)) * 128 + row;
+                        pool[idx] = f2bf(v[0][j]);
+                    }
             }
             break;
         }
         case TC_SHRINK_HM: {
-            const int slot = u.tile * kShrinkSlabsPerTile + (row >> 4);
-            if (slot >= sc.n_slabs) break;
-            const int c = __ldg(p.slabs + slot) * kSlab + (row & 15);
+            const int slot = u.tile * kShrinkGroupsPerTile + row / kGroup;
+            if (slot >= sc.n_groups) break;
+            const int c = __ldg(p.groups + slot) * kGroup + row % kGroup;
             const int owner = __ldg(p.col_owner + c);
-            uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]);
-            for (int j = 0; j < 32 && t0 + j < p.T; ++j) {
-                const int t = t0 + j;
-                const float coef = owner >= 0 ? gate_coef(p, es.rings[t], owner) : 0.0f;
-                o[(size_t)t * p.R + c] = f2bf(v[0][j] * coef);
-            }
+            // per-token gate * alpha/rank of the column's adapter (0 when the
+            // token did not select it); built by the routing prep each step
+            const float* ct = p.coef + (size_t)t0 * p.max_adapters + (owner >= 0 ? owner : 0);
+            float cf[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) cf[j] = (owner >= 0 && j < nt) ? __ldg(ct + (size_t)j * p.max_adapters) : 0.0f;
+            uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]) + (size_t)t0 * p.R + c;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < nt) o[(size_t)j * p.R] = f2bf(v[0][j] * cf[j]);
             break;
         }
         default:
@@ -315,7 +331,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
     int* flag = reinterpret_cast<int*>(tmem_slot + 1);
     float* xbuf = reinterpret_cast<float*>(tail + 512);
-    aos_router_ring* rings_s = reinterpret_cast<aos_router_ring*>(tail + 512 + 128 * 33 * 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const Sched sc = make_sched(p);
@@ -342,16 +357,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                      "r"(tmem_cols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    if (p.mode == TC_SHRINK_HM && warp >= 2) {
-        const int n_words = p.T * (int)(sizeof(aos_router_ring) / 4);
-        for (int i = threadIdx.x - 64; i < n_words; i += 128)
-            reinterpret_cast<uint32_t*>(rings_s)[i] = reinterpret_cast<const uint32_t*>(p.rings)[i];
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const uint32_t idesc = idesc_bf16(p.T_pad);
+    unsigned long long* tr = p.trace ? p.trace + (size_t)blockIdx.x * kTraceStride : nullptr;
+    if (tr && threadIdx.x == 0) tr[192] = gtimer();
 
     if (warp == 0) {
         // ============================ TMA producer ============================
@@ -360,6 +372,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             const uint64_t pol_x = policy_evict_last();
             uint32_t last_phase[16];
             uint32_t used_mask = 0;
+            int n_issued = 0;
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
@@ -373,12 +386,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     if (step < p.kb) {
                         const int kx = step * kTcBK;
                         if (p.shrink) {
-                            const int first = u.tile * kShrinkSlabsPerTile;
-                            const int nv = min(kShrinkSlabsPerTile, sc.n_slabs - first);
-                            mbar_expect_tx(fb, (uint32_t)(nv * kSlab * 128 + p.T_pad * 128));
-                            for (int q = 0; q < nv; ++q)
-                                tma_2d(&p.tm_w[u.seg], sbase + q * (kSlab * 128), fb, kx,
-                                       __ldg(p.slabs + first + q) * kSlab, pol_w);
+                            // lora_A rows of the tile's (up to) two touched groups; one
+                            // 64-row box, or one 128-row box when the groups are adjacent
+                            const int first = u.tile * kShrinkGroupsPerTile;
+                            const int nv = min(kShrinkGroupsPerTile, sc.n_groups - first);
+                            const int g0 = __ldg(p.groups + first);
+                            mbar_expect_tx(fb, (uint32_t)(nv * kGroup * 128 + p.T_pad * 128));
+                            if (nv == 2 && __ldg(p.groups + first + 1) == g0 + 1) {
+                                tma_2d(&p.tm_w[u.seg], sbase, fb, kx, g0 * kGroup, pol_w);
+                                tma_2d(&p.tm_w[u.seg], sbase + kGroup * 128, fb, kx, (g0 + 1) * kGroup, pol_w);
+                            } else {
+                                for (int q = 0; q < nv; ++q)
+                                    tma_2d(&p.tm_w[u.seg], sbase + q * (kGroup * 128), fb, kx,
+                                           __ldg(p.groups + first + q) * kGroup, pol_w);
+                            }
                         } else {
                             mbar_expect_tx(fb, (uint32_t)(p.n_sub * kTcBM * 128 + p.T_pad * 128));
                             for (int sub = 0; sub < p.n_sub; ++sub)
@@ -387,22 +408,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                         }
                         tma_2d(&p.tm_x, act, fb, kx, 0, pol_x);
                     } else {
-                        const int g0 = (step - p.kb) * kSlabsPerStep;
-                        const int nv = min(kSlabsPerStep, sc.n_slabs - g0);
-                        mbar_expect_tx(fb, (uint32_t)(p.n_sub * nv * (kTcBM * 32 + p.T_pad * 32)));
+                        // LoRA expand step: lora_B[tile rows, group cols] and the
+                        // gated shrink output hm[tokens, group cols] of each sub-tile
+                        const int gcol = __ldg(p.groups + (step - p.kb)) * kGroup;
+                        mbar_expect_tx(fb, (uint32_t)(p.n_sub * (kTcBM * 128 + p.T_pad * 128)));
                         for (int sub = 0; sub < p.n_sub; ++sub) {
                             const int set = u.seg * p.n_sub + sub;
-                            for (int q = 0; q < nv; ++q) {
-                                const int slab = __ldg(p.slabs + g0 + q);
-                                tma_3d(&p.tm_lb[set], sbase + sub * (kTcBM * 128) + q * (kTcBM * 32), fb, 0,
-                                       u.tile * kTcBM, slab, pol_w);
-                                tma_2d(&p.tm_lh[set], act + (sub * kSlabsPerStep + q) * (p.T_pad * 32), fb,
-                                       slab * kSlab, 0, pol_x);
-                            }
+                            tma_2d(&p.tm_lb[set], sbase + sub * (kTcBM * 128), fb, gcol, u.tile * kTcBM, pol_w);
+                            tma_2d(&p.tm_lh[set], act + sub * (p.T_pad * 128), fb, gcol, 0, pol_x);
                         }
                     }
                     last_phase[stage] = phase;
                     used_mask |= 1u << stage;
+                    if (tr && n_issued < 64) tr[n_issued] = gtimer();
+                    ++n_issued;
                     if (++stage == NS) { stage = 0; phase ^= 1u; }
                 }
             }
@@ -418,6 +437,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             int it = 0;
             bool ok = true;
             bool issued_any = false;
+            int n_waited = 0;
             for (int uidx = blockIdx.x; uidx < sc.units && ok; uidx += gridDim.x, ++it) {
                 const Unit u = unit_of(p, sc, uidx);
                 const int acc = it % acc_stages;
@@ -429,24 +449,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 for (int step = u.step0; step < u.step1; ++step) {
                     if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.err)) { ok = false; break; }
                     tc_fence_after();
+                    if (tr && n_waited < 64) tr[64 + n_waited] = gtimer();
+                    ++n_waited;
                     const uint32_t sbase = smem_u32(stages + (size_t)stage * p.stage_bytes);
                     const uint32_t act = sbase + p.act_off;
-                    if (step < p.kb) {
-                        for (int sub = 0; sub < p.n_sub; ++sub) {
-                            const uint32_t a0 = sbase + sub * (kTcBM * 128);
+                    // base steps share one activation box; LoRA steps have one per sub-tile
+                    const bool lora_step = step >= p.kb;
+                    for (int sub = 0; sub < p.n_sub; ++sub) {
+                        const uint32_t a0 = sbase + sub * (kTcBM * 128);
+                        const uint32_t b0 = act + (lora_step ? sub * (p.T_pad * 128) : 0);
 #pragma unroll
-                            for (int kk = 0; kk < kTcBK / 16; ++kk)
-                                umma_bf16(d0 + sub * p.T_pad, desc_sw128(a0 + kk * 32), desc_sw128(act + kk * 32), idesc,
-                                          (first && kk == 0) ? 0u : 1u);
-                        }
-                    } else {
-                        const int g0 = (step - p.kb) * kSlabsPerStep;
-                        const int nv = min(kSlabsPerStep, sc.n_slabs - g0);
-                        for (int sub = 0; sub < p.n_sub; ++sub)
-                            for (int q = 0; q < nv; ++q)
-                                umma_bf16(d0 + sub * p.T_pad, desc_sw32(sbase + sub * (kTcBM * 128) + q * (kTcBM * 32)),
-                                          desc_sw32(act + (sub * kSlabsPerStep + q) * (p.T_pad * 32)), idesc,
-                                          (first && q == 0) ? 0u : 1u);
+                        for (int kk = 0; kk < kTcBK / 16; ++kk)
+                            umma_bf16(d0 + sub * p.T_pad, desc_sw128(a0 + kk * 32), desc_sw128(b0 + kk * 32), idesc,
+                                      (first && kk == 0) ? 0u : 1u);
                     }
                     issued_any = true;
                     umma_commit(smem_u32(&empty_bar[stage]));  // frees the stage when these MMAs finish
@@ -466,7 +481,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         const int q = warp & 3;
         const int row = q * 32 + lane;
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-        EpiSmem es{xbuf, rings_s};
+        EpiSmem es{xbuf};
         int it = 0;
         for (int uidx = blockIdx.x; uidx < sc.units; uidx += gridDim.x, ++it) {
             const Unit u = unit_of(p, sc, uidx);
@@ -474,29 +489,38 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             const uint32_t tphase = (uint32_t)((it / acc_stages) & 1);
             const bool ok = mbar_wait(smem_u32(&tfull_bar[acc]), tphase, p.err);
             if (epi_bar_any(!ok)) break;
+            if (tr && threadIdx.x == 64 && it < 32) tr[128 + it] = gtimer();
             tc_fence_after();
             const uint32_t t_acc = tmem_base + lane_off + (uint32_t)(acc * cols_per_acc);
             float v[2][32];
             if (p.splits == 1) {
                 for (int t0 = 0; t0 < p.T_pad; t0 += 32) {
-                    for (int sub = 0; sub < p.n_sub; ++sub) tmem_ld32(t_acc + sub * p.T_pad + t0, v[sub]);
+                    tmem_ld32(t_acc + t0, v[0]);
+                    if (p.n_sub == 2) tmem_ld32(t_acc + p.T_pad + t0, v[1]);
+                    if (tr && threadIdx.x == 64 && it == 0 && t0 < 64) tr[194 + (t0 >> 5) * 2] = gtimer();
                     epilogue_chunk(p, es, u, sc, row, t0, v);
+                    if (tr && threadIdx.x == 64 && it == 0 && t0 < 64) tr[195 + (t0 >> 5) * 2] = gtimer();
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
+                if (tr && threadIdx.x == 64 && it < 32) tr[160 + it] = gtimer();
             } else {
                 // partial -> workspace [tile][split][sub][t][row]
                 const size_t tile_stride = (size_t)p.n_sub * p.T_pad * kTcBM;
                 float* wsu = p.ws + ((size_t)u.tile_global * p.splits + u.split) * tile_stride;
                 for (int t0 = 0; t0 < p.T_pad; t0 += 32)
-                    for (int sub = 0; sub < p.n_sub; ++sub) {
+#pragma unroll
+                    for (int sub = 0; sub < 2; ++sub) {
+                        if (sub >= p.n_sub) break;
                         tmem_ld32(t_acc + sub * p.T_pad + t0, v[sub]);
-                        for (int j = 0; j < 32; ++j) wsu[((size_t)sub * p.T_pad + t0 + j) * kTcBM + row] = v[sub][j];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) __stcg(wsu + ((size_t)sub * p.T_pad + t0 + j) * kTcBM + row, v[sub][j]);
                     }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
+                if (tr && threadIdx.x == 64 && it < 32) tr[160 + it] = gtimer();
                 __threadfence();
                 epi_bar();
                 if (threadIdx.x == 64) {
@@ -510,13 +534,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 __threadfence();
                 const float* wst = p.ws + (size_t)u.tile_global * p.splits * tile_stride;
                 for (int t0 = 0; t0 < p.T_pad; t0 += 32) {
-                    for (int sub = 0; sub < p.n_sub; ++sub)
-                        for (int j = 0; j < 32; ++j) {
-                            float s = 0.0f;
-                            for (int sp = 0; sp < p.splits; ++sp)
-                                s += __ldcg(wst + (size_t)sp * tile_stride + ((size_t)sub * p.T_pad + t0 + j) * kTcBM + row);
-                            v[sub][j] = s;
+#pragma unroll
+                    for (int sub = 0; sub < 2; ++sub) {
+                        if (sub >= p.n_sub) break;
+                        // sum the splits in split order: ((p0 + p1) + p2) + ...
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[sub][j] = 0.0f;
+                        for (int sp = 0; sp < p.splits; ++sp) {
+                            const float* src = wst + (size_t)sp * tile_stride + ((size_t)sub * p.T_pad + t0) * kTcBM + row;
+                            float part[32];
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) part[j] = __ldcg(src + (size_t)j * kTcBM);
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) v[sub][j] += part[j];
                         }
+                    }
                     epilogue_chunk(p, es, u, sc, row, t0, v);
                 }
                 if (threadIdx.x == 64) p.counters[u.tile_global] = 0;  // self-reset for the next launch
@@ -527,6 +559,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if (tr && threadIdx.x == 0) tr[193] = gtimer();
     if (warp == 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols));
 }
@@ -589,9 +622,7 @@ int tc_encode_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uin
     return r == CUDA_SUCCESS ? AOS_OK : AOS_ERR_CUDA;
 }
 
-size_t tc_tail_bytes(const TcParams& p) {
-    return 512 + 128 * 33 * 4 + (size_t)p.T_pad * sizeof(aos_router_ring);
-}
+size_t tc_tail_bytes(const TcParams&) { return 512 + 128 * 33 * 4; }
 
 size_t tc_smem_bytes(const TcParams& p) {
     return 1024 + (size_t)p.n_stages * p.stage_bytes + tc_tail_bytes(p);
@@ -605,13 +636,18 @@ int tc_prepare(TcParams& p, int smem_budget) {
     if (p.T_pad < 32) p.T_pad = 32;  // epilogue works in 32-token chunks
     const uint32_t w_bytes = (uint32_t)p.n_sub * kTcBM * 128;
     const uint32_t act_base = (uint32_t)p.T_pad * 128;
-    const uint32_t act_lora = (uint32_t)p.n_sub * kSlabsPerStep * p.T_pad * 32;
+    const uint32_t act_lora = (uint32_t)p.n_sub * p.T_pad * 128;
     const uint32_t act = std::max(act_base, p.lora ? act_lora : 0u);
     p.act_off = w_bytes;
     p.stage_bytes = (w_bytes + act + 1023) & ~1023u;
     const size_t fixed = 1024 + tc_tail_bytes(p);
     int ns = (int)((smem_budget - (int)fixed) / (int)p.stage_bytes);
-    ns = std::min(ns, 8);
+    static const int max_stages = [] {
+        const char* e = getenv("AOS_TC_MAX_STAGES");  // tuning knob, default 8
+        const int v = e ? atoi(e) : 8;
+        return v < 2 ? 2 : (v > 16 ? 16 : v);
+    }();
+    ns = std::min(ns, max_stages);
     if (ns < 2) return AOS_ERR_INVALID;
     p.n_stages = ns;
     if (2 * p.splits > p.kb + 1 && p.splits > 1) p.splits = std::max(1, p.kb / 2);

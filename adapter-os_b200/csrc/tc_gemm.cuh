@@ -1,10 +1,12 @@
 // tc_gemm.cuh — parameters of the tcgen05 weight-streaming GEMM (tc_gemm.cu).
 //
 // D[rows, tokens] = W[rows, K] . X[tokens, K]^T  (+ sum over touched LoRA rank
-// slabs of  B_slab[rows, 16] . Hm[tokens, slab cols]^T), i.e. the base
-// projection y = x W^T of mlx_cpp_wrapper_real.cpp:3372-3381 fused with the
-// LoRA expand of :3394-3419, computed "swap-AB": weight rows are the MMA's M
-// (128 per tile) and the decode tokens are its N (<= 256).
+// groups of  B_cat[rows, 64 group cols] . Hm[tokens, 64 group cols]^T), i.e. the
+// base projection y = x W^T of mlx_cpp_wrapper_real.cpp:3372-3381 fused with
+// the LoRA expand of :3394-3419, computed "swap-AB": weight rows are the MMA's
+// M (128 per tile) and the decode tokens are its N (<= 256).  Every pipeline
+// step, base or LoRA, is one 128-row x 128-byte box of weights plus one
+// T x 128-byte box of activations (SWIZZLE_128B) and four K=16 MMAs.
 #pragma once
 
 #include <cuda.h>
@@ -19,31 +21,30 @@ enum TcMode : int {
     TC_STORE_F32 = 2,   // out[t][col] = acc                           (lm_head logits)
     TC_QKV_ROPE = 3,    // q -> out (RoPE), k -> paged K (RoPE), v -> paged V
     TC_SWIGLU = 4,      // out[t][col] = bf16(silu(acc0) * acc1)        (n_sub = 2)
-    TC_SHRINK_HM = 5    // hm[t][slab col] = bf16(acc * gate(t, owner(col)))
+    TC_SHRINK_HM = 5    // hm[t][group col] = bf16(acc * gate(t, owner(col)))
 };
 
 constexpr int kTcMaxSets = 3;    // operand sets = segments x sub-tiles
 constexpr int kTcThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int kTcBM = 128;       // weight rows per tile
-constexpr int kTcBK = 64;        // K elements per base step (128 B, one SW128 row)
-constexpr int kSlab = 16;        // LoRA rank columns per slab (one K=16 MMA)
-constexpr int kSlabsPerStep = 4;
-constexpr int kShrinkSlabsPerTile = kTcBM / kSlab;  // 8
+constexpr int kTcBK = 64;        // K elements per step (128 B, one SW128 row)
+constexpr int kGroup = 64;       // LoRA rank columns per group (= one K step)
+constexpr int kShrinkGroupsPerTile = kTcBM / kGroup;  // 2
 
 struct TcParams {
     CUtensorMap tm_w[kTcMaxSets];   // base weights [rows, K] (or lora_A [R, K] for shrink), SW128
     CUtensorMap tm_x;               // activations [T, K], SW128
-    CUtensorMap tm_lb[kTcMaxSets];  // lora_B slabs [R/16][rows][16], SW32
-    CUtensorMap tm_lh[kTcMaxSets];  // gated shrink output [T, R], SW32
+    CUtensorMap tm_lb[kTcMaxSets];  // lora_B [rows, R], SW128
+    CUtensorMap tm_lh[kTcMaxSets];  // gated shrink output [T, R], SW128
     int mode, n_sub, n_seg, T, T_pad, kb, splits, n_stages, lora, shrink;
-    int seg_tiles[kTcMaxSets];      // tiles per segment (ignored for shrink: from n_slabs)
+    int seg_tiles[kTcMaxSets];      // tiles per segment (ignored for shrink: from n_groups)
     int seg_wrow0[kTcMaxSets];      // first W row of the segment
     int seg_out0[kTcMaxSets];       // first output feature of the segment
     int seg_rows[kTcMaxSets];       // valid output rows of the segment
     int seg_module[kTcMaxSets];
     uint32_t stage_bytes, act_off;  // bytes per pipeline stage; offset of the activation region
-    const int* slabs;               // touched slab list (ascending)
-    const int* n_slabs;             // its length
+    const int* groups;              // touched rank-group list (ascending)
+    const int* n_groups;            // its length
     // epilogue
     void* out[kTcMaxSets];
     int ld_out;
@@ -56,13 +57,18 @@ struct TcParams {
     int max_blocks, num_blocks, nkv, layer;
     int R;                          // arena rank capacity (columns of hm)
     const int* col_owner;           // [R] adapter id owning the column, -1 if free
-    const float* adapter_scale;     // [max_adapters] alpha / rank
-    const aos_router_ring* rings;   // [T]
+    const float* coef;              // [T][max_adapters] gate * alpha/rank (0 = not selected)
     int max_adapters;
     float* ws;                      // split-K partials
     int* counters;                  // per tile, self-resetting
     int* err;                       // device error word (0 = ok)
+    unsigned long long* trace;      // optional per-CTA %globaltimer trace (null = off)
 };
+
+// Trace layout per CTA (kTraceStride slots): [0,64) producer step issues,
+// [64,128) MMA full-barrier waits done, [128,160) epilogue unit starts,
+// [160,192) epilogue unit ends, 192 kernel start, 193 kernel end.
+constexpr int kTraceStride = 256;
 
 // Host helpers (tc_gemm.cu).
 int tc_encode_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,

@@ -92,7 +92,7 @@ typedef struct aos_model_config {
     uint32_t kv_block_size;       /* tokens per KV page; must be 16                        */
     uint32_t kv_num_blocks;       /* KV pages per layer in the pool                        */
     uint32_t max_seq_len;         /* longest sequence (tokens)                             */
-    uint32_t lora_rank_capacity;  /* rank columns in the adapter arena (multiple of 16)    */
+    uint32_t lora_rank_capacity;  /* rank columns in the adapter arena (rounded up to 64)   */
     uint32_t lora_max_adapters;   /* adapter ids are < this (<= 65535)                     */
     uint32_t lora_module_mask;    /* bit m: module m may carry LoRA (0 = all seven)        */
     int32_t device;               /* CUDA ordinal                                          */
@@ -248,7 +248,7 @@ typedef enum aos_kernel_class {
     AOS_K_SHRINK = 1,  /* LoRA shrink H = gate * (A x) (tcgen05)             */
     AOS_K_ATTN = 2,    /* paged decode attention + chunk combine             */
     AOS_K_NORM = 3,    /* RMSNorm                                            */
-    AOS_K_PREP = 4,    /* routing prep (touched rank slabs)                  */
+    AOS_K_PREP = 4,    /* routing prep (touched rank groups)                 */
     AOS_K_EMBED = 5,   /* embedding gather                                   */
     AOS_K_LM_HEAD = 6, /* lm_head GEMM (tcgen05)                             */
     AOS_K_NUM_CLASSES = 8
@@ -258,11 +258,15 @@ typedef struct aos_profile {
     uint64_t launches[AOS_K_NUM_CLASSES];
     double ms[AOS_K_NUM_CLASSES];
     uint64_t steps;
-    uint32_t last_touched_slabs; /* rank slabs the last step streamed        */
+    uint32_t last_touched_groups; /* 64-column rank groups the last step streamed */
 } aos_profile;
 
 int aos_profile_enable(aos_ctx* ctx, int enable);
 int aos_profile_read(aos_ctx* ctx, aos_profile* out, int reset);
+/* Diagnostics: with AOS_TC_TRACE=<g> set before aos_init, the GEMM (g = 0..3:
+ * qkv, o, gate/up, down; 4..7: their LoRA shrinks) of layer 0 writes per-CTA
+ * %globaltimer stamps (256 slots per CTA); this copies n of them to host. */
+int aos_debug_trace_read(aos_ctx* ctx, uint64_t* out, uint64_t n);
 
 /* ---- metrics / health / attestation (lib.rs:383, 559-593) ---------------- */
 int aos_get_metrics(const aos_ctx* ctx, aos_metrics* out);

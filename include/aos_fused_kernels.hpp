@@ -1,0 +1,237 @@
+// aos_fused_kernels.hpp — C++ host-side mirror of adapter-os's kernel API
+// over the C ABI in aos_cuda.h (header only).
+//
+//   RouterRing    <- crates/adapteros-lora-kernel-api/src/lib.rs:58-214
+//   IoBuffers     <- lib.rs:221-246
+//   FusedKernels  <- lib.rs:308-716 (the trait a backend implements)
+//   CudaKernels   <- the sm_100a backend (what kernel-mtl's MetalKernels,
+//                    src/lib.rs:287-322, is for Metal)
+//   Router        <- crates/adapteros-lora-router/src/router.rs:1517-1952,
+//                    batched: one RouterRing per token
+//
+// Errors follow adapteros_core::AosError: every fallible call returns a
+// Result with the C status and the backend's last-error text.
+#pragma once
+
+#include <cstdint>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "aos_cuda.h"
+
+namespace adapteros {
+
+struct AosError {
+    int code = AOS_OK;
+    std::string message;
+    bool ok() const { return code == AOS_OK; }
+};
+
+inline AosError status(int code, const aos_ctx* ctx = nullptr) {
+    if (code == AOS_OK) return {};
+    return AosError{code, aos_last_error(ctx)};
+}
+
+// RouterRing::set (lib.rs:140-193), release-build policy: mismatched lengths or
+// an index >= max_adapter zero-fill the ring and set k = 0.
+struct RouterRing {
+    uint16_t indices[AOS_MAX_K] = {};
+    int16_t gates_q15[AOS_MAX_K] = {};
+    uint32_t position = 0;
+    uint32_t k = 0;
+    uint32_t dropout_seed = 0;
+    float dropout_rate = 0.0f;
+
+    void set(const std::vector<uint16_t>& idx, const std::vector<int16_t>& gates, uint16_t max_adapter = 0xFFFF) {
+        std::memset(indices, 0, sizeof(indices));
+        std::memset(gates_q15, 0, sizeof(gates_q15));
+        k = 0;
+        if (idx.size() != gates.size()) return;
+        for (uint16_t i : idx)
+            if (i >= max_adapter) return;
+        const size_t n = idx.size() < AOS_MAX_K ? idx.size() : AOS_MAX_K;
+        for (size_t j = 0; j < n; ++j) {
+            indices[j] = idx[j];
+            gates_q15[j] = gates[j];
+        }
+        k = (uint32_t)n;
+    }
+    aos_router_ring device_layout() const {
+        aos_router_ring r{};
+        r.top_k = k;
+        r.position = position;
+        std::memcpy(r.indices, indices, sizeof(indices));
+        std::memcpy(r.gates_q15, gates_q15, sizeof(gates_q15));
+        return r;
+    }
+};
+
+struct IoBuffers {
+    std::vector<uint32_t> input_ids;
+    std::vector<float> output_logits;
+    size_t position = 0;
+    std::string session_id;
+    explicit IoBuffers(size_t vocab = 0) : output_logits(vocab, 0.0f) {}
+};
+
+struct AdapterLoadMetadata {
+    std::string adapter_id;
+    uint32_t rank = 16;
+    float alpha = 32.0f;
+};
+
+// One LoRA module's weights for one layer: A [rank, in], B [out, rank] (bf16 bits).
+struct LoraModuleWeights {
+    uint32_t layer;
+    aos_module module;
+    const uint16_t* A;
+    const uint16_t* B;
+};
+
+class FusedKernels {
+   public:
+    virtual ~FusedKernels() = default;
+    virtual AosError run_step(const RouterRing& ring, IoBuffers& io) = 0;
+    virtual std::string device_name() const = 0;
+    virtual AosError attest_determinism(aos_determinism_report* out) const = 0;
+    virtual AosError load_adapter_with_metadata(uint16_t id, const std::vector<LoraModuleWeights>& weights,
+                                                const AdapterLoadMetadata& meta) = 0;
+    virtual AosError unload_adapter(uint16_t id) = 0;
+    virtual AosError detach_adapter(uint16_t id) { return unload_adapter(id); }
+    virtual AosError attach_adapter(uint16_t) { return {}; }
+    virtual AosError switch_adapter(uint16_t) { return {}; }
+    virtual bool supports_kv_cache() const { return false; }
+    virtual void clear_session_cache(const std::string&) {}
+    virtual void clear_all_caches() {}
+    virtual size_t cache_memory_bytes() const { return 0; }
+    virtual AosError health_check() { return {}; }
+};
+
+// The sm_100a backend.  Single-threaded per instance (the trait is used
+// through &mut self).
+class CudaKernels final : public FusedKernels {
+   public:
+    explicit CudaKernels(const aos_model_config& cfg) : cfg_(cfg), ctx_(aos_init(&cfg)) {
+        if (!ctx_) throw std::runtime_error(std::string("aos_init: ") + aos_last_error(nullptr));
+    }
+    ~CudaKernels() override { aos_destroy(ctx_); }
+    CudaKernels(const CudaKernels&) = delete;
+    CudaKernels& operator=(const CudaKernels&) = delete;
+
+    aos_ctx* ctx() { return ctx_; }
+
+    AosError load_weight(aos_weight_kind kind, uint32_t layer, aos_module m, const uint16_t* data, uint64_t n,
+                         bool on_device = false) {
+        return status(aos_load_weight(ctx_, kind, layer, m, data, n, on_device ? 1 : 0), ctx_);
+    }
+
+    AosError load_adapter_with_metadata(uint16_t id, const std::vector<LoraModuleWeights>& w,
+                                        const AdapterLoadMetadata& meta) override {
+        AosError e = status(aos_adapter_new(ctx_, id, meta.rank, meta.alpha), ctx_);
+        if (!e.ok()) return e;
+        for (const auto& m : w) {
+            e = status(aos_adapter_set_module(ctx_, id, m.layer, m.module, m.A, m.B, 0), ctx_);
+            if (!e.ok()) {
+                aos_adapter_unload(ctx_, id);
+                return e;
+            }
+        }
+        return {};
+    }
+    AosError unload_adapter(uint16_t id) override { return status(aos_adapter_unload(ctx_, id), ctx_); }
+
+    // Batched step: one decode token per (ring, token, sequence).
+    AosError run_step_batch(const std::vector<RouterRing>& rings, const std::vector<uint32_t>& tokens,
+                            const std::vector<uint64_t>& seqs, float* logits) {
+        std::vector<aos_router_ring> r(rings.size());
+        for (size_t i = 0; i < rings.size(); ++i) r[i] = rings[i].device_layout();
+        return status(aos_run_step_batch(ctx_, r.data(), tokens.data(), seqs.data(), (uint32_t)r.size(), logits,
+                                         nullptr),
+                      ctx_);
+    }
+
+    // FusedKernels::run_step: decode io.input_ids in order at io.position for
+    // the io.session_id sequence; logits of the last token; position advances
+    // by input_ids.size() (mlx-ffi/src/backend.rs:1212-1310).
+    AosError run_step(const RouterRing& ring, IoBuffers& io) override {
+        if (io.input_ids.empty()) return AosError{AOS_ERR_INVALID, "Input token IDs cannot be empty"};
+        uint64_t seq = session(io.session_id);
+        AosError e = status(aos_kv_set_len(ctx_, seq, (uint32_t)io.position), ctx_);
+        if (!e.ok()) return e;
+        std::vector<float> logits(cfg_.vocab);
+        const aos_router_ring r = ring.device_layout();
+        for (uint32_t tok : io.input_ids) {
+            e = status(aos_run_step_batch(ctx_, &r, &tok, &seq, 1, logits.data(), nullptr), ctx_);
+            if (!e.ok()) return e;
+        }
+        const size_t n = io.output_logits.size() < logits.size() ? io.output_logits.size() : logits.size();
+        std::memcpy(io.output_logits.data(), logits.data(), n * sizeof(float));
+        io.position += io.input_ids.size();
+        return {};
+    }
+
+    std::string device_name() const override { return aos_device_name(ctx_); }
+    AosError attest_determinism(aos_determinism_report* out) const override {
+        return status(aos_attest_determinism(ctx_, out), ctx_);
+    }
+    bool supports_kv_cache() const override { return true; }
+    void clear_session_cache(const std::string& sid) override {
+        for (auto it = sessions_.begin(); it != sessions_.end(); ++it)
+            if (it->first == sid) {
+                aos_kv_free(ctx_, it->second);
+                sessions_.erase(it);
+                return;
+            }
+    }
+    void clear_all_caches() override {
+        aos_kv_clear_all(ctx_);
+        sessions_.clear();
+    }
+    size_t cache_memory_bytes() const override { return (size_t)aos_kv_memory_bytes(ctx_); }
+    AosError health_check() override { return status(aos_health_check(ctx_), ctx_); }
+
+   private:
+    uint64_t session(const std::string& sid) {
+        for (auto& kv : sessions_)
+            if (kv.first == sid) return kv.second;
+        const uint64_t id = (1ull << 62) + sessions_.size();
+        if (aos_kv_alloc(ctx_, id, cfg_.max_seq_len) != AOS_OK)
+            throw std::runtime_error(aos_last_error(ctx_));
+        sessions_.emplace_back(sid, id);
+        return id;
+    }
+    aos_model_config cfg_;
+    aos_ctx* ctx_;
+    std::vector<std::pair<std::string, uint64_t>> sessions_;
+};
+
+// Batched router (router.rs:1517-1952): one RouterRing per token.
+class Router {
+   public:
+    Router(uint32_t k, float tau, float eps) : p_{k, tau, eps, 1.0f} {}
+    void set_routing_bias(float b) { p_.routing_bias = b; }  // router.rs:556-561 (sanitised in the kernel call)
+    AosError route_batch(const float* priors, uint32_t T, uint32_t N, const uint64_t* stable_ids,
+                         std::vector<RouterRing>& out, const float* version_weights = nullptr,
+                         const uint8_t* allowed = nullptr) const {
+        std::vector<aos_router_ring> r(T);
+        AosError e =
+            status(aos_route_batch(priors, stable_ids, version_weights, allowed, nullptr, T, N, &p_, r.data(), nullptr,
+                                   nullptr));
+        out.resize(T);
+        for (uint32_t t = 0; t < T; ++t) {
+            out[t].k = r[t].top_k;
+            out[t].position = r[t].position;
+            std::memcpy(out[t].indices, r[t].indices, sizeof(r[t].indices));
+            std::memcpy(out[t].gates_q15, r[t].gates_q15, sizeof(r[t].gates_q15));
+        }
+        return e;
+    }
+
+   private:
+    aos_router_params p_;
+};
+
+}  // namespace adapteros
