@@ -143,6 +143,36 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     __syncthreads();
 
+    const int* bt = p.block_tables + (size_t)t * p.max_blocks;
+    const uint32_t buf0 = smem_u32(smem + warp * 2 * kBufBytes);
+    const uint32_t bar0 = smem_u32(&bars[warp * 2]);
+    auto page_row = [&](int pg) { return ((p.layer * p.num_blocks + __ldg(bt + pg)) * p.nkv + kvh) * 16; };
+    auto issue = [&](int pg, int b) {
+        const uint32_t bar = bar0 + b * 8, dst = buf0 + b * kBufBytes;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(kBufBytes) : "memory");
+        const int row = page_row(pg);
+        tma_page(&p.tm_k, dst, bar, row);
+        tma_page(&p.tm_v, dst + kPageBytes, bar, row);
+    };
+
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float o[16][4];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+
+    // Pages before the sequence's last one were written by earlier steps, so
+    // the first of them may be fetched before the previous launch (the QKV
+    // GEMM that appends this step's K/V) has finished.
+    int my_first = pg0 + warp;
+    bool first_issued = false;
+    if (lane == 0 && my_first < pg1 && my_first < n_pages - 1) {
+        issue(my_first, 0);
+        first_issued = true;
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (lane == 0 && my_first < pg1 && !first_issued) issue(my_first, 0);
+
     // Q fragments (rows = heads of the group, zero beyond G), all 8 k-chunks.
     const int g = lane >> 2, c2 = (lane & 3) * 2;
     uint32_t qa[8][4];
@@ -161,25 +191,6 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
         }
     }
 
-    const int* bt = p.block_tables + (size_t)t * p.max_blocks;
-    const uint32_t buf0 = smem_u32(smem + warp * 2 * kBufBytes);
-    const uint32_t bar0 = smem_u32(&bars[warp * 2]);
-    auto page_row = [&](int pg) { return ((p.layer * p.num_blocks + __ldg(bt + pg)) * p.nkv + kvh) * 16; };
-    auto issue = [&](int pg, int b) {
-        const uint32_t bar = bar0 + b * 8, dst = buf0 + b * kBufBytes;
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(kBufBytes) : "memory");
-        const int row = page_row(pg);
-        tma_page(&p.tm_k, dst, bar, row);
-        tma_page(&p.tm_v, dst + kPageBytes, bar, row);
-    };
-
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    float o[16][4];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-
-    int my_first = pg0 + warp;
-    if (lane == 0 && my_first < pg1) issue(my_first, 0);
     int it = 0;
     bool ok = true;
     for (int pg = my_first; pg < pg1; pg += kWarps, ++it) {
@@ -306,6 +317,8 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
 __global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restrict__ part, const float* __restrict__ part_ml,
                                                            const int* __restrict__ ctx_lens, int T, int nkv, int G,
                                                            int max_chunks, uint16_t* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const int kvh = blockIdx.x % nkv, t = blockIdx.x / nkv;
     if (t >= T) return;
     const int L = ctx_lens[t] + 1;
@@ -360,9 +373,12 @@ cudaError_t launch_attention(const CUtensorMap& tm_k, const CUtensorMap& tm_v, c
     p.scale_log2 = 1.4426950408889634f / sqrtf(128.0f);
     p.err = err;
     const size_t smem = attn_smem_bytes();
-    attn_decode_kernel<<<T * nkv * max_chunks, 128, smem, s>>>(p);
-    attn_combine_kernel<<<T * nkv, 128, 0, s>>>(part, part_ml, ctx_lens, T, nkv, nq / nkv, max_chunks, out);
-    return cudaGetLastError();
+    cudaError_t e = launch_k(attn_decode_kernel, dim3(T * nkv * max_chunks), dim3(128), smem, s, p);
+    if (e != cudaSuccess) return e;
+    const float* cpart = part;
+    const float* cml = part_ml;
+    return launch_k(attn_combine_kernel, dim3(T * nkv), dim3(128), 0, s, cpart, cml, ctx_lens, T, nkv, nq / nkv,
+                    max_chunks, out);
 }
 
 }  // namespace aos

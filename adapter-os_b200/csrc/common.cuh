@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "../../include/aos_cuda.h"
 
@@ -43,5 +44,32 @@ __device__ __forceinline__ int32_t total_key(float f) {
 
 // Upper bound for every device-side spin (~1 s at the B200's max SM clock).
 constexpr long long kSpinLimitCycles = 2000000000LL;
+
+// Programmatic dependent launch.  Every kernel of the decode step runs
+//   prologue (static data, or data produced two or more launches earlier)
+//   -> pdl_wait()   : the previous launch has completed and its writes are visible
+//   -> pdl_trigger(): the next launch may be scheduled (it still waits for us)
+//   -> main work.
+// Because each kernel triggers only after its own wait, a kernel's prologue
+// may read anything written by the launch before its predecessor.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch with the programmatic-stream-serialization attribute (when pdl).
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace aos

@@ -11,6 +11,8 @@ namespace {
 // the vocabulary give a zero row (metal/src/kernels/adapteros_kernels.metal:195-234).
 __global__ void embed_kernel(const uint16_t* __restrict__ table, const uint32_t* __restrict__ ids, int T, int H,
                              int V, uint16_t* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const int t = blockIdx.x;
     if (t >= T) return;
     const uint32_t id = ids[t];
@@ -23,6 +25,8 @@ __global__ void embed_kernel(const uint16_t* __restrict__ table, const uint32_t*
 // One CTA (256 threads) per token; fixed-order tree reduction; bf16 in/out.
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
                                                       int T, int H, float eps, uint16_t* __restrict__ y) {
+    pdl_wait();
+    pdl_trigger();
     const int t = blockIdx.x;
     if (t >= T) return;
     const uint16_t* xt = x + (size_t)t * H;
@@ -73,6 +77,8 @@ __global__ void __launch_bounds__(1024) lora_prep_kernel(const aos_router_ring* 
                                                          int* __restrict__ n_slabs) {
     extern __shared__ int marks[];  // [n_slab_total]
     __shared__ int warp_sums[32];
+    pdl_wait();
+    pdl_trigger();
     for (int i = threadIdx.x; i < n_slab_total; i += blockDim.x) marks[i] = 0;
     __syncthreads();
     for (int i = threadIdx.x; i < T * AOS_MAX_K; i += blockDim.x) {
@@ -116,6 +122,8 @@ __global__ void __launch_bounds__(1024) lora_prep_kernel(const aos_router_ring* 
 __global__ void __launch_bounds__(256) lora_coef_kernel(const aos_router_ring* __restrict__ rings,
                                                         const int* __restrict__ rank, const float* __restrict__ scale,
                                                         int max_adapters, float* __restrict__ coef) {
+    pdl_wait();
+    pdl_trigger();
     const int t = blockIdx.x;
     float* row = coef + (size_t)t * max_adapters;
     for (int a = threadIdx.x; a < max_adapters; a += blockDim.x) row[a] = 0.0f;
@@ -158,24 +166,22 @@ __global__ void fill_normal_bf16(uint16_t* __restrict__ p, size_t n, uint64_t se
 cudaError_t launch_embed(const uint16_t* table, const uint32_t* ids, int T, int H, int V, uint16_t* out,
                          cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
-    embed_kernel<<<T, 128, 0, s>>>(table, ids, T, H, V, out);
-    return cudaGetLastError();
+    return launch_k(embed_kernel, dim3(T), dim3(128), 0, s, table, ids, T, H, V, out);
 }
 
 cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* w, int T, int H, float eps, uint16_t* y,
                            cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
-    rmsnorm_kernel<<<T, 256, 0, s>>>(x, w, T, H, eps, y);
-    return cudaGetLastError();
+    return launch_k(rmsnorm_kernel, dim3(T), dim3(256), 0, s, x, w, T, H, eps, y);
 }
 
 cudaError_t launch_lora_prep(const aos_router_ring* rings, int T, const int* col_off, const int* rank,
                              const float* scale, int max_adapters, int n_slab_total, int* slabs, int* n_slabs,
                              float* coef, cudaStream_t s) {
-    lora_prep_kernel<<<1, 1024, (size_t)n_slab_total * sizeof(int), s>>>(rings, T, col_off, rank, max_adapters,
-                                                                        n_slab_total, slabs, n_slabs);
-    if (T > 0) lora_coef_kernel<<<T, 256, 0, s>>>(rings, rank, scale, max_adapters, coef);
-    return cudaGetLastError();
+    cudaError_t e = launch_k(lora_prep_kernel, dim3(1), dim3(1024), (size_t)n_slab_total * sizeof(int), s, rings, T,
+                             col_off, rank, max_adapters, n_slab_total, slabs, n_slabs);
+    if (e != cudaSuccess || T <= 0) return e;
+    return launch_k(lora_coef_kernel, dim3(T), dim3(256), 0, s, rings, rank, scale, max_adapters, coef);
 }
 
 cudaError_t launch_fill_normal(uint16_t* p, size_t n, uint64_t seed, float std, cudaStream_t s) {

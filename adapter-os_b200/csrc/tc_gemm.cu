@@ -367,6 +367,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
 
     if (warp == 0) {
         // ============================ TMA producer ============================
+        // The weight-side boxes (W, lora_A, lora_B) of the first NS stages are
+        // issued before pdl_wait(): weights are static, and the group list was
+        // written two or more launches earlier.  The activation-side boxes (X, hm)
+        // of those stages follow once the previous launch has completed.
         if (lane == 0) {
             const uint64_t pol_w = policy_evict_first();
             const uint64_t pol_x = policy_evict_last();
@@ -376,47 +380,73 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
+            bool waited = false;
+            int pre_step[16], pre_unit[16];
+            int n_pre = 0;
+            // weight-side boxes of one step; returns the step's total transaction bytes
+            auto step_bytes = [&](const Unit& u, int step) -> uint32_t {
+                if (step >= p.kb) return (uint32_t)(p.n_sub * (kTcBM * 128 + p.T_pad * 128));
+                if (p.shrink) {
+                    const int nv = min(kShrinkGroupsPerTile, sc.n_groups - u.tile * kShrinkGroupsPerTile);
+                    return (uint32_t)(nv * kGroup * 128 + p.T_pad * 128);
+                }
+                return (uint32_t)(p.n_sub * kTcBM * 128 + p.T_pad * 128);
+            };
+            auto issue_w = [&](const Unit& u, int step, uint32_t sbase, uint32_t fb) {
+                if (step < p.kb) {
+                    const int kx = step * kTcBK;
+                    if (p.shrink) {  // lora_A rows of the tile's (up to) two touched groups
+                        const int first = u.tile * kShrinkGroupsPerTile;
+                        const int nv = min(kShrinkGroupsPerTile, sc.n_groups - first);
+                        for (int q = 0; q < nv; ++q)
+                            tma_2d(&p.tm_w[u.seg], sbase + q * (kGroup * 128), fb, kx,
+                                   __ldg(p.groups + first + q) * kGroup, pol_w);
+                    } else {
+                        for (int sub = 0; sub < p.n_sub; ++sub)
+                            tma_2d(&p.tm_w[u.seg * p.n_sub + sub], sbase + sub * (kTcBM * 128), fb, kx,
+                                   p.seg_wrow0[u.seg] + u.tile * kTcBM, pol_w);
+                    }
+                } else {  // LoRA expand: lora_B[tile rows, group cols]
+                    const int gcol = __ldg(p.groups + (step - p.kb)) * kGroup;
+                    for (int sub = 0; sub < p.n_sub; ++sub)
+                        tma_2d(&p.tm_lb[u.seg * p.n_sub + sub], sbase + sub * (kTcBM * 128), fb, gcol, u.tile * kTcBM,
+                               pol_w);
+                }
+            };
+            auto issue_x = [&](const Unit& u, int step, uint32_t sbase, uint32_t fb) {
+                const uint32_t act = sbase + p.act_off;
+                if (step < p.kb) {
+                    tma_2d(&p.tm_x, act, fb, step * kTcBK, 0, pol_x);
+                } else {  // gated shrink output hm[tokens, group cols] of each sub-tile
+                    const int gcol = __ldg(p.groups + (step - p.kb)) * kGroup;
+                    for (int sub = 0; sub < p.n_sub; ++sub)
+                        tma_2d(&p.tm_lh[u.seg * p.n_sub + sub], act + sub * (p.T_pad * 128), fb, gcol, 0, pol_x);
+                }
+            };
+            auto finish_wait = [&]() {
+                pdl_wait();
+                pdl_trigger();
+                waited = true;
+                for (int i = 0; i < n_pre; ++i) {
+                    const Unit u = unit_of(p, sc, pre_unit[i]);
+                    issue_x(u, pre_step[i], smem_u32(stages + (size_t)i * p.stage_bytes), smem_u32(&full_bar[i]));
+                }
+            };
             for (int uidx = blockIdx.x; uidx < sc.units && ok; uidx += gridDim.x) {
                 const Unit u = unit_of(p, sc, uidx);
                 for (int step = u.step0; step < u.step1; ++step) {
+                    if (!waited && n_pre == NS) finish_wait();
                     if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, p.err)) { ok = false; break; }
                     const uint32_t fb = smem_u32(&full_bar[stage]);
                     const uint32_t sbase = smem_u32(stages + (size_t)stage * p.stage_bytes);
-                    const uint32_t act = sbase + p.act_off;
-                    if (step < p.kb) {
-                        const int kx = step * kTcBK;
-                        if (p.shrink) {
-                            // lora_A rows of the tile's (up to) two touched groups; one
-                            // 64-row box, or one 128-row box when the groups are adjacent
-                            const int first = u.tile * kShrinkGroupsPerTile;
-                            const int nv = min(kShrinkGroupsPerTile, sc.n_groups - first);
-                            const int g0 = __ldg(p.groups + first);
-                            mbar_expect_tx(fb, (uint32_t)(nv * kGroup * 128 + p.T_pad * 128));
-                            if (nv == 2 && __ldg(p.groups + first + 1) == g0 + 1) {
-                                tma_2d(&p.tm_w[u.seg], sbase, fb, kx, g0 * kGroup, pol_w);
-                                tma_2d(&p.tm_w[u.seg], sbase + kGroup * 128, fb, kx, (g0 + 1) * kGroup, pol_w);
-                            } else {
-                                for (int q = 0; q < nv; ++q)
-                                    tma_2d(&p.tm_w[u.seg], sbase + q * (kGroup * 128), fb, kx,
-                                           __ldg(p.groups + first + q) * kGroup, pol_w);
-                            }
-                        } else {
-                            mbar_expect_tx(fb, (uint32_t)(p.n_sub * kTcBM * 128 + p.T_pad * 128));
-                            for (int sub = 0; sub < p.n_sub; ++sub)
-                                tma_2d(&p.tm_w[u.seg * p.n_sub + sub], sbase + sub * (kTcBM * 128), fb, kx,
-                                       p.seg_wrow0[u.seg] + u.tile * kTcBM, pol_w);
-                        }
-                        tma_2d(&p.tm_x, act, fb, kx, 0, pol_x);
-                    } else {
-                        // LoRA expand step: lora_B[tile rows, group cols] and the
-                        // gated shrink output hm[tokens, group cols] of each sub-tile
-                        const int gcol = __ldg(p.groups + (step - p.kb)) * kGroup;
-                        mbar_expect_tx(fb, (uint32_t)(p.n_sub * (kTcBM * 128 + p.T_pad * 128)));
-                        for (int sub = 0; sub < p.n_sub; ++sub) {
-                            const int set = u.seg * p.n_sub + sub;
-                            tma_2d(&p.tm_lb[set], sbase + sub * (kTcBM * 128), fb, gcol, u.tile * kTcBM, pol_w);
-                            tma_2d(&p.tm_lh[set], act + sub * (p.T_pad * 128), fb, gcol, 0, pol_x);
-                        }
+                    mbar_expect_tx(fb, step_bytes(u, step));
+                    issue_w(u, step, sbase, fb);
+                    if (waited) {
+                        issue_x(u, step, sbase, fb);
+                    } else {  // first round of stages: stage index == n_pre
+                        pre_step[n_pre] = step;
+                        pre_unit[n_pre] = uidx;
+                        ++n_pre;
                     }
                     last_phase[stage] = phase;
                     used_mask |= 1u << stage;
@@ -425,6 +455,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     if (++stage == NS) { stage = 0; phase ^= 1u; }
                 }
             }
+            if (!waited) finish_wait();
             // Drain: every issued copy must land before the CTA may exit.
             for (int s = 0; s < NS; ++s)
                 if (used_mask & (1u << s)) mbar_wait_drain(smem_u32(&full_bar[s]), last_phase[s]);
@@ -482,6 +513,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         const int row = q * 32 + lane;
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
         EpiSmem es{xbuf};
+        pdl_wait();  // the epilogue reads and writes activations of the previous launches
         int it = 0;
         for (int uidx = blockIdx.x; uidx < sc.units; uidx += gridDim.x, ++it) {
             const Unit u = unit_of(p, sc, uidx);
@@ -674,8 +706,7 @@ cudaError_t tc_configure() {
 cudaError_t tc_launch(const TcParams& p, int grid, cudaStream_t stream) {
     const size_t smem = tc_smem_bytes(p);
     if (smem > 227 * 1024) return cudaErrorInvalidValue;
-    tc_gemm_kernel<<<grid, kTcThreads, smem, stream>>>(p);
-    return cudaGetLastError();
+    return launch_k(tc_gemm_kernel, dim3(grid), dim3(kTcThreads), smem, stream, p);
 }
 
 }  // namespace aos
