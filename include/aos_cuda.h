@@ -163,6 +163,23 @@ int aos_lora_op_f32_dev(const float* x, uint32_t T, uint32_t in_dim, uint32_t ou
                         uint32_t rank, const float* alpha, const aos_router_ring* rings, float* y,
                         void* stream);
 
+/* Same op as aos_lora_op_f32_dev, for callers that must not allocate device
+ * memory (no counterpart in the reference).  Hosts with a device-memory budget
+ * fixed at start-up, code sharing a device with an open CUDA graph capture
+ * (cudaMalloc/cudaFree synchronise the device and are illegal while a capture
+ * is open) and latency-critical loops can call this one: its scratch is a
+ * fixed 512 KiB device array in the library (131072 floats, held on every
+ * device that loads the library until exit), not an allocation.  Requires
+ * T * 8 * rank <= 131072, otherwise AOS_ERR_INVALID.  The first call on a
+ * device looks up the array's address (cudaGetSymbolAddress) and should be
+ * made before any stream capture on that device.  All calls share the array:
+ * calls that overlap on the GPU race, so serialise them (one stream).  It
+ * calls no cudaMalloc, cudaFree or allocating library routine. */
+int aos_lora_op_f32_noalloc_dev(const float* x, uint32_t T, uint32_t in_dim, uint32_t out_dim,
+                                const float* W, const float* A, const float* B, uint32_t n_adapters,
+                                uint32_t rank, const float* alpha, const aos_router_ring* rings,
+                                float* y, void* stream);
+
 /* ---- context: FusedKernels::load + hot-swap arena + KV cache ------------- */
 /* Create a backend on cfg->device; allocates the KV pool, adapter arena and
  * step scratch up front (kernel-mtl/src/lib.rs:1476-1537 load). */
