@@ -4,6 +4,7 @@
 #include <cstring>
 #include <mutex>
 #include <vector>
+#include <atomic>
 #include <string>
 
 #include "common.cuh"
@@ -47,11 +48,22 @@ int require_device(int device) {
     if (dev < 0) {
         if (cudaGetDevice(&dev) != cudaSuccess) return AOS_ERR_NO_DEVICE;
     }
-    cudaDeviceProp prop;
-    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return AOS_ERR_NO_DEVICE;
-    if (prop.major != 10) {
-        set_global_error("device is sm_" + std::to_string(prop.major) + std::to_string(prop.minor) +
-                         "; this build targets sm_100a only");
+    if (dev >= n) return AOS_ERR_NO_DEVICE;
+    // Compute capability per device, queried once (a per-call property query
+    // costs milliseconds of host time on the step path).
+    static std::atomic<int> cc[64];
+    int major = dev < 64 ? cc[dev].load(std::memory_order_relaxed) : 0;
+    if (major == 0) {
+        int mj = 0, mn = 0;
+        if (cudaDeviceGetAttribute(&mj, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&mn, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+            return AOS_ERR_NO_DEVICE;
+        major = mj * 16 + mn + 1;
+        if (dev < 64) cc[dev].store(major, std::memory_order_relaxed);
+    }
+    const int mj = (major - 1) / 16, mn = (major - 1) % 16;
+    if (mj != 10) {
+        set_global_error("device is sm_" + std::to_string(mj) + std::to_string(mn) + "; this build targets sm_100a only");
         return AOS_ERR_NO_DEVICE;
     }
     return AOS_OK;

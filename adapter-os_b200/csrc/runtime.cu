@@ -60,9 +60,8 @@ struct Sequence {
 };
 
 struct LayerPlan {
-    TcParams shrink[4];  // per group
-    TcParams gemm[4];
-    int shrink_grid[4], gemm_grid[4];
+    TcParams gemm[4];  // per input group: shrink + base + expand in one launch
+    int gemm_grid[4];
 };
 
 struct StepPlan {
@@ -116,7 +115,15 @@ struct aos_ctx {
     uint16_t* d_hm[AOS_NUM_MODULES] = {};
     int *d_groups = nullptr, *d_n_groups = nullptr;
     int *d_block_tables = nullptr, *d_ctx_lens = nullptr;
-    int *h_block_tables = nullptr, *h_ctx_lens = nullptr;  // pinned staging
+    // Pinned staging of the per-step block tables and lengths.  A ring of
+    // kStageSlots buffers, each reused only after the event recorded behind
+    // its last copy has completed, so the host may run steps ahead of the GPU
+    // without overwriting a table that a queued copy has not read yet.
+    static constexpr int kStageSlots = 4;
+    int* h_stage[kStageSlots] = {};
+    cudaEvent_t stage_ev[kStageSlots] = {};
+    int stage_slot = 0;
+    int *h_block_tables = nullptr, *h_ctx_lens = nullptr;  // the slot being filled
     aos_router_ring* d_rings = nullptr;
     uint32_t* d_tokens = nullptr;
     float* d_logits = nullptr;
@@ -125,7 +132,9 @@ struct aos_ctx {
     int attn_chunks = 0;
     float* d_ws = nullptr;
     size_t ws_bytes = 0;
-    int* d_counters = nullptr;
+    int* d_counters = nullptr;    // [kCounterTiles] pieces arrived per tile
+    int* d_tile_slots = nullptr;  // [kCounterTiles][kMaxPiecesPerTile]
+    int* d_sync = nullptr;        // [2] shrink tiles done, CTAs exited
     int* d_err = nullptr;
     unsigned long long* d_trace = nullptr;  // AOS_TC_TRACE diagnostics
     std::map<int, std::unique_ptr<StepPlan>> plans;
@@ -175,20 +184,6 @@ cudaError_t dalloc(T** p, size_t n_elems, uint64_t* counter = nullptr) {
     return e;
 }
 
-// Split-K factor: enough (tile, split) units to cover the SMs about
-// `AOS_TC_WAVES` times (tuning knob, default 1), at least 2 K-steps per split.
-int splits_for(int tiles, int kb) {
-    static const float waves = [] {
-        const char* e = getenv("AOS_TC_WAVES");
-        const float v = e ? (float)atof(e) : 1.0f;
-        return v > 0.f ? v : 1.0f;
-    }();
-    const int sms = tc_num_sms();
-    int s = tiles > 0 ? (int)(waves * sms) / tiles : 1;
-    s = std::max(1, std::min(s, kb / 2));
-    return std::min(s, 32);
-}
-
 // Build the TcParams of every GEMM of one layer for a padded batch T_pad.
 int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
     const uint32_t H = c->cfg.hidden, I = c->cfg.intermediate;
@@ -220,6 +215,8 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
         p.n_groups = c->d_n_groups;
         p.ws = c->d_ws;
         p.counters = c->d_counters;
+        p.tile_slots = c->d_tile_slots;
+        p.sync = c->d_sync;
         p.err = c->d_err;
         p.R = c->R;
         p.col_owner = c->d_col_owner;
@@ -235,38 +232,21 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
     const uint32_t group_k[4] = {H, c->QD, H, I};
 
     for (int g = 0; g < 4; ++g) {
-        // ---------------- shrink: hm = gate * (A_cat x) for every module of the group
-        TcParams& s = lp.shrink[g];
-        common(s);
-        lp.shrink_grid[g] = 0;
-        if (lora[g]) {
-            s.mode = TC_SHRINK_HM;
-            s.shrink = 1;
-            s.n_sub = 1;
-            s.kb = (int)(group_k[g] / 64);
-            int nseg = 0;
-            for (int j = 0; j < 3; ++j) {
-                const int mod = groups_mods[g][j];
-                if (mod < 0) continue;
-                if ((rc = a_map(&s.tm_w[nseg], mod))) return rc;
-                s.out[nseg] = c->d_hm[mod];
-                s.seg_module[nseg] = mod;
-                ++nseg;
-            }
-            s.n_seg = nseg;
-            if ((rc = x_map(&s.tm_x, group_x[g], group_k[g]))) return rc;
-            const int max_tiles = nseg * (c->R / 128 + 1);
-            s.splits = splits_for(max_tiles, s.kb);
-            if ((rc = tc_prepare(s, smem_budget))) return rc;
-            lp.shrink_grid[g] = std::min(max_tiles * s.splits, tc_num_sms());
-        }
-        // ---------------- base GEMM + fused LoRA expand + epilogue
+        // ---------------- LoRA shrink + base GEMM + fused LoRA expand + epilogue
         TcParams& p = lp.gemm[g];
         common(p);
         p.lora = lora[g] ? 1 : 0;
         p.kb = (int)(group_k[g] / 64);
         if ((rc = x_map(&p.tm_x, group_x[g], group_k[g]))) return rc;
-        int tiles = 0;
+        if (p.lora) {  // hm = gate * (A_cat x) of every module of the group, in the same launch
+            for (int j = 0; j < 3; ++j) {
+                const int mod = groups_mods[g][j];
+                if (mod < 0) continue;
+                if ((rc = a_map(&p.tm_a[p.sh_nseg], mod))) return rc;
+                p.sh_out[p.sh_nseg] = c->d_hm[mod];
+                ++p.sh_nseg;
+            }
+        }
         if (g == kGroupQKV) {
             p.mode = TC_QKV_ROPE;
             p.n_sub = 1;
@@ -285,9 +265,8 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
                     if ((rc = b_map(&p.tm_lb[j], groups_mods[g][j]))) return rc;
                     if ((rc = h_map(&p.tm_lh[j], groups_mods[g][j]))) return rc;
                 }
-                tiles += p.seg_tiles[j];
             }
-            p.out[0] = c->d_q;
+            p.out[0] = p.out[1] = p.out[2] = c->d_q;
             p.ld_out = (int)c->QD;
             p.rope = c->d_rope;
             p.k_pool = c->k_pool;
@@ -314,7 +293,6 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
             p.seg_module[0] = AOS_MOD_GATE;
             p.out[0] = c->d_act;
             p.ld_out = (int)I;
-            tiles = p.seg_tiles[0];
         } else {
             const int mod = g == kGroupO ? AOS_MOD_O : AOS_MOD_DOWN;
             p.mode = TC_RESID_BF16;
@@ -330,25 +308,14 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
             p.seg_module[0] = mod;
             p.resid = c->d_hidden;
             p.ld_out = (int)H;
-            tiles = p.seg_tiles[0];
         }
-        p.splits = splits_for(tiles, p.kb);
         if ((rc = tc_prepare(p, smem_budget))) return rc;
-        lp.gemm_grid[g] = std::min(tiles * p.splits, tc_num_sms());
-        // Diagnostics: AOS_TC_TRACE=<0..7> traces layer 0's GEMM g (0..3) or shrink g-4.
-        if (const char* tv = getenv("AOS_TC_TRACE")) {
-            const int want = atoi(tv);
-            if (layer == 0 && c->d_trace) {
-                if (want == g) p.trace = c->d_trace;
-                if (want == g + 4) lp.shrink[g].trace = c->d_trace;
-            }
-        }
+        lp.gemm_grid[g] = tc_num_sms();
+        // Diagnostics: AOS_TC_TRACE=<0..3> traces layer 0's GEMM g.
+        if (const char* tv = getenv("AOS_TC_TRACE"))
+            if (layer == 0 && c->d_trace && atoi(tv) == g) p.trace = c->d_trace;
     }
     return AOS_OK;
-}
-
-size_t ws_need(const TcParams& p, int tiles) {
-    return p.splits > 1 ? (size_t)tiles * p.splits * p.n_sub * p.T_pad * 128 * 4 : 0;
 }
 
 int get_plan(aos_ctx* c, int T, StepPlan** out) {
@@ -377,6 +344,8 @@ int get_plan(aos_ctx* c, int T, StepPlan** out) {
     p.err = c->d_err;
     p.ws = c->d_ws;
     p.counters = c->d_counters;
+    p.tile_slots = c->d_tile_slots;
+    p.sync = c->d_sync;
     const uint32_t V = c->cfg.vocab;
     int rc = tc_encode_2d(&p.tm_w[0], c->lm_head, c->cfg.hidden, V, (uint64_t)c->cfg.hidden * 2, 64, 128, 128);
     rc |= tc_encode_2d(&p.tm_x, c->d_normed, c->cfg.hidden, (uint64_t)c->T_cap, (uint64_t)c->cfg.hidden * 2, 64,
@@ -386,18 +355,12 @@ int get_plan(aos_ctx* c, int T, StepPlan** out) {
     p.seg_rows[0] = (int)V;
     p.out[0] = c->d_logits;
     p.ld_out = (int)V;
-    p.splits = 1;
     if ((rc = tc_prepare(p, 227 * 1024))) return c->fail(rc, "lm_head plan");
-    plan->lm_grid = std::min(p.seg_tiles[0], tc_num_sms());
-    // workspace for split-K partials
-    size_t need = 0;
+    plan->lm_grid = tc_num_sms();
+    // workspace for the fp32 partials of tiles cut between CTAs
+    size_t need = tc_ws_bytes(p, plan->lm_grid);
     for (auto& lp : plan->layers)
-        for (int g = 0; g < 4; ++g) {
-            int tiles = 0;
-            for (int j = 0; j < lp.gemm[g].n_seg; ++j) tiles += lp.gemm[g].seg_tiles[j];
-            need = std::max(need, ws_need(lp.gemm[g], tiles));
-            need = std::max(need, ws_need(lp.shrink[g], lp.shrink[g].n_seg * (c->R / 128 + 1)));
-        }
+        for (int g = 0; g < 4; ++g) need = std::max(need, tc_ws_bytes(lp.gemm[g], lp.gemm_grid[g]));
     if (need > c->ws_bytes) {
         if (c->d_ws) cudaFree(c->d_ws);
         c->d_ws = nullptr;
@@ -407,10 +370,14 @@ int get_plan(aos_ctx* c, int T, StepPlan** out) {
         // all cached plans point at the workspace: refresh them
         for (auto& kv : c->plans)
             for (auto& lp : kv.second->layers)
-                for (int g = 0; g < 4; ++g) lp.gemm[g].ws = lp.shrink[g].ws = c->d_ws;
-        for (auto& kv : c->plans) kv.second->graph_valid = false;
+                for (int g = 0; g < 4; ++g) lp.gemm[g].ws = c->d_ws;
+        for (auto& kv : c->plans) {
+            kv.second->lm_head.ws = c->d_ws;
+            kv.second->graph_valid = false;
+        }
         for (auto& lp : plan->layers)
-            for (int g = 0; g < 4; ++g) lp.gemm[g].ws = lp.shrink[g].ws = c->d_ws;
+            for (int g = 0; g < 4; ++g) lp.gemm[g].ws = c->d_ws;
+        p.ws = c->d_ws;
     }
     *out = plan.get();
     c->plans[T] = std::move(plan);
@@ -442,20 +409,14 @@ int enqueue_layer(aos_ctx* c, const StepPlan& plan, int layer, cudaStream_t s) {
     const int T = plan.T;
     const uint32_t H = c->cfg.hidden;
     PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(c->d_hidden, c->attn_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
-    if (lp.shrink_grid[kGroupQKV])
-        PLAUNCH(c, AOS_K_SHRINK, s, tc_launch(lp.shrink[kGroupQKV], lp.shrink_grid[kGroupQKV], s));
     PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupQKV], lp.gemm_grid[kGroupQKV], s));
     PLAUNCH(c, AOS_K_ATTN, s,
             launch_attention(c->tm_k, c->tm_v, c->d_q, c->d_block_tables, c->d_ctx_lens, c->d_attn_part, c->d_attn_ml, T,
                              (int)c->cfg.n_heads, (int)c->cfg.n_kv_heads, layer, (int)c->cfg.kv_num_blocks, c->max_blocks,
                              c->attn_chunks, c->d_err, c->d_attn, s));
-    if (lp.shrink_grid[kGroupO]) PLAUNCH(c, AOS_K_SHRINK, s, tc_launch(lp.shrink[kGroupO], lp.shrink_grid[kGroupO], s));
     PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupO], lp.gemm_grid[kGroupO], s));
     PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(c->d_hidden, c->mlp_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
-    if (lp.shrink_grid[kGroupGU])
-        PLAUNCH(c, AOS_K_SHRINK, s, tc_launch(lp.shrink[kGroupGU], lp.shrink_grid[kGroupGU], s));
     PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupGU], lp.gemm_grid[kGroupGU], s));
-    if (lp.shrink_grid[kGroupD]) PLAUNCH(c, AOS_K_SHRINK, s, tc_launch(lp.shrink[kGroupD], lp.shrink_grid[kGroupD], s));
     PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupD], lp.gemm_grid[kGroupD], s));
     return AOS_OK;
 }
@@ -549,6 +510,10 @@ int run_step_device(aos_ctx* c, int T, bool with_logits, cudaStream_t s) {
 // Resolve sequences to page tables and positions for a step (host side).
 int stage_sequences(aos_ctx* c, const uint64_t* seq_ids, uint32_t T) {
     if (T > (uint32_t)c->cfg.max_batch) return c->fail(AOS_ERR_INVALID, "T exceeds max_batch");
+    c->stage_slot = (c->stage_slot + 1) % aos_ctx::kStageSlots;
+    CTX_CUDA(c, cudaEventSynchronize(c->stage_ev[c->stage_slot]));  // its previous copy has been read
+    c->h_block_tables = c->h_stage[c->stage_slot];
+    c->h_ctx_lens = c->h_block_tables + (size_t)c->T_cap * c->max_blocks;
     for (uint32_t t = 0; t < T; ++t) {
         auto it = c->seqs.find(seq_ids[t]);
         if (it == c->seqs.end()) return c->fail(AOS_ERR_NOT_FOUND, "unknown sequence id " + std::to_string(seq_ids[t]));
@@ -568,6 +533,7 @@ int upload_tables(aos_ctx* c, uint32_t T, cudaStream_t s) {
     CTX_CUDA(c, cudaMemcpyAsync(c->d_block_tables, c->h_block_tables, (size_t)T * c->max_blocks * 4,
                                 cudaMemcpyHostToDevice, s));
     CTX_CUDA(c, cudaMemcpyAsync(c->d_ctx_lens, c->h_ctx_lens, (size_t)T * 4, cudaMemcpyHostToDevice, s));
+    CTX_CUDA(c, cudaEventRecord(c->stage_ev[c->stage_slot], s));
     return AOS_OK;
 }
 
@@ -580,7 +546,22 @@ void advance(aos_ctx* c, const uint64_t* seq_ids, uint32_t T) {
 int check_device_error(aos_ctx* c) {
     int e = 0;
     CTX_CUDA(c, cudaMemcpy(&e, c->d_err, 4, cudaMemcpyDeviceToHost));
-    if (e) return c->fail(e, "a bounded device-side wait timed out (the kernel returned early)");
+    if (e) {
+        // The failed launch may have left tile counters and the shrink
+        // counter part-way: clear them so the next step starts clean.
+        cudaDeviceSynchronize();  // nothing of this context may still be running
+        size_t tiles = 0;
+        {
+            const size_t rows = std::max<size_t>({(size_t)c->QD + 2 * c->KVD, c->cfg.intermediate, c->cfg.hidden,
+                                                  c->cfg.vocab});
+            tiles = (rows + 127) / 128 + 3 * ((size_t)c->R / 128 + 1);
+        }
+        cudaMemset(c->d_counters, 0, 2 * tiles * sizeof(int));
+        cudaMemset(c->d_sync, 0, 2 * sizeof(int));
+        cudaMemset(c->d_err, 0, sizeof(int));
+        cudaDeviceSynchronize();
+        return c->fail(e, "a bounded device-side wait timed out or a launch limit was exceeded (the kernel returned early)");
+    }
     return AOS_OK;
 }
 
@@ -698,8 +679,12 @@ aos_ctx* aos_init(const aos_model_config* cfg) {
     INIT_CHECK(dalloc(&c->d_n_groups, 1), "n_groups");
     INIT_CHECK(dalloc(&c->d_block_tables, TC * c->max_blocks), "block tables");
     INIT_CHECK(dalloc(&c->d_ctx_lens, TC), "ctx lens");
-    INIT_CHECK(cudaMallocHost((void**)&c->h_block_tables, TC * c->max_blocks * 4), "pinned tables");
-    INIT_CHECK(cudaMallocHost((void**)&c->h_ctx_lens, TC * 4), "pinned lens");
+    for (int i = 0; i < aos_ctx::kStageSlots; ++i) {
+        INIT_CHECK(cudaMallocHost((void**)&c->h_stage[i], (TC * c->max_blocks + TC) * 4), "pinned tables");
+        INIT_CHECK(cudaEventCreateWithFlags(&c->stage_ev[i], cudaEventDisableTiming), "staging event");
+    }
+    c->h_block_tables = c->h_stage[0];
+    c->h_ctx_lens = c->h_block_tables + TC * c->max_blocks;
     INIT_CHECK(dalloc(&c->d_rings, TC), "rings");
     INIT_CHECK(dalloc(&c->d_tokens, TC), "tokens");
     INIT_CHECK(dalloc(&c->d_logits, TC * V), "logits");
@@ -707,7 +692,13 @@ aos_ctx* aos_init(const aos_model_config* cfg) {
     c->attn_chunks = attn_max_chunks((int)k.max_seq_len);
     INIT_CHECK(dalloc(&c->d_attn_part, TC * k.n_kv_heads * c->attn_chunks * c->G * 128), "attn part");
     INIT_CHECK(dalloc(&c->d_attn_ml, TC * k.n_kv_heads * c->attn_chunks * c->G * 2), "attn ml");
-    INIT_CHECK(dalloc(&c->d_counters, 1 << 16), "counters");
+    {  // tiles of the largest launch: base tiles plus up to three shrink segments
+        const size_t rows = std::max<size_t>({(size_t)c->QD + 2 * c->KVD, I, H, V});
+        const size_t tiles = (rows + 127) / 128 + 3 * ((size_t)c->R / 128 + 1);
+        INIT_CHECK(dalloc(&c->d_counters, 2 * tiles), "counters");
+        INIT_CHECK(dalloc(&c->d_tile_slots, tiles * kMaxPiecesPerTile), "tile slots");
+        INIT_CHECK(dalloc(&c->d_sync, 2), "sync");
+    }
     INIT_CHECK(dalloc(&c->d_err, 1), "err");
     if (getenv("AOS_TC_TRACE")) INIT_CHECK(dalloc(&c->d_trace, (size_t)tc_num_sms() * kTraceStride), "trace");
     // RoPE table, angles as the reference computes them (mlx_cpp_wrapper_real.cpp:3249-3268)
@@ -767,9 +758,11 @@ void aos_destroy(aos_ctx* c) {
     f(c->d_hidden); f(c->d_normed); f(c->d_q); f(c->d_attn); f(c->d_act);
     f(c->d_groups); f(c->d_n_groups); f(c->d_block_tables); f(c->d_ctx_lens);
     f(c->d_rings); f(c->d_tokens); f(c->d_logits); f(c->d_rope);
-    f(c->d_attn_part); f(c->d_attn_ml); f(c->d_ws); f(c->d_counters); f(c->d_err); f(c->d_trace);
-    if (c->h_block_tables) cudaFreeHost(c->h_block_tables);
-    if (c->h_ctx_lens) cudaFreeHost(c->h_ctx_lens);
+    f(c->d_attn_part); f(c->d_attn_ml); f(c->d_ws); f(c->d_counters); f(c->d_tile_slots); f(c->d_sync); f(c->d_err); f(c->d_trace);
+    for (int i = 0; i < aos_ctx::kStageSlots; ++i) {
+        if (c->h_stage[i]) cudaFreeHost(c->h_stage[i]);
+        if (c->stage_ev[i]) cudaEventDestroy(c->stage_ev[i]);
+    }
     if (c->ev0) cudaEventDestroy(c->ev0);
     if (c->ev1) cudaEventDestroy(c->ev1);
     for (auto e : c->prof_ev) cudaEventDestroy(e);

@@ -1,26 +1,33 @@
-// tc_gemm.cu — tcgen05/TMEM/TMA weight-streaming GEMM with the LoRA expand
-// fused into the same accumulator, and the decoder's epilogues.
+// tc_gemm.cu — tcgen05/TMEM/TMA weight-streaming GEMM with the LoRA shrink
+// and expand fused into the same launch, and the decoder's epilogues.
 //
-// Per 128-row output tile (MMA M = weight rows, N = decode tokens, "swap-AB"):
-//   base steps : TMA W[128 x 64] + X[T x 64] (SWIZZLE_128B) -> 4 MMAs (K=16)
-//   LoRA steps : TMA lora_B[128 rows x one 64-column rank group] + gated H
-//                [T x the same group] (SWIZZLE_128B) -> 4 MMAs (K=16)
-// so the tile's accumulator ends as  W x + sum_a B_a (g_a * scale_a * A_a x)
-// (mlx_cpp_wrapper_real.cpp:3372-3419) without ever materialising the LoRA
-// delta.  The shrink GEMM (H = A_cat x) is the same kernel with lora_A rows
-// gathered group by group and the TC_SHRINK_HM epilogue.
+// One launch computes, for one input X (normed hidden, attention output or
+// SwiGLU activation):
+//   shrink tiles : hm[t, group cols] = gate(t, owner) * (A_cat[group rows] . x_t)
+//                  for every touched 64-column rank group of every LoRA module
+//                  that reads X (TC_SHRINK_HM epilogue);
+//   base tiles   : W[128 rows] . X^T  +  sum over touched groups of
+//                  B_cat[128 rows, group cols] . hm[group cols]^T
+// so a base tile's accumulator ends as  W x + sum_a B_a (g_a * scale_a * A_a x)
+// (mlx_cpp_wrapper_real.cpp:3372-3419) without materialising the LoRA delta.
+// MMA M = 128 weight rows, N = decode tokens ("swap-AB").
+//   K step      : TMA W[128 x 64] (or two lora_A group boxes [64 x 64]) + X[T x 64]
+//   expand step : TMA lora_B[128 rows x one group] + hm[T x the same group]
+// all SWIZZLE_128B, four K=16 MMAs per step and sub-tile.
 //
-// Roles (192 threads, one CTA per SM, persistent over work units):
+// Roles (192 threads, one CTA per SM, grid = SM count):
 //   warp 0      : TMA producer (one elected lane)
 //   warp 1      : TMEM allocator + MMA issuer (one elected lane)
 //   warps 2..5  : epilogue, TMEM lane quarter = warp % 4
-// Work unit = (segment, tile, split); splits > 1 write fp32 partials and the
-// last-arriving CTA of a tile reduces them in split order (fixed order, so the
-// result is bit-identical run to run; no float atomics).
+// Work is split stream-K style (see "schedule" below): every CTA streams the
+// same number of steps, a tile cut between CTAs is finished by the last piece
+// to arrive, which sums the pieces' fp32 partials in piece order (fixed order,
+// so the result is bit-identical run to run; no float atomics).  Expand steps
+// wait until every shrink tile of the launch has been written.
 //
-// Every mbarrier wait is bounded (kSpinLimitCycles): on timeout the kernel
-// records AOS_ERR_TIMEOUT in p.err, drains its own TMA copies and MMAs, frees
-// TMEM and returns.
+// Every wait is bounded (kSpinLimitCycles): on timeout the kernel records
+// AOS_ERR_TIMEOUT in p.err, drains its own TMA copies and MMAs, frees TMEM and
+// returns.
 
 #include <algorithm>
 #include <cstring>
@@ -156,46 +163,6 @@ __device__ __forceinline__ unsigned long long gtimer() {
     return t;
 }
 
-// ---------------------------------------------------------------- work units
-struct Unit {
-    int seg, tile, tile_global, split, step0, step1;
-};
-
-struct Sched {
-    int n_groups, lora_steps, total_steps, units;
-    int tiles[kTcMaxSets];
-};
-
-__device__ __forceinline__ Sched make_sched(const TcParams& p) {
-    Sched s;
-    s.n_groups = (p.lora || p.shrink) ? __ldg(p.n_groups) : 0;
-    s.lora_steps = p.lora ? s.n_groups : 0;  // one 64-column rank group per step
-    s.total_steps = p.kb + s.lora_steps;
-    s.units = 0;
-    for (int g = 0; g < kTcMaxSets; ++g) {
-        s.tiles[g] = g < p.n_seg ? (p.shrink ? cdiv(s.n_groups, kShrinkGroupsPerTile) : p.seg_tiles[g]) : 0;
-        s.units += s.tiles[g] * p.splits;
-    }
-    return s;
-}
-
-__device__ __forceinline__ Unit unit_of(const TcParams& p, const Sched& s, int u) {
-    Unit r;
-    int tile_u = u / p.splits;
-    r.split = u % p.splits;
-    int base = 0;
-    r.seg = 0;
-    while (r.seg < p.n_seg - 1 && tile_u >= s.tiles[r.seg]) {
-        tile_u -= s.tiles[r.seg];
-        base += s.tiles[r.seg];
-        ++r.seg;
-    }
-    r.tile = tile_u;
-    r.tile_global = base + tile_u;
-    r.step0 = (int)((long long)r.split * s.total_steps / p.splits);
-    r.step1 = (int)((long long)(r.split + 1) * s.total_steps / p.splits);
-    return r;
-}
 
 // ---------------------------------------------------------------- epilogue
 struct EpiSmem {
@@ -207,22 +174,21 @@ struct EpiSmem {
 // 128 epilogue threads (RoPE uses a named barrier).  Every loop is fully
 // unrolled with predicates, and all loads of a chunk are issued before its
 // stores, so a chunk costs one or two memory latencies, not 32.
-__device__ __forceinline__ void epilogue_chunk(const TcParams& p, const EpiSmem& es, const Unit& u, const Sched& sc,
-                                               int row, int t0, float (&v)[2][32]) {
-    const int seg = u.seg;
-    const int col = p.seg_out0[seg] + u.tile * kTcBM + row;
-    if (p.mode != TC_SHRINK_HM && p.mode != TC_QKV_ROPE && u.tile * kTcBM + row >= p.seg_rows[seg]) return;
+__device__ __forceinline__ void epilogue_chunk(const TcParams& p, const EpiSmem& es, int mode, int seg, int tile,
+                                               void* out_base, int ng, int row, int t0, float (&v)[2][32]) {
+    const int col = p.seg_out0[seg] + tile * kTcBM + row;
+    if (mode != TC_SHRINK_HM && mode != TC_QKV_ROPE && tile * kTcBM + row >= p.seg_rows[seg]) return;
     const int nt = min(32, p.T - t0);  // valid tokens in this chunk
-    switch (p.mode) {
+    switch (mode) {
         case TC_STORE_BF16: {
-            uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]) + (size_t)t0 * p.ld_out + col;
+            uint16_t* o = reinterpret_cast<uint16_t*>(out_base) + (size_t)t0 * p.ld_out + col;
 #pragma unroll
             for (int j = 0; j < 32; ++j)
                 if (j < nt) o[(size_t)j * p.ld_out] = f2bf(v[0][j]);
             break;
         }
         case TC_STORE_F32: {
-            float* o = reinterpret_cast<float*>(p.out[seg]) + (size_t)t0 * p.ld_out + col;
+            float* o = reinterpret_cast<float*>(out_base) + (size_t)t0 * p.ld_out + col;
 #pragma unroll
             for (int j = 0; j < 32; ++j)
                 if (j < nt) o[(size_t)j * p.ld_out] = v[0][j];
@@ -239,7 +205,7 @@ __device__ __forceinline__ void epilogue_chunk(const TcParams& p, const EpiSmem&
             break;
         }
         case TC_SWIGLU: {
-            uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]) + (size_t)t0 * p.ld_out + col;
+            uint16_t* o = reinterpret_cast<uint16_t*>(out_base) + (size_t)t0 * p.ld_out + col;
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
                 const float g = v[0][j], up = v[1][j];
@@ -272,13 +238,13 @@ __device__ __forceinline__ void epilogue_chunk(const TcParams& p, const EpiSmem&
                 epi_bar();
             }
             if (module == AOS_MOD_Q) {
-                uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]) + (size_t)t0 * p.ld_out + col;
+                uint16_t* o = reinterpret_cast<uint16_t*>(out_base) + (size_t)t0 * p.ld_out + col;
 #pragma unroll
                 for (int j = 0; j < 32; ++j)
                     if (j < nt) o[(size_t)j * p.ld_out] = f2bf(v[0][j]);
             } else {
                 uint16_t* pool = module == AOS_MOD_K ? p.k_pool : p.v_pool;
-                const int kvh = u.tile;  // one tile per kv head (head_dim == 128)
+                const int kvh = tile;  // one tile per kv head (head_dim == 128)
                 int blk[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j)
@@ -294,8 +260,8 @@ __device__ __forceinline__ void epilogue_chunk(const TcParams& p, const EpiSmem&
             break;
         }
         case TC_SHRINK_HM: {
-            const int slot = u.tile * kShrinkGroupsPerTile + row / kGroup;
-            if (slot >= sc.n_groups) break;
+            const int slot = tile * kShrinkGroupsPerTile + row / kGroup;
+            if (slot >= ng) break;
             const int c = __ldg(p.groups + slot) * kGroup + row % kGroup;
             const int owner = __ldg(p.col_owner + c);
             // per-token gate * alpha/rank of the column's adapter (0 when the
@@ -304,7 +270,7 @@ __device__ __forceinline__ void epilogue_chunk(const TcParams& p, const EpiSmem&
             float cf[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) cf[j] = (owner >= 0 && j < nt) ? __ldg(ct + (size_t)j * p.max_adapters) : 0.0f;
-            uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]) + (size_t)t0 * p.R + c;
+            uint16_t* o = reinterpret_cast<uint16_t*>(out_base) + (size_t)t0 * p.R + c;
 #pragma unroll
             for (int j = 0; j < 32; ++j)
                 if (j < nt) o[(size_t)j * p.R] = f2bf(v[0][j] * cf[j]);
@@ -312,6 +278,132 @@ __device__ __forceinline__ void epilogue_chunk(const TcParams& p, const EpiSmem&
         }
         default:
             break;
+    }
+}
+
+
+// ---------------------------------------------------------------- schedule
+// Stream-K over two pools.  Pool A holds the K steps of the shrink tiles
+// (64-column blocks of the input against two touched lora_A groups); pool B
+// holds the steps of the base tiles, each tile's K steps followed by its
+// expand steps (one per touched rank group).  CTA c takes the contiguous slice
+// [c*P/G, (c+1)*P/G) of pool A and then of pool B, so every SM streams the
+// same amount, every SM finishes its shrink share first, and only the expand
+// steps (which read the shrink output) wait for the shrink tiles.  A tile cut
+// between CTAs is finished by the piece that arrives last: it waits until the
+// other pieces have stored their fp32 partials and sums them with its own
+// accumulator in piece order.
+struct Sched {
+    int ng;            // touched rank groups
+    int kb;            // K steps per tile
+    int lenB;          // steps per base tile (K steps + expand steps)
+    int sh_per_seg;    // shrink tiles per shrink segment
+    int n_sh, n_base;  // shrink tiles, base tiles
+    long long PA, PB;  // pool lengths in steps
+    int GA, GB;        // CTAs that take part in each pool (<= pool length)
+};
+
+struct Piece {
+    int tile;          // global tile id: shrink tiles first, then base tiles
+    int s0, s1;        // step range within the tile
+    int idx, n;        // piece index within the tile, pieces of the tile in total
+    bool shrink;
+    int seg, t;        // segment, and tile index within the segment
+};
+
+__device__ __forceinline__ Sched make_sched(const TcParams& p) {
+    Sched s;
+    s.ng = (p.lora || p.sh_nseg) ? __ldg(p.n_groups) : 0;
+    s.kb = p.kb;
+    s.lenB = p.kb + (p.lora ? s.ng : 0);
+    s.sh_per_seg = p.sh_nseg ? cdiv(s.ng, kShrinkGroupsPerTile) : 0;
+    s.n_sh = p.sh_nseg * s.sh_per_seg;
+    s.n_base = 0;
+    for (int g = 0; g < p.n_seg; ++g) s.n_base += p.seg_tiles[g];
+    s.PA = (long long)s.n_sh * s.kb;
+    s.PB = (long long)s.n_base * s.lenB;
+    // Every slice is at least len/kMaxPiecesPerPool steps long, so no tile is
+    // cut into more than kMaxPiecesPerPool + 1 pieces.
+    const long long la = max(1, cdiv(s.kb, kMaxPiecesPerPool));
+    const long long lb = max(1, cdiv(s.lenB, kMaxPiecesPerPool));
+    s.GA = s.PA > 0 ? (int)max(1ll, min((long long)gridDim.x, s.PA / la)) : 0;
+    s.GB = (int)max(1ll, min((long long)gridDim.x, s.PB / lb));
+    return s;
+}
+__device__ __forceinline__ long long pstart(int c, long long P, int G) { return (long long)c * P / G; }
+// CTA whose slice of a pool (length P, G CTAs) contains step s.
+__device__ __forceinline__ int cta_of(long long s, long long P, int G) { return (int)(((s + 1) * G - 1) / P); }
+
+__device__ __forceinline__ void tile_info(const TcParams& p, const Sched& sc, int tile, Piece& pc) {
+    pc.tile = tile;
+    if (tile < sc.n_sh) {
+        pc.shrink = true;
+        pc.seg = tile / sc.sh_per_seg;
+        pc.t = tile % sc.sh_per_seg;
+    } else {
+        pc.shrink = false;
+        int b = tile - sc.n_sh, g = 0;
+        while (g < p.n_seg - 1 && b >= p.seg_tiles[g]) {
+            b -= p.seg_tiles[g];
+            ++g;
+        }
+        pc.seg = g;
+        pc.t = b;
+    }
+}
+
+// Iterates this CTA's pieces in order (pool A, then pool B).  All three roles
+// walk the same sequence.
+struct PieceIter {
+    int pool;
+    long long s, e;  // current step, end of this CTA's slice
+    __device__ __forceinline__ void init(const Sched& sc) {
+        pool = 0;
+        const int c = blockIdx.x;
+        s = c < sc.GA ? pstart(c, sc.PA, sc.GA) : 0;
+        e = c < sc.GA ? pstart(c + 1, sc.PA, sc.GA) : 0;
+    }
+    __device__ __forceinline__ bool next(const TcParams& p, const Sched& sc, Piece& pc) {
+        while (s >= e) {
+            if (pool == 1) return false;
+            pool = 1;
+            const int c = blockIdx.x;
+            s = c < sc.GB ? pstart(c, sc.PB, sc.GB) : 0;
+            e = c < sc.GB ? pstart(c + 1, sc.PB, sc.GB) : 0;
+        }
+        const long long P = pool == 0 ? sc.PA : sc.PB;
+        const int G = pool == 0 ? sc.GA : sc.GB;
+        const int len = pool == 0 ? sc.kb : sc.lenB;
+        const int local_tile = (int)(s / len);
+        const long long tstart = (long long)local_tile * len;
+        const long long tend = min(tstart + len, e);
+        tile_info(p, sc, pool == 0 ? local_tile : local_tile + sc.n_sh, pc);
+        pc.s0 = (int)(s - tstart);
+        pc.s1 = (int)(tend - tstart);
+        const int c0 = cta_of(tstart, P, G);
+        pc.n = cta_of(tstart + len - 1, P, G) - c0 + 1;
+        pc.idx = (int)blockIdx.x - c0;
+        s = tend;
+        return true;
+    }
+};
+
+// Bounded spin until *ptr >= target (acquire); false on timeout or when
+// another role already failed.
+__device__ __noinline__ bool spin_ge(const int* ptr, int target, int* err) {
+    const long long t0 = clock64();
+    uint32_t n = 0;
+    while (true) {
+        int v;
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+        if (v >= target) return true;
+        if ((++n & 255u) == 0) {
+            if (*(volatile int*)err != 0) return false;
+            if (clock64() - t0 > kSpinLimitCycles) {
+                atomicCAS(err, 0, AOS_ERR_TIMEOUT);
+                return false;
+            }
+        }
     }
 }
 
@@ -368,9 +460,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     if (warp == 0) {
         // ============================ TMA producer ============================
         // The weight-side boxes (W, lora_A, lora_B) of the first NS stages are
-        // issued before pdl_wait(): weights are static, and the group list was
-        // written two or more launches earlier.  The activation-side boxes (X, hm)
-        // of those stages follow once the previous launch has completed.
+        // issued before pdl_wait(): weights are static and the group list was
+        // written two or more launches earlier.  The activation-side boxes (X,
+        // hm) follow once the previous launch has completed; hm boxes also wait
+        // until every shrink tile of this launch is finished.
         if (lane == 0) {
             const uint64_t pol_w = policy_evict_first();
             const uint64_t pol_x = policy_evict_last();
@@ -379,73 +472,81 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             int n_issued = 0;
             int stage = 0;
             uint32_t phase = 0;
-            bool ok = true;
-            bool waited = false;
-            int pre_step[16], pre_unit[16];
+            bool ok = true, waited = false, shrink_ready = (sc.n_sh == 0);
+            int pre_tile[16], pre_step[16];
             int n_pre = 0;
-            // weight-side boxes of one step; returns the step's total transaction bytes
-            auto step_bytes = [&](const Unit& u, int step) -> uint32_t {
-                if (step >= p.kb) return (uint32_t)(p.n_sub * (kTcBM * 128 + p.T_pad * 128));
-                if (p.shrink) {
-                    const int nv = min(kShrinkGroupsPerTile, sc.n_groups - u.tile * kShrinkGroupsPerTile);
+            auto step_bytes = [&](const Piece& pc, int st) -> uint32_t {
+                if (pc.shrink) {
+                    const int nv = min(kShrinkGroupsPerTile, sc.ng - pc.t * kShrinkGroupsPerTile);
                     return (uint32_t)(nv * kGroup * 128 + p.T_pad * 128);
                 }
+                if (st >= sc.kb) return (uint32_t)(p.n_sub * (kTcBM * 128 + p.T_pad * 128));
                 return (uint32_t)(p.n_sub * kTcBM * 128 + p.T_pad * 128);
             };
-            auto issue_w = [&](const Unit& u, int step, uint32_t sbase, uint32_t fb) {
-                if (step < p.kb) {
-                    const int kx = step * kTcBK;
-                    if (p.shrink) {  // lora_A rows of the tile's (up to) two touched groups
-                        const int first = u.tile * kShrinkGroupsPerTile;
-                        const int nv = min(kShrinkGroupsPerTile, sc.n_groups - first);
-                        for (int q = 0; q < nv; ++q)
-                            tma_2d(&p.tm_w[u.seg], sbase + q * (kGroup * 128), fb, kx,
-                                   __ldg(p.groups + first + q) * kGroup, pol_w);
-                    } else {
-                        for (int sub = 0; sub < p.n_sub; ++sub)
-                            tma_2d(&p.tm_w[u.seg * p.n_sub + sub], sbase + sub * (kTcBM * 128), fb, kx,
-                                   p.seg_wrow0[u.seg] + u.tile * kTcBM, pol_w);
-                    }
-                } else {  // LoRA expand: lora_B[tile rows, group cols]
-                    const int gcol = __ldg(p.groups + (step - p.kb)) * kGroup;
+            auto issue_w = [&](const Piece& pc, int st, uint32_t sbase, uint32_t fb) {
+                if (pc.shrink) {  // lora_A rows of the tile's (up to) two touched groups
+                    const int first = pc.t * kShrinkGroupsPerTile;
+                    const int nv = min(kShrinkGroupsPerTile, sc.ng - first);
+                    for (int q = 0; q < nv; ++q)
+                        tma_2d(&p.tm_a[pc.seg], sbase + q * (kGroup * 128), fb, st * kTcBK,
+                               __ldg(p.groups + first + q) * kGroup, pol_w);
+                } else if (st < sc.kb) {
                     for (int sub = 0; sub < p.n_sub; ++sub)
-                        tma_2d(&p.tm_lb[u.seg * p.n_sub + sub], sbase + sub * (kTcBM * 128), fb, gcol, u.tile * kTcBM,
+                        tma_2d(&p.tm_w[pc.seg * p.n_sub + sub], sbase + sub * (kTcBM * 128), fb, st * kTcBK,
+                               p.seg_wrow0[pc.seg] + pc.t * kTcBM, pol_w);
+                } else {  // LoRA expand: lora_B[tile rows, group cols]
+                    const int gcol = __ldg(p.groups + (st - sc.kb)) * kGroup;
+                    for (int sub = 0; sub < p.n_sub; ++sub)
+                        tma_2d(&p.tm_lb[pc.seg * p.n_sub + sub], sbase + sub * (kTcBM * 128), fb, gcol, pc.t * kTcBM,
                                pol_w);
                 }
             };
-            auto issue_x = [&](const Unit& u, int step, uint32_t sbase, uint32_t fb) {
+            auto issue_x = [&](const Piece& pc, int st, uint32_t sbase, uint32_t fb) -> bool {
                 const uint32_t act = sbase + p.act_off;
-                if (step < p.kb) {
-                    tma_2d(&p.tm_x, act, fb, step * kTcBK, 0, pol_x);
-                } else {  // gated shrink output hm[tokens, group cols] of each sub-tile
-                    const int gcol = __ldg(p.groups + (step - p.kb)) * kGroup;
-                    for (int sub = 0; sub < p.n_sub; ++sub)
-                        tma_2d(&p.tm_lh[u.seg * p.n_sub + sub], act + sub * (p.T_pad * 128), fb, gcol, 0, pol_x);
+                if (pc.shrink || st < sc.kb) {
+                    tma_2d(&p.tm_x, act, fb, st * kTcBK, 0, pol_x);
+                    return true;
                 }
+                if (!shrink_ready) {  // hm is written by this launch's shrink tiles
+                    if (tr) tr[198] = gtimer();
+                    if (!spin_ge(p.sync, sc.n_sh, p.err)) return false;
+                    asm volatile("fence.proxy.async.global;" ::: "memory");
+                    if (tr) tr[199] = gtimer();
+                    shrink_ready = true;
+                }
+                const int gcol = __ldg(p.groups + (st - sc.kb)) * kGroup;
+                for (int sub = 0; sub < p.n_sub; ++sub)
+                    tma_2d(&p.tm_lh[pc.seg * p.n_sub + sub], act + sub * (p.T_pad * 128), fb, gcol, 0, pol_x);
+                return true;
             };
-            auto finish_wait = [&]() {
+            auto finish_wait = [&]() -> bool {
                 pdl_wait();
                 pdl_trigger();
                 waited = true;
                 for (int i = 0; i < n_pre; ++i) {
-                    const Unit u = unit_of(p, sc, pre_unit[i]);
-                    issue_x(u, pre_step[i], smem_u32(stages + (size_t)i * p.stage_bytes), smem_u32(&full_bar[i]));
+                    Piece pc;
+                    tile_info(p, sc, pre_tile[i], pc);
+                    if (!issue_x(pc, pre_step[i], smem_u32(stages + (size_t)i * p.stage_bytes), smem_u32(&full_bar[i])))
+                        return false;
                 }
+                return true;
             };
-            for (int uidx = blockIdx.x; uidx < sc.units && ok; uidx += gridDim.x) {
-                const Unit u = unit_of(p, sc, uidx);
-                for (int step = u.step0; step < u.step1; ++step) {
-                    if (!waited && n_pre == NS) finish_wait();
+            PieceIter itr;
+            itr.init(sc);
+            Piece pc;
+            while (ok && itr.next(p, sc, pc)) {
+                for (int st = pc.s0; st < pc.s1; ++st) {
+                    if (!waited && n_pre == NS && !finish_wait()) { ok = false; break; }
                     if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, p.err)) { ok = false; break; }
                     const uint32_t fb = smem_u32(&full_bar[stage]);
                     const uint32_t sbase = smem_u32(stages + (size_t)stage * p.stage_bytes);
-                    mbar_expect_tx(fb, step_bytes(u, step));
-                    issue_w(u, step, sbase, fb);
+                    mbar_expect_tx(fb, step_bytes(pc, st));
+                    issue_w(pc, st, sbase, fb);
                     if (waited) {
-                        issue_x(u, step, sbase, fb);
+                        if (!issue_x(pc, st, sbase, fb)) ok = false;
                     } else {  // first round of stages: stage index == n_pre
-                        pre_step[n_pre] = step;
-                        pre_unit[n_pre] = uidx;
+                        pre_tile[n_pre] = pc.tile;
+                        pre_step[n_pre] = st;
                         ++n_pre;
                     }
                     last_phase[stage] = phase;
@@ -453,6 +554,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     if (tr && n_issued < 64) tr[n_issued] = gtimer();
                     ++n_issued;
                     if (++stage == NS) { stage = 0; phase ^= 1u; }
+                    if (!ok) break;
                 }
             }
             if (!waited) finish_wait();
@@ -465,30 +567,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
-            int it = 0;
-            bool ok = true;
-            bool issued_any = false;
-            int n_waited = 0;
-            for (int uidx = blockIdx.x; uidx < sc.units && ok; uidx += gridDim.x, ++it) {
-                const Unit u = unit_of(p, sc, uidx);
+            int it = 0, n_waited = 0;
+            bool ok = true, issued_any = false;
+            PieceIter itr;
+            itr.init(sc);
+            Piece pc;
+            while (ok && itr.next(p, sc, pc)) {
                 const int acc = it % acc_stages;
                 const uint32_t tphase = (uint32_t)((it / acc_stages) & 1);
+                ++it;
                 if (!mbar_wait(smem_u32(&tempty_bar[acc]), tphase ^ 1u, p.err)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d0 = tmem_base + (uint32_t)(acc * cols_per_acc);
+                const int nsub = pc.shrink ? 1 : p.n_sub;
                 bool first = true;
-                for (int step = u.step0; step < u.step1; ++step) {
+                for (int st = pc.s0; st < pc.s1; ++st) {
                     if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.err)) { ok = false; break; }
                     tc_fence_after();
                     if (tr && n_waited < 64) tr[64 + n_waited] = gtimer();
                     ++n_waited;
                     const uint32_t sbase = smem_u32(stages + (size_t)stage * p.stage_bytes);
                     const uint32_t act = sbase + p.act_off;
-                    // base steps share one activation box; LoRA steps have one per sub-tile
-                    const bool lora_step = step >= p.kb;
-                    for (int sub = 0; sub < p.n_sub; ++sub) {
+                    const bool expand = !pc.shrink && st >= sc.kb;
+                    for (int sub = 0; sub < nsub; ++sub) {
                         const uint32_t a0 = sbase + sub * (kTcBM * 128);
-                        const uint32_t b0 = act + (lora_step ? sub * (p.T_pad * 128) : 0);
+                        const uint32_t b0 = act + (expand ? sub * (p.T_pad * 128) : 0);
 #pragma unroll
                         for (int kk = 0; kk < kTcBK / 16; ++kk)
                             umma_bf16(d0 + sub * p.T_pad, desc_sw128(a0 + kk * 32), desc_sw128(b0 + kk * 32), idesc,
@@ -514,9 +617,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
         EpiSmem es{xbuf};
         pdl_wait();  // the epilogue reads and writes activations of the previous launches
-        int it = 0;
-        for (int uidx = blockIdx.x; uidx < sc.units; uidx += gridDim.x, ++it) {
-            const Unit u = unit_of(p, sc, uidx);
+        const size_t slot_floats = (size_t)p.n_sub * p.T_pad * kTcBM;
+        int it = 0, n_partial = 0;
+        PieceIter itr;
+        itr.init(sc);
+        Piece pc;
+        while (itr.next(p, sc, pc)) {
             const int acc = it % acc_stages;
             const uint32_t tphase = (uint32_t)((it / acc_stages) & 1);
             const bool ok = mbar_wait(smem_u32(&tfull_bar[acc]), tphase, p.err);
@@ -524,74 +630,152 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             if (tr && threadIdx.x == 64 && it < 32) tr[128 + it] = gtimer();
             tc_fence_after();
             const uint32_t t_acc = tmem_base + lane_off + (uint32_t)(acc * cols_per_acc);
+            const int mode = pc.shrink ? TC_SHRINK_HM : p.mode;
+            void* out = pc.shrink ? p.sh_out[pc.seg] : p.out[pc.seg];
+            const int nsub = pc.shrink ? 1 : p.n_sub;
+            int* arrived = p.counters + 2 * pc.tile;  // [0] pieces arrived, [1] partials stored
             float v[2][32];
-            if (p.splits == 1) {
+            bool finished = false;  // this piece produced the tile's final output
+            bool last = pc.n == 1;
+            if (!last) {
+                if (threadIdx.x == 64) *flag = (atomicAdd(arrived, 1) == pc.n - 1);
+                epi_bar();
+                last = *flag != 0;
+                epi_bar();  // everyone has read the flag before it can be rewritten
+            }
+            if (pc.n == 1) {
                 for (int t0 = 0; t0 < p.T_pad; t0 += 32) {
                     tmem_ld32(t_acc + t0, v[0]);
-                    if (p.n_sub == 2) tmem_ld32(t_acc + p.T_pad + t0, v[1]);
-                    if (tr && threadIdx.x == 64 && it == 0 && t0 < 64) tr[194 + (t0 >> 5) * 2] = gtimer();
-                    epilogue_chunk(p, es, u, sc, row, t0, v);
-                    if (tr && threadIdx.x == 64 && it == 0 && t0 < 64) tr[195 + (t0 >> 5) * 2] = gtimer();
+                    if (nsub == 2) tmem_ld32(t_acc + p.T_pad + t0, v[1]);
+                    epilogue_chunk(p, es, mode, pc.seg, pc.t, out, sc.ng, row, t0, v);
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
-                if (tr && threadIdx.x == 64 && it < 32) tr[160 + it] = gtimer();
-            } else {
-                // partial -> workspace [tile][split][sub][t][row]
-                const size_t tile_stride = (size_t)p.n_sub * p.T_pad * kTcBM;
-                float* wsu = p.ws + ((size_t)u.tile_global * p.splits + u.split) * tile_stride;
+                finished = true;
+            } else if (!last) {
+                // store the partial in this CTA's next workspace slot [sub][t][row]
+                const bool room = n_partial < kMaxPartialsPerCta && pc.idx < kMaxPiecesPerTile;
+                const int slot = (int)blockIdx.x * kMaxPartialsPerCta + n_partial;
+                n_partial += room ? 1 : 0;
+                float* wsu = p.ws + (size_t)slot * slot_floats;
                 for (int t0 = 0; t0 < p.T_pad; t0 += 32)
 #pragma unroll
                     for (int sub = 0; sub < 2; ++sub) {
-                        if (sub >= p.n_sub) break;
+                        if (sub >= nsub) break;
                         tmem_ld32(t_acc + sub * p.T_pad + t0, v[sub]);
+                        if (room) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) __stcg(wsu + ((size_t)sub * p.T_pad + t0 + j) * kTcBM + row, v[sub][j]);
+                            for (int j = 0; j < 32; ++j)
+                                __stcg(wsu + ((size_t)sub * p.T_pad + t0 + j) * kTcBM + row, v[sub][j]);
+                        }
                     }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
-                if (tr && threadIdx.x == 64 && it < 32) tr[160 + it] = gtimer();
-                __threadfence();
-                epi_bar();
-                if (threadIdx.x == 64) {
-                    const int old = atomicAdd(p.counters + u.tile_global, 1);
-                    *flag = (old == p.splits - 1);
+                if (room) {
+                    if (threadIdx.x == 64) p.tile_slots[(size_t)pc.tile * kMaxPiecesPerTile + pc.idx] = slot;
+                    __threadfence();
+                    epi_bar();
+                    if (threadIdx.x == 64) atomicAdd(arrived + 1, 1);  // publish (after the fence)
+                } else if (threadIdx.x == 64) {
+                    atomicCAS(p.err, 0, AOS_ERR_INVALID);  // schedule limits exceeded
                 }
+            } else {
+                // last piece: wait for the other pieces' partials, then sum in
+                // piece order with this piece's own accumulator (from TMEM)
+                if (threadIdx.x == 64) *flag = spin_ge(arrived + 1, pc.n - 1, p.err) ? 1 : 0;
                 epi_bar();
-                const bool last = *flag != 0;
-                epi_bar();  // everyone has read the flag before it can be rewritten
-                if (!last) continue;
-                __threadfence();
-                const float* wst = p.ws + (size_t)u.tile_global * p.splits * tile_stride;
-                for (int t0 = 0; t0 < p.T_pad; t0 += 32) {
+                const bool ready = *flag != 0;
+                epi_bar();
+                if (ready) {
+                    __threadfence();
+                    for (int t0 = 0; t0 < p.T_pad; t0 += 32) {
 #pragma unroll
-                    for (int sub = 0; sub < 2; ++sub) {
-                        if (sub >= p.n_sub) break;
-                        // sum the splits in split order: ((p0 + p1) + p2) + ...
+                        for (int sub = 0; sub < 2; ++sub) {
+                            if (sub >= nsub) break;
+                            float part[2][32];
+                            int k = 0;
+                            // pieces before this one, two at a time (independent loads in flight)
+                            for (; k < pc.idx; k += 2) {
+                                const bool two = k + 1 < pc.idx;
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) v[sub][j] = 0.0f;
-                        for (int sp = 0; sp < p.splits; ++sp) {
-                            const float* src = wst + (size_t)sp * tile_stride + ((size_t)sub * p.T_pad + t0) * kTcBM + row;
-                            float part[32];
+                                for (int u = 0; u < 2; ++u) {
+                                    if (u == 1 && !two) break;
+                                    const int sl = __ldcg(p.tile_slots + (size_t)pc.tile * kMaxPiecesPerTile + k + u);
+                                    const float* src =
+                                        p.ws + (size_t)sl * slot_floats + ((size_t)sub * p.T_pad + t0) * kTcBM + row;
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) part[j] = __ldcg(src + (size_t)j * kTcBM);
+                                    for (int j = 0; j < 32; ++j) part[u][j] = __ldcg(src + (size_t)j * kTcBM);
+                                }
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) v[sub][j] += part[j];
+                                for (int j = 0; j < 32; ++j) {
+                                    float a = k == 0 ? part[0][j] : v[sub][j] + part[0][j];
+                                    if (two) a += part[1][j];
+                                    v[sub][j] = a;
+                                }
+                            }
+                            // this piece
+                            tmem_ld32(t_acc + sub * p.T_pad + t0, part[0]);
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) v[sub][j] = pc.idx == 0 ? part[0][j] : v[sub][j] + part[0][j];
+                            // pieces after this one
+                            for (k = pc.idx + 1; k < pc.n; k += 2) {
+                                const bool two = k + 1 < pc.n;
+#pragma unroll
+                                for (int u = 0; u < 2; ++u) {
+                                    if (u == 1 && !two) break;
+                                    const int sl = __ldcg(p.tile_slots + (size_t)pc.tile * kMaxPiecesPerTile + k + u);
+                                    const float* src =
+                                        p.ws + (size_t)sl * slot_floats + ((size_t)sub * p.T_pad + t0) * kTcBM + row;
+#pragma unroll
+                                    for (int j = 0; j < 32; ++j) part[u][j] = __ldcg(src + (size_t)j * kTcBM);
+                                }
+#pragma unroll
+                                for (int j = 0; j < 32; ++j) {
+                                    float a = v[sub][j] + part[0][j];
+                                    if (two) a += part[1][j];
+                                    v[sub][j] = a;
+                                }
+                            }
                         }
+                        epilogue_chunk(p, es, mode, pc.seg, pc.t, out, sc.ng, row, t0, v);
                     }
-                    epilogue_chunk(p, es, u, sc, row, t0, v);
+                    finished = true;
                 }
-                if (threadIdx.x == 64) p.counters[u.tile_global] = 0;  // self-reset for the next launch
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
+                if (threadIdx.x == 64) {  // self-reset for the next launch
+                    arrived[0] = 0;
+                    arrived[1] = 0;
+                }
             }
+            if (finished && pc.shrink) {
+                // this shrink tile's hm columns are written: publish them to the expand steps
+                __threadfence();
+                epi_bar();
+                if (threadIdx.x == 64) atomicAdd(p.sync, 1);
+            }
+            if (tr && threadIdx.x == 64 && it < 32) tr[160 + it] = gtimer();
+            ++it;
         }
     }
 
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (tr && threadIdx.x == 0) tr[193] = gtimer();
+    if (threadIdx.x == 0) {
+        if (tr) tr[193] = gtimer();
+        // the last CTA to leave resets the launch's shrink counter
+        __threadfence();
+        const int old = atomicAdd(p.sync + 1, 1);
+        if (old == (int)gridDim.x - 1) {
+            p.sync[0] = 0;
+            p.sync[1] = 0;
+            __threadfence();
+        }
+    }
     if (warp == 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols));
 }
@@ -662,7 +846,7 @@ size_t tc_smem_bytes(const TcParams& p) {
 
 int tc_prepare(TcParams& p, int smem_budget) {
     if (p.T <= 0 || p.T > 256 || p.n_sub < 1 || p.n_sub > 2 || p.n_seg < 1 || p.n_seg > kTcMaxSets ||
-        p.n_seg * p.n_sub > kTcMaxSets || p.splits < 1 || p.kb < 1)
+        p.n_seg * p.n_sub > kTcMaxSets || p.sh_nseg < 0 || p.sh_nseg > kTcMaxSets || p.kb < 1)
         return AOS_ERR_INVALID;
     p.T_pad = ((p.T + 15) / 16) * 16;
     if (p.T_pad < 32) p.T_pad = 32;  // epilogue works in 32-token chunks
@@ -682,7 +866,6 @@ int tc_prepare(TcParams& p, int smem_budget) {
     ns = std::min(ns, max_stages);
     if (ns < 2) return AOS_ERR_INVALID;
     p.n_stages = ns;
-    if (2 * p.splits > p.kb + 1 && p.splits > 1) p.splits = std::max(1, p.kb / 2);
     return AOS_OK;
 }
 
@@ -701,6 +884,10 @@ int tc_num_sms() {
 // outside any stream capture).
 cudaError_t tc_configure() {
     return cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+}
+
+size_t tc_ws_bytes(const TcParams& p, int grid) {
+    return (size_t)grid * kMaxPartialsPerCta * p.n_sub * p.T_pad * kTcBM * sizeof(float);
 }
 
 cudaError_t tc_launch(const TcParams& p, int grid, cudaStream_t stream) {

@@ -457,7 +457,9 @@ def main():
         cpu = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample}
 
     if rank == 0:
-        launches_per_step = 1 + 2 + args.layers * 12 + 2
+        # route; LoRA prep + coefficient table; embed; per layer 2 rmsnorm, 4 fused
+        # GEMMs (shrink + base + expand), attention + combine; final rmsnorm; lm_head
+        launches_per_step = 1 + 2 + 1 + args.layers * 8 + 2
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
