@@ -2,6 +2,8 @@
 // embedding gather, RMSNorm, the LoRA routing prep (touched rank groups), and
 // synthetic KV fill.  All reductions use a fixed order.
 
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace aos {
@@ -121,7 +123,10 @@ __global__ void __launch_bounds__(1024) lora_prep_kernel(const aos_router_ring* 
 // or that are not loaded).  One CTA per token.
 __global__ void __launch_bounds__(256) lora_coef_kernel(const aos_router_ring* __restrict__ rings,
                                                         const int* __restrict__ rank, const float* __restrict__ scale,
-                                                        int max_adapters, float* __restrict__ coef) {
+                                                        int max_adapters, float* __restrict__ coef,
+                                                        const int* __restrict__ groups, const int* __restrict__ n_groups,
+                                                        const int* __restrict__ col_owner, int n_group_total,
+                                                        float* __restrict__ ucoef) {
     pdl_wait();
     pdl_trigger();
     const int t = blockIdx.x;
@@ -136,6 +141,20 @@ __global__ void __launch_bounds__(256) lora_coef_kernel(const aos_router_ring* _
             if (r.gates_q15[s] <= 0 || a >= max_adapters || rank[a] <= 0) continue;
             row[a] += __fdiv_rn((float)r.gates_q15[s], AOS_Q15_DENOM) * scale[a];
         }
+    }
+    __syncthreads();
+    // Per 8-column unit of every touched group (list order): the coefficient
+    // of the unit's adapter for this token, so the GEMM gates a shrink tile
+    // with one contiguous load per token.  Adapter columns come in units of 8.
+    const int ng = *n_groups;
+    float* urow = ucoef + (size_t)t * n_group_total * 8;
+    for (int i = threadIdx.x; i < n_group_total * 8; i += blockDim.x) {
+        float v = 0.0f;
+        if (i / 8 < ng) {
+            const int owner = col_owner[groups[i / 8] * 64 + (i % 8) * 8];
+            if (owner >= 0 && owner < max_adapters) v = row[owner];
+        }
+        urow[i] = v;
     }
 }
 
@@ -161,6 +180,29 @@ __global__ void fill_normal_bf16(uint16_t* __restrict__ p, size_t n, uint64_t se
     }
 }
 
+
+// Packs rows x cols of a row-major bf16 matrix (src == nullptr: zeros) into
+// the blocked layout the GEMM streams: the destination matrix (dst_cols
+// columns) is cut into blocks of `br` rows x 64 columns, stored block after
+// block in (row block, column block) order; inside a block row r's 16-byte
+// chunk q sits at byte r*128 + (q ^ (r % 8)) * 16, which is the SWIZZLE_128B
+// shared-memory image of that block.  One thread moves one 16-byte chunk.
+__global__ void pack_blocks_kernel(const uint16_t* __restrict__ src, int rows, int cols, long long src_ld,
+                                   uint16_t* __restrict__ dst, int row0, int col0, int dst_cols, int br) {
+    const int c8n = cols / 8;
+    const long long n = (long long)rows * c8n;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / c8n), c8 = (int)(i % c8n);
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (src) v = *reinterpret_cast<const uint4*>(src + r * src_ld + c8 * 8);
+        const int dr = row0 + r, dc = col0 + c8 * 8;
+        const long long blk = (long long)(dr / br) * (dst_cols / 64) + dc / 64;
+        const int rr = dr % br, q = (dc % 64) / 8;
+        uint8_t* d = reinterpret_cast<uint8_t*>(dst) + blk * br * 128 + rr * 128 + ((q ^ (rr & 7)) * 16);
+        *reinterpret_cast<uint4*>(d) = v;
+    }
+}
+
 }  // namespace
 
 cudaError_t launch_embed(const uint16_t* table, const uint32_t* ids, int T, int H, int V, uint16_t* out,
@@ -177,11 +219,24 @@ cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* w, int T, int H, f
 
 cudaError_t launch_lora_prep(const aos_router_ring* rings, int T, const int* col_off, const int* rank,
                              const float* scale, int max_adapters, int n_slab_total, int* slabs, int* n_slabs,
-                             float* coef, cudaStream_t s) {
+                             float* coef, const int* col_owner, float* ucoef, cudaStream_t s) {
     cudaError_t e = launch_k(lora_prep_kernel, dim3(1), dim3(1024), (size_t)n_slab_total * sizeof(int), s, rings, T,
                              col_off, rank, max_adapters, n_slab_total, slabs, n_slabs);
     if (e != cudaSuccess || T <= 0) return e;
-    return launch_k(lora_coef_kernel, dim3(T), dim3(256), 0, s, rings, rank, scale, max_adapters, coef);
+    return launch_k(lora_coef_kernel, dim3(T), dim3(256), 0, s, rings, rank, scale, max_adapters, coef,
+                    (const int*)slabs, (const int*)n_slabs, col_owner, n_slab_total, ucoef);
+}
+
+cudaError_t launch_pack_blocks(const uint16_t* src, int rows, int cols, long long src_ld, uint16_t* dst, int row0,
+                               int col0, int dst_cols, int br, cudaStream_t s) {
+    if (rows <= 0 || cols <= 0) return cudaSuccess;
+    if (cols % 8 || col0 % 8 || dst_cols % 64 || (br != 64 && br != 128) || src_ld % 8 ||
+        (reinterpret_cast<uintptr_t>(src) & 15))
+        return cudaErrorInvalidValue;
+    const long long n = (long long)rows * (cols / 8);
+    const int blocks = (int)std::min<long long>((n + 255) / 256, 148 * 16);
+    pack_blocks_kernel<<<blocks, 256, 0, s>>>(src, rows, cols, src_ld, dst, row0, col0, dst_cols, br);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_fill_normal(uint16_t* p, size_t n, uint64_t seed, float std, cudaStream_t s) {

@@ -32,9 +32,12 @@
 namespace aos {
 cudaError_t launch_embed(const uint16_t*, const uint32_t*, int, int, int, uint16_t*, cudaStream_t);
 cudaError_t launch_rmsnorm(const uint16_t*, const uint16_t*, int, int, float, uint16_t*, cudaStream_t);
-cudaError_t launch_lora_prep(const aos_router_ring*, int, const int*, const int*, const float*, int, int, int*, int*,
-                             float*, cudaStream_t);
+cudaError_t launch_lora_prep(const aos_router_ring* rings, int T, const int* col_off, const int* rank,
+                             const float* scale, int max_adapters, int n_slab_total, int* slabs, int* n_slabs,
+                             float* coef, const int* col_owner, float* ucoef, cudaStream_t s);
 cudaError_t launch_fill_normal(uint16_t*, size_t, uint64_t, float, cudaStream_t);
+cudaError_t launch_pack_blocks(const uint16_t* src, int rows, int cols, long long src_ld, uint16_t* dst, int row0,
+                               int col0, int dst_cols, int br, cudaStream_t s);
 cudaError_t launch_attention(const CUtensorMap&, const CUtensorMap&, const uint16_t*, const int*, const int*, float*,
                              float*, int, int, int, int, int, int, int, int*, uint16_t*, cudaStream_t);
 int attn_max_chunks(int max_seq_len);
@@ -98,6 +101,7 @@ struct aos_ctx {
     int *d_col_owner = nullptr, *d_col_off = nullptr, *d_rank = nullptr;
     float* d_scale = nullptr;
     float* d_coef = nullptr;  // [T_cap][max_adapters] per-step gate * alpha/rank
+    float* d_ucoef = nullptr; // [T_cap][R/64 touched-group slots][8 units] per-step unit coefficients
     std::vector<int> col_owner;  // host mirror, 8-column units
     std::unordered_map<uint16_t, AdapterEntry> adapters;
     uint64_t arena_bytes = 0;
@@ -130,11 +134,11 @@ struct aos_ctx {
     float *d_rope = nullptr;
     float *d_attn_part = nullptr, *d_attn_ml = nullptr;
     int attn_chunks = 0;
-    float* d_ws = nullptr;
-    size_t ws_bytes = 0;
-    int* d_counters = nullptr;    // [kCounterTiles] pieces arrived per tile
-    int* d_tile_slots = nullptr;  // [kCounterTiles][kMaxPiecesPerTile]
-    int* d_sync = nullptr;        // [2] shrink tiles done, CTAs exited
+    uint16_t* d_stage = nullptr;  // bounded staging for packing host or unaligned weights
+    size_t stage_bytes = 0;
+    long long* d_acc = nullptr;   // GEMM fixed-point accumulators of split tiles (kept zero)
+    size_t acc_bytes = 0;
+    int* d_sync = nullptr;        // [4] GEMM grid-barrier counters
     int* d_err = nullptr;
     unsigned long long* d_trace = nullptr;  // AOS_TC_TRACE diagnostics
     std::map<int, std::unique_ptr<StepPlan>> plans;
@@ -184,44 +188,40 @@ cudaError_t dalloc(T** p, size_t n_elems, uint64_t* counter = nullptr) {
     return e;
 }
 
-// Build the TcParams of every GEMM of one layer for a padded batch T_pad.
+// Upper bound of the tiles of one GEMM launch (base tiles of the largest
+// projection plus shrink tiles of up to three LoRA modules).
+size_t max_launch_tiles(const aos_ctx* c) {
+    const size_t H = c->cfg.hidden, I = c->cfg.intermediate, V = c->cfg.vocab;
+    const size_t base = std::max<size_t>({(c->QD + 2 * (size_t)c->KVD) / kTcBN + 3, (I + 127) / 128, (H + kTcBN - 1) / kTcBN,
+                                          (V + kTcBN - 1) / kTcBN});
+    return base + 3 * ((size_t)c->R / kGroup / kShrinkGroupsPerTile + 1);
+}
+
+// Build the TcParams of every GEMM of one layer for a batch of T tokens.
 int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
     const uint32_t H = c->cfg.hidden, I = c->cfg.intermediate;
-    const int T_pad = std::max(32, ((T + 15) / 16) * 16);
+    const int T_box = tc_t_box(T);  // activation box rows (128 per token block at most)
     const int smem_budget = 227 * 1024;
     int rc;
     auto x_map = [&](CUtensorMap* m, const uint16_t* buf, uint32_t K) {
-        return tc_encode_2d(m, buf, K, (uint64_t)c->T_cap, (uint64_t)K * 2, 64, (uint32_t)T_pad, 128);
-    };
-    auto w_map = [&](CUtensorMap* m, const uint16_t* w, uint32_t rows, uint32_t K) {
-        return tc_encode_2d(m, w, K, rows, (uint64_t)K * 2, 64, 128, 128);
-    };
-    auto a_map = [&](CUtensorMap* m, int mod) {
-        const uint32_t K = mod_in(c, mod);
-        return tc_encode_2d(m, c->A[mod][layer], K, (uint64_t)c->R, (uint64_t)K * 2, 64, kGroup, 128);
-    };
-    auto b_map = [&](CUtensorMap* m, int mod) {  // B_cat [out][R]
-        const uint32_t out = mod_out(c, mod);
-        return tc_encode_2d(m, c->B[mod][layer], (uint64_t)c->R, out, (uint64_t)c->R * 2, kGroup, 128, 128);
+        return tc_encode_2d(m, buf, K, (uint64_t)c->T_cap, (uint64_t)K * 2, 64, (uint32_t)T_box, 128);
     };
     auto h_map = [&](CUtensorMap* m, int mod) {  // hm [T][R]
         return tc_encode_2d(m, c->d_hm[mod], (uint64_t)c->R, (uint64_t)c->T_cap, (uint64_t)c->R * 2, kGroup,
-                            (uint32_t)T_pad, 128);
+                            (uint32_t)T_box, 128);
     };
     auto common = [&](TcParams& p) {
         std::memset(&p, 0, sizeof(p));
         p.T = T;
         p.groups = c->d_groups;
         p.n_groups = c->d_n_groups;
-        p.ws = c->d_ws;
-        p.counters = c->d_counters;
-        p.tile_slots = c->d_tile_slots;
+        p.acc = c->d_acc;
+        p.acc_q = (c->T_cap + 31) / 32;
         p.sync = c->d_sync;
         p.err = c->d_err;
         p.R = c->R;
-        p.col_owner = c->d_col_owner;
-        p.coef = c->d_coef;
-        p.max_adapters = (int)c->cfg.lora_max_adapters;
+        p.n_rgroups = c->R / kGroup;
+        p.ucoef = c->d_ucoef;
         p.layer = layer;
     };
     const bool lora[4] = {(c->module_mask & 0x7u) != 0, (c->module_mask & 0x8u) != 0, (c->module_mask & 0x30u) != 0,
@@ -242,7 +242,7 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
             for (int j = 0; j < 3; ++j) {
                 const int mod = groups_mods[g][j];
                 if (mod < 0) continue;
-                if ((rc = a_map(&p.tm_a[p.sh_nseg], mod))) return rc;
+                p.a_pk[p.sh_nseg] = c->A[mod][layer];
                 p.sh_out[p.sh_nseg] = c->d_hm[mod];
                 ++p.sh_nseg;
             }
@@ -255,14 +255,14 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
             const uint32_t r0[3] = {0, c->QD, c->QD + c->KVD};
             const uint32_t nr[3] = {c->QD, c->KVD, c->KVD};
             for (int j = 0; j < 3; ++j) {
-                if ((rc = w_map(&p.tm_w[j], c->w_qkv[layer], rows_total, H))) return rc;
+                p.w_pk[j] = c->w_qkv[layer];
                 p.seg_wrow0[j] = (int)r0[j];
-                p.seg_tiles[j] = (int)(nr[j] / 128);
+                p.seg_tiles[j] = (int)((nr[j] + kTcBN - 1) / kTcBN);  // two heads per tile
                 p.seg_rows[j] = (int)nr[j];
                 p.seg_module[j] = groups_mods[g][j];
                 p.seg_out0[j] = 0;
                 if (p.lora) {
-                    if ((rc = b_map(&p.tm_lb[j], groups_mods[g][j]))) return rc;
+                    p.b_pk[j] = c->B[groups_mods[g][j]][layer];
                     if ((rc = h_map(&p.tm_lh[j], groups_mods[g][j]))) return rc;
                 }
             }
@@ -280,15 +280,15 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
             p.mode = TC_SWIGLU;
             p.n_sub = 2;
             p.n_seg = 1;
-            if ((rc = w_map(&p.tm_w[0], c->w_gate[layer], I, H))) return rc;
-            if ((rc = w_map(&p.tm_w[1], c->w_up[layer], I, H))) return rc;
+            p.w_pk[0] = c->w_gate[layer];
+            p.w_pk[1] = c->w_up[layer];
             if (p.lora) {
-                if ((rc = b_map(&p.tm_lb[0], AOS_MOD_GATE))) return rc;
-                if ((rc = b_map(&p.tm_lb[1], AOS_MOD_UP))) return rc;
+                p.b_pk[0] = c->B[AOS_MOD_GATE][layer];
+                p.b_pk[1] = c->B[AOS_MOD_UP][layer];
                 if ((rc = h_map(&p.tm_lh[0], AOS_MOD_GATE))) return rc;
                 if ((rc = h_map(&p.tm_lh[1], AOS_MOD_UP))) return rc;
             }
-            p.seg_tiles[0] = (int)((I + 127) / 128);
+            p.seg_tiles[0] = (int)((I + kTcBN / 2 - 1) / (kTcBN / 2));  // 128 gate + 128 up rows per tile
             p.seg_rows[0] = (int)I;
             p.seg_module[0] = AOS_MOD_GATE;
             p.out[0] = c->d_act;
@@ -298,12 +298,12 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
             p.mode = TC_RESID_BF16;
             p.n_sub = 1;
             p.n_seg = 1;
-            if ((rc = w_map(&p.tm_w[0], g == kGroupO ? c->w_o[layer] : c->w_down[layer], H, group_k[g]))) return rc;
+            p.w_pk[0] = g == kGroupO ? c->w_o[layer] : c->w_down[layer];
             if (p.lora) {
-                if ((rc = b_map(&p.tm_lb[0], mod))) return rc;
+                p.b_pk[0] = c->B[mod][layer];
                 if ((rc = h_map(&p.tm_lh[0], mod))) return rc;
             }
-            p.seg_tiles[0] = (int)((H + 127) / 128);
+            p.seg_tiles[0] = (int)((H + kTcBN - 1) / kTcBN);
             p.seg_rows[0] = (int)H;
             p.seg_module[0] = mod;
             p.resid = c->d_hidden;
@@ -342,43 +342,20 @@ int get_plan(aos_ctx* c, int T, StepPlan** out) {
     p.n_seg = 1;
     p.kb = (int)(c->cfg.hidden / 64);
     p.err = c->d_err;
-    p.ws = c->d_ws;
-    p.counters = c->d_counters;
-    p.tile_slots = c->d_tile_slots;
+    p.acc = c->d_acc;
+    p.acc_q = (c->T_cap + 31) / 32;
     p.sync = c->d_sync;
     const uint32_t V = c->cfg.vocab;
-    int rc = tc_encode_2d(&p.tm_w[0], c->lm_head, c->cfg.hidden, V, (uint64_t)c->cfg.hidden * 2, 64, 128, 128);
-    rc |= tc_encode_2d(&p.tm_x, c->d_normed, c->cfg.hidden, (uint64_t)c->T_cap, (uint64_t)c->cfg.hidden * 2, 64,
-                       (uint32_t)T_pad, 128);
+    p.w_pk[0] = c->lm_head;
+    int rc = tc_encode_2d(&p.tm_x, c->d_normed, c->cfg.hidden, (uint64_t)c->T_cap, (uint64_t)c->cfg.hidden * 2, 64,
+                       (uint32_t)tc_t_box(T), 128);
     if (rc) return c->fail(AOS_ERR_CUDA, "lm_head tensor map encode failed");
-    p.seg_tiles[0] = (int)((V + 127) / 128);
+    p.seg_tiles[0] = (int)((V + kTcBN - 1) / kTcBN);
     p.seg_rows[0] = (int)V;
     p.out[0] = c->d_logits;
     p.ld_out = (int)V;
     if ((rc = tc_prepare(p, 227 * 1024))) return c->fail(rc, "lm_head plan");
     plan->lm_grid = tc_num_sms();
-    // workspace for the fp32 partials of tiles cut between CTAs
-    size_t need = tc_ws_bytes(p, plan->lm_grid);
-    for (auto& lp : plan->layers)
-        for (int g = 0; g < 4; ++g) need = std::max(need, tc_ws_bytes(lp.gemm[g], lp.gemm_grid[g]));
-    if (need > c->ws_bytes) {
-        if (c->d_ws) cudaFree(c->d_ws);
-        c->d_ws = nullptr;
-        c->ws_bytes = 0;
-        CTX_CUDA(c, cudaMalloc((void**)&c->d_ws, need));
-        c->ws_bytes = need;
-        // all cached plans point at the workspace: refresh them
-        for (auto& kv : c->plans)
-            for (auto& lp : kv.second->layers)
-                for (int g = 0; g < 4; ++g) lp.gemm[g].ws = c->d_ws;
-        for (auto& kv : c->plans) {
-            kv.second->lm_head.ws = c->d_ws;
-            kv.second->graph_valid = false;
-        }
-        for (auto& lp : plan->layers)
-            for (int g = 0; g < 4; ++g) lp.gemm[g].ws = c->d_ws;
-        p.ws = c->d_ws;
-    }
     *out = plan.get();
     c->plans[T] = std::move(plan);
     return AOS_OK;
@@ -426,7 +403,7 @@ int enqueue_step(aos_ctx* c, StepPlan& plan, bool with_logits, cudaStream_t s) {
     const int T = plan.T;
     PLAUNCH(c, AOS_K_PREP, s,
             launch_lora_prep(c->d_rings, T, c->d_col_off, c->d_rank, c->d_scale, (int)c->cfg.lora_max_adapters,
-                             c->R / kGroup, c->d_groups, c->d_n_groups, c->d_coef, s));
+                             c->R / kGroup, c->d_groups, c->d_n_groups, c->d_coef, c->d_col_owner, c->d_ucoef, s));
     PLAUNCH(c, AOS_K_EMBED, s, launch_embed(c->embed, c->d_tokens, T, (int)c->cfg.hidden, (int)c->cfg.vocab, c->d_hidden, s));
     for (uint32_t l = 0; l < c->cfg.n_layers; ++l) {
         int rc = enqueue_layer(c, plan, (int)l, s);
@@ -543,6 +520,39 @@ void advance(aos_ctx* c, const uint64_t* seq_ids, uint32_t T) {
     c->m.tokens += T;
 }
 
+// Copies a rows x cols row-major bf16 matrix (leading dimension ld, host or
+// device memory; nullptr writes zeros) into the packed block layout of dst
+// (dst_cols columns, blocks of br rows x 64 columns, SWIZZLE_128B images) at
+// row0/col0, on the context stream.  Host or unaligned sources go through a
+// staging buffer of at most kMaxStage bytes, a slab of rows at a time.
+int pack_upload(aos_ctx* c, const uint16_t* src, int src_on_device, int rows, int cols, long long ld, uint16_t* dst,
+                int row0, int col0, int dst_cols, int br) {
+    constexpr size_t kMaxStage = 64u << 20;
+    cudaStream_t s = c->stream;
+    if (!src || (src_on_device && (reinterpret_cast<uintptr_t>(src) & 15) == 0 && ld % 8 == 0)) {
+        LAUNCH(c, launch_pack_blocks(src, rows, cols, ld, dst, row0, col0, dst_cols, br, s));
+        return AOS_OK;
+    }
+    const size_t row_bytes = (size_t)cols * 2;
+    const int slab = (int)std::max<size_t>(1, std::min<size_t>((size_t)rows, kMaxStage / row_bytes));
+    const size_t need = (size_t)slab * row_bytes;
+    if (need > c->stage_bytes) {
+        CTX_CUDA(c, cudaStreamSynchronize(s));
+        if (c->d_stage) cudaFree(c->d_stage);
+        c->d_stage = nullptr;
+        c->stage_bytes = 0;
+        CTX_CUDA(c, cudaMalloc((void**)&c->d_stage, need));
+        c->stage_bytes = need;
+    }
+    for (int r = 0; r < rows; r += slab) {
+        const int nr = std::min(slab, rows - r);
+        CTX_CUDA(c, cudaMemcpy2DAsync(c->d_stage, row_bytes, src + (size_t)r * ld, (size_t)ld * 2, row_bytes, nr,
+                                      src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s));
+        LAUNCH(c, launch_pack_blocks(c->d_stage, nr, cols, cols, dst, row0 + r, col0, dst_cols, br, s));
+    }
+    return AOS_OK;
+}
+
 int check_device_error(aos_ctx* c) {
     int e = 0;
     CTX_CUDA(c, cudaMemcpy(&e, c->d_err, 4, cudaMemcpyDeviceToHost));
@@ -550,14 +560,8 @@ int check_device_error(aos_ctx* c) {
         // The failed launch may have left tile counters and the shrink
         // counter part-way: clear them so the next step starts clean.
         cudaDeviceSynchronize();  // nothing of this context may still be running
-        size_t tiles = 0;
-        {
-            const size_t rows = std::max<size_t>({(size_t)c->QD + 2 * c->KVD, c->cfg.intermediate, c->cfg.hidden,
-                                                  c->cfg.vocab});
-            tiles = (rows + 127) / 128 + 3 * ((size_t)c->R / 128 + 1);
-        }
-        cudaMemset(c->d_counters, 0, 2 * tiles * sizeof(int));
-        cudaMemset(c->d_sync, 0, 2 * sizeof(int));
+        cudaMemset(c->d_sync, 0, 4 * sizeof(int));
+        cudaMemset(c->d_acc, 0, c->acc_bytes);
         cudaMemset(c->d_err, 0, sizeof(int));
         cudaDeviceSynchronize();
         return c->fail(e, "a bounded device-side wait timed out or a launch limit was exceeded (the kernel returned early)");
@@ -620,7 +624,8 @@ aos_ctx* aos_init(const aos_model_config* cfg) {
     const uint32_t L = k.n_layers, H = k.hidden, I = k.intermediate, V = k.vocab;
     // base weights
     INIT_CHECK(dalloc(&c->embed, (size_t)V * H, &c->base_bytes), "embed");
-    INIT_CHECK(dalloc(&c->lm_head, (size_t)V * H, &c->base_bytes), "lm_head");
+    // packed in 128-row blocks: rows padded to a multiple of 128 (zeros)
+    INIT_CHECK(dalloc(&c->lm_head, (size_t)((V + 127) / 128 * 128) * H, &c->base_bytes), "lm_head");
     INIT_CHECK(dalloc(&c->final_norm, (size_t)H, &c->base_bytes), "final_norm");
     c->attn_norm.resize(L);
     c->mlp_norm.resize(L);
@@ -689,15 +694,15 @@ aos_ctx* aos_init(const aos_model_config* cfg) {
     INIT_CHECK(dalloc(&c->d_tokens, TC), "tokens");
     INIT_CHECK(dalloc(&c->d_logits, TC * V), "logits");
     INIT_CHECK(dalloc(&c->d_coef, TC * NA), "lora coef");
+    INIT_CHECK(dalloc(&c->d_ucoef, TC * (size_t)(c->R / kGroup) * 8), "lora unit coef");
     c->attn_chunks = attn_max_chunks((int)k.max_seq_len);
     INIT_CHECK(dalloc(&c->d_attn_part, TC * k.n_kv_heads * c->attn_chunks * c->G * 128), "attn part");
     INIT_CHECK(dalloc(&c->d_attn_ml, TC * k.n_kv_heads * c->attn_chunks * c->G * 2), "attn ml");
     {  // tiles of the largest launch: base tiles plus up to three shrink segments
-        const size_t rows = std::max<size_t>({(size_t)c->QD + 2 * c->KVD, I, H, V});
-        const size_t tiles = (rows + 127) / 128 + 3 * ((size_t)c->R / 128 + 1);
-        INIT_CHECK(dalloc(&c->d_counters, 2 * tiles), "counters");
-        INIT_CHECK(dalloc(&c->d_tile_slots, tiles * kMaxPiecesPerTile), "tile slots");
-        INIT_CHECK(dalloc(&c->d_sync, 2), "sync");
+        const size_t tiles = max_launch_tiles(c.get());
+        c->acc_bytes = tiles * 8 * (size_t)((c->T_cap + 31) / 32) * 1024 * sizeof(long long);
+        INIT_CHECK(dalloc(&c->d_acc, c->acc_bytes / sizeof(long long)), "GEMM accumulators");
+        INIT_CHECK(dalloc(&c->d_sync, 4), "sync");
     }
     INIT_CHECK(dalloc(&c->d_err, 1), "err");
     if (getenv("AOS_TC_TRACE")) INIT_CHECK(dalloc(&c->d_trace, (size_t)tc_num_sms() * kTraceStride), "trace");
@@ -753,12 +758,12 @@ void aos_destroy(aos_ctx* c) {
         for (auto* p : c->B[m]) f(p);
         f(c->d_hm[m]);
     }
-    f(c->d_col_owner); f(c->d_col_off); f(c->d_rank); f(c->d_scale); f(c->d_coef);
+    f(c->d_col_owner); f(c->d_col_off); f(c->d_rank); f(c->d_scale); f(c->d_coef); f(c->d_ucoef);
     f(c->k_pool); f(c->v_pool);
     f(c->d_hidden); f(c->d_normed); f(c->d_q); f(c->d_attn); f(c->d_act);
     f(c->d_groups); f(c->d_n_groups); f(c->d_block_tables); f(c->d_ctx_lens);
     f(c->d_rings); f(c->d_tokens); f(c->d_logits); f(c->d_rope);
-    f(c->d_attn_part); f(c->d_attn_ml); f(c->d_ws); f(c->d_counters); f(c->d_tile_slots); f(c->d_sync); f(c->d_err); f(c->d_trace);
+    f(c->d_attn_part); f(c->d_attn_ml); f(c->d_stage); f(c->d_acc); f(c->d_sync); f(c->d_err); f(c->d_trace);
     for (int i = 0; i < aos_ctx::kStageSlots; ++i) {
         if (c->h_stage[i]) cudaFreeHost(c->h_stage[i]);
         if (c->stage_ev[i]) cudaEventDestroy(c->stage_ev[i]);
@@ -805,6 +810,27 @@ int aos_load_weight(aos_ctx* c, aos_weight_kind kind, uint32_t layer, aos_module
     }
     if (n != want) return c->fail(AOS_ERR_INVALID, "weight size mismatch: got " + std::to_string(n) + ", want " + std::to_string(want));
     CTX_CUDA(c, cudaSetDevice(c->device));
+    if (kind == AOS_W_PROJ || kind == AOS_W_LM_HEAD) {
+        // projection matrices are stored packed (128 x 64 SWIZZLE_128B blocks)
+        int rows, cols, row0 = 0;
+        uint16_t* base = dst;
+        if (kind == AOS_W_LM_HEAD) {
+            rows = (int)V;
+            cols = (int)H;
+        } else {
+            rows = (int)mod_out(c, module);
+            cols = (int)mod_in(c, module);
+            if (module == AOS_MOD_Q || module == AOS_MOD_K || module == AOS_MOD_V) {
+                base = c->w_qkv[layer];
+                row0 = module == AOS_MOD_Q ? 0 : (module == AOS_MOD_K ? (int)c->QD : (int)(c->QD + c->KVD));
+            }
+        }
+        int rc = pack_upload(c, data, src_on_device, rows, cols, cols, base, row0, 0, cols, 128);
+        if (rc) return rc;
+        CTX_CUDA(c, cudaStreamSynchronize(c->stream));
+        return AOS_OK;
+    }
+    CTX_CUDA(c, cudaStreamSynchronize(c->stream));  // no queued step may still read the tensor
     CTX_CUDA(c, cudaMemcpy(dst, data, n * 2, src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
     return AOS_OK;
 }
@@ -832,15 +858,17 @@ int aos_adapter_new(aos_ctx* c, uint16_t id, uint32_t rank, float alpha) {
     if (start < 0) return c->fail(AOS_ERR_NOMEM, "adapter arena full");
     const int off = start * 8;
     CTX_CUDA(c, cudaSetDevice(c->device));
-    // zero the adapter's rows/columns in every layer and module
+    // zero the adapter's lora_A rows and lora_B columns in every layer and module
     for (int m = 0; m < AOS_NUM_MODULES; ++m) {
         if (!(c->module_mask & (1u << m))) continue;
-        const uint32_t in = mod_in(c, m), out = mod_out(c, m);
+        const int in = (int)mod_in(c, m), out = (int)mod_out(c, m);
         for (uint32_t l = 0; l < c->cfg.n_layers; ++l) {
-            CTX_CUDA(c, cudaMemset(c->A[m][l] + (size_t)off * in, 0, (size_t)rank * in * 2));
-            CTX_CUDA(c, cudaMemset2D(c->B[m][l] + off, (size_t)c->R * 2, 0, (size_t)rank * 2, out));
+            int rc = pack_upload(c, nullptr, 1, (int)rank, in, in, c->A[m][l], off, 0, in, kGroup);
+            if (!rc) rc = pack_upload(c, nullptr, 1, out, (int)rank, (int)rank, c->B[m][l], 0, off, c->R, 128);
+            if (rc) return rc;
         }
     }
+    CTX_CUDA(c, cudaStreamSynchronize(c->stream));
     for (int j = 0; j < units; ++j) c->col_owner[start + j] = id;
     std::vector<int> owner((size_t)rank, (int)id);
     CTX_CUDA(c, cudaMemcpy(c->d_col_owner + off, owner.data(), rank * 4, cudaMemcpyHostToDevice));
@@ -865,11 +893,13 @@ int aos_adapter_set_module(aos_ctx* c, uint16_t id, uint32_t layer, aos_module m
     if (!(c->module_mask & (1u << module))) return c->fail(AOS_ERR_INVALID, "module not enabled for LoRA in this context");
     const int off = it->second.off, rank = it->second.rank;
     const uint32_t in = mod_in(c, module), out = mod_out(c, module);
-    const cudaMemcpyKind kind = src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
     CTX_CUDA(c, cudaSetDevice(c->device));
-    CTX_CUDA(c, cudaMemcpy(c->A[module][layer] + (size_t)off * in, A, (size_t)rank * in * 2, kind));
-    CTX_CUDA(c, cudaMemcpy2D(c->B[module][layer] + off, (size_t)c->R * 2, B, (size_t)rank * 2, (size_t)rank * 2, out,
-                             kind));
+    // lora_A [rank, in] -> arena rows [off, off + rank) (64-row blocks);
+    // lora_B [out, rank] -> arena columns [off, off + rank) (128-row blocks)
+    int rc = pack_upload(c, A, src_on_device, rank, (int)in, (long long)in, c->A[module][layer], off, 0, (int)in, kGroup);
+    if (!rc) rc = pack_upload(c, B, src_on_device, (int)out, rank, rank, c->B[module][layer], 0, off, c->R, 128);
+    if (rc) return rc;
+    CTX_CUDA(c, cudaStreamSynchronize(c->stream));
     return AOS_OK;
 }
 
@@ -1065,7 +1095,7 @@ int aos_layer_step_dev(aos_ctx* c, uint32_t layer, const aos_router_ring* rings,
         CTX_CUDA(c, cudaMemcpyAsync(c->d_rings, rings, (size_t)T * sizeof(aos_router_ring), cudaMemcpyDeviceToDevice, s));
     CTX_CUDA(c, cudaMemcpyAsync(c->d_hidden, hidden, (size_t)T * c->cfg.hidden * 2, cudaMemcpyDeviceToDevice, s));
     LAUNCH(c, launch_lora_prep(c->d_rings, (int)T, c->d_col_off, c->d_rank, c->d_scale, (int)c->cfg.lora_max_adapters,
-                               c->R / kGroup, c->d_groups, c->d_n_groups, c->d_coef, s));
+                               c->R / kGroup, c->d_groups, c->d_n_groups, c->d_coef, c->d_col_owner, c->d_ucoef, s));
     if ((rc = enqueue_layer(c, *plan, (int)layer, s))) return rc;
     CTX_CUDA(c, cudaMemcpyAsync(hidden, c->d_hidden, (size_t)T * c->cfg.hidden * 2, cudaMemcpyDeviceToDevice, s));
     if (adv) advance(c, seq_ids, T);

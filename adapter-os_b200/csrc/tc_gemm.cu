@@ -3,30 +3,32 @@
 //
 // One launch computes, for one input X (normed hidden, attention output or
 // SwiGLU activation):
-//   shrink tiles : hm[t, group cols] = gate(t, owner) * (A_cat[group rows] . x_t)
-//                  for every touched 64-column rank group of every LoRA module
-//                  that reads X (TC_SHRINK_HM epilogue);
-//   base tiles   : W[128 rows] . X^T  +  sum over touched groups of
-//                  B_cat[128 rows, group cols] . hm[group cols]^T
-// so a base tile's accumulator ends as  W x + sum_a B_a (g_a * scale_a * A_a x)
+//   shrink tiles : hm[t, group cols] = gate(t, owner) * (x_t . A_cat[group rows])
+//                  for four touched 64-column rank groups per tile, of every
+//                  LoRA module that reads X (TC_SHRINK_HM epilogue);
+//   base tiles   : X . W[256 rows]^T  +  sum over touched groups of
+//                  hm[group cols] . B_cat[256 rows, group cols]^T
+// so a base tile's accumulator ends as  x W^T + sum_a (g_a * scale_a * x A_a^T) B_a^T
 // (mlx_cpp_wrapper_real.cpp:3372-3419) without materialising the LoRA delta.
-// MMA M = 128 weight rows, N = decode tokens ("swap-AB").
-//   K step      : TMA W[128 x 64] (or two lora_A group boxes [64 x 64]) + X[T x 64]
-//   expand step : TMA lora_B[128 rows x one group] + hm[T x the same group]
-// all SWIZZLE_128B, four K=16 MMAs per step and sub-tile.
+// MMA M = 128 token lanes, N = 256 weight rows (a kind::f16 MMA takes the same
+// time for any N up to 256, so the wide side carries the weights).
+//   K step      : bulk copy of two packed 16 KB weight blocks (or four 8 KB
+//                 lora_A group blocks) + TMA box X[T x 64]
+//   expand step : two packed lora_B blocks [128 rows x one group] + TMA box
+//                 hm[T x the same group]
+// all SWIZZLE_128B shared-memory images, four K=16 MMAs per step.
 //
 // Roles (192 threads, one CTA per SM, grid = SM count):
-//   warp 0      : TMA producer (one elected lane)
+//   warp 0      : TMA / bulk-copy producer (one elected lane)
 //   warp 1      : TMEM allocator + MMA issuer (one elected lane)
-//   warps 2..5  : epilogue, TMEM lane quarter = warp % 4
-// Work is split stream-K style (see "schedule" below): every CTA streams the
-// same number of steps, a tile cut between CTAs is finished by the last piece
-// to arrive, which sums the pieces' fp32 partials in piece order (fixed order,
-// so the result is bit-identical run to run; no float atomics).  Expand steps
-// wait until every shrink tile of the launch has been written.
+//   warps 2..5  : drain (TMEM lane quarter = warp % 4, one token per lane)
+//                 and the parallel reduction of split tiles
+// Work is split stream-K style (see "schedule"): every CTA streams the same
+// number of steps.  Split tiles are summed in piece order after bounded grid
+// barriers (fixed order: bit-identical run to run; no float atomics).
 //
 // Every wait is bounded (kSpinLimitCycles): on timeout the kernel records
-// AOS_ERR_TIMEOUT in p.err, drains its own TMA copies and MMAs, frees TMEM and
+// AOS_ERR_TIMEOUT in p.err, drains its own copies and MMAs, frees TMEM and
 // returns.
 
 #include <algorithm>
@@ -98,6 +100,14 @@ __device__ __forceinline__ void tma_2d(const CUtensorMap* m, uint32_t dst, uint3
         "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(x), "r"(y), "l"(policy)
         : "memory");
 }
+// Contiguous global -> shared bulk copy (no tensor map), completing on `bar`.
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+        : "memory");
+}
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -164,116 +174,187 @@ __device__ __forceinline__ unsigned long long gtimer() {
 }
 
 
-// ---------------------------------------------------------------- epilogue
-struct EpiSmem {
-    float* xbuf;  // [128][33] exchange buffer (RoPE)
-};
+// Fixed-point scale of the split-tile accumulators (value * 2^32 in int64).
+constexpr float kFix = 4294967296.0f;
+constexpr float kFixInv = 2.3283064365386963e-10f;
+constexpr uint32_t kTcTailBytes = 512;  // mbarriers and flags after the stages
 
-// Apply the epilogue to tokens [t0, t0+32) of one tile row.  v[sub][j] holds
-// the fp32 accumulator for token t0 + j.  Must be called uniformly by all
-// 128 epilogue threads (RoPE uses a named barrier).  Every loop is fully
-// unrolled with predicates, and all loads of a chunk are issued before its
-// stores, so a chunk costs one or two memory latencies, not 32.
-__device__ __forceinline__ void epilogue_chunk(const TcParams& p, const EpiSmem& es, int mode, int seg, int tile,
-                                               void* out_base, int ng, int row, int t0, float (&v)[2][32]) {
-    const int col = p.seg_out0[seg] + tile * kTcBM + row;
-    if (mode != TC_SHRINK_HM && mode != TC_QKV_ROPE && tile * kTcBM + row >= p.seg_rows[seg]) return;
-    const int nt = min(32, p.T - t0);  // valid tokens in this chunk
+// ---------------------------------------------------------------- epilogue
+// The accumulator of a tile holds, per token (TMEM lane), 256 columns.  The
+// epilogue walks them as 4 chunks of 32 column PAIRS (cA + i, cB + i): the
+// pairs a mode needs together -- RoPE rotates d with d + 64 of the same head
+// (mlx_cpp_wrapper_real.cpp:3270-3280), SwiGLU combines gate feature f with up
+// feature f (:3522) -- so one thread finishes its token without exchanging
+// data with other threads.
+__device__ __forceinline__ void chunk_cols(int mode, int k, int& cA, int& cB) {
+    if (mode == TC_SWIGLU) {  // gate columns [0,128), up columns [128,256)
+        cA = 32 * k;
+        cB = 128 + 32 * k;
+    } else if (mode == TC_QKV_ROPE) {  // head k/2 of the tile, dims [32j, 32j+32) and +64
+        cA = 128 * (k >> 1) + 32 * (k & 1);
+        cB = cA + 64;
+    } else {
+        cA = 64 * k;
+        cB = 64 * k + 32;
+    }
+}
+
+template <int N>
+__device__ __forceinline__ void store_bf16_run(uint16_t* o, const float* v) {
+    if constexpr (N % 8 == 0) {
+#pragma unroll
+        for (int i = 0; i < N; i += 8) {
+            uint4 w;
+            w.x = (uint32_t)f2bf(v[i]) | ((uint32_t)f2bf(v[i + 1]) << 16);
+            w.y = (uint32_t)f2bf(v[i + 2]) | ((uint32_t)f2bf(v[i + 3]) << 16);
+            w.z = (uint32_t)f2bf(v[i + 4]) | ((uint32_t)f2bf(v[i + 5]) << 16);
+            w.w = (uint32_t)f2bf(v[i + 6]) | ((uint32_t)f2bf(v[i + 7]) << 16);
+            *reinterpret_cast<uint4*>(o + i) = w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < N; i += 4) {
+            uint2 w;
+            w.x = (uint32_t)f2bf(v[i]) | ((uint32_t)f2bf(v[i + 1]) << 16);
+            w.y = (uint32_t)f2bf(v[i + 2]) | ((uint32_t)f2bf(v[i + 3]) << 16);
+            *reinterpret_cast<uint2*>(o + i) = w;
+        }
+    }
+}
+
+// out/resid run of N columns starting at segment row `r0` for token t.
+template <int N>
+__device__ __forceinline__ void store_run(const TcParams& p, int mode, int seg, int t, int r0, const float* v) {
+    const int lim = p.seg_rows[seg];
+    if (r0 >= lim) return;
+    const size_t off = (size_t)t * p.ld_out + p.seg_out0[seg] + r0;
+    const bool full = r0 + N <= lim;
+    if (mode == TC_STORE_F32) {
+        float* o = reinterpret_cast<float*>(p.out[seg]) + off;
+        if (full) {
+#pragma unroll
+            for (int i = 0; i < N; i += 4) *reinterpret_cast<float4*>(o + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < N; ++i)
+                if (r0 + i < lim) o[i] = v[i];
+        }
+    } else if (mode == TC_RESID_BF16) {
+        uint16_t* h = p.resid + off;
+        float s[N];
+        if (full) {
+#pragma unroll
+            for (int i = 0; i < N; i += 4) {
+                const uint2 w = *reinterpret_cast<const uint2*>(h + i);
+                s[i] = bf2f((uint16_t)(w.x & 0xFFFFu)) + v[i];
+                s[i + 1] = bf2f((uint16_t)(w.x >> 16)) + v[i + 1];
+                s[i + 2] = bf2f((uint16_t)(w.y & 0xFFFFu)) + v[i + 2];
+                s[i + 3] = bf2f((uint16_t)(w.y >> 16)) + v[i + 3];
+            }
+            store_bf16_run<N>(h, s);
+        } else {
+#pragma unroll
+            for (int i = 0; i < N; ++i)
+                if (r0 + i < lim) h[i] = f2bf(bf2f(h[i]) + v[i]);
+        }
+    } else {  // TC_STORE_BF16
+        uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]) + off;
+        if (full) {
+            store_bf16_run<N>(o, v);
+        } else {
+#pragma unroll
+            for (int i = 0; i < N; ++i)
+                if (r0 + i < lim) o[i] = f2bf(v[i]);
+        }
+    }
+}
+
+// hm[t][c0 + cc + i] = bf16(v[i]): the values arrive already multiplied by
+// the gate * alpha/rank of each column's adapter for token t (applied when
+// the accumulator is drained, see gate_coefs).
+template <int N>
+__device__ __forceinline__ void shrink_run(const TcParams& p, int seg, int t, int c0, int cc, const float* v) {
+    store_bf16_run<N>(reinterpret_cast<uint16_t*>(p.sh_out[seg]) + (size_t)t * p.R + c0 + cc, v);
+}
+
+// Applies the epilogue of `mode` to pairs [pr0, pr0 + N) of chunk k of tile
+// `tile` (segment `seg`) for token t (t < T).  vA/vB: accumulator values of
+// the pairs' first and second columns.
+template <int N>
+__device__ __forceinline__ void apply_pairs(const TcParams& p, int mode, int seg, int tile, int k, int t, int pr0,
+                                            const float* vA, const float* vB, int ng) {
+    int cA, cB;
+    chunk_cols(mode, k, cA, cB);
+    cA += pr0;
+    cB += pr0;
     switch (mode) {
-        case TC_STORE_BF16: {
-            uint16_t* o = reinterpret_cast<uint16_t*>(out_base) + (size_t)t0 * p.ld_out + col;
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (j < nt) o[(size_t)j * p.ld_out] = f2bf(v[0][j]);
+        case TC_STORE_BF16:
+        case TC_STORE_F32:
+        case TC_RESID_BF16:
+            store_run<N>(p, mode, seg, t, tile * kTcBN + cA, vA);
+            store_run<N>(p, mode, seg, t, tile * kTcBN + cB, vB);
             break;
-        }
-        case TC_STORE_F32: {
-            float* o = reinterpret_cast<float*>(out_base) + (size_t)t0 * p.ld_out + col;
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (j < nt) o[(size_t)j * p.ld_out] = v[0][j];
-            break;
-        }
-        case TC_RESID_BF16: {
-            uint16_t* h = p.resid + (size_t)t0 * p.ld_out + col;
-            uint16_t hv[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) hv[j] = j < nt ? h[(size_t)j * p.ld_out] : (uint16_t)0;
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (j < nt) h[(size_t)j * p.ld_out] = f2bf(bf2f(hv[j]) + v[0][j]);
-            break;
-        }
         case TC_SWIGLU: {
-            uint16_t* o = reinterpret_cast<uint16_t*>(out_base) + (size_t)t0 * p.ld_out + col;
+            const int f0 = tile * (kTcBN / 2) + cA;
+            if (f0 >= p.seg_rows[seg]) break;
+            float s[N];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const float g = v[0][j], up = v[1][j];
-                const float sg = 1.0f / (1.0f + expf(-g));  // gate * sigmoid(gate) * up (:3522)
-                if (j < nt) o[(size_t)j * p.ld_out] = f2bf((g * sg) * up);
+            for (int i = 0; i < N; ++i) {
+                const float g = vA[i], up = vB[i];
+                const float sg = 1.0f / (1.0f + expf(-g));  // gate * sigmoid(gate) * up
+                s[i] = (g * sg) * up;
+            }
+            uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]) + (size_t)t * p.ld_out + f0;
+            if (f0 + N <= p.seg_rows[seg]) {
+                store_bf16_run<N>(o, s);
+            } else {
+#pragma unroll
+                for (int i = 0; i < N; ++i)
+                    if (f0 + i < p.seg_rows[seg]) o[i] = f2bf(s[i]);
             }
             break;
         }
         case TC_QKV_ROPE: {
             const int module = p.seg_module[seg];
-            int pos[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) pos[j] = j < nt ? __ldg(p.ctx_lens + t0 + j) : 0;
+            const int head = tile * 2 + (cA >> 7);  // one head = 128 columns
+            if (head * 128 >= p.seg_rows[seg]) break;
+            const int d = cA & 127;  // < 64; its partner is d + 64
+            const int pos = __ldg(p.ctx_lens + t);
+            float a[N], b[N];
             if (module != AOS_MOD_V) {
-                // half-split RoPE (mlx_cpp_wrapper_real.cpp:3270-3280): pair (d, d+64)
-                const int half = kTcBM / 2, i = row & (half - 1);
-                const int partner = row ^ half;
-                float2 cs[32];
+                // half-split RoPE: (x_d, x_{d+64}) -> (x_d c - x_{d+64} s, x_d s + x_{d+64} c)
+                const float2* cs = reinterpret_cast<const float2*>(p.rope) + (size_t)pos * 64 + d;
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    cs[j] = *reinterpret_cast<const float2*>(p.rope + ((size_t)pos[j] * half + i) * 2);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) es.xbuf[row * 33 + j] = v[0][j];
-                epi_bar();
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float x = v[0][j], y = es.xbuf[partner * 33 + j];
-                    v[0][j] = row < half ? (x * cs[j].x - y * cs[j].y) : (y * cs[j].y + x * cs[j].x);
+                for (int i = 0; i < N; ++i) {
+                    const float2 c = __ldg(cs + i);
+                    a[i] = vA[i] * c.x - vB[i] * c.y;
+                    b[i] = vB[i] * c.x + vA[i] * c.y;
                 }
-                epi_bar();
-            }
-            if (module == AOS_MOD_Q) {
-                uint16_t* o = reinterpret_cast<uint16_t*>(out_base) + (size_t)t0 * p.ld_out + col;
+            } else {
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (j < nt) o[(size_t)j * p.ld_out] = f2bf(v[0][j]);
+                for (int i = 0; i < N; ++i) {
+                    a[i] = vA[i];
+                    b[i] = vB[i];
+                }
+            }
+            uint16_t* dst;
+            if (module == AOS_MOD_Q) {
+                dst = reinterpret_cast<uint16_t*>(p.out[seg]) + (size_t)t * p.ld_out + head * 128 + d;
             } else {
                 uint16_t* pool = module == AOS_MOD_K ? p.k_pool : p.v_pool;
-                const int kvh = tile;  // one tile per kv head (head_dim == 128)
-                int blk[32];
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    blk[j] = j < nt ? __ldg(p.block_tables + (size_t)(t0 + j) * p.max_blocks + (pos[j] >> 4)) : 0;
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (j < nt) {
-                        const size_t idx =
-                            ((((size_t)p.layer * p.num_blocks + blk[j]) * p.nkv + kvh) * 16 + (pos[j] & 15)) * 128 + row;
-                        pool[idx] = f2bf(v[0][j]);
-                    }
+                const int blk = __ldg(p.block_tables + (size_t)t * p.max_blocks + (pos >> 4));
+                dst = pool + ((((size_t)p.layer * p.num_blocks + blk) * p.nkv + head) * 16 + (pos & 15)) * 128 + d;
             }
+            store_bf16_run<N>(dst, a);
+            store_bf16_run<N>(dst + 64, b);
             break;
         }
         case TC_SHRINK_HM: {
-            const int slot = tile * kShrinkGroupsPerTile + row / kGroup;
+            const int slot = tile * kShrinkGroupsPerTile + k;
             if (slot >= ng) break;
-            const int c = __ldg(p.groups + slot) * kGroup + row % kGroup;
-            const int owner = __ldg(p.col_owner + c);
-            // per-token gate * alpha/rank of the column's adapter (0 when the
-            // token did not select it); built by the routing prep each step
-            const float* ct = p.coef + (size_t)t0 * p.max_adapters + (owner >= 0 ? owner : 0);
-            float cf[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) cf[j] = (owner >= 0 && j < nt) ? __ldg(ct + (size_t)j * p.max_adapters) : 0.0f;
-            uint16_t* o = reinterpret_cast<uint16_t*>(out_base) + (size_t)t0 * p.R + c;
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (j < nt) o[(size_t)j * p.R] = f2bf(v[0][j] * cf[j]);
+            const int c0 = __ldg(p.groups + slot) * kGroup;  // rank column of the group's first column
+            shrink_run<N>(p, seg, t, c0, cA - 64 * k, vA);
+            shrink_run<N>(p, seg, t, c0, cB - 64 * k, vB);
             break;
         }
         default:
@@ -281,31 +362,32 @@ __device__ __forceinline__ void epilogue_chunk(const TcParams& p, const EpiSmem&
     }
 }
 
-
 // ---------------------------------------------------------------- schedule
-// Stream-K over two pools.  Pool A holds the K steps of the shrink tiles
-// (64-column blocks of the input against two touched lora_A groups); pool B
-// holds the steps of the base tiles, each tile's K steps followed by its
-// expand steps (one per touched rank group).  CTA c takes the contiguous slice
-// [c*P/G, (c+1)*P/G) of pool A and then of pool B, so every SM streams the
-// same amount, every SM finishes its shrink share first, and only the expand
-// steps (which read the shrink output) wait for the shrink tiles.  A tile cut
-// between CTAs is finished by the piece that arrives last: it waits until the
-// other pieces have stored their fp32 partials and sums them with its own
-// accumulator in piece order.
+// Stream-K over three pools, taken by every CTA in this order:
+//   A: the K steps of the shrink tiles (four touched lora_A groups each);
+//   B: the K steps of the base tiles;
+//   C: the expand steps of the base tiles (one per touched rank group).
+// CTA c takes the contiguous slice [c*P/G, (c+1)*P/G) of each pool, so every
+// SM streams the same amount in each phase.  A tile cut into several pieces
+// (across CTAs, or across pools B and C) has each piece's fp32 partial stored
+// and is finished after a grid barrier by the parallel reduction, which sums
+// the pieces in piece order (fixed order: results are bit-identical run to
+// run).  The expand steps read the shrink output, so they start only after
+// the second grid barrier (shrink tiles reduced and gated).
 struct Sched {
-    int ng;            // touched rank groups
-    int kb;            // K steps per tile
-    int lenB;          // steps per base tile (K steps + expand steps)
-    int sh_per_seg;    // shrink tiles per shrink segment
-    int n_sh, n_base;  // shrink tiles, base tiles
-    long long PA, PB;  // pool lengths in steps
-    int GA, GB;        // CTAs that take part in each pool (<= pool length)
+    int ng;              // touched rank groups
+    int kb;              // K steps per tile
+    int sh_per_seg;      // shrink tiles per shrink segment
+    int n_sh, n_base;    // shrink tiles, base tiles
+    long long P[3];      // pool lengths in steps
+    int G[3];            // CTAs that take part in each pool
+    int len[3];          // steps per tile in each pool
 };
 
 struct Piece {
     int tile;          // global tile id: shrink tiles first, then base tiles
-    int s0, s1;        // step range within the tile
+    int pool;          // 0 A, 1 B, 2 C
+    int s0, s1;        // step range within the tile's part of the pool
     int idx, n;        // piece index within the tile, pieces of the tile in total
     bool shrink;
     int seg, t;        // segment, and tile index within the segment
@@ -315,19 +397,22 @@ __device__ __forceinline__ Sched make_sched(const TcParams& p) {
     Sched s;
     s.ng = (p.lora || p.sh_nseg) ? __ldg(p.n_groups) : 0;
     s.kb = p.kb;
-    s.lenB = p.kb + (p.lora ? s.ng : 0);
     s.sh_per_seg = p.sh_nseg ? cdiv(s.ng, kShrinkGroupsPerTile) : 0;
     s.n_sh = p.sh_nseg * s.sh_per_seg;
     s.n_base = 0;
     for (int g = 0; g < p.n_seg; ++g) s.n_base += p.seg_tiles[g];
-    s.PA = (long long)s.n_sh * s.kb;
-    s.PB = (long long)s.n_base * s.lenB;
+    s.len[0] = s.kb;
+    s.len[1] = s.kb;
+    s.len[2] = s.ng;
+    s.P[0] = (long long)s.n_sh * s.kb;
+    s.P[1] = (long long)s.n_base * s.kb;
+    s.P[2] = p.lora ? (long long)s.n_base * s.ng : 0;
     // Every slice is at least len/kMaxPiecesPerPool steps long, so no tile is
-    // cut into more than kMaxPiecesPerPool + 1 pieces.
-    const long long la = max(1, cdiv(s.kb, kMaxPiecesPerPool));
-    const long long lb = max(1, cdiv(s.lenB, kMaxPiecesPerPool));
-    s.GA = s.PA > 0 ? (int)max(1ll, min((long long)gridDim.x, s.PA / la)) : 0;
-    s.GB = (int)max(1ll, min((long long)gridDim.x, s.PB / lb));
+    // cut into more than kMaxPiecesPerPool + 1 pieces per pool.
+    for (int q = 0; q < 3; ++q) {
+        const long long l = max(1, cdiv(max(s.len[q], 1), kMaxPiecesPerPool));
+        s.G[q] = s.P[q] > 0 ? (int)max(1ll, min((long long)gridDim.x, s.P[q] / l)) : 0;
+    }
     return s;
 }
 __device__ __forceinline__ long long pstart(int c, long long P, int G) { return (long long)c * P / G; }
@@ -351,38 +436,68 @@ __device__ __forceinline__ void tile_info(const TcParams& p, const Sched& sc, in
         pc.t = b;
     }
 }
+// First CTA and piece count of `tile` in pool q.
+__device__ __forceinline__ void pool_pieces(const Sched& sc, int q, int local, int& c0, int& n) {
+    const long long a = (long long)local * sc.len[q];
+    c0 = cta_of(a, sc.P[q], sc.G[q]);
+    n = cta_of(a + sc.len[q] - 1, sc.P[q], sc.G[q]) - c0 + 1;
+}
+// Pieces of `tile` in total: a shrink tile has its pool-A pieces, a base tile
+// its pool-B pieces followed by its pool-C pieces.
+__device__ __forceinline__ int tile_npieces(const Sched& sc, int tile, int* nB = nullptr) {
+    int c0, n;
+    if (tile < sc.n_sh) {
+        pool_pieces(sc, 0, tile, c0, n);
+        return n;
+    }
+    const int b = tile - sc.n_sh;
+    pool_pieces(sc, 1, b, c0, n);
+    if (nB) *nB = n;
+    if (sc.P[2] > 0) {
+        int c2, n2;
+        pool_pieces(sc, 2, b, c2, n2);
+        n += n2;
+    }
+    return n;
+}
 
-// Iterates this CTA's pieces in order (pool A, then pool B).  All three roles
-// walk the same sequence.
+// Iterates this CTA's pieces in order (pool A, B, C).  All three roles walk
+// the same sequence.
 struct PieceIter {
     int pool;
-    long long s, e;  // current step, end of this CTA's slice
+    long long s, e;  // current step, end of this CTA's slice of the pool
+    __device__ __forceinline__ void set(const Sched& sc) {
+        const int c = blockIdx.x;
+        s = c < sc.G[pool] ? pstart(c, sc.P[pool], sc.G[pool]) : 0;
+        e = c < sc.G[pool] ? pstart(c + 1, sc.P[pool], sc.G[pool]) : 0;
+    }
     __device__ __forceinline__ void init(const Sched& sc) {
         pool = 0;
-        const int c = blockIdx.x;
-        s = c < sc.GA ? pstart(c, sc.PA, sc.GA) : 0;
-        e = c < sc.GA ? pstart(c + 1, sc.PA, sc.GA) : 0;
+        set(sc);
     }
     __device__ __forceinline__ bool next(const TcParams& p, const Sched& sc, Piece& pc) {
         while (s >= e) {
-            if (pool == 1) return false;
-            pool = 1;
-            const int c = blockIdx.x;
-            s = c < sc.GB ? pstart(c, sc.PB, sc.GB) : 0;
-            e = c < sc.GB ? pstart(c + 1, sc.PB, sc.GB) : 0;
+            if (pool == 2) return false;
+            ++pool;
+            set(sc);
         }
-        const long long P = pool == 0 ? sc.PA : sc.PB;
-        const int G = pool == 0 ? sc.GA : sc.GB;
-        const int len = pool == 0 ? sc.kb : sc.lenB;
-        const int local_tile = (int)(s / len);
-        const long long tstart = (long long)local_tile * len;
+        const int len = sc.len[pool];
+        const int local = (int)(s / len);
+        const long long tstart = (long long)local * len;
         const long long tend = min(tstart + len, e);
-        tile_info(p, sc, pool == 0 ? local_tile : local_tile + sc.n_sh, pc);
+        tile_info(p, sc, pool == 0 ? local : local + sc.n_sh, pc);
+        pc.pool = pool;
         pc.s0 = (int)(s - tstart);
         pc.s1 = (int)(tend - tstart);
-        const int c0 = cta_of(tstart, P, G);
-        pc.n = cta_of(tstart + len - 1, P, G) - c0 + 1;
+        int c0, n;
+        pool_pieces(sc, pool, local, c0, n);
         pc.idx = (int)blockIdx.x - c0;
+        if (pool == 2) {
+            int cB, nB;
+            pool_pieces(sc, 1, local, cB, nB);
+            pc.idx += nB;
+        }
+        pc.n = tile_npieces(sc, pc.tile);
         s = tend;
         return true;
     }
@@ -406,6 +521,11 @@ __device__ __noinline__ bool spin_ge(const int* ptr, int target, int* err) {
         }
     }
 }
+__device__ __forceinline__ bool ld_acquire_ge(const int* ptr, int target) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+    return v >= target;
+}
 
 // ---------------------------------------------------------------- the kernel
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
@@ -420,16 +540,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     uint64_t* tfull_bar = empty_bar + NS;   // [2]
     uint64_t* tempty_bar = tfull_bar + 2;   // [2]
     uint64_t* drain_bar = tempty_bar + 2;   // [1]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+    uint64_t* a_done_bar = drain_bar + 1;   // drain warps: shrink pieces added (4 arrivals)
+    uint64_t* all_done_bar = a_done_bar + 1;  // drain warps: every piece added (4 arrivals)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(all_done_bar + 1);
     int* flag = reinterpret_cast<int*>(tmem_slot + 1);
-    float* xbuf = reinterpret_cast<float*>(tail + 512);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const Sched sc = make_sched(p);
-    const int cols_per_acc = p.n_sub * p.T_pad;
+    const int cols_per_acc = p.tb * kTcBN;
     const int acc_stages = (2 * cols_per_acc <= 512) ? 2 : 1;
-    int tmem_cols = 32;
-    while (tmem_cols < acc_stages * cols_per_acc) tmem_cols <<= 1;
+    constexpr int tmem_cols = 512;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
@@ -441,6 +561,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             mbar_init(smem_u32(&tempty_bar[a]), 4);
         }
         mbar_init(smem_u32(drain_bar), 1);
+        mbar_init(smem_u32(a_done_bar), 4);
+        mbar_init(smem_u32(all_done_bar), 4);
+        flag[1] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
@@ -453,17 +576,86 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const uint32_t idesc = idesc_bf16(p.T_pad);
     unsigned long long* tr = p.trace ? p.trace + (size_t)blockIdx.x * kTraceStride : nullptr;
-    if (tr && threadIdx.x == 0) tr[192] = gtimer();
+    if (tr && threadIdx.x == 0) {
+        tr[192] = gtimer();
+        uint32_t smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        tr[220] = smid;
+    }
+    constexpr uint32_t kBlkW = kBlkRows * kTcBK;  // elements of a 128 x 64 weight block (16 KB)
+    constexpr uint32_t kBlkA = kGroup * kTcBK;    // elements of a 64 x 64 lora_A block (8 KB)
+    constexpr uint32_t kActBox = kTcTok * 128;    // shared-memory bytes reserved per activation box
+
+    // Conversion of the split tiles in [lo, hi) by `nthr` threads of every CTA
+    // (thread index `ti`): an item is (tile, pair chunk k, 32 tokens, half g);
+    // its thread reads 16 pairs of one token from the fixed-point
+    // accumulator, zeroes them for the next launch and applies the epilogue.
+    // Two items per thread are loaded before either is used.
+    auto convert = [&](int lo, int hi, int nthr, int ti) {
+        const int nq = (p.T + 31) / 32;
+        const long long n_items = (long long)(hi - lo) * 4 * nq * 64;
+        const long long stride = (long long)gridDim.x * nthr;
+        for (long long base = (long long)blockIdx.x * nthr + ti; base < n_items; base += 2 * stride) {
+            longlong2 w[2][2][8];
+            bool live[2];
+            int tile_[2], k_[2], tok_[2], g_[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const long long item = base + e * stride;
+                live[e] = item < n_items;
+                if (!live[e]) continue;
+                const long long unit = item / 64;
+                const int wi = (int)(item % 64);
+                tile_[e] = lo + (int)(unit / (4 * nq));
+                const int rem = (int)(unit % (4 * nq));
+                k_[e] = rem / nq;
+                const int qq = rem % nq;
+                g_[e] = wi >> 5;
+                tok_[e] = qq * 32 + (wi & 31);
+                live[e] = tile_npieces(sc, tile_[e]) > 1;  // else finished straight from TMEM
+                if (!live[e]) continue;
+                const int mode = tile_[e] < sc.n_sh ? TC_SHRINK_HM : p.mode;
+                int cA, cB;
+                chunk_cols(mode, k_[e], cA, cB);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int c = h ? cB : cA;  // multiple of 32: one accumulator chunk
+                    longlong2* src = reinterpret_cast<longlong2*>(
+                        p.acc + (((size_t)tile_[e] * 8 + c / 32) * p.acc_q + qq) * 1024) + (size_t)(8 * g_[e]) * 32 + (wi & 31);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) w[e][h][j] = __ldcg(src + j * 32);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) __stcg(src + j * 32, make_longlong2(0, 0));
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                if (!live[e] || tok_[e] >= p.T) continue;
+                Piece pc;
+                tile_info(p, sc, tile_[e], pc);
+                const int mode = pc.shrink ? TC_SHRINK_HM : p.mode;
+                float a[16], b[16];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    a[2 * j] = __ll2float_rn(w[e][0][j].x) * kFixInv;
+                    a[2 * j + 1] = __ll2float_rn(w[e][0][j].y) * kFixInv;
+                    b[2 * j] = __ll2float_rn(w[e][1][j].x) * kFixInv;
+                    b[2 * j + 1] = __ll2float_rn(w[e][1][j].y) * kFixInv;
+                }
+                apply_pairs<16>(p, mode, pc.seg, pc.t, k_[e], tok_[e], 16 * g_[e], a, b, sc.ng);
+            }
+        }
+    };
+    volatile int* go_final = flag + 1;  // converter -> drain: 1 = every CTA's pieces are in, -1 = failed
 
     if (warp == 0) {
         // ============================ TMA producer ============================
-        // The weight-side boxes (W, lora_A, lora_B) of the first NS stages are
+        // The weight-side copies (W, lora_A, lora_B) of the first NS stages are
         // issued before pdl_wait(): weights are static and the group list was
         // written two or more launches earlier.  The activation-side boxes (X,
         // hm) follow once the previous launch has completed; hm boxes also wait
-        // until every shrink tile of this launch is finished.
+        // for the grid barrier after which every shrink tile is gated and stored.
         if (lane == 0) {
             const uint64_t pol_w = policy_evict_first();
             const uint64_t pol_x = policy_evict_last();
@@ -473,50 +665,63 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true, waited = false, shrink_ready = (sc.n_sh == 0);
-            int pre_tile[16], pre_step[16];
+            int pre_tile[16], pre_pool[16], pre_step[16];
             int n_pre = 0;
-            auto step_bytes = [&](const Piece& pc, int st) -> uint32_t {
+            // weight blocks of a step: shrink -> lora_A groups (8 KB each); base / expand -> two 16 KB blocks
+            auto weights = [&](const Piece& pc, int st, uint32_t sbase, uint32_t fb, bool issue) -> uint32_t {
+                uint32_t bytes = 0;
                 if (pc.shrink) {
-                    const int nv = min(kShrinkGroupsPerTile, sc.ng - pc.t * kShrinkGroupsPerTile);
-                    return (uint32_t)(nv * kGroup * 128 + p.T_pad * 128);
-                }
-                if (st >= sc.kb) return (uint32_t)(p.n_sub * (kTcBM * 128 + p.T_pad * 128));
-                return (uint32_t)(p.n_sub * kTcBM * 128 + p.T_pad * 128);
-            };
-            auto issue_w = [&](const Piece& pc, int st, uint32_t sbase, uint32_t fb) {
-                if (pc.shrink) {  // lora_A rows of the tile's (up to) two touched groups
                     const int first = pc.t * kShrinkGroupsPerTile;
                     const int nv = min(kShrinkGroupsPerTile, sc.ng - first);
-                    for (int q = 0; q < nv; ++q)
-                        tma_2d(&p.tm_a[pc.seg], sbase + q * (kGroup * 128), fb, st * kTcBK,
-                               __ldg(p.groups + first + q) * kGroup, pol_w);
-                } else if (st < sc.kb) {
-                    for (int sub = 0; sub < p.n_sub; ++sub)
-                        tma_2d(&p.tm_w[pc.seg * p.n_sub + sub], sbase + sub * (kTcBM * 128), fb, st * kTcBK,
-                               p.seg_wrow0[pc.seg] + pc.t * kTcBM, pol_w);
-                } else {  // LoRA expand: lora_B[tile rows, group cols]
-                    const int gcol = __ldg(p.groups + (st - sc.kb)) * kGroup;
-                    for (int sub = 0; sub < p.n_sub; ++sub)
-                        tma_2d(&p.tm_lb[pc.seg * p.n_sub + sub], sbase + sub * (kTcBM * 128), fb, gcol, pc.t * kTcBM,
-                               pol_w);
+                    for (int q = 0; q < nv; ++q) {
+                        if (issue)
+                            bulk_g2s(sbase + q * (kBlkA * 2),
+                                     p.a_pk[pc.seg] + ((size_t)__ldg(p.groups + first + q) * sc.kb + st) * kBlkA,
+                                     kBlkA * 2, fb, pol_w);
+                        bytes += kBlkA * 2;
+                    }
+                    return bytes;
                 }
+                const int seg_blocks = (p.seg_rows[pc.seg] + kBlkRows - 1) / kBlkRows;
+                const int g = pc.pool == 2 ? __ldg(p.groups + st) : 0;
+                for (int h = 0; h < 2; ++h) {
+                    const uint16_t* src;
+                    if (p.n_sub == 2) {  // gate / up: block t of each
+                        src = pc.pool == 1 ? p.w_pk[pc.seg * 2 + h] + (((size_t)(p.seg_wrow0[pc.seg] / kBlkRows + pc.t)) * sc.kb + st) * kBlkW
+                                           : p.b_pk[pc.seg * 2 + h] + ((size_t)pc.t * p.n_rgroups + g) * kBlkW;
+                    } else {  // blocks 2t and 2t+1 of the segment
+                        if (2 * pc.t + h >= seg_blocks) continue;
+                        src = pc.pool == 1
+                                  ? p.w_pk[pc.seg] + (((size_t)(p.seg_wrow0[pc.seg] / kBlkRows + 2 * pc.t + h)) * sc.kb + st) * kBlkW
+                                  : p.b_pk[pc.seg] + ((size_t)(2 * pc.t + h) * p.n_rgroups + g) * kBlkW;
+                    }
+                    if (issue) bulk_g2s(sbase + h * (kBlkW * 2), src, kBlkW * 2, fb, pol_w);
+                    bytes += kBlkW * 2;
+                }
+                return bytes;
+            };
+            auto act_bytes = [&](const Piece& pc) -> uint32_t {
+                const int nh = (pc.pool == 2 && p.n_sub == 2) ? 2 : 1;
+                return (uint32_t)(nh * p.tb * p.T_box * 128);
             };
             auto issue_x = [&](const Piece& pc, int st, uint32_t sbase, uint32_t fb) -> bool {
                 const uint32_t act = sbase + p.act_off;
-                if (pc.shrink || st < sc.kb) {
-                    tma_2d(&p.tm_x, act, fb, st * kTcBK, 0, pol_x);
+                if (pc.pool != 2) {
+                    for (int b = 0; b < p.tb; ++b) tma_2d(&p.tm_x, act + b * kActBox, fb, st * kTcBK, b * kTcTok, pol_x);
                     return true;
                 }
-                if (!shrink_ready) {  // hm is written by this launch's shrink tiles
-                    if (tr) tr[198] = gtimer();
-                    if (!spin_ge(p.sync, sc.n_sh, p.err)) return false;
+                if (!shrink_ready) {  // hm is written by this launch's shrink tiles and reduction
+                    if (tr) tr[202] = gtimer();
+                    if (!spin_ge(p.sync + 1, (int)gridDim.x, p.err)) return false;
                     asm volatile("fence.proxy.async.global;" ::: "memory");
-                    if (tr) tr[199] = gtimer();
+                    if (tr) tr[203] = gtimer();
                     shrink_ready = true;
                 }
-                const int gcol = __ldg(p.groups + (st - sc.kb)) * kGroup;
-                for (int sub = 0; sub < p.n_sub; ++sub)
-                    tma_2d(&p.tm_lh[pc.seg * p.n_sub + sub], act + sub * (p.T_pad * 128), fb, gcol, 0, pol_x);
+                const int gcol = __ldg(p.groups + st) * kGroup;
+                const int nh = p.n_sub == 2 ? 2 : 1;
+                for (int h = 0; h < nh; ++h)
+                    for (int b = 0; b < p.tb; ++b)
+                        tma_2d(&p.tm_lh[pc.seg * p.n_sub + h], act + (h * p.tb + b) * kActBox, fb, gcol, b * kTcTok, pol_x);
                 return true;
             };
             auto finish_wait = [&]() -> bool {
@@ -526,6 +731,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 for (int i = 0; i < n_pre; ++i) {
                     Piece pc;
                     tile_info(p, sc, pre_tile[i], pc);
+                    pc.pool = pre_pool[i];
                     if (!issue_x(pc, pre_step[i], smem_u32(stages + (size_t)i * p.stage_bytes), smem_u32(&full_bar[i])))
                         return false;
                 }
@@ -540,12 +746,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, p.err)) { ok = false; break; }
                     const uint32_t fb = smem_u32(&full_bar[stage]);
                     const uint32_t sbase = smem_u32(stages + (size_t)stage * p.stage_bytes);
-                    mbar_expect_tx(fb, step_bytes(pc, st));
-                    issue_w(pc, st, sbase, fb);
+                    mbar_expect_tx(fb, weights(pc, st, sbase, fb, false) + act_bytes(pc));
+                    weights(pc, st, sbase, fb, true);
                     if (waited) {
                         if (!issue_x(pc, st, sbase, fb)) ok = false;
                     } else {  // first round of stages: stage index == n_pre
                         pre_tile[n_pre] = pc.tile;
+                        pre_pool[n_pre] = pc.pool;
                         pre_step[n_pre] = st;
                         ++n_pre;
                     }
@@ -565,6 +772,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     } else if (warp == 1) {
         // ============================ MMA issuer ==============================
         if (lane == 0) {
+            const uint32_t idesc256 = idesc_bf16(kTcBN), idesc128 = idesc_bf16(kTcBN / 2);
             int stage = 0;
             uint32_t phase = 0;
             int it = 0, n_waited = 0;
@@ -579,7 +787,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 if (!mbar_wait(smem_u32(&tempty_bar[acc]), tphase ^ 1u, p.err)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d0 = tmem_base + (uint32_t)(acc * cols_per_acc);
-                const int nsub = pc.shrink ? 1 : p.n_sub;
+                const bool split = pc.pool == 2 && p.n_sub == 2;  // gate / up expand: two N=128 halves
                 bool first = true;
                 for (int st = pc.s0; st < pc.s1; ++st) {
                     if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.err)) { ok = false; break; }
@@ -588,14 +796,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     ++n_waited;
                     const uint32_t sbase = smem_u32(stages + (size_t)stage * p.stage_bytes);
                     const uint32_t act = sbase + p.act_off;
-                    const bool expand = !pc.shrink && st >= sc.kb;
-                    for (int sub = 0; sub < nsub; ++sub) {
-                        const uint32_t a0 = sbase + sub * (kTcBM * 128);
-                        const uint32_t b0 = act + (expand ? sub * (p.T_pad * 128) : 0);
+                    for (int b = 0; b < p.tb; ++b) {
+                        if (split) {
+                            for (int h = 0; h < 2; ++h) {
+                                const uint32_t a0 = act + (h * p.tb + b) * kActBox, b0 = sbase + h * (kBlkW * 2);
 #pragma unroll
-                        for (int kk = 0; kk < kTcBK / 16; ++kk)
-                            umma_bf16(d0 + sub * p.T_pad, desc_sw128(a0 + kk * 32), desc_sw128(b0 + kk * 32), idesc,
-                                      (first && kk == 0) ? 0u : 1u);
+                                for (int kk = 0; kk < kTcBK / 16; ++kk)
+                                    umma_bf16(d0 + b * kTcBN + h * (kTcBN / 2), desc_sw128(a0 + kk * 32),
+                                              desc_sw128(b0 + kk * 32), idesc128, (first && kk == 0) ? 0u : 1u);
+                            }
+                        } else {
+                            const uint32_t a0 = act + b * kActBox;
+#pragma unroll
+                            for (int kk = 0; kk < kTcBK / 16; ++kk)
+                                umma_bf16(d0 + b * kTcBN, desc_sw128(a0 + kk * 32), desc_sw128(sbase + kk * 32), idesc256,
+                                          (first && kk == 0) ? 0u : 1u);
+                        }
                     }
                     issued_any = true;
                     umma_commit(smem_u32(&empty_bar[stage]));  // frees the stage when these MMAs finish
@@ -610,155 +826,207 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 mbar_wait_drain(smem_u32(drain_bar), 0);
             }
         }
-    } else {
-        // ============================ epilogue ================================
+    } else if (warp < 6) {
+        // ============================ drain (warps 2-5) =========================
+        // A warp reads TMEM lanes 32 * (warp % 4) ... + 31, i.e. those tokens.
+        // Whole tiles get their epilogue straight from TMEM; pieces of split
+        // tiles are added into the fixed-point accumulators.  The drain never
+        // waits on other CTAs: it tells the converter warps through shared-
+        // memory barriers when its shrink pieces and all its pieces are in.
         const int q = warp & 3;
-        const int row = q * 32 + lane;
+        const int tok_lane = q * 32 + lane;
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-        EpiSmem es{xbuf};
-        pdl_wait();  // the epilogue reads and writes activations of the previous launches
-        const size_t slot_floats = (size_t)p.n_sub * p.T_pad * kTcBM;
-        int it = 0, n_partial = 0;
+        const int tid = threadIdx.x - 64;  // 0..127
+        // per-warp 8 KB staging of one fixed-point chunk: [16 column pairs][32 tokens][2]
+        long long* stg = reinterpret_cast<long long*>(tail + kTcTailBytes) + (size_t)(warp - 2) * 1024;
+        pdl_wait();  // reads and writes activations and accumulators of earlier launches
+        // signal a converter barrier once this warp's bulk reductions have landed
+        auto signal = [&](uint64_t* bar) {
+            if (lane == 0) {
+                asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+                asm volatile("fence.proxy.async.global;" ::: "memory");
+                mbar_arrive(smem_u32(bar));
+            }
+            __syncwarp();
+        };
+        // Gate * alpha/rank for token `tok` of the 32 eight-column units of
+        // shrink tile `t`: one contiguous 128-byte run of the prep table.
+        auto gate_coefs = [&](int t, int tok, float (&cf)[32]) {
+            const float4* src = reinterpret_cast<const float4*>(
+                p.ucoef + ((size_t)(tok < p.T ? tok : 0) * p.n_rgroups + (size_t)t * kShrinkGroupsPerTile) * 8);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float4 w = __ldg(src + j);
+                cf[4 * j] = w.x;
+                cf[4 * j + 1] = w.y;
+                cf[4 * j + 2] = w.z;
+                cf[4 * j + 3] = w.w;
+            }
+        };
+
+        int it = 0;
+        bool a_signalled = false;
         PieceIter itr;
         itr.init(sc);
         Piece pc;
         while (itr.next(p, sc, pc)) {
+            if (!a_signalled && pc.pool != 0) {  // this CTA's shrink pieces are all in
+                signal(a_done_bar);
+                a_signalled = true;
+            }
             const int acc = it % acc_stages;
             const uint32_t tphase = (uint32_t)((it / acc_stages) & 1);
-            const bool ok = mbar_wait(smem_u32(&tfull_bar[acc]), tphase, p.err);
-            if (epi_bar_any(!ok)) break;
-            if (tr && threadIdx.x == 64 && it < 32) tr[128 + it] = gtimer();
+            float cf[32];
+            if (pc.shrink) gate_coefs(pc.t, tok_lane, cf);  // loads overlap the MMAs of this piece
+            const bool okw = mbar_wait(smem_u32(&tfull_bar[acc]), tphase, p.err);
+            if (epi_bar_any(!okw)) break;
+            if (tr && tid == 0 && it < 32) tr[128 + it] = gtimer();
             tc_fence_after();
             const uint32_t t_acc = tmem_base + lane_off + (uint32_t)(acc * cols_per_acc);
             const int mode = pc.shrink ? TC_SHRINK_HM : p.mode;
-            void* out = pc.shrink ? p.sh_out[pc.seg] : p.out[pc.seg];
-            const int nsub = pc.shrink ? 1 : p.n_sub;
-            int* arrived = p.counters + 2 * pc.tile;  // [0] pieces arrived, [1] partials stored
-            float v[2][32];
-            bool finished = false;  // this piece produced the tile's final output
-            bool last = pc.n == 1;
-            if (!last) {
-                if (threadIdx.x == 64) *flag = (atomicAdd(arrived, 1) == pc.n - 1);
-                epi_bar();
-                last = *flag != 0;
-                epi_bar();  // everyone has read the flag before it can be rewritten
-            }
-            if (pc.n == 1) {
-                for (int t0 = 0; t0 < p.T_pad; t0 += 32) {
-                    tmem_ld32(t_acc + t0, v[0]);
-                    if (nsub == 2) tmem_ld32(t_acc + p.T_pad + t0, v[1]);
-                    epilogue_chunk(p, es, mode, pc.seg, pc.t, out, sc.ng, row, t0, v);
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
-                finished = true;
-            } else if (!last) {
-                // store the partial in this CTA's next workspace slot [sub][t][row]
-                const bool room = n_partial < kMaxPartialsPerCta && pc.idx < kMaxPiecesPerTile;
-                const int slot = (int)blockIdx.x * kMaxPartialsPerCta + n_partial;
-                n_partial += room ? 1 : 0;
-                float* wsu = p.ws + (size_t)slot * slot_floats;
-                for (int t0 = 0; t0 < p.T_pad; t0 += 32)
+            if (pc.n == 1 && pc.shrink) {  // whole shrink tile: gate and store hm from TMEM
+                for (int b = 0; b < p.tb; ++b) {
+                    const int tok = b * kTcTok + tok_lane;
+                    if (b > 0) gate_coefs(pc.t, tok, cf);
 #pragma unroll
-                    for (int sub = 0; sub < 2; ++sub) {
-                        if (sub >= nsub) break;
-                        tmem_ld32(t_acc + sub * p.T_pad + t0, v[sub]);
-                        if (room) {
+                    for (int k = 0; k < 4; ++k) {
+                        float vA[32], vB[32];
+                        tmem_ld32(t_acc + b * kTcBN + 64 * k, vA);
+                        tmem_ld32(t_acc + b * kTcBN + 64 * k + 32, vB);
 #pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                __stcg(wsu + ((size_t)sub * p.T_pad + t0 + j) * kTcBM + row, v[sub][j]);
+                        for (int i = 0; i < 32; ++i) {
+                            vA[i] *= cf[8 * k + i / 8];
+                            vB[i] *= cf[8 * k + 4 + i / 8];
                         }
+                        if (tok < p.T) apply_pairs<32>(p, mode, pc.seg, pc.t, k, tok, 0, vA, vB, sc.ng);
                     }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
-                if (room) {
-                    if (threadIdx.x == 64) p.tile_slots[(size_t)pc.tile * kMaxPiecesPerTile + pc.idx] = slot;
-                    __threadfence();
-                    epi_bar();
-                    if (threadIdx.x == 64) atomicAdd(arrived + 1, 1);  // publish (after the fence)
-                } else if (threadIdx.x == 64) {
-                    atomicCAS(p.err, 0, AOS_ERR_INVALID);  // schedule limits exceeded
+                }
+            } else if (pc.n == 1) {  // the whole tile is here: epilogue straight from TMEM
+                for (int b = 0; b < p.tb; ++b) {
+                    const int tok = b * kTcTok + tok_lane;
+#pragma unroll 1
+                    for (int k = 0; k < 4; ++k) {
+                        int cA, cB;
+                        chunk_cols(mode, k, cA, cB);
+                        float vA[32], vB[32];
+                        tmem_ld32(t_acc + b * kTcBN + cA, vA);
+                        tmem_ld32(t_acc + b * kTcBN + cB, vB);
+                        if (tok < p.T) apply_pairs<32>(p, mode, pc.seg, pc.t, k, tok, 0, vA, vB, sc.ng);
+                    }
                 }
             } else {
-                // last piece: wait for the other pieces' partials, then sum in
-                // piece order with this piece's own accumulator (from TMEM)
-                if (threadIdx.x == 64) *flag = spin_ge(arrived + 1, pc.n - 1, p.err) ? 1 : 0;
-                epi_bar();
-                const bool ready = *flag != 0;
-                epi_bar();
-                if (ready) {
-                    __threadfence();
-                    for (int t0 = 0; t0 < p.T_pad; t0 += 32) {
+                // add the piece into the tile's fixed-point accumulator: value * 2^32
+                // rounded to int64, summed by TMA bulk reductions in L2 (integer
+                // addition is order-independent, so the sum is exact and the same
+                // on every run); shrink pieces are gated first
+                for (int b = 0; b < p.tb; ++b) {
+                    const int tok = b * kTcTok + tok_lane;
+                    const int qq = b * 4 + q;  // 32-token quarter
+                    const bool any = qq * 32 < p.T;
+                    if (b > 0 && pc.shrink) gate_coefs(pc.t, tok, cf);
+                    const bool valid = tok < p.T;
 #pragma unroll
-                        for (int sub = 0; sub < 2; ++sub) {
-                            if (sub >= nsub) break;
-                            float part[2][32];
-                            int k = 0;
-                            // pieces before this one, two at a time (independent loads in flight)
-                            for (; k < pc.idx; k += 2) {
-                                const bool two = k + 1 < pc.idx;
+                    for (int c = 0; c < kTcBN / 32; ++c) {
+                        float v[32];
+                        tmem_ld32(t_acc + b * kTcBN + c * 32, v);
+                        if (!any) continue;  // warp-uniform
+                        if (pc.shrink) {
 #pragma unroll
-                                for (int u = 0; u < 2; ++u) {
-                                    if (u == 1 && !two) break;
-                                    const int sl = __ldcg(p.tile_slots + (size_t)pc.tile * kMaxPiecesPerTile + k + u);
-                                    const float* src =
-                                        p.ws + (size_t)sl * slot_floats + ((size_t)sub * p.T_pad + t0) * kTcBM + row;
-#pragma unroll
-                                    for (int j = 0; j < 32; ++j) part[u][j] = __ldcg(src + (size_t)j * kTcBM);
-                                }
-#pragma unroll
-                                for (int j = 0; j < 32; ++j) {
-                                    float a = k == 0 ? part[0][j] : v[sub][j] + part[0][j];
-                                    if (two) a += part[1][j];
-                                    v[sub][j] = a;
-                                }
-                            }
-                            // this piece
-                            tmem_ld32(t_acc + sub * p.T_pad + t0, part[0]);
-#pragma unroll
-                            for (int j = 0; j < 32; ++j) v[sub][j] = pc.idx == 0 ? part[0][j] : v[sub][j] + part[0][j];
-                            // pieces after this one
-                            for (k = pc.idx + 1; k < pc.n; k += 2) {
-                                const bool two = k + 1 < pc.n;
-#pragma unroll
-                                for (int u = 0; u < 2; ++u) {
-                                    if (u == 1 && !two) break;
-                                    const int sl = __ldcg(p.tile_slots + (size_t)pc.tile * kMaxPiecesPerTile + k + u);
-                                    const float* src =
-                                        p.ws + (size_t)sl * slot_floats + ((size_t)sub * p.T_pad + t0) * kTcBM + row;
-#pragma unroll
-                                    for (int j = 0; j < 32; ++j) part[u][j] = __ldcg(src + (size_t)j * kTcBM);
-                                }
-#pragma unroll
-                                for (int j = 0; j < 32; ++j) {
-                                    float a = v[sub][j] + part[0][j];
-                                    if (two) a += part[1][j];
-                                    v[sub][j] = a;
-                                }
-                            }
+                            for (int i = 0; i < 32; ++i) v[i] *= cf[4 * c + i / 8];
                         }
-                        epilogue_chunk(p, es, mode, pc.seg, pc.t, out, sc.ng, row, t0, v);
+                        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                        __syncwarp();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const long long x = valid ? __float2ll_rn(v[2 * j] * kFix) : 0ll;
+                            const long long y = valid ? __float2ll_rn(v[2 * j + 1] * kFix) : 0ll;
+                            reinterpret_cast<longlong2*>(stg)[j * 32 + lane] = make_longlong2(x, y);
+                        }
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        __syncwarp();
+                        if (lane == 0) {
+                            long long* dst = p.acc + (((size_t)pc.tile * 8 + c) * p.acc_q + qq) * 1024;
+                            asm volatile(
+                                "cp.reduce.async.bulk.global.shared::cta.bulk_group.add.u64 [%0], [%1], %2;" ::"l"(dst),
+                                "r"(smem_u32(stg)), "r"(8192)
+                                : "memory");
+                            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                        }
                     }
-                    finished = true;
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
-                if (threadIdx.x == 64) {  // self-reset for the next launch
-                    arrived[0] = 0;
-                    arrived[1] = 0;
                 }
             }
-            if (finished && pc.shrink) {
-                // this shrink tile's hm columns are written: publish them to the expand steps
-                __threadfence();
-                epi_bar();
-                if (threadIdx.x == 64) atomicAdd(p.sync, 1);
-            }
-            if (tr && threadIdx.x == 64 && it < 32) tr[160 + it] = gtimer();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
+            if (tr && tid == 0 && it < 32) tr[160 + it] = gtimer();
             ++it;
+        }
+        // also on the error path: the converter warps wait (bounded) for these
+        if (!a_signalled) signal(a_done_bar);
+        signal(all_done_bar);
+        // then help with the final conversion once every CTA's pieces are in
+        {
+            const long long t0 = clock64();
+            int go = 0;
+            while ((go = *go_final) == 0)
+                if (clock64() - t0 > 2 * kSpinLimitCycles) break;  // the converter's own waits are bounded
+            if (go == 1) {
+                __threadfence();
+                convert(sc.n_sh, sc.n_sh + sc.n_base, 192, tid);
+            }
+        }
+    } else {
+        // ===================== converter (warps 6-7, 64 threads) =================
+        // Grid barriers over all CTAs and the conversion of split tiles: after
+        // every CTA's shrink pieces are in, the split shrink tiles' fixed-point
+        // sums become gated bf16 hm (then the expand steps may start); after
+        // every piece is in, the split base tiles get their epilogue.  Thread
+        // cid 0 does the atomics; the other drain and MMA work never waits here.
+        const int cid = threadIdx.x - 192;  // 0..63
+        pdl_wait();
+        auto cv_bar = [] { asm volatile("bar.sync 2, 64;" ::: "memory"); };
+        // every converter thread's writes happen before thread 0's release
+        auto release = [&](int i) {
+            cv_bar();
+            if (cid == 0) {
+                __threadfence();
+                atomicAdd(p.sync + i, 1);
+                if (tr) tr[194 + 2 * i] = gtimer();
+            }
+        };
+        // wait (thread 0, bounded) for an smem barrier phase, then for every CTA's arrival at sync[i]
+        auto await = [&](uint64_t* bar, int i) -> bool {
+            if (cid == 0) {
+                bool ok = mbar_wait(smem_u32(bar), 0, p.err);
+                if (ok && i >= 0) {
+                    __threadfence();
+                    atomicAdd(p.sync + i, 1);
+                    if (tr) tr[194 + 2 * i] = gtimer();
+                    ok = spin_ge(p.sync + i, (int)gridDim.x, p.err);
+                    if (ok && tr) tr[195 + 2 * i] = gtimer();
+                }
+                *flag = ok ? 1 : 0;
+            }
+            cv_bar();
+            const bool ok = *flag != 0;
+            cv_bar();
+            if (ok) __threadfence();
+            return ok;
+        };
+        bool ok = true;
+        if (sc.n_sh > 0) {
+            ok = await(a_done_bar, 0);
+            if (ok) {
+                convert(0, sc.n_sh, 64, cid);
+                release(1);
+            }
+        }
+        ok = ok && await(all_done_bar, 2);
+        if (cid == 0) *go_final = ok ? 1 : -1;  // the drain warps join the final conversion
+        if (ok) {
+            if (tr && cid == 0) tr[200] = gtimer();
+            convert(sc.n_sh, sc.n_sh + sc.n_base, 192, 128 + cid);
+            if (tr && cid == 0) tr[201] = gtimer();
         }
     }
 
@@ -767,12 +1035,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     tc_fence_after();
     if (threadIdx.x == 0) {
         if (tr) tr[193] = gtimer();
-        // the last CTA to leave resets the launch's shrink counter
+        // the last CTA to leave resets the launch's grid-barrier counters
         __threadfence();
-        const int old = atomicAdd(p.sync + 1, 1);
+        const int old = atomicAdd(p.sync + 3, 1);
         if (old == (int)gridDim.x - 1) {
             p.sync[0] = 0;
             p.sync[1] = 0;
+            p.sync[2] = 0;
+            p.sync[3] = 0;
             __threadfence();
         }
     }
@@ -780,7 +1050,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols));
 }
 
+}  // namespace
+
 // ---------------------------------------------------------------- host side
+namespace {
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -838,7 +1111,8 @@ int tc_encode_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uin
     return r == CUDA_SUCCESS ? AOS_OK : AOS_ERR_CUDA;
 }
 
-size_t tc_tail_bytes(const TcParams&) { return 512 + 128 * 33 * 4; }
+// mbarriers and flags, then the drain warps' 4 x 8 KB fixed-point staging
+size_t tc_tail_bytes(const TcParams&) { return kTcTailBytes + 4 * 8192; }
 
 size_t tc_smem_bytes(const TcParams& p) {
     return 1024 + (size_t)p.n_stages * p.stage_bytes + tc_tail_bytes(p);
@@ -848,19 +1122,19 @@ int tc_prepare(TcParams& p, int smem_budget) {
     if (p.T <= 0 || p.T > 256 || p.n_sub < 1 || p.n_sub > 2 || p.n_seg < 1 || p.n_seg > kTcMaxSets ||
         p.n_seg * p.n_sub > kTcMaxSets || p.sh_nseg < 0 || p.sh_nseg > kTcMaxSets || p.kb < 1)
         return AOS_ERR_INVALID;
-    p.T_pad = ((p.T + 15) / 16) * 16;
-    if (p.T_pad < 32) p.T_pad = 32;  // epilogue works in 32-token chunks
-    const uint32_t w_bytes = (uint32_t)p.n_sub * kTcBM * 128;
-    const uint32_t act_base = (uint32_t)p.T_pad * 128;
-    const uint32_t act_lora = (uint32_t)p.n_sub * p.T_pad * 128;
-    const uint32_t act = std::max(act_base, p.lora ? act_lora : 0u);
-    p.act_off = w_bytes;
-    p.stage_bytes = (w_bytes + act + 1023) & ~1023u;
+    p.T_pad = tc_t_pad(p.T);
+    p.T_box = tc_t_box(p.T);
+    p.tb = (p.T_pad + kTcTok - 1) / kTcTok;
+    // stage: 256 weight rows x 128 B, then one 128-row activation box per
+    // token block (two for the gate/up expand, whose halves read different hm)
+    const int n_act = p.tb * ((p.n_sub == 2 && p.lora) ? 2 : 1);
+    p.act_off = (uint32_t)kTcBN * 128;
+    p.stage_bytes = p.act_off + (uint32_t)n_act * kTcTok * 128;
     const size_t fixed = 1024 + tc_tail_bytes(p);
     int ns = (int)((smem_budget - (int)fixed) / (int)p.stage_bytes);
     static const int max_stages = [] {
-        const char* e = getenv("AOS_TC_MAX_STAGES");  // tuning knob, default 8
-        const int v = e ? atoi(e) : 8;
+        const char* e = getenv("AOS_TC_MAX_STAGES");  // tuning knob, default 4
+        const int v = e ? atoi(e) : 4;
         return v < 2 ? 2 : (v > 16 ? 16 : v);
     }();
     ns = std::min(ns, max_stages);
@@ -886,8 +1160,8 @@ cudaError_t tc_configure() {
     return cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
 }
 
-size_t tc_ws_bytes(const TcParams& p, int grid) {
-    return (size_t)grid * kMaxPartialsPerCta * p.n_sub * p.T_pad * kTcBM * sizeof(float);
+size_t tc_acc_bytes(const TcParams& p, int n_tiles) {
+    return (size_t)n_tiles * 8 * p.acc_q * 1024 * sizeof(long long);
 }
 
 cudaError_t tc_launch(const TcParams& p, int grid, cudaStream_t stream) {
