@@ -63,7 +63,9 @@ struct Sequence {
 };
 
 struct LayerPlan {
-    TcParams gemm[4];  // per input group: shrink + base + expand in one launch
+    TcParams gemm[4];    // per input group: shrink + base (+ expand when fused) in one launch
+    TcParams expand[4];  // q/k/v and o: the LoRA expand as a launch of its own
+    bool split[4];
     int gemm_grid[4];
 };
 
@@ -216,7 +218,7 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
         p.groups = c->d_groups;
         p.n_groups = c->d_n_groups;
         p.acc = c->d_acc;
-        p.acc_q = (c->T_cap + 31) / 32;
+        p.acc_T = c->T_cap;
         p.sync = c->d_sync;
         p.err = c->d_err;
         p.R = c->R;
@@ -309,11 +311,31 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
             p.resid = c->d_hidden;
             p.ld_out = (int)H;
         }
+        // Tuning knob AOS_SPLIT_EXPAND=1: run the q/k/v and o LoRA expand as a
+        // launch of its own (RoPE is linear, and the o epilogue adds into the
+        // residual anyway).  Off by default: measured slower than the fused launch.
+        p.pools = 7;
+        static const bool split_expand = [] {
+            const char* e = getenv("AOS_SPLIT_EXPAND");
+            return e && e[0] == '1';
+        }();
+        lp.split[g] = split_expand && p.lora && (g == kGroupQKV || g == kGroupO);
+        if (lp.split[g]) {
+            TcParams& e = lp.expand[g];
+            e = p;
+            e.pools = 4;
+            e.sh_nseg = 0;
+            e.add_out = g == kGroupQKV ? 1 : 0;
+            if ((rc = tc_prepare(e, smem_budget))) return rc;
+            p.pools = 3;
+        }
         if ((rc = tc_prepare(p, smem_budget))) return rc;
         lp.gemm_grid[g] = tc_num_sms();
         // Diagnostics: AOS_TC_TRACE=<0..3> traces layer 0's GEMM g.
-        if (const char* tv = getenv("AOS_TC_TRACE"))
+        if (const char* tv = getenv("AOS_TC_TRACE")) {  // 0-3: layer 0's GEMM g; 4-7: its expand launch
             if (layer == 0 && c->d_trace && atoi(tv) == g) p.trace = c->d_trace;
+            if (layer == 0 && c->d_trace && atoi(tv) == g + 4 && lp.split[g]) lp.expand[g].trace = c->d_trace;
+        }
     }
     return AOS_OK;
 }
@@ -338,12 +360,13 @@ int get_plan(aos_ctx* c, int T, StepPlan** out) {
     std::memset(&p, 0, sizeof(p));
     p.T = T;
     p.mode = TC_STORE_F32;
+    p.pools = 7;
     p.n_sub = 1;
     p.n_seg = 1;
     p.kb = (int)(c->cfg.hidden / 64);
     p.err = c->d_err;
     p.acc = c->d_acc;
-    p.acc_q = (c->T_cap + 31) / 32;
+    p.acc_T = c->T_cap;
     p.sync = c->d_sync;
     const uint32_t V = c->cfg.vocab;
     p.w_pk[0] = c->lm_head;
@@ -387,11 +410,13 @@ int enqueue_layer(aos_ctx* c, const StepPlan& plan, int layer, cudaStream_t s) {
     const uint32_t H = c->cfg.hidden;
     PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(c->d_hidden, c->attn_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
     PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupQKV], lp.gemm_grid[kGroupQKV], s));
+    if (lp.split[kGroupQKV]) PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.expand[kGroupQKV], lp.gemm_grid[kGroupQKV], s));
     PLAUNCH(c, AOS_K_ATTN, s,
             launch_attention(c->tm_k, c->tm_v, c->d_q, c->d_block_tables, c->d_ctx_lens, c->d_attn_part, c->d_attn_ml, T,
                              (int)c->cfg.n_heads, (int)c->cfg.n_kv_heads, layer, (int)c->cfg.kv_num_blocks, c->max_blocks,
                              c->attn_chunks, c->d_err, c->d_attn, s));
     PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupO], lp.gemm_grid[kGroupO], s));
+    if (lp.split[kGroupO]) PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.expand[kGroupO], lp.gemm_grid[kGroupO], s));
     PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(c->d_hidden, c->mlp_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
     PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupGU], lp.gemm_grid[kGroupGU], s));
     PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupD], lp.gemm_grid[kGroupD], s));
@@ -700,7 +725,7 @@ aos_ctx* aos_init(const aos_model_config* cfg) {
     INIT_CHECK(dalloc(&c->d_attn_ml, TC * k.n_kv_heads * c->attn_chunks * c->G * 2), "attn ml");
     {  // tiles of the largest launch: base tiles plus up to three shrink segments
         const size_t tiles = max_launch_tiles(c.get());
-        c->acc_bytes = tiles * 8 * (size_t)((c->T_cap + 31) / 32) * 1024 * sizeof(long long);
+        c->acc_bytes = tiles * kTcBN * (size_t)c->T_cap * sizeof(long long);
         INIT_CHECK(dalloc(&c->d_acc, c->acc_bytes / sizeof(long long)), "GEMM accumulators");
         INIT_CHECK(dalloc(&c->d_sync, 4), "sync");
     }

@@ -144,18 +144,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-// Barrier over the 4 epilogue warps that also ORs a predicate, so a failed
-// (timed-out) wait in any thread makes every epilogue thread leave together.
-__device__ __forceinline__ bool epi_bar_any(bool pred) {
-    uint32_t r;
-    asm volatile(
-        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}\n"
-        : "=r"(r)
-        : "r"((uint32_t)pred)
-        : "memory");
-    return r != 0;
-}
-
 // Shared-memory matrix descriptors (tcgen05 "version 1"), K-major operands.
 __device__ __forceinline__ uint64_t desc_sw128(uint32_t addr) {
     return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)(1024u >> 4) << 32) |
@@ -345,6 +333,13 @@ __device__ __forceinline__ void apply_pairs(const TcParams& p, int mode, int seg
                 const int blk = __ldg(p.block_tables + (size_t)t * p.max_blocks + (pos >> 4));
                 dst = pool + ((((size_t)p.layer * p.num_blocks + blk) * p.nkv + head) * 16 + (pos & 15)) * 128 + d;
             }
+            if (p.add_out) {  // expand-only launch: add the rotated LoRA term to the stored value
+#pragma unroll
+                for (int i = 0; i < N; ++i) {
+                    a[i] += bf2f(dst[i]);
+                    b[i] += bf2f(dst[64 + i]);
+                }
+            }
             store_bf16_run<N>(dst, a);
             store_bf16_run<N>(dst + 64, b);
             break;
@@ -363,34 +358,34 @@ __device__ __forceinline__ void apply_pairs(const TcParams& p, int mode, int seg
 }
 
 // ---------------------------------------------------------------- schedule
-// Stream-K over three pools, taken by every CTA in this order:
+// Stream-K over two pools, taken by every CTA in this order:
 //   A: the K steps of the shrink tiles (four touched lora_A groups each);
-//   B: the K steps of the base tiles;
-//   C: the expand steps of the base tiles (one per touched rank group).
-// CTA c takes the contiguous slice [c*P/G, (c+1)*P/G) of each pool, so every
-// SM streams the same amount in each phase.  A tile cut into several pieces
-// (across CTAs, or across pools B and C) has each piece's fp32 partial stored
-// and is finished after a grid barrier by the parallel reduction, which sums
-// the pieces in piece order (fixed order: results are bit-identical run to
-// run).  The expand steps read the shrink output, so they start only after
-// the second grid barrier (shrink tiles reduced and gated).
+//   B: the "positions" of the base tiles.  A base tile has kbe K steps and
+//      nge expand steps (one per touched rank group); position q of the tile
+//      is a K step or an expand step in proportion (bpos), so any range of
+//      positions holds both kinds in the tile's ratio.
+// CTA c takes the contiguous slice [c*P/G, (c+1)*P/G) of each pool.  A piece
+// (one tile's share of one slice) accumulates its K steps and then its expand
+// steps in one TMEM accumulator.  A CTA with at most two base pieces runs
+// both pieces' K steps before either's expand steps, so it has its whole
+// base share to stream while the shrink output is being finished.  A tile
+// cut into several pieces is summed in fixed point (see the drain).
 struct Sched {
-    int ng;              // touched rank groups
-    int kb;              // K steps per tile
-    int sh_per_seg;      // shrink tiles per shrink segment
-    int n_sh, n_base;    // shrink tiles, base tiles
-    long long P[3];      // pool lengths in steps
-    int G[3];            // CTAs that take part in each pool
-    int len[3];          // steps per tile in each pool
+    int ng;            // touched rank groups
+    int kb;            // K steps per tile
+    int sh_per_seg;    // shrink tiles per shrink segment
+    int n_sh, n_base;  // shrink tiles, base tiles
+    int kbe, nge;      // K steps and expand steps per base tile in this launch
+    long long P[2];    // pool lengths: shrink K steps, base positions
+    int G[2];          // CTAs that take part in each pool
+    int len[2];        // steps (positions) per tile
 };
 
 struct Piece {
-    int tile;          // global tile id: shrink tiles first, then base tiles
-    int pool;          // 0 A, 1 B, 2 C
-    int s0, s1;        // step range within the tile's part of the pool
-    int idx, n;        // piece index within the tile, pieces of the tile in total
+    int tile;  // global tile id: shrink tiles first, then base tiles
+    int n;     // pieces of the tile in total
     bool shrink;
-    int seg, t;        // segment, and tile index within the segment
+    int seg, t;  // segment, and tile index within the segment
 };
 
 __device__ __forceinline__ Sched make_sched(const TcParams& p) {
@@ -401,15 +396,15 @@ __device__ __forceinline__ Sched make_sched(const TcParams& p) {
     s.n_sh = p.sh_nseg * s.sh_per_seg;
     s.n_base = 0;
     for (int g = 0; g < p.n_seg; ++g) s.n_base += p.seg_tiles[g];
+    s.kbe = (p.pools & 2) ? s.kb : 0;
+    s.nge = (p.lora && (p.pools & 4)) ? s.ng : 0;
     s.len[0] = s.kb;
-    s.len[1] = s.kb;
-    s.len[2] = s.ng;
+    s.len[1] = s.kbe + s.nge;
     s.P[0] = (long long)s.n_sh * s.kb;
-    s.P[1] = (long long)s.n_base * s.kb;
-    s.P[2] = p.lora ? (long long)s.n_base * s.ng : 0;
+    s.P[1] = (long long)s.n_base * s.len[1];
     // Every slice is at least len/kMaxPiecesPerPool steps long, so no tile is
-    // cut into more than kMaxPiecesPerPool + 1 pieces per pool.
-    for (int q = 0; q < 3; ++q) {
+    // cut into more than kMaxPiecesPerPool + 1 pieces.
+    for (int q = 0; q < 2; ++q) {
         const long long l = max(1, cdiv(max(s.len[q], 1), kMaxPiecesPerPool));
         s.G[q] = s.P[q] > 0 ? (int)max(1ll, min((long long)gridDim.x, s.P[q] / l)) : 0;
     }
@@ -418,6 +413,10 @@ __device__ __forceinline__ Sched make_sched(const TcParams& p) {
 __device__ __forceinline__ long long pstart(int c, long long P, int G) { return (long long)c * P / G; }
 // CTA whose slice of a pool (length P, G CTAs) contains step s.
 __device__ __forceinline__ int cta_of(long long s, long long P, int G) { return (int)(((s + 1) * G - 1) / P); }
+// K steps among the first `pos` positions of a base tile.
+__device__ __forceinline__ int bpos(const Sched& sc, int pos) {
+    return sc.len[1] ? (int)((long long)pos * sc.kbe / sc.len[1]) : 0;
+}
 
 __device__ __forceinline__ void tile_info(const TcParams& p, const Sched& sc, int tile, Piece& pc) {
     pc.tile = tile;
@@ -436,72 +435,103 @@ __device__ __forceinline__ void tile_info(const TcParams& p, const Sched& sc, in
         pc.t = b;
     }
 }
-// First CTA and piece count of `tile` in pool q.
-__device__ __forceinline__ void pool_pieces(const Sched& sc, int q, int local, int& c0, int& n) {
+// Pieces of `tile` (CTAs whose slice touches it).
+__device__ __forceinline__ int tile_npieces(const Sched& sc, int tile) {
+    const int q = tile < sc.n_sh ? 0 : 1;
+    const int local = q ? tile - sc.n_sh : tile;
+    if (sc.P[q] <= 0) return 0;
     const long long a = (long long)local * sc.len[q];
-    c0 = cta_of(a, sc.P[q], sc.G[q]);
-    n = cta_of(a + sc.len[q] - 1, sc.P[q], sc.G[q]) - c0 + 1;
-}
-// Pieces of `tile` in total: a shrink tile has its pool-A pieces, a base tile
-// its pool-B pieces followed by its pool-C pieces.
-__device__ __forceinline__ int tile_npieces(const Sched& sc, int tile, int* nB = nullptr) {
-    int c0, n;
-    if (tile < sc.n_sh) {
-        pool_pieces(sc, 0, tile, c0, n);
-        return n;
-    }
-    const int b = tile - sc.n_sh;
-    pool_pieces(sc, 1, b, c0, n);
-    if (nB) *nB = n;
-    if (sc.P[2] > 0) {
-        int c2, n2;
-        pool_pieces(sc, 2, b, c2, n2);
-        n += n2;
-    }
-    return n;
+    return cta_of(a + sc.len[q] - 1, sc.P[q], sc.G[q]) - cta_of(a, sc.P[q], sc.G[q]) + 1;
 }
 
-// Iterates this CTA's pieces in order (pool A, B, C).  All three roles walk
-// the same sequence.
-struct PieceIter {
-    int pool;
-    long long s, e;  // current step, end of this CTA's slice of the pool
-    __device__ __forceinline__ void set(const Sched& sc) {
-        const int c = blockIdx.x;
-        s = c < sc.G[pool] ? pstart(c, sc.P[pool], sc.G[pool]) : 0;
-        e = c < sc.G[pool] ? pstart(c + 1, sc.P[pool], sc.G[pool]) : 0;
-    }
-    __device__ __forceinline__ void init(const Sched& sc) {
-        pool = 0;
-        set(sc);
-    }
-    __device__ __forceinline__ bool next(const TcParams& p, const Sched& sc, Piece& pc) {
-        while (s >= e) {
-            if (pool == 2) return false;
-            ++pool;
-            set(sc);
-        }
-        const int len = sc.len[pool];
-        const int local = (int)(s / len);
-        const long long tstart = (long long)local * len;
-        const long long tend = min(tstart + len, e);
-        tile_info(p, sc, pool == 0 ? local : local + sc.n_sh, pc);
-        pc.pool = pool;
-        pc.s0 = (int)(s - tstart);
-        pc.s1 = (int)(tend - tstart);
-        int c0, n;
-        pool_pieces(sc, pool, local, c0, n);
-        pc.idx = (int)blockIdx.x - c0;
-        if (pool == 2) {
-            int cB, nB;
-            pool_pieces(sc, 1, local, cB, nB);
-            pc.idx += nB;
-        }
-        pc.n = tile_npieces(sc, pc.tile);
-        s = tend;
-        return true;
-    }
+// This CTA's work, built once by thread 0 in shared memory and read by every
+// role: its pieces (in drain order) and the parts the producer and the MMA
+// run (a piece's K steps, or its expand steps), in execution order.
+constexpr int kMaxPieces = 24;
+constexpr int kMaxParts = 40;
+struct PieceRec {
+    int tile, n;      // tile, pieces of the tile in total
+    int b0, b1;       // K steps [b0, b1) of the tile
+    int c0, c1;       // expand steps [c0, c1) (touched-group list indices)
 };
+struct PartRec {
+    uint16_t piece;   // index into pc[]
+    uint8_t expand;   // 1: expand steps, 0: K steps
+    uint8_t flags;    // 1: first part of its piece (fresh accumulator), 2: last part (commit)
+};
+struct WorkTable {
+    int n_pieces, n_parts;
+    PieceRec pc[kMaxPieces];
+    PartRec pt[kMaxParts];
+};
+
+__device__ bool build_work(const Sched& sc, int acc_stages, WorkTable& w) {
+    const int c = blockIdx.x;
+    int np = 0;
+    for (int q = 0; q < 2; ++q) {
+        if (c >= sc.G[q]) continue;
+        long long s = pstart(c, sc.P[q], sc.G[q]);
+        const long long e = pstart(c + 1, sc.P[q], sc.G[q]);
+        const int L = sc.len[q];
+        while (s < e) {
+            const int local = (int)(s / L);
+            const long long ts = (long long)local * L, te = min(ts + L, e);
+            if (np == kMaxPieces) return false;
+            PieceRec& r = w.pc[np++];
+            const int p0 = (int)(s - ts), p1 = (int)(te - ts);
+            if (q == 0) {
+                r.tile = local;
+                r.b0 = p0;
+                r.b1 = p1;
+                r.c0 = r.c1 = 0;
+            } else {
+                r.tile = sc.n_sh + local;
+                r.b0 = bpos(sc, p0);
+                r.b1 = bpos(sc, p1);
+                r.c0 = p0 - r.b0;
+                r.c1 = p1 - r.b1;
+            }
+            r.n = tile_npieces(sc, r.tile);
+            s = te;
+        }
+    }
+    w.n_pieces = np;
+    int first_base = 0;
+    while (first_base < np && w.pc[first_base].tile < sc.n_sh) ++first_base;
+    int nt = 0;
+    bool ok = true;
+    auto add = [&](int i, int ex) {
+        const PieceRec& r = w.pc[i];
+        if ((ex ? r.c1 - r.c0 : r.b1 - r.b0) <= 0) return;
+        if (nt == kMaxParts) {
+            ok = false;
+            return;
+        }
+        w.pt[nt].piece = (uint16_t)i;
+        w.pt[nt].expand = (uint8_t)ex;
+        w.pt[nt].flags = 0;
+        ++nt;
+    };
+    for (int i = 0; i < first_base; ++i) add(i, 0);
+    if (acc_stages == 2 && np - first_base <= 2) {  // both base pieces' K steps first
+        for (int i = first_base; i < np; ++i) add(i, 0);
+        for (int i = first_base; i < np; ++i) add(i, 1);
+    } else {
+        for (int i = first_base; i < np; ++i) {
+            add(i, 0);
+            add(i, 1);
+        }
+    }
+    if (!ok) return false;
+    for (int k = 0; k < nt; ++k) {
+        bool first = true, last = true;
+        for (int j = 0; j < k; ++j) first = first && w.pt[j].piece != w.pt[k].piece;
+        for (int j = k + 1; j < nt; ++j) last = last && w.pt[j].piece != w.pt[k].piece;
+        w.pt[k].flags = (uint8_t)((first ? 1 : 0) | (last ? 2 : 0));
+    }
+    w.n_parts = nt;
+    return true;
+}
 
 // Bounded spin until *ptr >= target (acquire); false on timeout or when
 // another role already failed.
@@ -521,11 +551,6 @@ __device__ __noinline__ bool spin_ge(const int* ptr, int target, int* err) {
         }
     }
 }
-__device__ __forceinline__ bool ld_acquire_ge(const int* ptr, int target) {
-    int v;
-    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
-    return v >= target;
-}
 
 // ---------------------------------------------------------------- the kernel
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
@@ -542,7 +567,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     uint64_t* drain_bar = tempty_bar + 2;   // [1]
     uint64_t* a_done_bar = drain_bar + 1;   // drain warps: shrink pieces added (4 arrivals)
     uint64_t* all_done_bar = a_done_bar + 1;  // drain warps: every piece added (4 arrivals)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(all_done_bar + 1);
+    uint64_t* sh_conv_bar = all_done_bar + 1;  // drain warps: their share of the shrink conversion done (4)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sh_conv_bar + 1);
     int* flag = reinterpret_cast<int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -550,8 +576,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     const int cols_per_acc = p.tb * kTcBN;
     const int acc_stages = (2 * cols_per_acc <= 512) ? 2 : 1;
     constexpr int tmem_cols = 512;
+    __shared__ WorkTable wt;
 
     if (threadIdx.x == 0) {
+        if (!build_work(sc, acc_stages, wt)) {  // schedule limits exceeded: report, do nothing
+            atomicCAS(p.err, 0, AOS_ERR_INVALID);
+            wt.n_pieces = 0;
+            wt.n_parts = 0;
+        }
         for (int s = 0; s < NS; ++s) {
             mbar_init(smem_u32(&full_bar[s]), 1);
             mbar_init(smem_u32(&empty_bar[s]), 1);
@@ -563,7 +595,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         mbar_init(smem_u32(drain_bar), 1);
         mbar_init(smem_u32(a_done_bar), 4);
         mbar_init(smem_u32(all_done_bar), 4);
+        mbar_init(smem_u32(sh_conv_bar), 4);
         flag[1] = 0;
+        flag[2] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
@@ -588,16 +622,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     constexpr uint32_t kActBox = kTcTok * 128;    // shared-memory bytes reserved per activation box
 
     // Conversion of the split tiles in [lo, hi) by `nthr` threads of every CTA
-    // (thread index `ti`): an item is (tile, pair chunk k, 32 tokens, half g);
-    // its thread reads 16 pairs of one token from the fixed-point
+    // (thread index `ti`): an item is (tile, pair chunk k, token, 8-column
+    // group g); its thread reads 8 pairs of one token from the fixed-point
     // accumulator, zeroes them for the next launch and applies the epilogue.
     // Two items per thread are loaded before either is used.
     auto convert = [&](int lo, int hi, int nthr, int ti) {
-        const int nq = (p.T + 31) / 32;
-        const long long n_items = (long long)(hi - lo) * 4 * nq * 64;
+        // item = (tile, pair chunk k, 8-column group g, token), token fastest
+        const long long n_items = (long long)(hi - lo) * 16 * p.T;
         const long long stride = (long long)gridDim.x * nthr;
         for (long long base = (long long)blockIdx.x * nthr + ti; base < n_items; base += 2 * stride) {
-            longlong2 w[2][2][8];
+            unsigned long long w[2][2][8];
             bool live[2];
             int tile_[2], k_[2], tok_[2], g_[2];
 #pragma unroll
@@ -605,14 +639,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 const long long item = base + e * stride;
                 live[e] = item < n_items;
                 if (!live[e]) continue;
-                const long long unit = item / 64;
-                const int wi = (int)(item % 64);
-                tile_[e] = lo + (int)(unit / (4 * nq));
-                const int rem = (int)(unit % (4 * nq));
-                k_[e] = rem / nq;
-                const int qq = rem % nq;
-                g_[e] = wi >> 5;
-                tok_[e] = qq * 32 + (wi & 31);
+                tok_[e] = (int)(item % p.T);
+                const long long r = item / p.T;
+                g_[e] = (int)(r % 4);
+                k_[e] = (int)((r / 4) % 4);
+                tile_[e] = lo + (int)(r / 16);
                 live[e] = tile_npieces(sc, tile_[e]) > 1;  // else finished straight from TMEM
                 if (!live[e]) continue;
                 const int mode = tile_[e] < sc.n_sh ? TC_SHRINK_HM : p.mode;
@@ -620,34 +651,33 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 chunk_cols(mode, k_[e], cA, cB);
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    const int c = h ? cB : cA;  // multiple of 32: one accumulator chunk
-                    longlong2* src = reinterpret_cast<longlong2*>(
-                        p.acc + (((size_t)tile_[e] * 8 + c / 32) * p.acc_q + qq) * 1024) + (size_t)(8 * g_[e]) * 32 + (wi & 31);
+                    unsigned long long* src = reinterpret_cast<unsigned long long*>(p.acc) +
+                                              ((size_t)tile_[e] * kTcBN + (h ? cB : cA) + 8 * g_[e]) * p.acc_T + tok_[e];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) w[e][h][j] = __ldcg(src + j * 32);
+                    for (int j = 0; j < 8; ++j) w[e][h][j] = __ldcg(src + (size_t)j * p.acc_T);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) __stcg(src + j * 32, make_longlong2(0, 0));
+                    for (int j = 0; j < 8; ++j) __stcg(src + (size_t)j * p.acc_T, 0ull);
                 }
             }
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-                if (!live[e] || tok_[e] >= p.T) continue;
+                if (!live[e]) continue;
                 Piece pc;
                 tile_info(p, sc, tile_[e], pc);
                 const int mode = pc.shrink ? TC_SHRINK_HM : p.mode;
-                float a[16], b[16];
+                float a[8], b[8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    a[2 * j] = __ll2float_rn(w[e][0][j].x) * kFixInv;
-                    a[2 * j + 1] = __ll2float_rn(w[e][0][j].y) * kFixInv;
-                    b[2 * j] = __ll2float_rn(w[e][1][j].x) * kFixInv;
-                    b[2 * j + 1] = __ll2float_rn(w[e][1][j].y) * kFixInv;
+                    a[j] = __ll2float_rn((long long)w[e][0][j]) * kFixInv;
+                    b[j] = __ll2float_rn((long long)w[e][1][j]) * kFixInv;
                 }
-                apply_pairs<16>(p, mode, pc.seg, pc.t, k_[e], tok_[e], 16 * g_[e], a, b, sc.ng);
+                apply_pairs<8>(p, mode, pc.seg, pc.t, k_[e], tok_[e], 8 * g_[e], a, b, sc.ng);
             }
         }
     };
     volatile int* go_final = flag + 1;  // converter -> drain: 1 = every CTA's pieces are in, -1 = failed
+    volatile int* go_shrink = flag + 2;  // converter -> drain: 1 = every CTA's shrink pieces are in, -1 = failed
+    const bool handoff = sc.n_sh > 0 && sc.nge > 0;  // expand steps wait for this launch's shrink
 
     if (warp == 0) {
         // ============================ TMA producer ============================
@@ -665,10 +695,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true, waited = false, shrink_ready = (sc.n_sh == 0);
-            int pre_tile[16], pre_pool[16], pre_step[16];
+            int pre_tile[16], pre_ex[16], pre_step[16];
             int n_pre = 0;
             // weight blocks of a step: shrink -> lora_A groups (8 KB each); base / expand -> two 16 KB blocks
-            auto weights = [&](const Piece& pc, int st, uint32_t sbase, uint32_t fb, bool issue) -> uint32_t {
+            auto weights = [&](const Piece& pc, bool ex, int st, uint32_t sbase, uint32_t fb, bool issue) -> uint32_t {
                 uint32_t bytes = 0;
                 if (pc.shrink) {
                     const int first = pc.t * kShrinkGroupsPerTile;
@@ -683,15 +713,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     return bytes;
                 }
                 const int seg_blocks = (p.seg_rows[pc.seg] + kBlkRows - 1) / kBlkRows;
-                const int g = pc.pool == 2 ? __ldg(p.groups + st) : 0;
+                const int g = ex ? __ldg(p.groups + st) : 0;
                 for (int h = 0; h < 2; ++h) {
                     const uint16_t* src;
                     if (p.n_sub == 2) {  // gate / up: block t of each
-                        src = pc.pool == 1 ? p.w_pk[pc.seg * 2 + h] + (((size_t)(p.seg_wrow0[pc.seg] / kBlkRows + pc.t)) * sc.kb + st) * kBlkW
+                        src = !ex ? p.w_pk[pc.seg * 2 + h] + (((size_t)(p.seg_wrow0[pc.seg] / kBlkRows + pc.t)) * sc.kb + st) * kBlkW
                                            : p.b_pk[pc.seg * 2 + h] + ((size_t)pc.t * p.n_rgroups + g) * kBlkW;
                     } else {  // blocks 2t and 2t+1 of the segment
                         if (2 * pc.t + h >= seg_blocks) continue;
-                        src = pc.pool == 1
+                        src = !ex
                                   ? p.w_pk[pc.seg] + (((size_t)(p.seg_wrow0[pc.seg] / kBlkRows + 2 * pc.t + h)) * sc.kb + st) * kBlkW
                                   : p.b_pk[pc.seg] + ((size_t)(2 * pc.t + h) * p.n_rgroups + g) * kBlkW;
                     }
@@ -700,14 +730,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 }
                 return bytes;
             };
-            auto act_bytes = [&](const Piece& pc) -> uint32_t {
-                const int nh = (pc.pool == 2 && p.n_sub == 2) ? 2 : 1;
-                return (uint32_t)(nh * p.tb * p.T_box * 128);
+            auto act_bytes = [&](bool ex) -> uint32_t {
+                const int nh = (ex && p.n_sub == 2) ? 2 : 1;
+                return (uint32_t)(nh * (p.spread ? p.n_xbox * 16 : p.tb * p.T_box) * 128);
             };
-            auto issue_x = [&](const Piece& pc, int st, uint32_t sbase, uint32_t fb) -> bool {
+            auto issue_x = [&](const Piece& pc, bool ex, int st, uint32_t sbase, uint32_t fb) -> bool {
                 const uint32_t act = sbase + p.act_off;
-                if (pc.pool != 2) {
-                    for (int b = 0; b < p.tb; ++b) tma_2d(&p.tm_x, act + b * kActBox, fb, st * kTcBK, b * kTcTok, pol_x);
+                if (!ex) {
+                    if (p.spread) {  // 16-token groups to lane quarters: rows 32j .. 32j + 15
+                        for (int j = 0; j < p.n_xbox; ++j) tma_2d(&p.tm_x, act + j * 4096, fb, st * kTcBK, 16 * j, pol_x);
+                    } else {
+                        for (int b = 0; b < p.tb; ++b) tma_2d(&p.tm_x, act + b * kActBox, fb, st * kTcBK, b * kTcTok, pol_x);
+                    }
                     return true;
                 }
                 if (!shrink_ready) {  // hm is written by this launch's shrink tiles and reduction
@@ -719,9 +753,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 }
                 const int gcol = __ldg(p.groups + st) * kGroup;
                 const int nh = p.n_sub == 2 ? 2 : 1;
-                for (int h = 0; h < nh; ++h)
-                    for (int b = 0; b < p.tb; ++b)
-                        tma_2d(&p.tm_lh[pc.seg * p.n_sub + h], act + (h * p.tb + b) * kActBox, fb, gcol, b * kTcTok, pol_x);
+                for (int h = 0; h < nh; ++h) {
+                    if (p.spread) {
+                        for (int j = 0; j < p.n_xbox; ++j)
+                            tma_2d(&p.tm_lh[pc.seg * p.n_sub + h], act + h * kActBox + j * 4096, fb, gcol, 16 * j, pol_x);
+                    } else {
+                        for (int b = 0; b < p.tb; ++b)
+                            tma_2d(&p.tm_lh[pc.seg * p.n_sub + h], act + (h * p.tb + b) * kActBox, fb, gcol, b * kTcTok, pol_x);
+                    }
+                }
                 return true;
             };
             auto finish_wait = [&]() -> bool {
@@ -731,28 +771,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 for (int i = 0; i < n_pre; ++i) {
                     Piece pc;
                     tile_info(p, sc, pre_tile[i], pc);
-                    pc.pool = pre_pool[i];
-                    if (!issue_x(pc, pre_step[i], smem_u32(stages + (size_t)i * p.stage_bytes), smem_u32(&full_bar[i])))
+                    if (!issue_x(pc, pre_ex[i] != 0, pre_step[i], smem_u32(stages + (size_t)i * p.stage_bytes),
+                                 smem_u32(&full_bar[i])))
                         return false;
                 }
                 return true;
             };
-            PieceIter itr;
-            itr.init(sc);
-            Piece pc;
-            while (ok && itr.next(p, sc, pc)) {
-                for (int st = pc.s0; st < pc.s1; ++st) {
+            for (int k = 0; ok && k < wt.n_parts; ++k) {
+                const PartRec pt = wt.pt[k];
+                const PieceRec& r = wt.pc[pt.piece];
+                const bool ex = pt.expand != 0;
+                Piece pc;
+                tile_info(p, sc, r.tile, pc);
+                const int s0 = ex ? r.c0 : r.b0, s1 = ex ? r.c1 : r.b1;
+                for (int st = s0; st < s1; ++st) {
                     if (!waited && n_pre == NS && !finish_wait()) { ok = false; break; }
                     if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, p.err)) { ok = false; break; }
                     const uint32_t fb = smem_u32(&full_bar[stage]);
                     const uint32_t sbase = smem_u32(stages + (size_t)stage * p.stage_bytes);
-                    mbar_expect_tx(fb, weights(pc, st, sbase, fb, false) + act_bytes(pc));
-                    weights(pc, st, sbase, fb, true);
+                    mbar_expect_tx(fb, weights(pc, ex, st, sbase, fb, false) + act_bytes(ex));
+                    weights(pc, ex, st, sbase, fb, true);
                     if (waited) {
-                        if (!issue_x(pc, st, sbase, fb)) ok = false;
+                        if (!issue_x(pc, ex, st, sbase, fb)) ok = false;
                     } else {  // first round of stages: stage index == n_pre
-                        pre_tile[n_pre] = pc.tile;
-                        pre_pool[n_pre] = pc.pool;
+                        pre_tile[n_pre] = r.tile;
+                        pre_ex[n_pre] = ex ? 1 : 0;
                         pre_step[n_pre] = st;
                         ++n_pre;
                     }
@@ -775,21 +818,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             const uint32_t idesc256 = idesc_bf16(kTcBN), idesc128 = idesc_bf16(kTcBN / 2);
             int stage = 0;
             uint32_t phase = 0;
-            int it = 0, n_waited = 0;
+            int n_waited = 0;
             bool ok = true, issued_any = false;
-            PieceIter itr;
-            itr.init(sc);
-            Piece pc;
-            while (ok && itr.next(p, sc, pc)) {
-                const int acc = it % acc_stages;
-                const uint32_t tphase = (uint32_t)((it / acc_stages) & 1);
-                ++it;
-                if (!mbar_wait(smem_u32(&tempty_bar[acc]), tphase ^ 1u, p.err)) { ok = false; break; }
-                tc_fence_after();
+            bool fresh[2] = {false, false};  // accumulator slot gets its first MMA next
+            for (int k = 0; ok && k < wt.n_parts; ++k) {
+                const PartRec pt = wt.pt[k];
+                const PieceRec& r = wt.pc[pt.piece];
+                const int acc = pt.piece % acc_stages;
+                if (pt.flags & 1) {  // a new piece takes the slot once its previous piece is drained
+                    const uint32_t tphase = (uint32_t)((pt.piece / acc_stages) & 1);
+                    if (!mbar_wait(smem_u32(&tempty_bar[acc]), tphase ^ 1u, p.err)) { ok = false; break; }
+                    tc_fence_after();
+                    fresh[acc] = true;
+                }
                 const uint32_t d0 = tmem_base + (uint32_t)(acc * cols_per_acc);
-                const bool split = pc.pool == 2 && p.n_sub == 2;  // gate / up expand: two N=128 halves
-                bool first = true;
-                for (int st = pc.s0; st < pc.s1; ++st) {
+                const bool ex = pt.expand != 0;
+                const bool split = ex && p.n_sub == 2;  // gate / up expand: two N=128 halves
+                const int s0 = ex ? r.c0 : r.b0, s1 = ex ? r.c1 : r.b1;
+                for (int st = s0; st < s1; ++st) {
+                    const bool first = fresh[acc];
                     if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.err)) { ok = false; break; }
                     tc_fence_after();
                     if (tr && n_waited < 64) tr[64 + n_waited] = gtimer();
@@ -815,11 +862,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     }
                     issued_any = true;
                     umma_commit(smem_u32(&empty_bar[stage]));  // frees the stage when these MMAs finish
-                    first = false;
+                    fresh[acc] = false;
                     if (++stage == NS) { stage = 0; phase ^= 1u; }
                 }
                 if (!ok) break;
-                umma_commit(smem_u32(&tfull_bar[acc]));
+                if (pt.flags & 2) umma_commit(smem_u32(&tfull_bar[acc]));  // the piece is complete
             }
             if (!ok && issued_any) {
                 umma_commit(smem_u32(drain_bar));
@@ -837,17 +884,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         const int tok_lane = q * 32 + lane;
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
         const int tid = threadIdx.x - 64;  // 0..127
-        // per-warp 8 KB staging of one fixed-point chunk: [16 column pairs][32 tokens][2]
-        long long* stg = reinterpret_cast<long long*>(tail + kTcTailBytes) + (size_t)(warp - 2) * 1024;
         pdl_wait();  // reads and writes activations and accumulators of earlier launches
-        // signal a converter barrier once this warp's bulk reductions have landed
+        // signal a converter barrier once this warp's atomic adds have landed
         auto signal = [&](uint64_t* bar) {
-            if (lane == 0) {
-                asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-                asm volatile("fence.proxy.async.global;" ::: "memory");
-                mbar_arrive(smem_u32(bar));
-            }
+            __threadfence();  // this thread's atomic adds are performed
             __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(bar));
         };
         // Gate * alpha/rank for token `tok` of the 32 eight-column units of
         // shrink tile `t`: one contiguous 128-byte run of the prep table.
@@ -864,30 +906,73 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             }
         };
 
-        int it = 0;
+        bool sh_joined = false;
+        auto join_shrink = [&]() {  // the drain warps' share (threads 0..127 of 192)
+            if (*go_shrink == 1) {
+                __threadfence();
+                convert(0, sc.n_sh, 192, tid);
+            }
+            signal(sh_conv_bar);
+            sh_joined = true;
+        };
         bool a_signalled = false;
-        PieceIter itr;
-        itr.init(sc);
-        Piece pc;
-        while (itr.next(p, sc, pc)) {
-            if (!a_signalled && pc.pool != 0) {  // this CTA's shrink pieces are all in
+        for (int it = 0; it < wt.n_pieces; ++it) {
+            const PieceRec& r = wt.pc[it];
+            Piece pc;
+            tile_info(p, sc, r.tile, pc);
+            pc.n = r.n;
+            if (!a_signalled && !pc.shrink) {  // this CTA's shrink pieces are all in
                 signal(a_done_bar);
                 a_signalled = true;
             }
             const int acc = it % acc_stages;
             const uint32_t tphase = (uint32_t)((it / acc_stages) & 1);
             float cf[32];
-            if (pc.shrink) gate_coefs(pc.t, tok_lane, cf);  // loads overlap the MMAs of this piece
-            const bool okw = mbar_wait(smem_u32(&tfull_bar[acc]), tphase, p.err);
-            if (epi_bar_any(!okw)) break;
+            if (pc.shrink)  // loads overlap the MMAs of this piece
+                gate_coefs(pc.t, p.spread ? (lane < 16 ? 16 * q + lane : 0) : tok_lane, cf);
+            // Wait for this piece's accumulator; meanwhile take a share of the
+            // shrink conversion as soon as the converter opens it (the expand
+            // steps of every CTA wait for it).
+            int ev = 0;
+            while (true) {
+                if (tid == 0) {
+                    const long long t0 = clock64();
+                    uint32_t n = 0;
+                    ev = 0;
+                    while (ev == 0) {
+                        if (mbar_try(smem_u32(&tfull_bar[acc]), tphase)) ev = 1;
+                        else if (handoff && !sh_joined && *go_shrink != 0) ev = 2;
+                        else if ((++n & 1023u) == 0) {
+                            if (*(volatile int*)p.err != 0) ev = -1;
+                            else if (clock64() - t0 > kSpinLimitCycles) {
+                                atomicCAS(p.err, 0, AOS_ERR_TIMEOUT);
+                                ev = -1;
+                            }
+                        }
+                    }
+                    *flag = ev;
+                }
+                epi_bar();
+                ev = *flag;
+                epi_bar();
+                if (ev != 2) break;
+                join_shrink();
+            }
+            if (ev < 0) break;
+            mbar_wait(smem_u32(&tfull_bar[acc]), tphase, p.err);  // completed: every thread observes it
             if (tr && tid == 0 && it < 32) tr[128 + it] = gtimer();
             tc_fence_after();
             const uint32_t t_acc = tmem_base + lane_off + (uint32_t)(acc * cols_per_acc);
             const int mode = pc.shrink ? TC_SHRINK_HM : p.mode;
+            // token held by this thread's TMEM lane in token block b (-1: none)
+            auto token_of = [&](int b) -> int {
+                if (p.spread) return lane < 16 ? 16 * q + lane : -1;
+                return b * kTcTok + tok_lane;
+            };
             if (pc.n == 1 && pc.shrink) {  // whole shrink tile: gate and store hm from TMEM
                 for (int b = 0; b < p.tb; ++b) {
-                    const int tok = b * kTcTok + tok_lane;
-                    if (b > 0) gate_coefs(pc.t, tok, cf);
+                    const int tok = token_of(b);
+                    if (b > 0) gate_coefs(pc.t, tok < 0 ? 0 : tok, cf);
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
                         float vA[32], vB[32];
@@ -898,12 +983,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                             vA[i] *= cf[8 * k + i / 8];
                             vB[i] *= cf[8 * k + 4 + i / 8];
                         }
-                        if (tok < p.T) apply_pairs<32>(p, mode, pc.seg, pc.t, k, tok, 0, vA, vB, sc.ng);
+                        if (tok >= 0 && tok < p.T) apply_pairs<32>(p, mode, pc.seg, pc.t, k, tok, 0, vA, vB, sc.ng);
                     }
                 }
             } else if (pc.n == 1) {  // the whole tile is here: epilogue straight from TMEM
                 for (int b = 0; b < p.tb; ++b) {
-                    const int tok = b * kTcTok + tok_lane;
+                    const int tok = token_of(b);
 #pragma unroll 1
                     for (int k = 0; k < 4; ++k) {
                         int cA, cB;
@@ -911,46 +996,36 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                         float vA[32], vB[32];
                         tmem_ld32(t_acc + b * kTcBN + cA, vA);
                         tmem_ld32(t_acc + b * kTcBN + cB, vB);
-                        if (tok < p.T) apply_pairs<32>(p, mode, pc.seg, pc.t, k, tok, 0, vA, vB, sc.ng);
+                        if (tok >= 0 && tok < p.T) apply_pairs<32>(p, mode, pc.seg, pc.t, k, tok, 0, vA, vB, sc.ng);
                     }
                 }
             } else {
                 // add the piece into the tile's fixed-point accumulator: value * 2^32
-                // rounded to int64, summed by TMA bulk reductions in L2 (integer
-                // addition is order-independent, so the sum is exact and the same
-                // on every run); shrink pieces are gated first
+                // rounded to int64, summed by atomic adds in L2 (integer addition
+                // is order-independent, so the sum is exact and the same on every
+                // run); shrink pieces are gated first.  Layout [tile][column][token]:
+                // one red instruction adds a column for 32 consecutive tokens.
                 for (int b = 0; b < p.tb; ++b) {
-                    const int tok = b * kTcTok + tok_lane;
-                    const int qq = b * 4 + q;  // 32-token quarter
-                    const bool any = qq * 32 < p.T;
-                    if (b > 0 && pc.shrink) gate_coefs(pc.t, tok, cf);
-                    const bool valid = tok < p.T;
+                    const int tok = token_of(b);
+                    if (b > 0 && pc.shrink) gate_coefs(pc.t, tok < 0 ? 0 : tok, cf);
+                    const bool valid = tok >= 0 && tok < p.T;
+                    unsigned long long* dst =
+                        reinterpret_cast<unsigned long long*>(p.acc) + (size_t)pc.tile * kTcBN * p.acc_T + (valid ? tok : 0);
 #pragma unroll
                     for (int c = 0; c < kTcBN / 32; ++c) {
                         float v[32];
                         tmem_ld32(t_acc + b * kTcBN + c * 32, v);
-                        if (!any) continue;  // warp-uniform
+                        if (!valid) continue;
                         if (pc.shrink) {
 #pragma unroll
                             for (int i = 0; i < 32; ++i) v[i] *= cf[4 * c + i / 8];
                         }
-                        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-                        __syncwarp();
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            const long long x = valid ? __float2ll_rn(v[2 * j] * kFix) : 0ll;
-                            const long long y = valid ? __float2ll_rn(v[2 * j + 1] * kFix) : 0ll;
-                            reinterpret_cast<longlong2*>(stg)[j * 32 + lane] = make_longlong2(x, y);
-                        }
-                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                        __syncwarp();
-                        if (lane == 0) {
-                            long long* dst = p.acc + (((size_t)pc.tile * 8 + c) * p.acc_q + qq) * 1024;
-                            asm volatile(
-                                "cp.reduce.async.bulk.global.shared::cta.bulk_group.add.u64 [%0], [%1], %2;" ::"l"(dst),
-                                "r"(smem_u32(stg)), "r"(8192)
-                                : "memory");
-                            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                        for (int i = 0; i < 32; ++i) {
+                            const long long x = __float2ll_rn(v[i] * kFix);
+                            asm volatile("red.global.add.u64 [%0], %1;" ::"l"(dst + (size_t)(c * 32 + i) * p.acc_T),
+                                         "l"((unsigned long long)x)
+                                         : "memory");
                         }
                     }
                 }
@@ -959,10 +1034,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
             if (tr && tid == 0 && it < 32) tr[160 + it] = gtimer();
-            ++it;
         }
         // also on the error path: the converter warps wait (bounded) for these
         if (!a_signalled) signal(a_done_bar);
+        if (handoff && !sh_joined) {
+            const long long t0 = clock64();
+            while (*go_shrink == 0)
+                if (clock64() - t0 > 2 * kSpinLimitCycles) break;  // the converter's own waits are bounded
+            join_shrink();
+        }
         signal(all_done_bar);
         // then help with the final conversion once every CTA's pieces are in
         {
@@ -972,7 +1052,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 if (clock64() - t0 > 2 * kSpinLimitCycles) break;  // the converter's own waits are bounded
             if (go == 1) {
                 __threadfence();
-                convert(sc.n_sh, sc.n_sh + sc.n_base, 192, tid);
+                convert(handoff ? sc.n_sh : 0, sc.n_sh + sc.n_base, 192, tid);
             }
         }
     } else {
@@ -1014,10 +1094,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             return ok;
         };
         bool ok = true;
-        if (sc.n_sh > 0) {
+        // Without expand steps in this launch nothing waits for hm here: the
+        // shrink tiles are converted with the base tiles after one barrier.
+        if (handoff) {
             ok = await(a_done_bar, 0);
+            if (cid == 0) *go_shrink = ok ? 1 : -1;  // the drain warps take two thirds
             if (ok) {
-                convert(0, sc.n_sh, 64, cid);
+                convert(0, sc.n_sh, 192, 128 + cid);
+                if (cid == 0) ok = mbar_wait(smem_u32(sh_conv_bar), 0, p.err);
+                cv_bar();
                 release(1);
             }
         }
@@ -1025,7 +1110,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         if (cid == 0) *go_final = ok ? 1 : -1;  // the drain warps join the final conversion
         if (ok) {
             if (tr && cid == 0) tr[200] = gtimer();
-            convert(sc.n_sh, sc.n_sh + sc.n_base, 192, 128 + cid);
+            convert(handoff ? sc.n_sh : 0, sc.n_sh + sc.n_base, 192, 128 + cid);  // handoff: shrink done above
             if (tr && cid == 0) tr[201] = gtimer();
         }
     }
@@ -1111,8 +1196,16 @@ int tc_encode_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uin
     return r == CUDA_SUCCESS ? AOS_OK : AOS_ERR_CUDA;
 }
 
-// mbarriers and flags, then the drain warps' 4 x 8 KB fixed-point staging
-size_t tc_tail_bytes(const TcParams&) { return kTcTailBytes + 4 * 8192; }
+size_t tc_tail_bytes(const TcParams&) { return kTcTailBytes; }  // mbarriers and flags
+int tc_max_dynamic_smem();
+
+bool tc_spread(int T) {
+    static const bool on = [] {  // tuning knob, off by default (measured slower on config 3)
+        const char* e = getenv("AOS_SPREAD");
+        return e && e[0] == '1';
+    }();
+    return on && tc_t_pad(T) <= 64;
+}
 
 size_t tc_smem_bytes(const TcParams& p) {
     return 1024 + (size_t)p.n_stages * p.stage_bytes + tc_tail_bytes(p);
@@ -1125,12 +1218,15 @@ int tc_prepare(TcParams& p, int smem_budget) {
     p.T_pad = tc_t_pad(p.T);
     p.T_box = tc_t_box(p.T);
     p.tb = (p.T_pad + kTcTok - 1) / kTcTok;
+    p.spread = tc_spread(p.T) ? 1 : 0;
+    p.n_xbox = p.spread ? p.T_pad / 16 : 0;
     // stage: 256 weight rows x 128 B, then one 128-row activation box per
     // token block (two for the gate/up expand, whose halves read different hm)
     const int n_act = p.tb * ((p.n_sub == 2 && p.lora) ? 2 : 1);
     p.act_off = (uint32_t)kTcBN * 128;
     p.stage_bytes = p.act_off + (uint32_t)n_act * kTcTok * 128;
     const size_t fixed = 1024 + tc_tail_bytes(p);
+    smem_budget = std::min(smem_budget, tc_max_dynamic_smem());
     int ns = (int)((smem_budget - (int)fixed) / (int)p.stage_bytes);
     static const int max_stages = [] {
         const char* e = getenv("AOS_TC_MAX_STAGES");  // tuning knob, default 4
@@ -1156,17 +1252,28 @@ int tc_num_sms() {
 
 // Opt the kernel in to the full 227 KB of shared memory (once per device,
 // outside any stream capture).
+// The dynamic budget is the device's opt-in limit minus the kernel's static
+// shared memory (its work table).
+static int g_tc_max_dyn = 0;
 cudaError_t tc_configure() {
-    return cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    int dev = 0, optin = 0;
+    cudaFuncAttributes fa{};
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, tc_gemm_kernel);
+    if (e != cudaSuccess) return e;
+    g_tc_max_dyn = optin - (int)fa.sharedSizeBytes;
+    return cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, g_tc_max_dyn);
 }
+int tc_max_dynamic_smem() { return g_tc_max_dyn > 0 ? g_tc_max_dyn : 227 * 1024 - 4096; }
 
 size_t tc_acc_bytes(const TcParams& p, int n_tiles) {
-    return (size_t)n_tiles * 8 * p.acc_q * 1024 * sizeof(long long);
+    return (size_t)n_tiles * kTcBN * p.acc_T * sizeof(long long);
 }
 
 cudaError_t tc_launch(const TcParams& p, int grid, cudaStream_t stream) {
     const size_t smem = tc_smem_bytes(p);
-    if (smem > 227 * 1024) return cudaErrorInvalidValue;
+    if ((int)smem > tc_max_dynamic_smem()) return cudaErrorInvalidValue;
     return launch_k(tc_gemm_kernel, dim3(grid), dim3(kTcThreads), smem, stream, p);
 }
 

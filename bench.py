@@ -457,9 +457,11 @@ def main():
         cpu = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample}
 
     if rank == 0:
-        # route; LoRA prep + coefficient table; embed; per layer 2 rmsnorm, 4 fused
-        # GEMMs (shrink + base + expand), attention + combine; final rmsnorm; lm_head
-        launches_per_step = 1 + 2 + 1 + args.layers * 8 + 2
+        # kernels per step, from the instrumented pass: one route kernel, plus every
+        # launch the step enqueues (the LoRA prep and the attention enqueue two
+        # kernels each: prep + coefficient table, decode + combine)
+        lc = prof["launches"]
+        launches_per_step = 1 + (sum(lc.values()) + lc["prep"] + lc["attention"]) / PS
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
