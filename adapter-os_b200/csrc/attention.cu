@@ -312,31 +312,52 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     }
 }
 
-// Merge chunk partials of one (token, kv head) in chunk order; bf16 output
-// attn[t][head*128 + d].
-__global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restrict__ part, const float* __restrict__ part_ml,
+// Merge the chunk partials of one (token, kv head, query head) in chunk
+// order: one warp per head row, lane i owning dims 4i .. 4i+3.  Lane c holds
+// chunk c's (m, l); the running sums of l and of O are taken in chunk order,
+// so the result is the same on every run.  bf16 output attn[t][head*128 + d].
+__global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restrict__ part, const float* __restrict__ part_ml,
                                                            const int* __restrict__ ctx_lens, int T, int nkv, int G,
                                                            int max_chunks, uint16_t* __restrict__ out) {
     pdl_wait();
     pdl_trigger();
-    const int kvh = blockIdx.x % nkv, t = blockIdx.x / nkv;
+    const int wg = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    const int r = wg % G, rest = wg / G;
+    const int kvh = rest % nkv, t = rest / nkv;
     if (t >= T) return;
-    const int L = ctx_lens[t] + 1;
+    const int L = __ldg(ctx_lens + t) + 1;
     const int n_chunks = ((L + 15) / 16 + kPages - 1) / kPages;
-    for (int e = threadIdx.x; e < G * 128; e += blockDim.x) {
-        const int r = e >> 7, d = e & 127;
-        const size_t base = ((size_t)t * nkv + kvh) * max_chunks;
-        float m = -INFINITY;
-        for (int c = 0; c < n_chunks; ++c) m = fmaxf(m, part_ml[((base + c) * G + r) * 2]);
-        float acc = 0.f, l = 0.f;
-        for (int c = 0; c < n_chunks; ++c) {
-            const float mc = part_ml[((base + c) * G + r) * 2];
-            const float sc = mc == -INFINITY ? 0.f : exp2f(mc - m);
-            acc += part[((base + c) * G + r) * 128 + d] * sc;
-            l += part_ml[((base + c) * G + r) * 2 + 1] * sc;
+    const size_t base = ((size_t)t * nkv + kvh) * max_chunks;
+    float m = -INFINITY;
+    for (int c = lane; c < n_chunks; c += 32) m = fmaxf(m, __ldg(part_ml + ((base + c) * G + r) * 2));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float l = 0.f;
+    for (int c0 = 0; c0 < n_chunks; c0 += 32) {
+        const int c = c0 + lane;
+        float sc = 0.f, lc = 0.f;
+        if (c < n_chunks) {
+            const float2 ml = __ldg(reinterpret_cast<const float2*>(part_ml) + (base + c) * G + r);
+            sc = ml.x == -INFINITY ? 0.f : exp2f(ml.x - m);
+            lc = ml.y;
         }
-        out[(size_t)t * nkv * G * 128 + (size_t)(kvh * G + r) * 128 + d] = f2bf(acc / l);
+        const int nc = min(32, n_chunks - c0);
+#pragma unroll 4
+        for (int j = 0; j < nc; ++j) {
+            const float scj = __shfl_sync(0xffffffffu, sc, j);
+            l += __shfl_sync(0xffffffffu, lc, j) * scj;
+            const float4 v = __ldg(reinterpret_cast<const float4*>(part + ((base + c0 + j) * G + r) * 128) + lane);
+            acc.x += v.x * scj;
+            acc.y += v.y * scj;
+            acc.z += v.z * scj;
+            acc.w += v.w * scj;
+        }
     }
+    uint2 w;
+    w.x = (uint32_t)f2bf(acc.x / l) | ((uint32_t)f2bf(acc.y / l) << 16);
+    w.y = (uint32_t)f2bf(acc.z / l) | ((uint32_t)f2bf(acc.w / l) << 16);
+    *reinterpret_cast<uint2*>(out + (size_t)t * nkv * G * 128 + (size_t)(kvh * G + r) * 128 + lane * 4) = w;
 }
 
 }  // namespace
@@ -377,7 +398,8 @@ cudaError_t launch_attention(const CUtensorMap& tm_k, const CUtensorMap& tm_v, c
     if (e != cudaSuccess) return e;
     const float* cpart = part;
     const float* cml = part_ml;
-    return launch_k(attn_combine_kernel, dim3(T * nkv), dim3(128), 0, s, cpart, cml, ctx_lens, T, nkv, nq / nkv,
+    const int rows = T * nkv * (nq / nkv);  // one warp per (token, kv head, query head)
+    return launch_k(attn_combine_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, cpart, cml, ctx_lens, T, nkv, nq / nkv,
                     max_chunks, out);
 }
 
