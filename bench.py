@@ -37,6 +37,10 @@ sys.path.insert(0, ROOT)
 CFG = dict(hidden=4096, n_heads=32, n_kv_heads=8, head_dim=128, intermediate=14336, vocab=128256, n_layers=32,
            n_adapters=128, ranks=(8, 16, 32, 64), K=4, batch=64, ctx_lo=512, ctx_hi=4096)
 METRIC = "decode tok/s, 8B-shape, K=4 of 128 LoRAs; LoRA+attn % of HBM roofline"
+# DRAM bytes (read + write) of one layer's four GEMM launches of this workload
+# (q/k/v 201.6 MB, o 102.8 MB, gate/up 532.9 MB, down 263.7 MB), from an ncu
+# capture of the 2-layer case: profiles/tc_gemm_kernel_decode_config3_2layer.md.
+GEMM_DRAM_BYTES_PER_LAYER = 1101.05e6
 SEED = 20261201
 
 
@@ -473,7 +477,10 @@ def main():
                        "l2": "inputs larger than L2 (~56 GB weights+adapters+KV per GPU)"},
             "roofline": {"bound": "hbm", "kernel": "tc_gemm_kernel (base + fused LoRA shrink/expand)",
                          "achieved": proj_gbs, "peak": peak, "unit": "GB/s", "frac": proj_gbs / peak,
-                         "traffic": None, "peak_kind": peak_kind,
+                         "traffic": GEMM_DRAM_BYTES_PER_LAYER * args.layers, "traffic_unit": "bytes per step",
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one layer's GEMM "
+                                           "launches (2-layer case), times the layers",
+                         "peak_kind": peak_kind,
                          "bytes_per_step": proj_bytes / PS, "ms_per_step": proj_ms / PS,
                          "launches_per_step": n_gemm_launches / PS, "unique_adapters_per_step": n_sel / PS},
             "roofline_attention": {"bound": "hbm", "kernel": "attn_decode_kernel + attn_combine_kernel",
