@@ -76,7 +76,7 @@ class Metrics(C.Structure):
     ]
 
 
-KERNEL_CLASSES = ("gemm", "shrink", "attention", "rmsnorm", "prep", "embed", "lm_head", "other")
+KERNEL_CLASSES = ("gemm", "owner_lora", "attention", "rmsnorm", "prep", "embed", "lm_head", "comm")
 
 
 class Profile(C.Structure):
@@ -130,6 +130,9 @@ def lib():
             "aos_run_step_batch": (C.c_int, [vp, vp, vp, vp, u32, vp, vp]),
             "aos_run_step_batch_dev": (C.c_int, [vp, vp, vp, vp, u32, vp, vp, vp]),
             "aos_layer_step_dev": (C.c_int, [vp, u32, vp, vp, u32, vp, C.c_int, vp]),
+            "aos_shard_get_unique_id": (C.c_int, [vp]),
+            "aos_shard_init": (C.c_int, [vp, u32, u32, vp]),
+            "aos_run_step_sharded_dev": (C.c_int, [vp, vp, vp, vp, u32, vp, vp, vp]),
             "aos_get_metrics": (C.c_int, [vp, vp]),
             "aos_profile_enable": (C.c_int, [vp, C.c_int]),
             "aos_profile_read": (C.c_int, [vp, vp, C.c_int]),
@@ -144,6 +147,23 @@ def lib():
             fn.argtypes = args
         _lib = L
     return _lib
+
+
+SHARD_ID_BYTES = 128
+
+
+def shard_unique_id() -> bytes:
+    """NCCL unique id for aos_shard_init (made on one rank, shared by the caller)."""
+    buf = C.create_string_buffer(SHARD_ID_BYTES)
+    rc = lib().aos_shard_get_unique_id(buf)
+    if rc != 0:
+        raise AosError(rc, last_error())
+    return buf.raw
+
+
+def shard_owner(adapter_id: int, world: int) -> int:
+    """Rank that holds an adapter in the adapter-sharded step (id mod world)."""
+    return int(adapter_id) % int(world)
 
 
 def last_error(ctx=None) -> str:
@@ -485,6 +505,21 @@ class CudaKernels:
         sid = np.ascontiguousarray(seq_ids, np.uint64)
         self._check(self._L.aos_run_step_batch_dev(self.ctx, _p(rings), _p(token_ids), _p(sid), len(sid),
                                                   _p(logits), _p(hidden), stream))
+
+    # -- adapter-sharded step ---------------------------------------------
+    def shard_init(self, rank, world, unique_id: bytes):
+        """Join the adapter-sharded group (collective over the world ranks).
+        This context must hold only adapters with id % world == rank."""
+        buf = C.create_string_buffer(bytes(unique_id), SHARD_ID_BYTES)
+        self._check(self._L.aos_shard_init(self.ctx, int(rank), int(world), buf))
+        self.shard = (int(rank), int(world))
+
+    def run_step_sharded_dev(self, rings, token_ids, seq_ids, logits=None, hidden=None, stream=None):
+        """Decode step of this rank's home tokens (collective; same T on every
+        rank).  Arguments as run_step_batch_dev; rings carry global adapter ids."""
+        sid = np.ascontiguousarray(seq_ids, np.uint64)
+        self._check(self._L.aos_run_step_sharded_dev(self.ctx, _p(rings), _p(token_ids), _p(sid), len(sid),
+                                                    _p(logits), _p(hidden), stream))
 
     def layer_step_dev(self, layer, rings, seq_ids, hidden, advance=False, stream=None):
         sid = np.ascontiguousarray(seq_ids, np.uint64)

@@ -20,13 +20,31 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libaoscuda.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
+
+
+def _nccl_dir():
+    """NCCL of the PyTorch install (the same libnccl.so.2 torch.distributed loads)."""
+    try:
+        import nvidia.nccl as n  # noqa: PLC0415
+        d = list(n.__path__)[0]
+        if os.path.exists(os.path.join(d, "include", "nccl.h")):
+            return d
+    except Exception:
+        pass
+    return None
+
+
+NCCL_DIR = _nccl_dir()
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
     "-Xcompiler", "-fPIC,-O3,-fno-fast-math",
     "--expt-relaxed-constexpr",
     "-ccbin", "/usr/bin/g++",
-]
+] + (["-I" + os.path.join(NCCL_DIR, "include")] if NCCL_DIR else [])
+# the adapter-sharded step calls NCCL (send/recv over NVLink)
+LINK_NCCL = (["-L" + os.path.join(NCCL_DIR, "lib"), "-l:libnccl.so.2", "-Xlinker", "-rpath," + os.path.join(NCCL_DIR, "lib")]
+             if NCCL_DIR else ["-lnccl"])
 
 
 def _sources():
@@ -75,7 +93,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
     if failed:
         raise RuntimeError("CUDA build failed")
     cmd = [NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", LIB, *objs,
-           "-cudart", "static", "-ccbin", "/usr/bin/g++", "-Xcompiler", "-fPIC"]
+           "-cudart", "static", "-ccbin", "/usr/bin/g++", "-Xcompiler", "-fPIC", *LINK_NCCL]
     subprocess.run(cmd, check=True)
     with open(stamp_file, "w") as f:
         f.write(stamp)

@@ -239,6 +239,25 @@ cudaError_t launch_pack_blocks(const uint16_t* src, int rows, int cols, long lon
     return cudaGetLastError();
 }
 
+// p[0, n) = 0 when the step touched no rank group (*n_groups == 0).
+__global__ void zero_if_no_groups_kernel(const int* __restrict__ n_groups, uint16_t* __restrict__ p, size_t n) {
+    pdl_wait();
+    pdl_trigger();
+    if (*n_groups != 0) return;
+    uint4* q = reinterpret_cast<uint4*>(p);
+    const size_t n16 = n / 8;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x)
+        q[i] = make_uint4(0, 0, 0, 0);
+    for (size_t i = n16 * 8 + (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        p[i] = 0;
+}
+
+cudaError_t launch_zero_if_no_groups(const int* n_groups, uint16_t* p, size_t n, cudaStream_t s) {
+    if (!n) return cudaSuccess;
+    if (reinterpret_cast<uintptr_t>(p) & 15) return cudaErrorInvalidValue;
+    return launch_k(zero_if_no_groups_kernel, dim3(148 * 4), dim3(256), 0, s, n_groups, p, n);
+}
+
 cudaError_t launch_fill_normal(uint16_t* p, size_t n, uint64_t seed, float std, cudaStream_t s) {
     if (!n) return cudaSuccess;
     fill_normal_bf16<<<148 * 8, 256, 0, s>>>(p, n, seed, std);

@@ -27,6 +27,8 @@
 #include <unordered_map>
 #include <vector>
 
+#include <nccl.h>
+
 #include "tc_gemm.cuh"
 
 namespace aos {
@@ -36,6 +38,7 @@ cudaError_t launch_lora_prep(const aos_router_ring* rings, int T, const int* col
                              const float* scale, int max_adapters, int n_slab_total, int* slabs, int* n_slabs,
                              float* coef, const int* col_owner, float* ucoef, cudaStream_t s);
 cudaError_t launch_fill_normal(uint16_t*, size_t, uint64_t, float, cudaStream_t);
+cudaError_t launch_zero_if_no_groups(const int* n_groups, uint16_t* p, size_t n, cudaStream_t s);
 cudaError_t launch_pack_blocks(const uint16_t* src, int rows, int cols, long long src_ld, uint16_t* dst, int row0,
                                int col0, int dst_cols, int br, cudaStream_t s);
 cudaError_t launch_attention(const CUtensorMap&, const CUtensorMap&, const uint16_t*, const int*, const int*, float*,
@@ -65,12 +68,14 @@ struct Sequence {
 struct LayerPlan {
     TcParams gemm[4];    // per input group: shrink + base (+ expand when fused) in one launch
     TcParams expand[4];  // q/k/v and o: the LoRA expand as a launch of its own
+    TcParams owner[4];   // adapter-sharded step: this rank's LoRA (shrink + expand) for every rank's rows
     bool split[4];
     int gemm_grid[4];
 };
 
 struct StepPlan {
     int T = 0, T_pad = 0;
+    bool sharded = false;  // adapter-sharded step: T home tokens, T * world rows at the owner
     std::vector<LayerPlan> layers;
     TcParams lm_head;
     int lm_grid = 0;
@@ -143,6 +148,19 @@ struct aos_ctx {
     int* d_sync = nullptr;        // [4] GEMM grid-barrier counters
     int* d_err = nullptr;
     unsigned long long* d_trace = nullptr;  // AOS_TC_TRACE diagnostics
+
+    // Adapter-sharded decode (aos_shard_init): this rank owns the adapters
+    // with id % world == rank.  Per layer and input site every rank sends its
+    // T input rows to every rank (NCCL send/recv), each rank runs the LoRA of
+    // its own adapters on all world * T rows, and the bf16 deltas go back to
+    // the rows' home ranks, which add them in owner order in the base GEMM's
+    // epilogue.
+    int shard_rank = 0, shard_world = 1;
+    ncclComm_t nccl = nullptr;
+    uint16_t* d_xrecv = nullptr;       // [world * T][in]  rows from every rank (rank-major)
+    uint16_t* d_dsend = nullptr;       // [world * T][W]   this rank's deltas for every rank's rows
+    uint16_t* d_drecv = nullptr;       // [world][T][W]    deltas for the home rows, by owner
+    aos_router_ring* d_rings_all = nullptr;  // [world * T] every rank's rings (rank-major)
     std::map<int, std::unique_ptr<StepPlan>> plans;
 
     // metrics
@@ -199,8 +217,65 @@ size_t max_launch_tiles(const aos_ctx* c) {
     return base + 3 * ((size_t)c->R / kGroup / kShrinkGroupsPerTile + 1);
 }
 
+// This rank's LoRA for input site g of one layer over the T rows of every
+// rank (rank-major in d_xrecv): shrink of each module's touched groups, then
+// the expand, stored as bf16 deltas [T][W] (modules side by side) in d_dsend.
+// Adapters this rank does not own have no arena columns, so the prep kernel's
+// touched-group list and coefficients cover only this rank's adapters.
+int build_owner_plan(aos_ctx* c, int layer, int g, int T, TcParams& p) {
+    const uint32_t H = c->cfg.hidden, I = c->cfg.intermediate;
+    const int T_box = tc_t_box(T);
+    const int mods[4][3] = {{AOS_MOD_Q, AOS_MOD_K, AOS_MOD_V}, {AOS_MOD_O, -1, -1}, {AOS_MOD_GATE, AOS_MOD_UP, -1},
+                            {AOS_MOD_DOWN, -1, -1}};
+    const uint32_t K[4] = {H, c->QD, H, I};
+    std::memset(&p, 0, sizeof(p));
+    p.T = T;
+    p.groups = c->d_groups;
+    p.n_groups = c->d_n_groups;
+    p.acc = c->d_acc;
+    p.acc_T = c->T_cap;
+    p.sync = c->d_sync;
+    p.err = c->d_err;
+    p.R = c->R;
+    p.n_rgroups = c->R / kGroup;
+    p.ucoef = c->d_ucoef;
+    p.layer = layer;
+    p.lora = 1;
+    p.kb = (int)(K[g] / 64);
+    int rc = tc_encode_2d(&p.tm_x, c->d_xrecv, K[g], (uint64_t)c->T_cap, (uint64_t)K[g] * 2, 64, (uint32_t)T_box, 128);
+    if (rc) return rc;
+    p.mode = TC_STORE_BF16;
+    p.n_sub = 1;
+    int col = 0;
+    for (int j = 0; j < 3; ++j) {
+        const int mod = mods[g][j];
+        if (mod < 0) continue;
+        p.a_pk[p.sh_nseg] = c->A[mod][layer];
+        p.sh_out[p.sh_nseg] = c->d_hm[mod];
+        ++p.sh_nseg;
+        const int s = p.n_seg++;
+        const int rows = (int)mod_out(c, mod);
+        p.b_pk[s] = c->B[mod][layer];
+        if ((rc = tc_encode_2d(&p.tm_lh[s], c->d_hm[mod], (uint64_t)c->R, (uint64_t)c->T_cap, (uint64_t)c->R * 2, kGroup,
+                               (uint32_t)T_box, 128)))
+            return rc;
+        p.seg_tiles[s] = (rows + kTcBN - 1) / kTcBN;
+        p.seg_rows[s] = rows;
+        p.seg_module[s] = mod;
+        p.seg_out0[s] = col;
+        p.out[s] = c->d_dsend;
+        col += rows;
+    }
+    p.ld_out = col;
+    p.pools = 1 | 4;  // shrink and expand, no base weights
+    return tc_prepare(p, 227 * 1024);
+}
+
 // Build the TcParams of every GEMM of one layer for a batch of T tokens.
-int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
+// sharded: the base GEMMs carry no LoRA of their own but add the deltas the
+// adapter owners return, and owner[g] is this rank's LoRA launch over the
+// world * T rows of every rank.
+int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp, bool sharded = false) {
     const uint32_t H = c->cfg.hidden, I = c->cfg.intermediate;
     const int T_box = tc_t_box(T);  // activation box rows (128 per token block at most)
     const int smem_budget = 227 * 1024;
@@ -237,7 +312,7 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
         // ---------------- LoRA shrink + base GEMM + fused LoRA expand + epilogue
         TcParams& p = lp.gemm[g];
         common(p);
-        p.lora = lora[g] ? 1 : 0;
+        p.lora = (lora[g] && !sharded) ? 1 : 0;
         p.kb = (int)(group_k[g] / 64);
         if ((rc = x_map(&p.tm_x, group_x[g], group_k[g]))) return rc;
         if (p.lora) {  // hm = gate * (A_cat x) of every module of the group, in the same launch
@@ -311,6 +386,23 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
             p.resid = c->d_hidden;
             p.ld_out = (int)H;
         }
+        if (sharded && lora[g]) {
+            // deltas of every owner rank: [world][T][W], W = the site's output width
+            const uint32_t W[4] = {c->QD + 2 * c->KVD, H, 2 * I, H};
+            p.delta = c->d_drecv;
+            p.n_delta = c->shard_world;
+            p.ld_delta = (int)W[g];
+            p.delta_stride = (long long)T * W[g];
+            if (g == kGroupQKV) {
+                p.dseg0[0] = 0;
+                p.dseg0[1] = (int)c->QD;
+                p.dseg0[2] = (int)(c->QD + c->KVD);
+            } else if (g == kGroupGU) {
+                p.dseg0[0] = 0;
+                p.dseg0[1] = (int)I;
+            }
+            if ((rc = build_owner_plan(c, layer, g, T * c->shard_world, lp.owner[g]))) return rc;
+        }
         // Tuning knob AOS_SPLIT_EXPAND=1: run the q/k/v and o LoRA expand as a
         // launch of its own (RoPE is linear, and the o epilogue adds into the
         // residual anyway).  Off by default: measured slower than the fused launch.
@@ -319,7 +411,7 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
             const char* e = getenv("AOS_SPLIT_EXPAND");
             return e && e[0] == '1';
         }();
-        lp.split[g] = split_expand && p.lora && (g == kGroupQKV || g == kGroupO);
+        lp.split[g] = split_expand && p.lora && !sharded && (g == kGroupQKV || g == kGroupO);
         if (lp.split[g]) {
             TcParams& e = lp.expand[g];
             e = p;
@@ -340,9 +432,10 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp) {
     return AOS_OK;
 }
 
-int get_plan(aos_ctx* c, int T, StepPlan** out) {
+int get_plan(aos_ctx* c, int T, StepPlan** out, bool sharded = false) {
     const int T_pad = std::max(32, ((T + 15) / 16) * 16);
-    auto it = c->plans.find(T);
+    const int key = sharded ? -T : T;
+    auto it = c->plans.find(key);
     if (it != c->plans.end()) {
         *out = it->second.get();
         return AOS_OK;
@@ -350,9 +443,10 @@ int get_plan(aos_ctx* c, int T, StepPlan** out) {
     auto plan = std::make_unique<StepPlan>();
     plan->T = T;
     plan->T_pad = T_pad;
+    plan->sharded = sharded;
     plan->layers.resize(c->cfg.n_layers);
     for (uint32_t l = 0; l < c->cfg.n_layers; ++l) {
-        int rc = build_layer_plan(c, (int)l, T, plan->layers[l]);
+        int rc = build_layer_plan(c, (int)l, T, plan->layers[l], sharded);
         if (rc) return c->fail(rc, "building the GEMM plan failed (tensor map encode)");
     }
     // lm_head: logits = normed . lm_head^T (f32 out)
@@ -380,7 +474,7 @@ int get_plan(aos_ctx* c, int T, StepPlan** out) {
     if ((rc = tc_prepare(p, 227 * 1024))) return c->fail(rc, "lm_head plan");
     plan->lm_grid = tc_num_sms();
     *out = plan.get();
-    c->plans[T] = std::move(plan);
+    c->plans[key] = std::move(plan);
     return AOS_OK;
 }
 
@@ -403,11 +497,66 @@ void prof_end(aos_ctx* c, int slot, cudaStream_t s);
         prof_end(ctx, _slot, s);                   \
     } while (0)
 
+#define NCCL_CHECK(ctx, expr)                                                                      \
+    do {                                                                                           \
+        ncclResult_t _r = (expr);                                                                  \
+        if (_r != ncclSuccess) return (ctx)->fail(AOS_ERR_CUDA, std::string(#expr ": ") + ncclGetErrorString(_r)); \
+    } while (0)
+
+// Adapter-sharded step, input site g of one layer: x [T][in] (the home rows)
+// goes to every rank; this rank's LoRA over the world * T rows it received
+// writes deltas [world * T][W]; block o of them goes back to rank o, and the
+// base GEMM of the site adds the blocks it receives, in owner order, in its
+// epilogue (lp.gemm[g].delta).
+int shard_site(aos_ctx* c, const StepPlan& plan, const LayerPlan& lp, int g, const uint16_t* x, uint32_t in,
+               cudaStream_t s) {
+    const int world = c->shard_world;
+    const size_t nx = (size_t)plan.T * in, nd = (size_t)plan.T * lp.gemm[g].ld_delta;
+    int slot = prof_begin(c, AOS_K_COMM, s);
+    NCCL_CHECK(c, ncclGroupStart());
+    for (int o = 0; o < world; ++o) {
+        NCCL_CHECK(c, ncclSend(x, nx, ncclBfloat16, o, c->nccl, s));
+        NCCL_CHECK(c, ncclRecv(c->d_xrecv + (size_t)o * nx, nx, ncclBfloat16, o, c->nccl, s));
+    }
+    NCCL_CHECK(c, ncclGroupEnd());
+    prof_end(c, slot, s);
+    PLAUNCH(c, AOS_K_SHRINK, s, tc_launch(lp.owner[g], lp.gemm_grid[g], s));
+    slot = prof_begin(c, AOS_K_COMM, s);
+    NCCL_CHECK(c, ncclGroupStart());
+    for (int o = 0; o < world; ++o) {
+        NCCL_CHECK(c, ncclSend(c->d_dsend + (size_t)o * nd, nd, ncclBfloat16, o, c->nccl, s));
+        NCCL_CHECK(c, ncclRecv(c->d_drecv + (size_t)o * nd, nd, ncclBfloat16, o, c->nccl, s));
+    }
+    NCCL_CHECK(c, ncclGroupEnd());
+    prof_end(c, slot, s);
+    return AOS_OK;
+}
+
 // Enqueue one decoder layer on `s` (hidden state in ctx->d_hidden).
 int enqueue_layer(aos_ctx* c, const StepPlan& plan, int layer, cudaStream_t s) {
     const LayerPlan& lp = plan.layers[layer];
     const int T = plan.T;
     const uint32_t H = c->cfg.hidden;
+    if (plan.sharded) {
+        const bool lora[4] = {lp.gemm[kGroupQKV].delta != nullptr, lp.gemm[kGroupO].delta != nullptr,
+                              lp.gemm[kGroupGU].delta != nullptr, lp.gemm[kGroupD].delta != nullptr};
+        int rc;
+        PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(c->d_hidden, c->attn_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
+        if (lora[kGroupQKV] && (rc = shard_site(c, plan, lp, kGroupQKV, c->d_normed, H, s))) return rc;
+        PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupQKV], lp.gemm_grid[kGroupQKV], s));
+        PLAUNCH(c, AOS_K_ATTN, s,
+                launch_attention(c->tm_k, c->tm_v, c->d_q, c->d_block_tables, c->d_ctx_lens, c->d_attn_part, c->d_attn_ml,
+                                 T, (int)c->cfg.n_heads, (int)c->cfg.n_kv_heads, layer, (int)c->cfg.kv_num_blocks,
+                                 c->max_blocks, c->attn_chunks, c->d_err, c->d_attn, s));
+        if (lora[kGroupO] && (rc = shard_site(c, plan, lp, kGroupO, c->d_attn, c->QD, s))) return rc;
+        PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupO], lp.gemm_grid[kGroupO], s));
+        PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(c->d_hidden, c->mlp_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
+        if (lora[kGroupGU] && (rc = shard_site(c, plan, lp, kGroupGU, c->d_normed, H, s))) return rc;
+        PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupGU], lp.gemm_grid[kGroupGU], s));
+        if (lora[kGroupD] && (rc = shard_site(c, plan, lp, kGroupD, c->d_act, c->cfg.intermediate, s))) return rc;
+        PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupD], lp.gemm_grid[kGroupD], s));
+        return AOS_OK;
+    }
     PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(c->d_hidden, c->attn_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
     PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupQKV], lp.gemm_grid[kGroupQKV], s));
     if (lp.split[kGroupQKV]) PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.expand[kGroupQKV], lp.gemm_grid[kGroupQKV], s));
@@ -426,9 +575,25 @@ int enqueue_layer(aos_ctx* c, const StepPlan& plan, int layer, cudaStream_t s) {
 // Device part of a decode step: routing prep, embedding, layers, final norm, lm_head.
 int enqueue_step(aos_ctx* c, StepPlan& plan, bool with_logits, cudaStream_t s) {
     const int T = plan.T;
-    PLAUNCH(c, AOS_K_PREP, s,
-            launch_lora_prep(c->d_rings, T, c->d_col_off, c->d_rank, c->d_scale, (int)c->cfg.lora_max_adapters,
-                             c->R / kGroup, c->d_groups, c->d_n_groups, c->d_coef, c->d_col_owner, c->d_ucoef, s));
+    if (plan.sharded) {
+        // every rank's rings (rank-major), then the touched groups and
+        // coefficients of this rank's adapters over all world * T rows
+        const int slot = prof_begin(c, AOS_K_COMM, s);
+        NCCL_CHECK(c, ncclAllGather(c->d_rings, c->d_rings_all, (size_t)T * sizeof(aos_router_ring), ncclUint8, c->nccl, s));
+        prof_end(c, slot, s);
+        const int TG = T * c->shard_world;
+        PLAUNCH(c, AOS_K_PREP, s,
+                launch_lora_prep(c->d_rings_all, TG, c->d_col_off, c->d_rank, c->d_scale, (int)c->cfg.lora_max_adapters,
+                                 c->R / kGroup, c->d_groups, c->d_n_groups, c->d_coef, c->d_col_owner, c->d_ucoef, s));
+        // no touched group: the owner launches have no work and write no
+        // deltas, so the delta rows must read as zero
+        PLAUNCH(c, AOS_K_PREP, s,
+                launch_zero_if_no_groups(c->d_n_groups, c->d_dsend, (size_t)TG * 2 * c->cfg.intermediate, s));
+    } else {
+        PLAUNCH(c, AOS_K_PREP, s,
+                launch_lora_prep(c->d_rings, T, c->d_col_off, c->d_rank, c->d_scale, (int)c->cfg.lora_max_adapters,
+                                 c->R / kGroup, c->d_groups, c->d_n_groups, c->d_coef, c->d_col_owner, c->d_ucoef, s));
+    }
     PLAUNCH(c, AOS_K_EMBED, s, launch_embed(c->embed, c->d_tokens, T, (int)c->cfg.hidden, (int)c->cfg.vocab, c->d_hidden, s));
     for (uint32_t l = 0; l < c->cfg.n_layers; ++l) {
         int rc = enqueue_layer(c, plan, (int)l, s);
@@ -468,9 +633,9 @@ bool use_graphs() {
     return !(e && e[0] == '1');
 }
 
-int run_step_device(aos_ctx* c, int T, bool with_logits, cudaStream_t s) {
+int run_step_device(aos_ctx* c, int T, bool with_logits, cudaStream_t s, bool sharded = false) {
     StepPlan* plan = nullptr;
-    int rc = get_plan(c, T, &plan);
+    int rc = get_plan(c, T, &plan, sharded);
     if (rc) return rc;
     if (c->prof_on) {  // instrumented, graph-less step; times are collected after the step
         rc = enqueue_step(c, *plan, with_logits, s);
@@ -767,9 +932,11 @@ void aos_destroy(aos_ctx* c) {
     cudaStreamSynchronize(c->stream);
     for (auto& kv : c->plans)
         if (kv.second->graph) cudaGraphExecDestroy(kv.second->graph);
+    if (c->nccl) ncclCommDestroy(c->nccl);  // after the graphs that hold its calls
     auto f = [](void* p) {
         if (p) cudaFree(p);
     };
+    f(c->d_xrecv); f(c->d_dsend); f(c->d_drecv); f(c->d_rings_all);
     f(c->embed); f(c->lm_head); f(c->final_norm);
     for (auto* p : c->attn_norm) f(p);
     for (auto* p : c->mlp_norm) f(p);
@@ -1103,6 +1270,67 @@ int aos_run_step_batch(aos_ctx* c, const aos_router_ring* rings, const uint32_t*
     cudaEventElapsedTime(&ms, c->ev0, c->ev1);
     c->m.last_step_ms = ms;
     return check_device_error(c);
+}
+
+// ------------------------------------------------------------------ adapter-sharded step
+int aos_shard_get_unique_id(void* id) {
+    if (!id) return AOS_ERR_INVALID;
+    static_assert(sizeof(ncclUniqueId) == AOS_SHARD_ID_BYTES, "NCCL unique id size");
+    ncclUniqueId u;
+    const ncclResult_t r = ncclGetUniqueId(&u);
+    if (r != ncclSuccess) {
+        set_global_error(std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+        return AOS_ERR_CUDA;
+    }
+    std::memcpy(id, &u, sizeof(u));
+    return AOS_OK;
+}
+
+int aos_shard_init(aos_ctx* c, uint32_t rank, uint32_t world, const void* id) {
+    if (!c || !id || world == 0 || rank >= world) return AOS_ERR_INVALID;
+    if (c->nccl) return c->fail(AOS_ERR_STATE, "the context is already sharded");
+    if (c->T_cap < (int)world) return c->fail(AOS_ERR_INVALID, "max_batch must hold one token of every rank");
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    ncclUniqueId u;
+    std::memcpy(&u, id, sizeof(u));
+    NCCL_CHECK(c, ncclCommInitRank(&c->nccl, (int)world, u, (int)rank));
+    c->shard_rank = (int)rank;
+    c->shard_world = (int)world;
+    const size_t TC = (size_t)c->T_cap, H = c->cfg.hidden, I = c->cfg.intermediate;
+    const size_t in_max = std::max<size_t>({H, (size_t)c->QD, I});
+    const size_t w_max = std::max<size_t>({(size_t)c->QD + 2 * c->KVD, H, 2 * I});
+    CTX_CUDA(c, dalloc(&c->d_xrecv, TC * in_max));
+    CTX_CUDA(c, dalloc(&c->d_dsend, TC * w_max));
+    CTX_CUDA(c, dalloc(&c->d_drecv, TC * w_max));
+    CTX_CUDA(c, dalloc(&c->d_rings_all, TC));
+    for (auto& kv : c->plans)  // plans are built per mode; drop any built before
+        if (kv.second->graph) cudaGraphExecDestroy(kv.second->graph);
+    c->plans.clear();
+    return AOS_OK;
+}
+
+int aos_run_step_sharded_dev(aos_ctx* c, const aos_router_ring* rings, const uint32_t* token_ids, const uint64_t* seq_ids,
+                             uint32_t T, float* logits, uint16_t* hidden_out, void* stream) {
+    if (!c || !rings || !token_ids || !seq_ids || T == 0) return AOS_ERR_INVALID;
+    if (!c->nccl) return c->fail(AOS_ERR_STATE, "aos_shard_init has not been called");
+    if ((size_t)T * c->shard_world > (size_t)c->T_cap)
+        return c->fail(AOS_ERR_INVALID, "T * world exceeds max_batch (the owner side runs every rank's rows)");
+    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    int rc = stage_sequences(c, seq_ids, T);
+    if (rc) return rc;
+    if ((rc = upload_tables(c, T, s))) return rc;
+    if (rings != c->d_rings)
+        CTX_CUDA(c, cudaMemcpyAsync(c->d_rings, rings, (size_t)T * sizeof(aos_router_ring), cudaMemcpyDeviceToDevice, s));
+    if (token_ids != c->d_tokens)
+        CTX_CUDA(c, cudaMemcpyAsync(c->d_tokens, token_ids, (size_t)T * 4, cudaMemcpyDeviceToDevice, s));
+    if ((rc = run_step_device(c, (int)T, true, s, true))) return rc;
+    if (logits && logits != c->d_logits)
+        CTX_CUDA(c, cudaMemcpyAsync(logits, c->d_logits, (size_t)T * c->cfg.vocab * 4, cudaMemcpyDeviceToDevice, s));
+    if (hidden_out)
+        CTX_CUDA(c, cudaMemcpyAsync(hidden_out, c->d_hidden, (size_t)T * c->cfg.hidden * 2, cudaMemcpyDeviceToDevice, s));
+    advance(c, seq_ids, T);
+    return AOS_OK;
 }
 
 int aos_layer_step_dev(aos_ctx* c, uint32_t layer, const aos_router_ring* rings, const uint64_t* seq_ids, uint32_t T,

@@ -265,16 +265,56 @@ __device__ __forceinline__ void shrink_run(const TcParams& p, int seg, int t, in
     store_bf16_run<N>(reinterpret_cast<uint16_t*>(p.sh_out[seg]) + (size_t)t * p.R + c0 + cc, v);
 }
 
+// v[i] += sum over owners o (in order) of delta[o][t][col + i], i < n.
+template <int N>
+__device__ __forceinline__ void add_delta_run(const TcParams& p, int t, int col, int n, float (&v)[N]) {
+    const uint16_t* d = p.delta + (size_t)t * p.ld_delta + col;
+    if (n >= N) {
+        for (int o = 0; o < p.n_delta; ++o, d += p.delta_stride) {
+#pragma unroll
+            for (int i = 0; i < N; i += 8) {
+                const uint4 w = __ldg(reinterpret_cast<const uint4*>(d + i));
+                const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    v[i + 2 * j] += bf2f((uint16_t)(u[j] & 0xFFFFu));
+                    v[i + 2 * j + 1] += bf2f((uint16_t)(u[j] >> 16));
+                }
+            }
+        }
+    } else {
+        for (int o = 0; o < p.n_delta; ++o, d += p.delta_stride) {
+#pragma unroll
+            for (int i = 0; i < N; ++i)
+                if (i < n) v[i] += bf2f(__ldg(d + i));
+        }
+    }
+}
+
 // Applies the epilogue of `mode` to pairs [pr0, pr0 + N) of chunk k of tile
 // `tile` (segment `seg`) for token t (t < T).  vA/vB: accumulator values of
-// the pairs' first and second columns.
+// the pairs' first and second columns (the owners' deltas, if any, are added
+// in place).
 template <int N>
 __device__ __forceinline__ void apply_pairs(const TcParams& p, int mode, int seg, int tile, int k, int t, int pr0,
-                                            const float* vA, const float* vB, int ng) {
+                                            float (&vA)[N], float (&vB)[N], int ng) {
     int cA, cB;
     chunk_cols(mode, k, cA, cB);
     cA += pr0;
     cB += pr0;
+    if (p.delta && mode != TC_SHRINK_HM) {  // owners' LoRA deltas join the accumulator
+        if (mode == TC_SWIGLU) {
+            const int f0 = tile * (kTcBN / 2) + cA, n = p.seg_rows[seg] - f0;
+            if (n > 0) {
+                add_delta_run<N>(p, t, p.dseg0[0] + f0, n, vA);
+                add_delta_run<N>(p, t, p.dseg0[1] + f0, n, vB);
+            }
+        } else {
+            const int rA = tile * kTcBN + cA, rB = tile * kTcBN + cB, lim = p.seg_rows[seg];
+            if (rA < lim) add_delta_run<N>(p, t, p.dseg0[seg] + rA, lim - rA, vA);
+            if (rB < lim) add_delta_run<N>(p, t, p.dseg0[seg] + rB, lim - rB, vB);
+        }
+    }
     switch (mode) {
         case TC_STORE_BF16:
         case TC_STORE_F32:
@@ -802,6 +842,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     last_phase[stage] = phase;
                     used_mask |= 1u << stage;
                     if (tr && n_issued < 64) tr[n_issued] = gtimer();
+                    if (tr && pc.shrink) tr[204] = gtimer();
                     ++n_issued;
                     if (++stage == NS) { stage = 0; phase ^= 1u; }
                     if (!ok) break;
@@ -840,6 +881,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                     if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.err)) { ok = false; break; }
                     tc_fence_after();
                     if (tr && n_waited < 64) tr[64 + n_waited] = gtimer();
+                    if (tr && r.tile < sc.n_sh) tr[205] = gtimer();
                     ++n_waited;
                     const uint32_t sbase = smem_u32(stages + (size_t)stage * p.stage_bytes);
                     const uint32_t act = sbase + p.act_off;

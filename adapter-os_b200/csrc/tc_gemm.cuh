@@ -68,6 +68,16 @@ struct TcParams {
     const int* block_tables;
     const int* ctx_lens;
     int max_blocks, num_blocks, nkv, layer;
+    // LoRA deltas computed by the adapter owners (adapter-sharded decode):
+    // n_delta blocks of [T][ld_delta] bf16, delta_stride elements apart, one
+    // per owner rank.  The epilogue adds their sum, taken in owner order, to
+    // the accumulator before the mode's own math.  Segment s's columns start
+    // at dseg0[s]; TC_SWIGLU reads the gate deltas at dseg0[0] and the up
+    // deltas at dseg0[1].  Null = none.
+    const uint16_t* delta;
+    long long delta_stride;
+    int n_delta, ld_delta;
+    int dseg0[kTcMaxSets];
     int R;                          // arena rank capacity (columns of hm)
     // [T][n_rgroups slots][8]: gate * alpha/rank of the adapter owning each
     // 8-column unit of the slot-th touched group for each token (0 when the
@@ -93,7 +103,8 @@ constexpr int kMaxPiecesPerPool = 30;  // a slice is at least 1/30 of a tile
 // [64,128) MMA full-barrier waits done, [128,160) drain piece starts,
 // [160,192) drain piece ends, 192 kernel start, 193 kernel end, 194-199 grid
 // barrier events (arrive/complete of the three barriers), 200/201 final
-// reduction start/end, 202/203 producer wait for the shrink output.
+// reduction start/end, 202/203 producer wait for the shrink output, 204
+// producer's last shrink step issued, 205 MMA's last shrink step consumed.
 constexpr int kTraceStride = 256;
 
 // Host helpers (tc_gemm.cu).

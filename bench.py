@@ -119,23 +119,21 @@ def ctx_lens_of(rng, B):
     return rng.integers(CFG["ctx_lo"], CFG["ctx_hi"] + 1, size=B)
 
 
-def build_gpu_model(aos, torch, device, steps_total, layers):
+def module_shapes():
+    """(out, in) of q, k, v, o, gate, up, down."""
     c = CFG
-    rng = np.random.default_rng(SEED)
-    ranks = ranks_of(rng)
-    ctx = ctx_lens_of(rng, c["batch"])
-    cap = int(sum(((int(r) + 15) // 16) * 16 for r in ranks)) + 64
-    max_seq = c["ctx_hi"] + steps_total + 16
-    blocks = int(sum((int(n) + steps_total + 16 + 15) // 16 for n in ctx)) + 16
-    gpu = aos.CudaKernels(c["hidden"], c["n_heads"], c["n_kv_heads"], c["head_dim"], c["intermediate"], c["vocab"],
-                          layers, max_batch=c["batch"], kv_num_blocks=blocks, max_seq_len=max_seq,
-                          lora_rank_capacity=cap, lora_max_adapters=c["n_adapters"], device=device)
+    H, I = c["hidden"], c["intermediate"]
+    QD, KVD = c["n_heads"] * 128, c["n_kv_heads"] * 128
+    return [(QD, H), (KVD, H), (KVD, H), (H, QD), (I, H), (I, H), (H, I)]
+
+
+def load_base(gpu, aos, torch, device, layers):
+    """Random-init base weights (seeded); returns the seeded bf16 generator used."""
+    c = CFG
     g = torch.Generator(device=f"cuda:{device}")
     g.manual_seed(SEED)
     dev = f"cuda:{device}"
-    H, I, V = c["hidden"], c["intermediate"], c["vocab"]
-    QD, KVD = c["n_heads"] * 128, c["n_kv_heads"] * 128
-    shapes = [(QD, H), (KVD, H), (KVD, H), (H, QD), (I, H), (I, H), (H, I)]
+    H, V = c["hidden"], c["vocab"]
 
     def randn(shape, std):
         return (torch.randn(shape, generator=g, device=dev, dtype=torch.float32) * std).to(torch.bfloat16)
@@ -147,10 +145,26 @@ def build_gpu_model(aos, torch, device, steps_total, layers):
     for l in range(layers):
         gpu.load_weight(aos.W_ATTN_NORM, (1 + randn((H,), 0.1).float()).to(torch.bfloat16), layer=l, on_device=True)
         gpu.load_weight(aos.W_MLP_NORM, (1 + randn((H,), 0.1).float()).to(torch.bfloat16), layer=l, on_device=True)
-        for m, shp in enumerate(shapes):
+        for m, shp in enumerate(module_shapes()):
             gpu.load_weight(aos.W_PROJ, randn(shp, 0.02), layer=l, module=m, on_device=True)
     torch.cuda.synchronize()
     log(f"[bench] base weights loaded in {time.time() - t0:.1f}s")
+    return randn
+
+
+def build_gpu_model(aos, torch, device, steps_total, layers):
+    c = CFG
+    rng = np.random.default_rng(SEED)
+    ranks = ranks_of(rng)
+    ctx = ctx_lens_of(rng, c["batch"])
+    cap = int(sum(((int(r) + 15) // 16) * 16 for r in ranks)) + 64
+    max_seq = c["ctx_hi"] + steps_total + 16
+    blocks = int(sum((int(n) + steps_total + 16 + 15) // 16 for n in ctx)) + 16
+    gpu = aos.CudaKernels(c["hidden"], c["n_heads"], c["n_kv_heads"], c["head_dim"], c["intermediate"], c["vocab"],
+                          layers, max_batch=c["batch"], kv_num_blocks=blocks, max_seq_len=max_seq,
+                          lora_rank_capacity=cap, lora_max_adapters=c["n_adapters"], device=device)
+    randn = load_base(gpu, aos, torch, device, layers)
+    shapes = module_shapes()
     t0 = time.time()
     L = gpu._L
     for a in range(c["n_adapters"]):
@@ -309,6 +323,182 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ config 5
+CFG5 = dict(n_adapters=1024, rank=16, K=8, batch=256, ctx_lo=512, ctx_hi=1024, zipf_s=1.1)
+METRIC5 = "decode tok/s, 8B-shape, K=8 of 1024 rank-16 LoRAs sharded by adapter id, batch 256"
+
+
+def run_config5(args, rank, world, local, dist):
+    """BASELINE config 5 (large adapter pool): 1024 rank-16 adapters on all 7
+    modules, sharded by id (rank r holds ids with id % world == r); popularity
+    Zipf(s=1.1) over a seeded permutation of ids; K=8; decode batch 256 split
+    evenly over the ranks (strong scaling: the box decodes 256 tokens per
+    step at every N).  At N > 1 every LoRA term crosses the NCCL exchange of
+    aos_run_step_sharded_dev; at N = 1 the whole pool is local and the step
+    is the fused one.  Context lengths U[512, 1024] (not stated by the
+    config; chosen so the whole pool, the base and the KV of 256 sequences
+    fit one GPU)."""
+    import torch
+    aos = importlib.import_module("adapter-os_b200")
+    c, c5 = CFG, CFG5
+    B, NA, R = c5["batch"], c5["n_adapters"], c5["rank"]
+    if B % world:
+        raise SystemExit("config 5 needs a world size that divides 256")
+    T = B // world
+    dev = f"cuda:{local}"
+    W, K, PS = max(3, args.warmup), args.steps, 2
+    total = W + K + PS + 2
+    layers = args.layers
+    rng = np.random.default_rng(SEED + 5)
+    ctx_all = rng.integers(c5["ctx_lo"], c5["ctx_hi"] + 1, size=B)
+    perm = rng.permutation(NA)  # popularity rank -> adapter id
+    pop = 1.0 / np.arange(1, NA + 1) ** c5["zipf_s"]
+    logp = np.empty(NA)
+    logp[perm] = np.log(pop / pop.sum())
+    owned = [a for a in range(NA) if a % world == rank]
+    home = slice(rank * T, (rank + 1) * T)
+    ctx = ctx_all[home]
+    blocks = int(sum((int(n) + total + 16 + 15) // 16 for n in ctx)) + 16
+    gpu = aos.CudaKernels(c["hidden"], c["n_heads"], c["n_kv_heads"], c["head_dim"], c["intermediate"], c["vocab"],
+                          layers, max_batch=B, kv_num_blocks=blocks, max_seq_len=c5["ctx_hi"] + total + 16,
+                          lora_rank_capacity=len(owned) * R, lora_max_adapters=NA, device=local)
+    load_base(gpu, aos, torch, local, layers)
+    t0 = time.time()
+    L = gpu._L
+    shapes = module_shapes()
+    g = torch.Generator(device=dev)
+    for a in owned:  # adapter a's weights depend on a only, so every N decodes the same model
+        g.manual_seed(SEED * 7 + a)
+        aos.check(L.aos_adapter_new(gpu.ctx, a, R, float(2 * R)), gpu.ctx)
+        for m, (out, inn) in enumerate(shapes):
+            A = (torch.randn((layers, R, inn), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            Bm = (torch.randn((layers, out, R), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            for l in range(layers):
+                aos.check(L.aos_adapter_set_module(gpu.ctx, a, l, m, A[l].data_ptr(), Bm[l].data_ptr(), 1), gpu.ctx)
+    torch.cuda.synchronize()
+    log(f"[bench] config 5 rank {rank}: {len(owned)} adapters loaded in {time.time() - t0:.1f}s")
+    seq_ids = np.arange(rank * T, (rank + 1) * T, dtype=np.uint64)
+    for i in range(T):
+        gpu.kv_alloc(int(seq_ids[i]), int(ctx[i]) + total + 16)
+    gpu.kv_fill_synthetic(seed=SEED + rank, std=1.0)
+    for i in range(T):
+        gpu.kv_set_len(int(seq_ids[i]), int(ctx[i]))
+    if world > 1:
+        uid = [aos.shard_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        gpu.shard_init(rank, world, uid[0])
+    stream_ptr = gpu.stream()
+    stream = torch.cuda.ExternalStream(stream_ptr)
+    # priors: log popularity + Gumbel noise, so top-K is a popularity-weighted
+    # draw without replacement; generated for all 256 tokens, home rows kept
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED + 50)
+    lp = torch.tensor(logp, dtype=torch.float32, device=dev)
+    priors, tokens = [], []
+    for i in range(total):
+        u = torch.rand((B, NA), generator=gen, device=dev).clamp_(1e-12, 1 - 1e-7)
+        priors.append((lp - torch.log(-torch.log(u)))[home].contiguous())
+        tokens.append(torch.randint(0, c["vocab"], (B,), generator=gen, device=dev, dtype=torch.int32)[home].contiguous())
+    sids = torch.arange(NA, device=dev, dtype=torch.int64)
+    rings = torch.zeros((T, 40), dtype=torch.uint8, device=dev)
+    logits = torch.empty((T, c["vocab"]), dtype=torch.float32, device=dev)
+
+    def step(i):
+        aos.route_batch_dev(priors[i], sids, rings, k=c5["K"], tau=1.0, eps=0.02, stream=stream_ptr)
+        if world > 1:
+            gpu.run_step_sharded_dev(rings, tokens[i], seq_ids, logits=logits, stream=stream_ptr)
+        else:
+            gpu.run_step_batch_dev(rings, tokens[i], seq_ids, logits=logits, stream=stream_ptr)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if not dist:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for i in range(W):
+        step(i)
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    ev0.record(stream)
+    for i in range(W, W + K):
+        step(i)
+    ev1.record(stream)
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    value = B * K / (ms / 1000.0)
+    gpu.health_check()
+
+    # instrumented steps: per-class device time and this rank's bytes
+    gpu.profile_enable(True)
+    gpu.profile_read(reset=True)
+    H, I, V = c["hidden"], c["intermediate"], c["vocab"]
+    QD, KVD = c["n_heads"] * 128, c["n_kv_heads"] * 128
+    per_col = sum(o + i_ for o, i_ in shapes)  # bytes / 2 of one rank column over the 7 modules
+    slot = {a: j for j, a in enumerate(owned)}  # arena order: adapter j at columns [16j, 16j + 16)
+    lora_b, kv_b, groups_n = 0, 0, 0
+    for i in range(W + K, W + K + PS):
+        ctx_now = [gpu.kv_len(int(s_)) for s_ in seq_ids]
+        step(i)
+        torch.cuda.synchronize()
+        rg = rings
+        if dist:
+            allr = torch.empty((B, 40), dtype=torch.uint8, device=dev)
+            dist.all_gather_into_tensor(allr, rings)
+            rg = allr
+        rn = rg.cpu().numpy().view(aos.RING_DTYPE).reshape(-1)
+        groups = set()
+        for r_ in rn:
+            for j in range(int(r_["top_k"])):
+                a = int(r_["indices"][j])
+                if r_["gates_q15"][j] > 0 and a in slot:
+                    groups.add(slot[a] * R // 64)
+        groups_n += len(groups)
+        lora_b += len(groups) * 64 * per_col * 2 * layers
+        kv_b += attn_bytes(ctx_now, layers)
+    prof = gpu.profile_read(reset=True)
+    gpu.profile_enable(False)
+    peak, peak_kind = peaks()
+    act = act_bytes(layers, T)
+    step_bytes = (base_bytes(layers) + V * H * 2 + act) + (lora_b + kv_b) / PS
+    achieved = step_bytes / (ms / K / 1000.0) / 1e9
+    ins, wid = (H, QD, H, I), (QD + 2 * KVD, H, 2 * I, H)
+    x_b = sum(T * n * 2 for n in ins) * layers          # rows sent to each peer
+    d_b = sum(T * w_ * 2 for w_ in wid) * layers        # deltas sent back to each peer
+    nvlink = (world - 1) * (x_b + d_b) if world > 1 else 0
+    if rank == 0:
+        line = {
+            "metric": METRIC5, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config 5: 32-layer 8B-shape decode, 1024 rank-16 adapters on 7 modules sharded "
+                                   "by id mod N, Zipf(1.1) popularity, K=8, global batch 256, ctx U[512,1024]",
+                       "layers": layers, "global_batch": B, "tokens_per_gpu": T,
+                       "parallelism": f"adapter-sharded x{world} (NCCL send/recv per layer and input site)"
+                       if world > 1 else "single GPU, whole pool local (fused step)"},
+            "roofline": {"bound": "hbm", "kernel": "whole step (rank 0)", "achieved": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
+                         "bytes_per_step": step_bytes, "lora_bytes_per_step": lora_b / PS,
+                         "touched_groups_per_step": groups_n / PS, "kv_bytes_per_step": kv_b / PS},
+            "nvlink_bytes_per_step_per_gpu": nvlink,
+            "kernel_ms_per_step": {k: v / PS for k, v in prof["ms"].items()},
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    barrier()
+    gpu.close()
+
+
 # ------------------------------------------------------------------ GPU arm
 def main():
     ap = argparse.ArgumentParser()
@@ -318,6 +508,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=CFG["n_layers"], help="debug only: fewer layers is not a valid number")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", type=int, default=3, choices=[3, 5],
+                    help="3: the headline decode workload; 5: the adapter-sharded large pool")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -339,6 +531,12 @@ def main():
 
         dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
         dist = dist_mod
+    if args.config == 5:
+        run_config5(args, rank, world, local, dist)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     aos = importlib.import_module("adapter-os_b200")
     c = CFG
     W, K = max(3, args.warmup), args.steps
@@ -410,10 +608,10 @@ def main():
     gpu.profile_enable(False)
     peak, peak_kind = peaks()
     proj_bytes = (base_bytes(args.layers) + act_bytes(args.layers, B)) * PS + lbytes
-    proj_ms = prof["ms"]["gemm"] + prof["ms"]["shrink"]
+    proj_ms = prof["ms"]["gemm"] + prof["ms"]["owner_lora"]
     proj_gbs = proj_bytes / (proj_ms / 1000.0) / 1e9
     attn_gbs = abytes / (prof["ms"]["attention"] / 1000.0) / 1e9
-    n_gemm_launches = prof["launches"]["gemm"] + prof["launches"]["shrink"]
+    n_gemm_launches = prof["launches"]["gemm"] + prof["launches"]["owner_lora"]
     step_ms_prof = sum(prof["ms"].values()) / PS
 
     # ---------------- e2e through the host-pointer C ABI

@@ -255,6 +255,27 @@ int aos_layer_step_dev(aos_ctx* ctx, uint32_t layer, const aos_router_ring* ring
                        const uint64_t* seq_ids, uint32_t T, uint16_t* hidden, int advance,
                        void* stream);
 
+/* ---- adapter-sharded decode (the large-pool config) -------------------------
+ * No reference counterpart: the reference keeps every adapter on one device
+ * (kernel-mtl/src/lib.rs:1897-2046).  Adapters are sharded by id: rank r
+ * loads only the adapters with id % world == r.  Per layer and input site
+ * (normed -> q/k/v, attention output -> o, normed -> gate/up, SwiGLU ->
+ * down) every rank sends its T input rows to every rank over NCCL, each rank
+ * runs the LoRA of its own adapters on all world * T rows, the bf16 deltas go
+ * back to the rows' home ranks, and each base GEMM adds them in owner order.
+ * T must be the same on every rank and world * T <= max_batch.
+ * aos_shard_get_unique_id fills AOS_SHARD_ID_BYTES bytes on one rank; the
+ * caller hands them to every rank's aos_shard_init (collective: every rank
+ * calls it). */
+#define AOS_SHARD_ID_BYTES 128
+int aos_shard_get_unique_id(void* id);
+int aos_shard_init(aos_ctx* ctx, uint32_t rank, uint32_t world, const void* id);
+/* One decode step of the home tokens, like aos_run_step_batch_dev
+ * (collective: every rank calls it once per step, with the same T). */
+int aos_run_step_sharded_dev(aos_ctx* ctx, const aos_router_ring* rings, const uint32_t* token_ids,
+                             const uint64_t* seq_ids, uint32_t T, float* logits,
+                             uint16_t* hidden_out, void* stream);
+
 /* ---- per-kernel device timing (replaces Metal counter sampling,
  * crates/adapteros-lora-kernel-prof/src/lib.rs:1-21) ------------------------
  * While enabled, steps run without CUDA graphs and every launch is bracketed
@@ -262,12 +283,13 @@ int aos_layer_step_dev(aos_ctx* ctx, uint32_t layer, const aos_router_ring* ring
  * kernel class. */
 typedef enum aos_kernel_class {
     AOS_K_GEMM = 0,    /* base projection + fused LoRA expand (tcgen05)      */
-    AOS_K_SHRINK = 1,  /* LoRA shrink H = gate * (A x) (tcgen05)             */
+    AOS_K_SHRINK = 1,  /* LoRA-only launch of an adapter owner (sharded step) */
     AOS_K_ATTN = 2,    /* paged decode attention + chunk combine             */
     AOS_K_NORM = 3,    /* RMSNorm                                            */
     AOS_K_PREP = 4,    /* routing prep (touched rank groups)                 */
     AOS_K_EMBED = 5,   /* embedding gather                                   */
     AOS_K_LM_HEAD = 6, /* lm_head GEMM (tcgen05)                             */
+    AOS_K_COMM = 7,    /* NCCL exchange of the adapter-sharded step          */
     AOS_K_NUM_CLASSES = 8
 } aos_kernel_class;
 
