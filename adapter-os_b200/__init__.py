@@ -130,6 +130,7 @@ def lib():
             "aos_run_step_batch": (C.c_int, [vp, vp, vp, vp, u32, vp, vp]),
             "aos_run_step_batch_dev": (C.c_int, [vp, vp, vp, vp, u32, vp, vp, vp]),
             "aos_layer_step_dev": (C.c_int, [vp, u32, vp, vp, u32, vp, C.c_int, vp]),
+            "aos_prefill_dev": (C.c_int, [vp, u32, vp, vp, vp, vp, vp, vp]),
             "aos_shard_get_unique_id": (C.c_int, [vp]),
             "aos_shard_init": (C.c_int, [vp, u32, u32, vp]),
             "aos_run_step_sharded_dev": (C.c_int, [vp, vp, vp, vp, u32, vp, vp, vp]),
@@ -505,6 +506,17 @@ class CudaKernels:
         sid = np.ascontiguousarray(seq_ids, np.uint64)
         self._check(self._L.aos_run_step_batch_dev(self.ctx, _p(rings), _p(token_ids), _p(sid), len(sid),
                                                   _p(logits), _p(hidden), stream))
+
+    # -- prefill ----------------------------------------------------------
+    def prefill_dev(self, seq_ids, n_tok, rings, token_ids, logits=None, stream=None):
+        """Prompt pass: sequence i takes n_tok[i] tokens from its current length
+        on (causal attention over its cache).  rings/token_ids/logits are torch
+        CUDA tensors (the concatenation over sequences; logits [n_seq, vocab]
+        for each sequence's last token, optional); seq_ids/n_tok host arrays."""
+        sid = np.ascontiguousarray(seq_ids, np.uint64)
+        nt = np.ascontiguousarray(n_tok, np.uint32)
+        self._check(self._L.aos_prefill_dev(self.ctx, len(sid), _p(sid), _p(nt), _p(rings), _p(token_ids),
+                                           _p(logits), stream))
 
     # -- adapter-sharded step ---------------------------------------------
     def shard_init(self, rank, world, unique_id: bytes):

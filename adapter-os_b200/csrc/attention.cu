@@ -360,13 +360,216 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
     *reinterpret_cast<uint2*>(out + (size_t)t * nkv * G * 128 + (size_t)(kvh * G + r) * 128 + lane * 4) = w;
 }
 
+// ---------------------------------------------------------------- prefill
+// Causal attention of a prompt over the paged cache: the prompt's own K/V rows
+// were appended by the q/k/v GEMM of this layer, so query token t (position
+// pos_t) attends to positions 0..pos_t of its sequence.  One CTA per (block of
+// up to 16 consecutive query tokens of one sequence, kv head); warp w takes
+// query head kvh * G + w with the block's tokens as its 16 MMA rows, and all
+// warps share each K/V page (TMA into a 4-deep ring).  Output bf16
+// attn[t][head * 128 + d]; every reduction runs in a fixed order.
+constexpr int kPfRing = 4;
+
+struct PrefillAttnParams {
+    CUtensorMap tm_k, tm_v;
+    const uint16_t* q;         // [T][nq*128]
+    const int* block_tables;   // [T][max_blocks] (the token's sequence)
+    const int* pos;            // [T] position of each token
+    const int2* qblk;          // [n_qblk] (first token, tokens <= 16)
+    uint16_t* out;             // [T][nq*128]
+    int n_qblk, nq, nkv, G, layer, num_blocks, max_blocks;
+    float scale_log2;
+    int* err;
+};
+
+__global__ void __launch_bounds__(512) attn_prefill_kernel(const __grid_constant__ PrefillAttnParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPfRing * kBufBytes);
+    uint64_t* empty = full + kPfRing;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // longest blocks (latest in each prompt) first
+    const int qb = p.n_qblk - 1 - (int)(blockIdx.x / p.nkv);
+    const int kvh = (int)(blockIdx.x % p.nkv);
+    const int2 d = __ldg(p.qblk + qb);
+    const int t0 = d.x, nt = d.y;
+    const int p0 = __ldg(p.pos + t0);
+    const int n_pages = (p0 + nt - 1) / 16 + 1;  // through the block's last position
+    if (threadIdx.x < kPfRing) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&full[threadIdx.x])) : "memory");
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&empty[threadIdx.x])), "r"(p.G) : "memory");
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    __syncthreads();
+    pdl_wait();
+    pdl_trigger();
+    const int* bt = p.block_tables + (size_t)t0 * p.max_blocks;
+    auto issue = [&](int pg) {
+        const int b = pg % kPfRing;
+        const uint32_t bar = smem_u32(&full[b]), dst = smem_u32(smem + b * kBufBytes);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(kBufBytes) : "memory");
+        const int row = ((p.layer * p.num_blocks + __ldg(bt + pg)) * p.nkv + kvh) * 16;
+        tma_page(&p.tm_k, dst, bar, row);
+        tma_page(&p.tm_v, dst + kPageBytes, bar, row);
+    };
+    int n_issued = 0;  // thread 0: pages issued so far
+    if (threadIdx.x == 0)
+        for (; n_issued < min(kPfRing, n_pages); ++n_issued) issue(n_issued);
+
+    const int g = lane >> 2, c2 = (lane & 3) * 2;
+    const int h = kvh * p.G + warp;
+    uint32_t qa[8][4];
+    {
+        const bool v0 = g < nt, v1 = g + 8 < nt;
+        const uint16_t* q0 = p.q + (size_t)(t0 + (v0 ? g : 0)) * p.nq * 128 + (size_t)h * 128;
+        const uint16_t* q1 = p.q + (size_t)(t0 + (v1 ? g + 8 : 0)) * p.nq * 128 + (size_t)h * 128;
+#pragma unroll
+        for (int kc = 0; kc < 8; ++kc) {
+            const int c = kc * 16 + c2;
+            qa[kc][0] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + c) : 0u;
+            qa[kc][1] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + c) : 0u;
+            qa[kc][2] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + c + 8) : 0u;
+            qa[kc][3] = v1 ? *reinterpret_cast<const uint32_t*>(q1 + c + 8) : 0u;
+        }
+    }
+    const int qpos0 = p0 + g, qpos1 = p0 + g + 8;  // causal limits of the thread's two rows
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float o[16][4];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    bool ok = true;
+    const int mat = lane >> 3, r8 = lane & 7;
+    for (int pg = 0; pg < n_pages; ++pg) {
+        const int b = pg % kPfRing;
+        const bool got = mbar_wait(smem_u32(&full[b]), (uint32_t)((pg / kPfRing) & 1), p.err);
+        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+        const uint32_t kb = smem_u32(smem + b * kBufBytes), vb = kb + kPageBytes;
+        float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int kc = 0; kc < 8; ++kc) {
+            uint32_t b00, b01, b10, b11;
+            ldsm_x4(sw_addr(kb, (mat >> 1) * 8 + r8, kc * 2 + (mat & 1)), b00, b01, b10, b11);
+            mma16816(s[0], qa[kc][0], qa[kc][1], qa[kc][2], qa[kc][3], b00, b01);
+            mma16816(s[1], qa[kc][0], qa[kc][1], qa[kc][2], qa[kc][3], b10, b11);
+        }
+        const int base_pos = pg * 16;
+        float x[2][4];
+#pragma unroll
+        for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int kp = base_pos + nb * 8 + c2 + (e & 1);
+                x[nb][e] = kp <= (e < 2 ? qpos0 : qpos1) ? s[nb][e] * p.scale_log2 : -INFINITY;
+            }
+        float mx0 = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
+        float mx1 = fmaxf(fmaxf(x[0][2], x[0][3]), fmaxf(x[1][2], x[1][3]));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float nm0 = fmaxf(m0, mx0), nm1 = fmaxf(m1, mx1);
+        // a row whose every key so far is masked keeps m = -inf: scale factors 0 / 1 without NaN
+        const float a0 = nm0 == -INFINITY ? 1.f : exp2f(m0 - nm0), a1 = nm1 == -INFINITY ? 1.f : exp2f(m1 - nm1);
+        m0 = nm0;
+        m1 = nm1;
+        float pr[2][4];
+#pragma unroll
+        for (int nb = 0; nb < 2; ++nb) {
+            pr[nb][0] = nm0 == -INFINITY ? 0.f : exp2f(x[nb][0] - nm0);
+            pr[nb][1] = nm0 == -INFINITY ? 0.f : exp2f(x[nb][1] - nm0);
+            pr[nb][2] = nm1 == -INFINITY ? 0.f : exp2f(x[nb][2] - nm1);
+            pr[nb][3] = nm1 == -INFINITY ? 0.f : exp2f(x[nb][3] - nm1);
+        }
+        l0 = l0 * a0 + (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
+        l1 = l1 * a1 + (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            o[i][0] *= a0;
+            o[i][1] *= a0;
+            o[i][2] *= a1;
+            o[i][3] *= a1;
+        }
+        const uint32_t pa0 = pack_bf16(pr[0][0], pr[0][1]), pa1 = pack_bf16(pr[0][2], pr[0][3]);
+        const uint32_t pa2 = pack_bf16(pr[1][0], pr[1][1]), pa3 = pack_bf16(pr[1][2], pr[1][3]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            uint32_t v0, v1, v2, v3;
+            ldsm_x4_t(sw_addr(vb, (mat & 1) * 8 + r8, 2 * j + (mat >> 1)), v0, v1, v2, v3);
+            mma16816(o[2 * j], pa0, pa1, pa2, pa3, v0, v1);
+            mma16816(o[2 * j + 1], pa0, pa1, pa2, pa3, v2, v3);
+        }
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[b])) : "memory");
+        // Thread 0 refills buffer b with page pg + kPfRing once every warp
+        // released it.  If that wait fails it has set the error word, and the
+        // next wait of every warp on an unfilled page fails with it, so all
+        // lanes leave the loop together.
+        if (threadIdx.x == 0 && pg + kPfRing < n_pages &&
+            mbar_wait(smem_u32(&empty[b]), (uint32_t)((pg / kPfRing) & 1), p.err)) {
+            issue(pg + kPfRing);
+            ++n_issued;
+        }
+    }
+    // Error path: thread 0 waits (bounded) for the pages it still has in flight
+    // (the last kPfRing issued; earlier ones were consumed before their refill).
+    if (!ok && threadIdx.x == 0)
+        for (int pg = max(0, n_issued - kPfRing); pg < n_issued; ++pg)
+            mbar_wait_drain(smem_u32(&full[pg % kPfRing]), (uint32_t)((pg / kPfRing) & 1));
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    if (!ok) return;
+    const float i0 = l0 > 0.f ? 1.f / l0 : 0.f, i1 = l1 > 0.f ? 1.f / l1 : 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const int col = h * 128 + i * 8 + c2;
+        if (g < nt)
+            *reinterpret_cast<uint32_t*>(p.out + (size_t)(t0 + g) * p.nq * 128 + col) = pack_bf16(o[i][0] * i0, o[i][1] * i0);
+        if (g + 8 < nt)
+            *reinterpret_cast<uint32_t*>(p.out + (size_t)(t0 + g + 8) * p.nq * 128 + col) =
+                pack_bf16(o[i][2] * i1, o[i][3] * i1);
+    }
+}
+
 }  // namespace
+
+size_t attn_prefill_smem_bytes() { return 1024 + kPfRing * kBufBytes + 2 * kPfRing * 8; }
+
+cudaError_t launch_attention_prefill(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const uint16_t* q,
+                                     const int* block_tables, const int* pos, const int2* qblk, int n_qblk, int nq,
+                                     int nkv, int layer, int num_blocks, int max_blocks, int* err, uint16_t* out,
+                                     cudaStream_t s) {
+    if (n_qblk <= 0) return cudaSuccess;
+    if (nq % nkv || nq / nkv > 16) return cudaErrorInvalidValue;
+    PrefillAttnParams p;
+    p.tm_k = tm_k;
+    p.tm_v = tm_v;
+    p.q = q;
+    p.block_tables = block_tables;
+    p.pos = pos;
+    p.qblk = qblk;
+    p.out = out;
+    p.n_qblk = n_qblk;
+    p.nq = nq;
+    p.nkv = nkv;
+    p.G = nq / nkv;
+    p.layer = layer;
+    p.num_blocks = num_blocks;
+    p.max_blocks = max_blocks;
+    p.scale_log2 = 1.4426950408889634f / sqrtf(128.0f);
+    p.err = err;
+    return launch_k(attn_prefill_kernel, dim3(n_qblk * nkv), dim3(32 * p.G), attn_prefill_smem_bytes(), s, p);
+}
 
 size_t attn_smem_bytes() { return 1024 + kWarps * 2 * kBufBytes + 64; }
 static_assert(kWarps * 16 * 128 * 4 + kWarps * 16 * 2 * 4 <= kWarps * 2 * kBufBytes, "combine scratch fits the page buffers");
 
 cudaError_t attn_configure() {
-    return cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem_bytes());
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem_bytes());
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)attn_prefill_smem_bytes());
 }
 
 int attn_max_chunks(int max_seq_len) { return ((max_seq_len + 15) / 16 + kPages - 1) / kPages; }

@@ -44,6 +44,10 @@ cudaError_t launch_pack_blocks(const uint16_t* src, int rows, int cols, long lon
 cudaError_t launch_attention(const CUtensorMap&, const CUtensorMap&, const uint16_t*, const int*, const int*, float*,
                              float*, int, int, int, int, int, int, int, int*, uint16_t*, cudaStream_t);
 int attn_max_chunks(int max_seq_len);
+cudaError_t launch_attention_prefill(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const uint16_t* q,
+                                     const int* block_tables, const int* pos, const int2* qblk, int n_qblk, int nq,
+                                     int nkv, int layer, int num_blocks, int max_blocks, int* err, uint16_t* out,
+                                     cudaStream_t s);
 cudaError_t attn_configure();
 }  // namespace aos
 
@@ -76,6 +80,7 @@ struct LayerPlan {
 struct StepPlan {
     int T = 0, T_pad = 0;
     bool sharded = false;  // adapter-sharded step: T home tokens, T * world rows at the owner
+    bool eager_done = false;  // sharded: the first step runs uncaptured (NCCL connects its peers)
     std::vector<LayerPlan> layers;
     TcParams lm_head;
     int lm_grid = 0;
@@ -161,6 +166,19 @@ struct aos_ctx {
     uint16_t* d_dsend = nullptr;       // [world * T][W]   this rank's deltas for every rank's rows
     uint16_t* d_drecv = nullptr;       // [world][T][W]    deltas for the home rows, by owner
     aos_router_ring* d_rings_all = nullptr;  // [world * T] every rank's rings (rank-major)
+
+    // Prefill (aos_prefill_dev): activations of every prompt token, grown on
+    // demand to the largest prompt batch seen.
+    struct Prefill {
+        int cap = 0;  // tokens
+        uint16_t *hidden = nullptr, *normed = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
+        uint16_t* hm[AOS_NUM_MODULES] = {};
+        float *coef = nullptr, *ucoef = nullptr;
+        aos_router_ring* rings = nullptr;
+        uint32_t* tokens = nullptr;
+        int *pos = nullptr, *block_tables = nullptr;
+        int2* qblk = nullptr;
+    } pf;
     std::map<int, std::unique_ptr<StepPlan>> plans;
 
     // metrics
@@ -655,6 +673,10 @@ int run_step_device(aos_ctx* c, int T, bool with_logits, cudaStream_t s, bool sh
         return AOS_OK;
     }
     if (!use_graphs()) return enqueue_step(c, *plan, with_logits, s);
+    if (plan->sharded && !plan->eager_done) {
+        plan->eager_done = true;
+        return enqueue_step(c, *plan, with_logits, s);
+    }
     if (!plan->graph_valid || (plan->graph_logits != (void*)(with_logits ? c->d_logits : nullptr))) {
         if (plan->graph) cudaGraphExecDestroy(plan->graph);
         plan->graph = nullptr;
@@ -757,6 +779,165 @@ int check_device_error(aos_ctx* c) {
         return c->fail(e, "a bounded device-side wait timed out or a launch limit was exceeded (the kernel returned early)");
     }
     return AOS_OK;
+}
+
+// ------------------------------------------------------------------ prefill
+int prefill_reserve(aos_ctx* c, int T) {
+    auto& b = c->pf;
+    if (T <= b.cap) return AOS_OK;
+    CTX_CUDA(c, cudaDeviceSynchronize());  // earlier prefills on any stream may still read the old buffers
+    auto f = [](void* p) {
+        if (p) cudaFree(p);
+    };
+    f(b.hidden); f(b.normed); f(b.q); f(b.attn); f(b.act); f(b.coef); f(b.ucoef);
+    f(b.rings); f(b.tokens); f(b.pos); f(b.block_tables); f(b.qblk);
+    for (int m = 0; m < AOS_NUM_MODULES; ++m) f(b.hm[m]);
+    b = aos_ctx::Prefill{};
+    const size_t Tc = (size_t)((T + kTcTok - 1) / kTcTok) * kTcTok, H = c->cfg.hidden, I = c->cfg.intermediate;
+    const size_t NA = std::max(1u, c->cfg.lora_max_adapters);
+    CTX_CUDA(c, dalloc(&b.hidden, Tc * H));
+    CTX_CUDA(c, dalloc(&b.normed, Tc * H));
+    CTX_CUDA(c, dalloc(&b.q, Tc * c->QD));
+    CTX_CUDA(c, dalloc(&b.attn, Tc * c->QD));
+    CTX_CUDA(c, dalloc(&b.act, Tc * I));
+    for (int m = 0; m < AOS_NUM_MODULES; ++m)
+        if (c->module_mask & (1u << m)) CTX_CUDA(c, dalloc(&b.hm[m], Tc * c->R));
+    CTX_CUDA(c, dalloc(&b.coef, Tc * NA));
+    CTX_CUDA(c, dalloc(&b.ucoef, Tc * (size_t)(c->R / kGroup) * 8));
+    CTX_CUDA(c, dalloc(&b.rings, Tc));
+    CTX_CUDA(c, dalloc(&b.tokens, Tc));
+    CTX_CUDA(c, dalloc(&b.pos, Tc));
+    CTX_CUDA(c, dalloc(&b.block_tables, Tc * c->max_blocks));
+    CTX_CUDA(c, dalloc(&b.qblk, Tc + 1));
+    b.cap = (int)Tc;
+    return AOS_OK;
+}
+
+// TcParams of one prefill GEMM launch of group g (shrink: the LoRA modules
+// that read the group's input; else the base projection + expand + epilogue).
+int prefill_gemm_params(aos_ctx* c, int layer, int g, int T, bool shrink, TcParams& p) {
+    const uint32_t H = c->cfg.hidden, I = c->cfg.intermediate;
+    auto& b = c->pf;
+    const int mods[4][3] = {{AOS_MOD_Q, AOS_MOD_K, AOS_MOD_V}, {AOS_MOD_O, -1, -1}, {AOS_MOD_GATE, AOS_MOD_UP, -1},
+                            {AOS_MOD_DOWN, -1, -1}};
+    const uint16_t* xs[4] = {b.normed, b.attn, b.normed, b.act};
+    const uint32_t K[4] = {H, c->QD, H, I};
+    const bool lora = (c->module_mask & (1u << mods[g][0])) != 0;
+    std::memset(&p, 0, sizeof(p));
+    p.T = T;
+    p.groups = c->d_groups;
+    p.n_groups = c->d_n_groups;
+    p.err = c->d_err;
+    p.R = c->R;
+    p.n_rgroups = c->R / kGroup;
+    p.ucoef = b.ucoef;
+    p.layer = layer;
+    p.kb = (int)(K[g] / 64);
+    p.n_sub = 1;
+    int rc = tc_encode_2d(&p.tm_x, xs[g], K[g], (uint64_t)b.cap, (uint64_t)K[g] * 2, 64, kTcTok, 128);
+    if (rc) return rc;
+    auto h_map = [&](CUtensorMap* m, int mod) {
+        return tc_encode_2d(m, b.hm[mod], (uint64_t)c->R, (uint64_t)b.cap, (uint64_t)c->R * 2, kGroup, kTcTok, 128);
+    };
+    if (shrink) {
+        for (int j = 0; j < 3; ++j) {
+            const int mod = mods[g][j];
+            if (mod < 0) continue;
+            p.a_pk[p.sh_nseg] = c->A[mod][layer];
+            p.sh_out[p.sh_nseg] = b.hm[mod];
+            ++p.sh_nseg;
+        }
+        p.mode = TC_SHRINK_HM;
+        return pf_prepare(p);
+    }
+    p.lora = lora ? 1 : 0;
+    if (g == kGroupQKV) {
+        p.mode = TC_QKV_ROPE;
+        p.n_seg = 3;
+        const uint32_t r0[3] = {0, c->QD, c->QD + c->KVD}, nr[3] = {c->QD, c->KVD, c->KVD};
+        for (int j = 0; j < 3; ++j) {
+            p.w_pk[j] = c->w_qkv[layer];
+            p.seg_wrow0[j] = (int)r0[j];
+            p.seg_tiles[j] = (int)((nr[j] + kTcBN - 1) / kTcBN);
+            p.seg_rows[j] = (int)nr[j];
+            p.seg_module[j] = mods[g][j];
+            if (lora) {
+                p.b_pk[j] = c->B[mods[g][j]][layer];
+                if ((rc = h_map(&p.tm_lh[j], mods[g][j]))) return rc;
+            }
+        }
+        p.out[0] = p.out[1] = p.out[2] = b.q;
+        p.ld_out = (int)c->QD;
+        p.rope = c->d_rope;
+        p.k_pool = c->k_pool;
+        p.v_pool = c->v_pool;
+        p.block_tables = b.block_tables;
+        p.ctx_lens = b.pos;
+        p.max_blocks = c->max_blocks;
+        p.num_blocks = (int)c->cfg.kv_num_blocks;
+        p.nkv = (int)c->cfg.n_kv_heads;
+    } else if (g == kGroupGU) {
+        p.mode = TC_SWIGLU;
+        p.n_sub = 2;
+        p.n_seg = 1;
+        p.w_pk[0] = c->w_gate[layer];
+        p.w_pk[1] = c->w_up[layer];
+        if (lora) {
+            p.b_pk[0] = c->B[AOS_MOD_GATE][layer];
+            p.b_pk[1] = c->B[AOS_MOD_UP][layer];
+            if ((rc = h_map(&p.tm_lh[0], AOS_MOD_GATE)) || (rc = h_map(&p.tm_lh[1], AOS_MOD_UP))) return rc;
+        }
+        p.seg_tiles[0] = (int)((I + kTcBN / 2 - 1) / (kTcBN / 2));
+        p.seg_rows[0] = (int)I;
+        p.seg_module[0] = AOS_MOD_GATE;
+        p.out[0] = b.act;
+        p.ld_out = (int)I;
+    } else {
+        const int mod = mods[g][0];
+        p.mode = TC_RESID_BF16;
+        p.n_seg = 1;
+        p.w_pk[0] = g == kGroupO ? c->w_o[layer] : c->w_down[layer];
+        if (lora) {
+            p.b_pk[0] = c->B[mod][layer];
+            if ((rc = h_map(&p.tm_lh[0], mod))) return rc;
+        }
+        p.seg_tiles[0] = (int)((H + kTcBN - 1) / kTcBN);
+        p.seg_rows[0] = (int)H;
+        p.seg_module[0] = mod;
+        p.resid = b.hidden;
+        p.ld_out = (int)H;
+    }
+    return pf_prepare(p);
+}
+
+// One prefill layer: per input group, the LoRA shrink launch then the base +
+// expand launch (data-parallel prefill GEMM), with causal attention between.
+int enqueue_prefill_layer(aos_ctx* c, int layer, int T, int n_qblk, cudaStream_t s) {
+    auto& b = c->pf;
+    const uint32_t H = c->cfg.hidden;
+    const int gmod[4] = {AOS_MOD_Q, AOS_MOD_O, AOS_MOD_GATE, AOS_MOD_DOWN};
+    auto gemm = [&](int g) -> int {
+        TcParams p;
+        int rc;
+        if (c->module_mask & (1u << gmod[g])) {
+            if ((rc = prefill_gemm_params(c, layer, g, T, true, p))) return c->fail(rc, "prefill shrink plan");
+            PLAUNCH(c, AOS_K_SHRINK, s, pf_launch(p, s));
+        }
+        if ((rc = prefill_gemm_params(c, layer, g, T, false, p))) return c->fail(rc, "prefill GEMM plan");
+        PLAUNCH(c, AOS_K_GEMM, s, pf_launch(p, s));
+        return AOS_OK;
+    };
+    int rc;
+    PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(b.hidden, c->attn_norm[layer], T, (int)H, c->cfg.rms_eps, b.normed, s));
+    if ((rc = gemm(kGroupQKV))) return rc;
+    PLAUNCH(c, AOS_K_ATTN, s,
+            launch_attention_prefill(c->tm_k, c->tm_v, b.q, b.block_tables, b.pos, b.qblk, n_qblk, (int)c->cfg.n_heads,
+                                     (int)c->cfg.n_kv_heads, layer, (int)c->cfg.kv_num_blocks, c->max_blocks, c->d_err,
+                                     b.attn, s));
+    if ((rc = gemm(kGroupO))) return rc;
+    PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(b.hidden, c->mlp_norm[layer], T, (int)H, c->cfg.rms_eps, b.normed, s));
+    if ((rc = gemm(kGroupGU))) return rc;
+    return gemm(kGroupD);
 }
 
 }  // namespace
@@ -937,6 +1118,9 @@ void aos_destroy(aos_ctx* c) {
         if (p) cudaFree(p);
     };
     f(c->d_xrecv); f(c->d_dsend); f(c->d_drecv); f(c->d_rings_all);
+    f(c->pf.hidden); f(c->pf.normed); f(c->pf.q); f(c->pf.attn); f(c->pf.act); f(c->pf.coef); f(c->pf.ucoef);
+    f(c->pf.rings); f(c->pf.tokens); f(c->pf.pos); f(c->pf.block_tables); f(c->pf.qblk);
+    for (int m = 0; m < AOS_NUM_MODULES; ++m) f(c->pf.hm[m]);
     f(c->embed); f(c->lm_head); f(c->final_norm);
     for (auto* p : c->attn_norm) f(p);
     for (auto* p : c->mlp_norm) f(p);
@@ -1270,6 +1454,79 @@ int aos_run_step_batch(aos_ctx* c, const aos_router_ring* rings, const uint32_t*
     cudaEventElapsedTime(&ms, c->ev0, c->ev1);
     c->m.last_step_ms = ms;
     return check_device_error(c);
+}
+
+// ------------------------------------------------------------------ prefill
+int aos_prefill_dev(aos_ctx* c, uint32_t n_seq, const uint64_t* seq_ids, const uint32_t* n_tok,
+                    const aos_router_ring* rings, const uint32_t* token_ids, float* logits, void* stream) {
+    if (!c || !seq_ids || !n_tok || !rings || !token_ids || n_seq == 0) return AOS_ERR_INVALID;
+    if (n_seq > c->cfg.max_batch) return c->fail(AOS_ERR_INVALID, "more sequences than max_batch");
+    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    // host side: positions, per-token page tables, query blocks of <= 16 tokens of one sequence
+    size_t T = 0;
+    for (uint32_t i = 0; i < n_seq; ++i) {
+        if (n_tok[i] == 0) return c->fail(AOS_ERR_INVALID, "a sequence with no prompt tokens");
+        T += n_tok[i];
+    }
+    if (T > (1u << 24)) return c->fail(AOS_ERR_INVALID, "prompt batch too large");
+    std::vector<int> pos(T), bt(T * (size_t)c->max_blocks, 0);
+    std::vector<int2> qblk;
+    std::vector<size_t> last(n_seq);
+    size_t t = 0;
+    for (uint32_t i = 0; i < n_seq; ++i) {
+        auto it = c->seqs.find(seq_ids[i]);
+        if (it == c->seqs.end()) return c->fail(AOS_ERR_NOT_FOUND, "unknown sequence id " + std::to_string(seq_ids[i]));
+        for (uint32_t u = 0; u < i; ++u)
+            if (seq_ids[u] == seq_ids[i]) return c->fail(AOS_ERR_INVALID, "a sequence appears twice in one prefill");
+        const Sequence& sq = it->second;
+        if (sq.len + n_tok[i] > sq.cap) return c->fail(AOS_ERR_NOMEM, "prompt exceeds the sequence's KV capacity");
+        for (uint32_t j = 0; j < n_tok[i]; ++j, ++t) {
+            pos[t] = (int)(sq.len + j);
+            std::copy(sq.blocks.begin(), sq.blocks.end(), bt.begin() + t * c->max_blocks);
+            if (j % 16 == 0) qblk.push_back(make_int2((int)t, (int)std::min<uint32_t>(16, n_tok[i] - j)));
+        }
+        last[i] = t - 1;
+    }
+    int rc = prefill_reserve(c, (int)T);
+    if (rc) return rc;
+    auto& b = c->pf;
+    CTX_CUDA(c, cudaMemcpyAsync(b.pos, pos.data(), T * 4, cudaMemcpyHostToDevice, s));
+    CTX_CUDA(c, cudaMemcpyAsync(b.block_tables, bt.data(), bt.size() * 4, cudaMemcpyHostToDevice, s));
+    CTX_CUDA(c, cudaMemcpyAsync(b.qblk, qblk.data(), qblk.size() * sizeof(int2), cudaMemcpyHostToDevice, s));
+    CTX_CUDA(c, cudaMemcpyAsync(b.rings, rings, T * sizeof(aos_router_ring), cudaMemcpyDeviceToDevice, s));
+    CTX_CUDA(c, cudaMemcpyAsync(b.tokens, token_ids, T * 4, cudaMemcpyDeviceToDevice, s));
+    PLAUNCH(c, AOS_K_PREP, s,
+            launch_lora_prep(b.rings, (int)T, c->d_col_off, c->d_rank, c->d_scale, (int)c->cfg.lora_max_adapters,
+                             c->R / kGroup, c->d_groups, c->d_n_groups, b.coef, c->d_col_owner, b.ucoef, s));
+    PLAUNCH(c, AOS_K_EMBED, s, launch_embed(c->embed, b.tokens, (int)T, (int)c->cfg.hidden, (int)c->cfg.vocab, b.hidden, s));
+    for (uint32_t l = 0; l < c->cfg.n_layers; ++l)
+        if ((rc = enqueue_prefill_layer(c, (int)l, (int)T, (int)qblk.size(), s))) return rc;
+    // every sequence's last token: final norm and lm_head on the decode buffers
+    const size_t H = c->cfg.hidden;
+    for (uint32_t i = 0; i < n_seq; ++i)
+        CTX_CUDA(c, cudaMemcpyAsync(c->d_hidden + i * H, b.hidden + last[i] * H, H * 2, cudaMemcpyDeviceToDevice, s));
+    if (logits) {
+        StepPlan* plan = nullptr;
+        if ((rc = get_plan(c, (int)n_seq, &plan))) return rc;
+        PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(c->d_hidden, c->final_norm, (int)n_seq, (int)H, c->cfg.rms_eps, c->d_normed, s));
+        PLAUNCH(c, AOS_K_LM_HEAD, s, tc_launch(plan->lm_head, plan->lm_grid, s));
+        if (logits != c->d_logits)
+            CTX_CUDA(c, cudaMemcpyAsync(logits, c->d_logits, (size_t)n_seq * c->cfg.vocab * 4, cudaMemcpyDeviceToDevice, s));
+    }
+    for (uint32_t i = 0; i < n_seq; ++i) c->seqs[seq_ids[i]].len += n_tok[i];
+    c->m.tokens += T;
+    if (c->prof_on) {  // instrumented: collect the launch times now
+        CTX_CUDA(c, cudaStreamSynchronize(s));
+        for (size_t i = 0; i + 1 < c->prof_used; i += 2) {
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, c->prof_ev[i], c->prof_ev[i + 1]);
+            c->prof.ms[c->prof_cls[i / 2]] += ms;
+            c->prof.launches[c->prof_cls[i / 2]] += 1;
+        }
+        c->prof_used = 0;
+    }
+    return AOS_OK;
 }
 
 // ------------------------------------------------------------------ adapter-sharded step

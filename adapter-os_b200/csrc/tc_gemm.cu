@@ -1177,6 +1177,285 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(tmem_cols));
 }
 
+// ---------------------------------------------------------------- prefill GEMM
+// Prompt-sized token counts (prefill) have enough output tiles to fill the GPU
+// without cutting K: every tile of 128 tokens (MMA M) x 256 weight rows (MMA N)
+// is one CTA iteration over the whole K -- the base K steps, then one expand
+// step per touched LoRA rank group -- so the epilogue runs straight from TMEM
+// and nothing is reduced across CTAs.  Persistent CTAs walk the tiles in
+// bands of kPfBand token tiles per weight tile, so the tiles running at the
+// same time share their weight and activation boxes in L2.
+// A shrink launch (p.n_seg == 0, p.sh_nseg > 0) has tiles of 128 tokens x four
+// touched rank groups of one LoRA module and writes the gated hm (bf16).
+constexpr int kPfBand = 16;
+
+struct PfTile {
+    int m;              // token tile
+    int seg, t;         // segment and tile within it (shrink: module and group quad)
+    bool shrink;
+};
+
+__device__ __forceinline__ void pf_tile(const TcParams& p, int n_m, int n_n, int ng, int it, PfTile& pt) {
+    const int band = it / (kPfBand * n_n), in = it % (kPfBand * n_n);
+    const int bm = min(kPfBand, n_m - band * kPfBand);
+    const int n = in / bm;
+    pt.m = band * kPfBand + in % bm;
+    if (p.n_seg == 0) {
+        const int per = cdiv(ng, kShrinkGroupsPerTile);
+        pt.shrink = true;
+        pt.seg = n / per;
+        pt.t = n % per;
+    } else {
+        int b = n, g = 0;
+        while (g < p.n_seg - 1 && b >= p.seg_tiles[g]) {
+            b -= p.seg_tiles[g];
+            ++g;
+        }
+        pt.shrink = false;
+        pt.seg = g;
+        pt.t = b;
+    }
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_constant__ TcParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int NS = p.n_stages;
+    uint8_t* stages = smem;
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + (size_t)NS * p.stage_bytes);
+    uint64_t* empty_bar = full_bar + NS;
+    uint64_t* tfull_bar = empty_bar + NS;  // [2]
+    uint64_t* tempty_bar = tfull_bar + 2;  // [2]
+    uint64_t* drain_bar = tempty_bar + 2;  // [1]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ng = (p.lora || p.sh_nseg) ? __ldg(p.n_groups) : 0;
+    const int n_m = cdiv(p.T, kTcTok);
+    int n_n = 0;
+    if (p.n_seg == 0) {
+        n_n = p.sh_nseg * cdiv(ng, kShrinkGroupsPerTile);
+    } else {
+        for (int g = 0; g < p.n_seg; ++g) n_n += p.seg_tiles[g];
+    }
+    const int n_tiles = n_m * n_n;
+    const int nge = (p.n_seg > 0 && p.lora) ? ng : 0;  // expand steps per base tile
+    const int steps = p.kb + nge;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(smem_u32(&full_bar[s]), 1);
+            mbar_init(smem_u32(&empty_bar[s]), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(smem_u32(&tfull_bar[a]), 1);
+            mbar_init(smem_u32(&tempty_bar[a]), 4);
+        }
+        mbar_init(smem_u32(drain_bar), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(512));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    constexpr uint32_t kBlkW = kBlkRows * kTcBK;
+    constexpr uint32_t kBlkA = kGroup * kTcBK;
+    constexpr uint32_t kActBox = kTcTok * 128;
+
+    if (warp == 0) {
+        // ---------------- producer
+        if (lane == 0) {
+            const uint64_t pol_w = policy_evict_last();  // weights are re-read by the other token tiles
+            const uint64_t pol_x = policy_evict_last();
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t last_phase[16];
+            uint32_t used = 0;
+            bool ok = true, waited = false;
+            for (int it = blockIdx.x; ok && it < n_tiles; it += gridDim.x) {
+                PfTile pt;
+                pf_tile(p, n_m, n_n, ng, it, pt);
+                const int nsteps = pt.shrink ? p.kb : steps;
+                for (int st = 0; st < nsteps; ++st) {
+                    if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, p.err)) { ok = false; break; }
+                    const uint32_t fb = smem_u32(&full_bar[stage]);
+                    const uint32_t sb = smem_u32(stages + (size_t)stage * p.stage_bytes);
+                    const bool ex = !pt.shrink && st >= p.kb;
+                    const int nh = (ex && p.n_sub == 2) ? 2 : 1;
+                    uint32_t bytes = (uint32_t)nh * kActBox;
+                    if (pt.shrink) {
+                        const int first = pt.t * kShrinkGroupsPerTile;
+                        bytes += (uint32_t)min(kShrinkGroupsPerTile, ng - first) * kBlkA * 2;
+                    } else if (p.n_sub == 2) {
+                        bytes += 2 * kBlkW * 2;
+                    } else {
+                        const int seg_blocks = (p.seg_rows[pt.seg] + kBlkRows - 1) / kBlkRows;
+                        bytes += (uint32_t)min(2, seg_blocks - 2 * pt.t) * kBlkW * 2;
+                    }
+                    mbar_expect_tx(fb, bytes);
+                    // weights
+                    if (pt.shrink) {
+                        const int first = pt.t * kShrinkGroupsPerTile;
+                        const int nv = min(kShrinkGroupsPerTile, ng - first);
+                        for (int q = 0; q < nv; ++q)
+                            bulk_g2s(sb + q * (kBlkA * 2),
+                                     p.a_pk[pt.seg] + ((size_t)__ldg(p.groups + first + q) * p.kb + st) * kBlkA, kBlkA * 2,
+                                     fb, pol_w);
+                    } else {
+                        const int seg_blocks = (p.seg_rows[pt.seg] + kBlkRows - 1) / kBlkRows;
+                        const int g = ex ? __ldg(p.groups + (st - p.kb)) : 0;
+                        for (int h = 0; h < 2; ++h) {
+                            const uint16_t* src;
+                            if (p.n_sub == 2) {
+                                src = !ex ? p.w_pk[pt.seg * 2 + h] +
+                                                (((size_t)(p.seg_wrow0[pt.seg] / kBlkRows + pt.t)) * p.kb + st) * kBlkW
+                                          : p.b_pk[pt.seg * 2 + h] + ((size_t)pt.t * p.n_rgroups + g) * kBlkW;
+                            } else {
+                                if (2 * pt.t + h >= seg_blocks) continue;
+                                src = !ex ? p.w_pk[pt.seg] +
+                                                (((size_t)(p.seg_wrow0[pt.seg] / kBlkRows + 2 * pt.t + h)) * p.kb + st) * kBlkW
+                                          : p.b_pk[pt.seg] + ((size_t)(2 * pt.t + h) * p.n_rgroups + g) * kBlkW;
+                            }
+                            bulk_g2s(sb + h * (kBlkW * 2), src, kBlkW * 2, fb, pol_w);
+                        }
+                    }
+                    if (!waited) {  // activations come from the previous launch
+                        pdl_wait();
+                        pdl_trigger();
+                        waited = true;
+                    }
+                    const uint32_t act = sb + p.act_off;
+                    if (!ex) {
+                        tma_2d(&p.tm_x, act, fb, st * kTcBK, pt.m * kTcTok, pol_x);
+                    } else {
+                        const int gcol = __ldg(p.groups + (st - p.kb)) * kGroup;
+                        for (int h = 0; h < nh; ++h)
+                            tma_2d(&p.tm_lh[pt.seg * p.n_sub + h], act + h * kActBox, fb, gcol, pt.m * kTcTok, pol_x);
+                    }
+                    last_phase[stage] = phase;
+                    used |= 1u << stage;
+                    if (++stage == NS) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (!waited) {
+                pdl_wait();
+                pdl_trigger();
+            }
+            for (int s = 0; s < NS; ++s)
+                if (used & (1u << s)) mbar_wait_drain(smem_u32(&full_bar[s]), last_phase[s]);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc256 = idesc_bf16(kTcBN), idesc128 = idesc_bf16(kTcBN / 2);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true, issued = false;
+            int local = 0;
+            for (int it = blockIdx.x; ok && it < n_tiles; it += gridDim.x, ++local) {
+                PfTile pt;
+                pf_tile(p, n_m, n_n, ng, it, pt);
+                const int acc = local & 1;
+                if (!mbar_wait(smem_u32(&tempty_bar[acc]), (uint32_t)(((local >> 1) & 1) ^ 1), p.err)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d0 = tmem_base + (uint32_t)(acc * kTcBN);
+                const int nsteps = pt.shrink ? p.kb : steps;
+                for (int st = 0; st < nsteps; ++st) {
+                    if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t sb = smem_u32(stages + (size_t)stage * p.stage_bytes);
+                    const uint32_t act = sb + p.act_off;
+                    const bool ex = !pt.shrink && st >= p.kb;
+                    if (ex && p.n_sub == 2) {
+                        for (int h = 0; h < 2; ++h)
+#pragma unroll
+                            for (int kk = 0; kk < kTcBK / 16; ++kk)
+                                umma_bf16(d0 + h * (kTcBN / 2), desc_sw128(act + h * kActBox + kk * 32),
+                                          desc_sw128(sb + h * (kBlkW * 2) + kk * 32), idesc128, 1u);
+                    } else {
+#pragma unroll
+                        for (int kk = 0; kk < kTcBK / 16; ++kk)
+                            umma_bf16(d0, desc_sw128(act + kk * 32), desc_sw128(sb + kk * 32), idesc256,
+                                      (st == 0 && kk == 0) ? 0u : 1u);
+                    }
+                    issued = true;
+                    umma_commit(smem_u32(&empty_bar[stage]));
+                    if (++stage == NS) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                umma_commit(smem_u32(&tfull_bar[acc]));
+            }
+            if (!ok && issued) {
+                umma_commit(smem_u32(drain_bar));
+                mbar_wait_drain(smem_u32(drain_bar), 0);
+            }
+        }
+    } else if (warp < 6) {
+        // ---------------- drain + epilogue from TMEM (warps 2-5)
+        const int q = warp & 3;
+        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+        pdl_wait();
+        int local = 0;
+        for (int it = blockIdx.x; it < n_tiles; it += gridDim.x, ++local) {
+            PfTile pt;
+            pf_tile(p, n_m, n_n, ng, it, pt);
+            const int acc = local & 1;
+            if (!mbar_wait(smem_u32(&tfull_bar[acc]), (uint32_t)((local >> 1) & 1), p.err)) break;
+            tc_fence_after();
+            const uint32_t t_acc = tmem_base + lane_off + (uint32_t)(acc * kTcBN);
+            const int tok = pt.m * kTcTok + q * 32 + lane;
+            const bool valid = tok < p.T;
+            if (pt.shrink) {
+                float cf[32];
+                const float4* src = reinterpret_cast<const float4*>(
+                    p.ucoef + ((size_t)(valid ? tok : 0) * p.n_rgroups + (size_t)pt.t * kShrinkGroupsPerTile) * 8);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float4 w = __ldg(src + j);
+                    cf[4 * j] = w.x;
+                    cf[4 * j + 1] = w.y;
+                    cf[4 * j + 2] = w.z;
+                    cf[4 * j + 3] = w.w;
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    float vA[32], vB[32];
+                    tmem_ld32(t_acc + 64 * k, vA);
+                    tmem_ld32(t_acc + 64 * k + 32, vB);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        vA[i] *= cf[8 * k + i / 8];
+                        vB[i] *= cf[8 * k + 4 + i / 8];
+                    }
+                    if (valid) apply_pairs<32>(p, TC_SHRINK_HM, pt.seg, pt.t, k, tok, 0, vA, vB, ng);
+                }
+            } else {
+#pragma unroll 1
+                for (int k = 0; k < 4; ++k) {
+                    int cA, cB;
+                    chunk_cols(p.mode, k, cA, cB);
+                    float vA[32], vB[32];
+                    tmem_ld32(t_acc + cA, vA);
+                    tmem_ld32(t_acc + cB, vB);
+                    if (valid) apply_pairs<32>(p, p.mode, pt.seg, pt.t, k, tok, 0, vA, vB, ng);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(512));
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------- host side
@@ -1305,12 +1584,37 @@ cudaError_t tc_configure() {
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, tc_gemm_kernel);
     if (e != cudaSuccess) return e;
     g_tc_max_dyn = optin - (int)fa.sharedSizeBytes;
-    return cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, g_tc_max_dyn);
+    e = cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, g_tc_max_dyn);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(pf_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, g_tc_max_dyn);
 }
 int tc_max_dynamic_smem() { return g_tc_max_dyn > 0 ? g_tc_max_dyn : 227 * 1024 - 4096; }
 
 size_t tc_acc_bytes(const TcParams& p, int n_tiles) {
     return (size_t)n_tiles * kTcBN * p.acc_T * sizeof(long long);
+}
+
+// Prefill GEMM (pf_gemm_kernel): same operand layout as the decode GEMM, any
+// T; stages of 256 weight rows x 128 B plus one 128-token activation box (two
+// for the gate/up expand).
+int pf_prepare(TcParams& p) {
+    if (p.T <= 0 || p.n_sub < 1 || p.n_sub > 2 || p.n_seg < 0 || p.n_seg > kTcMaxSets ||
+        p.n_seg * p.n_sub > kTcMaxSets || p.sh_nseg < 0 || p.sh_nseg > kTcMaxSets || p.kb < 1 ||
+        (p.n_seg == 0 && p.sh_nseg == 0))
+        return AOS_ERR_INVALID;
+    p.T_box = kTcTok;
+    p.tb = 1;
+    p.act_off = (uint32_t)kTcBN * 128;
+    p.stage_bytes = p.act_off + (uint32_t)((p.n_sub == 2 && p.lora) ? 2 : 1) * kTcTok * 128;
+    const int budget = tc_max_dynamic_smem() - 1024 - (int)kTcTailBytes;
+    p.n_stages = std::min(4, budget / (int)p.stage_bytes);
+    return p.n_stages >= 2 ? AOS_OK : AOS_ERR_INVALID;
+}
+
+cudaError_t pf_launch(const TcParams& p, cudaStream_t stream) {
+    const size_t smem = tc_smem_bytes(p);
+    if ((int)smem > tc_max_dynamic_smem()) return cudaErrorInvalidValue;
+    return launch_k(pf_gemm_kernel, dim3(tc_num_sms()), dim3(kTcThreads), smem, stream, p);
 }
 
 cudaError_t tc_launch(const TcParams& p, int grid, cudaStream_t stream) {

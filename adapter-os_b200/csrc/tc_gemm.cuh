@@ -123,6 +123,10 @@ int tc_prepare(TcParams& p, int smem_budget);
 // Launch on `grid` CTAs; every CTA must be resident at once (grid <= SM
 // count): the launch synchronises its CTAs through bounded grid barriers.
 cudaError_t tc_launch(const TcParams& p, int grid, cudaStream_t stream);
+// Prefill GEMM: data-parallel tiles of 128 tokens over the whole K (no split),
+// for any T.  n_seg == 0 with sh_nseg > 0 is a shrink launch (gated hm out).
+int pf_prepare(TcParams& p);
+cudaError_t pf_launch(const TcParams& p, cudaStream_t stream);
 // Bytes of the accumulator for n_tiles tiles (p.acc_T set).
 size_t tc_acc_bytes(const TcParams& p, int n_tiles);
 cudaError_t tc_configure();

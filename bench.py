@@ -323,6 +323,126 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ config 4
+CFG4 = dict(n_prompts=8, prompt_len=2048, n_adapters=64, rank=16, K=4)
+METRIC4 = "prefill tok/s, 8B-shape, 8 x 2048-token prompts, K=4 of 64 rank-16 LoRAs; % of bf16 tensor roofline"
+
+
+def peak_tflops():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def run_config4(args, rank, world, local):
+    """BASELINE config 4 (prefill): 8 prompts of 2048 tokens (ids uniform over
+    the vocabulary), per-token K=4 routing over 64 rank-16 adapters on all 7
+    modules, causal attention.  One step = the prompt pass of all 8 prompts
+    (aos_prefill_dev) from empty caches, logits of each prompt's last token.
+    Each GPU prefills its own 8 prompts (replicas, weak scaling)."""
+    import torch
+    aos = importlib.import_module("adapter-os_b200")
+    c, c4 = CFG, CFG4
+    S, P, NA, R = c4["n_prompts"], c4["prompt_len"], c4["n_adapters"], c4["rank"]
+    T = S * P
+    layers = args.layers
+    dev = f"cuda:{local}"
+    W, K = max(3, args.warmup), args.steps
+    gpu = aos.CudaKernels(c["hidden"], c["n_heads"], c["n_kv_heads"], c["head_dim"], c["intermediate"], c["vocab"],
+                          layers, max_batch=S, kv_num_blocks=S * ((P + 15) // 16) + 16, max_seq_len=P + 16,
+                          lora_rank_capacity=NA * R, lora_max_adapters=NA, device=local)
+    randn = load_base(gpu, aos, torch, local, layers)
+    L = gpu._L
+    for a in range(NA):
+        aos.check(L.aos_adapter_new(gpu.ctx, a, R, float(2 * R)), gpu.ctx)
+        for m, (out, inn) in enumerate(module_shapes()):
+            A = randn((layers, R, inn), 0.02)
+            Bm = randn((layers, out, R), 0.02)
+            for l in range(layers):
+                aos.check(L.aos_adapter_set_module(gpu.ctx, a, l, m, A[l].data_ptr(), Bm[l].data_ptr(), 1), gpu.ctx)
+    torch.cuda.synchronize()
+    sids = np.arange(S, dtype=np.uint64)
+    for i in range(S):
+        gpu.kv_alloc(int(sids[i]), P + 16)
+    n_tok = np.full(S, P, np.uint32)
+    stream_ptr = gpu.stream()
+    stream = torch.cuda.ExternalStream(stream_ptr)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED + 4)
+    priors = torch.randn((T, NA), generator=gen, device=dev, dtype=torch.float32)
+    tokens = torch.randint(0, c["vocab"], (T,), generator=gen, device=dev, dtype=torch.int32)
+    rings = torch.zeros((T, 40), dtype=torch.uint8, device=dev)
+    nsids = torch.arange(NA, device=dev, dtype=torch.int64)
+    logits = torch.empty((S, c["vocab"]), dtype=torch.float32, device=dev)
+
+    def step():
+        for i in range(S):
+            gpu.kv_set_len(int(sids[i]), 0)
+        aos.route_batch_dev(priors, nsids, rings, k=c4["K"], tau=1.0, eps=0.02, stream=stream_ptr)
+        gpu.prefill_dev(sids, n_tok, rings, tokens, logits=logits, stream=stream_ptr)
+
+    for _ in range(W):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(K):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1) / K
+    gpu.health_check()
+    gpu.profile_enable(True)
+    gpu.profile_read(reset=True)
+    step()
+    torch.cuda.synchronize()
+    prof = gpu.profile_read(reset=True)
+    gpu.profile_enable(False)
+    H, I, V = c["hidden"], c["intermediate"], c["vocab"]
+    QD, KVD = c["n_heads"] * 128, c["n_kv_heads"] * 128
+    per_layer = (QD + 2 * KVD) * H + H * QD + 2 * I * H + H * I
+    gemm_flop = 2.0 * T * per_layer * layers
+    io = sum(o + i_ for o, i_ in module_shapes())
+    lora_flop = 2.0 * T * io * c4["K"] * R * layers  # the K selected adapters of each token (algorithmic)
+    lora_exec_flop = 2.0 * T * io * NA * R * layers  # what the dense-over-touched-groups LoRA launches execute
+    attn_flop = 4.0 * S * (P * (P + 1) / 2) * QD * layers  # QK^T and PV over the causal triangle
+    lm_flop = 2.0 * S * H * V
+    flop = gemm_flop + lora_flop + attn_flop + lm_flop
+    peak, kind = peak_tflops()
+    gemm_ms = prof["ms"]["gemm"] + prof["ms"]["owner_lora"]
+    gemm_tf = (gemm_flop + lora_flop) / (gemm_ms / 1000.0) / 1e12
+    attn_tf = attn_flop / (prof["ms"]["attention"] / 1000.0) / 1e12
+    if rank == 0:
+        tf = flop / (ms / 1000.0) / 1e12
+        line = {
+            "metric": METRIC4, "value": T * world / (ms / 1000.0), "unit": "tok/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config 4: 32-layer 8B-shape prefill, 8 prompts x 2048 tokens (ids uniform), "
+                                   "K=4 of 64 rank-16 LoRAs on 7 modules, causal attention",
+                       "layers": layers, "tokens_per_step": T, "parallelism": f"dp{world} (replicas)"},
+            "roofline": {"bound": "tensor", "kernel": "whole prefill", "achieved": tf, "peak": peak,
+                         "unit": "TFLOP/s", "frac": tf / peak, "peak_kind": kind, "flop_per_step": flop},
+            "roofline_gemm": {"bound": "tensor", "kernel": "pf_gemm_kernel (base + LoRA shrink/expand)",
+                              "achieved": gemm_tf, "peak": peak, "unit": "TFLOP/s", "frac": gemm_tf / peak,
+                              "ms_per_step": gemm_ms},
+            "roofline_attention": {"bound": "tensor", "kernel": "attn_prefill_kernel (mma.sync)",
+                                   "achieved": attn_tf, "peak": peak, "unit": "TFLOP/s", "frac": attn_tf / peak,
+                                   "ms_per_step": prof["ms"]["attention"]},
+            "lora_flop_executed_per_step": lora_exec_flop,
+            "kernel_ms_per_step": prof["ms"],
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    gpu.close()
+
+
 # ------------------------------------------------------------------ config 5
 CFG5 = dict(n_adapters=1024, rank=16, K=8, batch=256, ctx_lo=512, ctx_hi=1024, zipf_s=1.1)
 METRIC5 = "decode tok/s, 8B-shape, K=8 of 1024 rank-16 LoRAs sharded by adapter id, batch 256"
@@ -508,8 +628,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=CFG["n_layers"], help="debug only: fewer layers is not a valid number")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", type=int, default=3, choices=[3, 5],
-                    help="3: the headline decode workload; 5: the adapter-sharded large pool")
+    ap.add_argument("--config", type=int, default=3, choices=[3, 4, 5],
+                    help="3: the headline decode workload; 4: prefill; 5: the adapter-sharded large pool")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -531,8 +651,11 @@ def main():
 
         dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
         dist = dist_mod
-    if args.config == 5:
-        run_config5(args, rank, world, local, dist)
+    if args.config in (4, 5):
+        if args.config == 4:
+            run_config4(args, rank, world, local)
+        else:
+            run_config5(args, rank, world, local, dist)
         if dist:
             dist.barrier()
             dist.destroy_process_group()

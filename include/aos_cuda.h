@@ -255,6 +255,18 @@ int aos_layer_step_dev(aos_ctx* ctx, uint32_t layer, const aos_router_ring* ring
                        const uint64_t* seq_ids, uint32_t T, uint16_t* hidden, int advance,
                        void* stream);
 
+/* ---- prefill (the prompt path) ---------------------------------------------
+ * InferencePipeline's prompt pass (inference_pipeline.rs:983-1154, MLX
+ * forward over the prompt, mlx_cpp_wrapper_real.cpp:3338-3559 with T > 1):
+ * sequence i contributes n_tok[i] tokens at positions len_i, len_i + 1, ...
+ * (its current length onward) with causal attention over its cache.
+ * rings / token_ids: device arrays, the concatenation over the sequences (one
+ * RouterRing per token).  logits: device [n_seq][vocab] f32 of each
+ * sequence's last prompt token, or NULL.  Each sequence advances by n_tok[i];
+ * n_seq <= max_batch. */
+int aos_prefill_dev(aos_ctx* ctx, uint32_t n_seq, const uint64_t* seq_ids, const uint32_t* n_tok,
+                    const aos_router_ring* rings, const uint32_t* token_ids, float* logits, void* stream);
+
 /* ---- adapter-sharded decode (the large-pool config) -------------------------
  * No reference counterpart: the reference keeps every adapter on one device
  * (kernel-mtl/src/lib.rs:1897-2046).  Adapters are sharded by id: rank r

@@ -60,7 +60,7 @@ def _rank_main(rank, port, out_dir):
     m, ad, kv = cs["m"], cs["ad"], cs["kv"]
     home = slice(rank * T_HOME, (rank + 1) * T_HOME)
     mb = cs["bt"].shape[1]
-    gpu = aos.CudaKernels(m.hidden, m.n_heads, m.n_kv_heads, 128, m.intermediate, m.vocab, m.n_layers,
+    gpu = aos.CudaKernels(m.hidden, m.n_heads, m.n_kv_heads, 128, m.inter, m.vocab, m.n_layers,
                           max_batch=WORLD * T_HOME, kv_num_blocks=T_HOME * mb + 8, max_seq_len=cs["max_seq"],
                           lora_rank_capacity=cs["n_ad"] * 16, lora_max_adapters=cs["n_ad"], device=rank)
     gpu.load_host_model(m)
