@@ -793,7 +793,8 @@ int prefill_reserve(aos_ctx* c, int T) {
     f(b.rings); f(b.tokens); f(b.pos); f(b.block_tables); f(b.qblk);
     for (int m = 0; m < AOS_NUM_MODULES; ++m) f(b.hm[m]);
     b = aos_ctx::Prefill{};
-    const size_t Tc = (size_t)((T + kTcTok - 1) / kTcTok) * kTcTok, H = c->cfg.hidden, I = c->cfg.intermediate;
+    // whole 256-token tiles of the prefill GEMM
+    const size_t Tc = (size_t)((T + 255) / 256) * 256, H = c->cfg.hidden, I = c->cfg.intermediate;
     const size_t NA = std::max(1u, c->cfg.lora_max_adapters);
     CTX_CUDA(c, dalloc(&b.hidden, Tc * H));
     CTX_CUDA(c, dalloc(&b.normed, Tc * H));

@@ -665,25 +665,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     // (thread index `ti`): an item is (tile, pair chunk k, token, 8-column
     // group g); its thread reads 8 pairs of one token from the fixed-point
     // accumulator, zeroes them for the next launch and applies the epilogue.
-    // Two items per thread are loaded before either is used.
+    // kConvItems items per thread are loaded before any is used (the pass is
+    // bound by L2 round trips, not bandwidth).
+    constexpr int kConvItems = 2;
     auto convert = [&](int lo, int hi, int nthr, int ti) {
         // item = (tile, pair chunk k, 8-column group g, token), token fastest
-        const long long n_items = (long long)(hi - lo) * 16 * p.T;
-        const long long stride = (long long)gridDim.x * nthr;
-        for (long long base = (long long)blockIdx.x * nthr + ti; base < n_items; base += 2 * stride) {
-            unsigned long long w[2][2][8];
-            bool live[2];
-            int tile_[2], k_[2], tok_[2], g_[2];
+        const int n_items = (hi - lo) * 16 * p.T;
+        const int stride = (int)gridDim.x * nthr;
+        for (int base = (int)blockIdx.x * nthr + ti; base < n_items; base += kConvItems * stride) {
+            unsigned long long w[kConvItems][2][8];
+            bool live[kConvItems];
+            int tile_[kConvItems], k_[kConvItems], tok_[kConvItems], g_[kConvItems];
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const long long item = base + e * stride;
+            for (int e = 0; e < kConvItems; ++e) {
+                const int item = base + e * stride;
                 live[e] = item < n_items;
                 if (!live[e]) continue;
-                tok_[e] = (int)(item % p.T);
-                const long long r = item / p.T;
-                g_[e] = (int)(r % 4);
-                k_[e] = (int)((r / 4) % 4);
-                tile_[e] = lo + (int)(r / 16);
+                tok_[e] = item % p.T;
+                const int r = item / p.T;
+                g_[e] = r % 4;
+                k_[e] = (r / 4) % 4;
+                tile_[e] = lo + r / 16;
                 live[e] = tile_npieces(sc, tile_[e]) > 1;  // else finished straight from TMEM
                 if (!live[e]) continue;
                 const int mode = tile_[e] < sc.n_sh ? TC_SHRINK_HM : p.mode;
@@ -700,7 +702,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 }
             }
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
+            for (int e = 0; e < kConvItems; ++e) {
                 if (!live[e]) continue;
                 Piece pc;
                 tile_info(p, sc, tile_[e], pc);
@@ -952,7 +954,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         auto join_shrink = [&]() {  // the drain warps' share (threads 0..127 of 192)
             if (*go_shrink == 1) {
                 __threadfence();
+                if (tr && tid == 0) tr[208] = gtimer();
                 convert(0, sc.n_sh, 192, tid);
+                if (tr && tid == 0) tr[209] = gtimer();
             }
             signal(sh_conv_bar);
             sh_joined = true;
@@ -1143,7 +1147,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             if (cid == 0) *go_shrink = ok ? 1 : -1;  // the drain warps take two thirds
             if (ok) {
                 convert(0, sc.n_sh, 192, 128 + cid);
+                if (tr && cid == 0) tr[206] = gtimer();
                 if (cid == 0) ok = mbar_wait(smem_u32(sh_conv_bar), 0, p.err);
+                if (tr && cid == 0) tr[207] = gtimer();
                 cv_bar();
                 release(1);
             }
@@ -1179,18 +1185,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
 
 // ---------------------------------------------------------------- prefill GEMM
 // Prompt-sized token counts (prefill) have enough output tiles to fill the GPU
-// without cutting K: every tile of 128 tokens (MMA M) x 256 weight rows (MMA N)
-// is one CTA iteration over the whole K -- the base K steps, then one expand
-// step per touched LoRA rank group -- so the epilogue runs straight from TMEM
-// and nothing is reduced across CTAs.  Persistent CTAs walk the tiles in
-// bands of kPfBand token tiles per weight tile, so the tiles running at the
-// same time share their weight and activation boxes in L2.
-// A shrink launch (p.n_seg == 0, p.sh_nseg > 0) has tiles of 128 tokens x four
-// touched rank groups of one LoRA module and writes the gated hm (bf16).
-constexpr int kPfBand = 16;
+// without cutting K: every tile of 256 tokens (two MMA M blocks of 128) x 256
+// weight rows (MMA N) is one CTA iteration over the whole K -- the base K
+// steps, then the LoRA expand steps of every touched rank group -- so the
+// epilogue runs straight from TMEM and nothing is reduced across CTAs.  Two
+// token blocks share each weight box: a step is 32 KB of weights plus 32 KB of
+// activations for eight MMAs, which halves the L2 bytes per MMA of a
+// 128-token tile.  The 256 x 256 fp32 accumulator takes all 512 TMEM columns,
+// so the MMA waits while a tile drains (a few percent of a tile's time).
+// Persistent CTAs walk the tiles in bands of kPfBand token tiles per weight
+// tile, so the tiles running at the same time share boxes in L2.
+// Gate/up expand steps come in halves (gate rows, then up rows, N = 128 each),
+// so every stage has the same size.  A shrink launch (p.n_seg == 0,
+// p.sh_nseg > 0) has tiles of 256 tokens x four touched rank groups of one
+// LoRA module and writes the gated hm (bf16).
+constexpr int kPfBand = 8;
+constexpr int kPfTok = 2 * kTcTok;  // tokens per tile
 
 struct PfTile {
-    int m;              // token tile
+    int m;              // token tile (256 tokens)
     int seg, t;         // segment and tile within it (shrink: module and group quad)
     bool shrink;
 };
@@ -1224,13 +1237,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
     uint8_t* stages = smem;
     uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + (size_t)NS * p.stage_bytes);
     uint64_t* empty_bar = full_bar + NS;
-    uint64_t* tfull_bar = empty_bar + NS;  // [2]
-    uint64_t* tempty_bar = tfull_bar + 2;  // [2]
-    uint64_t* drain_bar = tempty_bar + 2;  // [1]
+    uint64_t* tfull_bar = empty_bar + NS;  // [1]
+    uint64_t* tempty_bar = tfull_bar + 1;  // [1]
+    uint64_t* drain_bar = tempty_bar + 1;  // [1]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ng = (p.lora || p.sh_nseg) ? __ldg(p.n_groups) : 0;
-    const int n_m = cdiv(p.T, kTcTok);
+    const int n_m = cdiv(p.T, kPfTok);
     int n_n = 0;
     if (p.n_seg == 0) {
         n_n = p.sh_nseg * cdiv(ng, kShrinkGroupsPerTile);
@@ -1238,7 +1251,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
         for (int g = 0; g < p.n_seg; ++g) n_n += p.seg_tiles[g];
     }
     const int n_tiles = n_m * n_n;
-    const int nge = (p.n_seg > 0 && p.lora) ? ng : 0;  // expand steps per base tile
+    const int ex_per_group = p.n_sub == 2 ? 2 : 1;  // gate/up: gate half, then up half
+    const int nge = (p.n_seg > 0 && p.lora) ? ng * ex_per_group : 0;
     const int steps = p.kb + nge;
 
     if (threadIdx.x == 0) {
@@ -1246,10 +1260,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
             mbar_init(smem_u32(&full_bar[s]), 1);
             mbar_init(smem_u32(&empty_bar[s]), 1);
         }
-        for (int a = 0; a < 2; ++a) {
-            mbar_init(smem_u32(&tfull_bar[a]), 1);
-            mbar_init(smem_u32(&tempty_bar[a]), 4);
-        }
+        mbar_init(smem_u32(tfull_bar), 1);
+        mbar_init(smem_u32(tempty_bar), 4);
         mbar_init(smem_u32(drain_bar), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -1281,24 +1293,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
                 PfTile pt;
                 pf_tile(p, n_m, n_n, ng, it, pt);
                 const int nsteps = pt.shrink ? p.kb : steps;
+                const int seg_blocks = pt.shrink ? 0 : (p.seg_rows[pt.seg] + kBlkRows - 1) / kBlkRows;
                 for (int st = 0; st < nsteps; ++st) {
                     if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1u, p.err)) { ok = false; break; }
                     const uint32_t fb = smem_u32(&full_bar[stage]);
                     const uint32_t sb = smem_u32(stages + (size_t)stage * p.stage_bytes);
                     const bool ex = !pt.shrink && st >= p.kb;
-                    const int nh = (ex && p.n_sub == 2) ? 2 : 1;
-                    uint32_t bytes = (uint32_t)nh * kActBox;
+                    const int e = st - p.kb;
+                    const int gi = ex ? e / ex_per_group : 0;  // touched-group list index
+                    const int hh = (ex && p.n_sub == 2) ? e % 2 : -1;  // gate/up expand half
+                    uint32_t bytes = 2 * kActBox;
                     if (pt.shrink) {
                         const int first = pt.t * kShrinkGroupsPerTile;
                         bytes += (uint32_t)min(kShrinkGroupsPerTile, ng - first) * kBlkA * 2;
+                    } else if (hh >= 0) {
+                        bytes += kBlkW * 2;
                     } else if (p.n_sub == 2) {
                         bytes += 2 * kBlkW * 2;
                     } else {
-                        const int seg_blocks = (p.seg_rows[pt.seg] + kBlkRows - 1) / kBlkRows;
                         bytes += (uint32_t)min(2, seg_blocks - 2 * pt.t) * kBlkW * 2;
                     }
                     mbar_expect_tx(fb, bytes);
-                    // weights
                     if (pt.shrink) {
                         const int first = pt.t * kShrinkGroupsPerTile;
                         const int nv = min(kShrinkGroupsPerTile, ng - first);
@@ -1306,15 +1321,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
                             bulk_g2s(sb + q * (kBlkA * 2),
                                      p.a_pk[pt.seg] + ((size_t)__ldg(p.groups + first + q) * p.kb + st) * kBlkA, kBlkA * 2,
                                      fb, pol_w);
+                    } else if (hh >= 0) {  // one 128-row block of lora_B (gate or up)
+                        const int g = __ldg(p.groups + gi);
+                        bulk_g2s(sb, p.b_pk[pt.seg * 2 + hh] + ((size_t)pt.t * p.n_rgroups + g) * kBlkW, kBlkW * 2, fb,
+                                 pol_w);
                     } else {
-                        const int seg_blocks = (p.seg_rows[pt.seg] + kBlkRows - 1) / kBlkRows;
-                        const int g = ex ? __ldg(p.groups + (st - p.kb)) : 0;
+                        const int g = ex ? __ldg(p.groups + gi) : 0;
                         for (int h = 0; h < 2; ++h) {
                             const uint16_t* src;
                             if (p.n_sub == 2) {
-                                src = !ex ? p.w_pk[pt.seg * 2 + h] +
-                                                (((size_t)(p.seg_wrow0[pt.seg] / kBlkRows + pt.t)) * p.kb + st) * kBlkW
-                                          : p.b_pk[pt.seg * 2 + h] + ((size_t)pt.t * p.n_rgroups + g) * kBlkW;
+                                src = p.w_pk[pt.seg * 2 + h] +
+                                      (((size_t)(p.seg_wrow0[pt.seg] / kBlkRows + pt.t)) * p.kb + st) * kBlkW;
                             } else {
                                 if (2 * pt.t + h >= seg_blocks) continue;
                                 src = !ex ? p.w_pk[pt.seg] +
@@ -1330,12 +1347,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
                         waited = true;
                     }
                     const uint32_t act = sb + p.act_off;
-                    if (!ex) {
-                        tma_2d(&p.tm_x, act, fb, st * kTcBK, pt.m * kTcTok, pol_x);
-                    } else {
-                        const int gcol = __ldg(p.groups + (st - p.kb)) * kGroup;
-                        for (int h = 0; h < nh; ++h)
-                            tma_2d(&p.tm_lh[pt.seg * p.n_sub + h], act + h * kActBox, fb, gcol, pt.m * kTcTok, pol_x);
+                    for (int b = 0; b < 2; ++b) {
+                        if (!ex) {
+                            tma_2d(&p.tm_x, act + b * kActBox, fb, st * kTcBK, pt.m * kPfTok + b * kTcTok, pol_x);
+                        } else {
+                            const int gcol = __ldg(p.groups + gi) * kGroup;
+                            const int map = pt.seg * p.n_sub + (hh >= 0 ? hh : 0);
+                            tma_2d(&p.tm_lh[map], act + b * kActBox, fb, gcol, pt.m * kPfTok + b * kTcTok, pol_x);
+                        }
                     }
                     last_phase[stage] = phase;
                     used |= 1u << stage;
@@ -1360,10 +1379,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
             for (int it = blockIdx.x; ok && it < n_tiles; it += gridDim.x, ++local) {
                 PfTile pt;
                 pf_tile(p, n_m, n_n, ng, it, pt);
-                const int acc = local & 1;
-                if (!mbar_wait(smem_u32(&tempty_bar[acc]), (uint32_t)(((local >> 1) & 1) ^ 1), p.err)) { ok = false; break; }
+                if (!mbar_wait(smem_u32(tempty_bar), (uint32_t)((local & 1) ^ 1), p.err)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t d0 = tmem_base + (uint32_t)(acc * kTcBN);
                 const int nsteps = pt.shrink ? p.kb : steps;
                 for (int st = 0; st < nsteps; ++st) {
                     if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.err)) { ok = false; break; }
@@ -1371,24 +1388,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
                     const uint32_t sb = smem_u32(stages + (size_t)stage * p.stage_bytes);
                     const uint32_t act = sb + p.act_off;
                     const bool ex = !pt.shrink && st >= p.kb;
-                    if (ex && p.n_sub == 2) {
-                        for (int h = 0; h < 2; ++h)
+                    const int hh = (ex && p.n_sub == 2) ? (st - p.kb) % 2 : -1;
+                    for (int b = 0; b < 2; ++b) {
+                        const uint32_t a0 = act + b * kActBox, d = tmem_base + (uint32_t)(b * kTcBN);
+                        if (hh >= 0) {
 #pragma unroll
                             for (int kk = 0; kk < kTcBK / 16; ++kk)
-                                umma_bf16(d0 + h * (kTcBN / 2), desc_sw128(act + h * kActBox + kk * 32),
-                                          desc_sw128(sb + h * (kBlkW * 2) + kk * 32), idesc128, 1u);
-                    } else {
+                                umma_bf16(d + hh * (kTcBN / 2), desc_sw128(a0 + kk * 32), desc_sw128(sb + kk * 32), idesc128,
+                                          1u);
+                        } else {
 #pragma unroll
-                        for (int kk = 0; kk < kTcBK / 16; ++kk)
-                            umma_bf16(d0, desc_sw128(act + kk * 32), desc_sw128(sb + kk * 32), idesc256,
-                                      (st == 0 && kk == 0) ? 0u : 1u);
+                            for (int kk = 0; kk < kTcBK / 16; ++kk)
+                                umma_bf16(d, desc_sw128(a0 + kk * 32), desc_sw128(sb + kk * 32), idesc256,
+                                          (st == 0 && kk == 0) ? 0u : 1u);
+                        }
                     }
                     issued = true;
                     umma_commit(smem_u32(&empty_bar[stage]));
                     if (++stage == NS) { stage = 0; phase ^= 1u; }
                 }
                 if (!ok) break;
-                umma_commit(smem_u32(&tfull_bar[acc]));
+                umma_commit(smem_u32(tfull_bar));
             }
             if (!ok && issued) {
                 umma_commit(smem_u32(drain_bar));
@@ -1404,50 +1424,51 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
         for (int it = blockIdx.x; it < n_tiles; it += gridDim.x, ++local) {
             PfTile pt;
             pf_tile(p, n_m, n_n, ng, it, pt);
-            const int acc = local & 1;
-            if (!mbar_wait(smem_u32(&tfull_bar[acc]), (uint32_t)((local >> 1) & 1), p.err)) break;
+            if (!mbar_wait(smem_u32(tfull_bar), (uint32_t)(local & 1), p.err)) break;
             tc_fence_after();
-            const uint32_t t_acc = tmem_base + lane_off + (uint32_t)(acc * kTcBN);
-            const int tok = pt.m * kTcTok + q * 32 + lane;
-            const bool valid = tok < p.T;
-            if (pt.shrink) {
-                float cf[32];
-                const float4* src = reinterpret_cast<const float4*>(
-                    p.ucoef + ((size_t)(valid ? tok : 0) * p.n_rgroups + (size_t)pt.t * kShrinkGroupsPerTile) * 8);
+            for (int b = 0; b < 2; ++b) {
+                const uint32_t t_acc = tmem_base + lane_off + (uint32_t)(b * kTcBN);
+                const int tok = pt.m * kPfTok + b * kTcTok + q * 32 + lane;
+                const bool valid = tok < p.T;
+                if (pt.shrink) {
+                    float cf[32];
+                    const float4* src = reinterpret_cast<const float4*>(
+                        p.ucoef + ((size_t)(valid ? tok : 0) * p.n_rgroups + (size_t)pt.t * kShrinkGroupsPerTile) * 8);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float4 w = __ldg(src + j);
-                    cf[4 * j] = w.x;
-                    cf[4 * j + 1] = w.y;
-                    cf[4 * j + 2] = w.z;
-                    cf[4 * j + 3] = w.w;
-                }
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    float vA[32], vB[32];
-                    tmem_ld32(t_acc + 64 * k, vA);
-                    tmem_ld32(t_acc + 64 * k + 32, vB);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        vA[i] *= cf[8 * k + i / 8];
-                        vB[i] *= cf[8 * k + 4 + i / 8];
+                    for (int j = 0; j < 8; ++j) {
+                        const float4 w = __ldg(src + j);
+                        cf[4 * j] = w.x;
+                        cf[4 * j + 1] = w.y;
+                        cf[4 * j + 2] = w.z;
+                        cf[4 * j + 3] = w.w;
                     }
-                    if (valid) apply_pairs<32>(p, TC_SHRINK_HM, pt.seg, pt.t, k, tok, 0, vA, vB, ng);
-                }
-            } else {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        float vA[32], vB[32];
+                        tmem_ld32(t_acc + 64 * k, vA);
+                        tmem_ld32(t_acc + 64 * k + 32, vB);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            vA[i] *= cf[8 * k + i / 8];
+                            vB[i] *= cf[8 * k + 4 + i / 8];
+                        }
+                        if (valid) apply_pairs<32>(p, TC_SHRINK_HM, pt.seg, pt.t, k, tok, 0, vA, vB, ng);
+                    }
+                } else {
 #pragma unroll 1
-                for (int k = 0; k < 4; ++k) {
-                    int cA, cB;
-                    chunk_cols(p.mode, k, cA, cB);
-                    float vA[32], vB[32];
-                    tmem_ld32(t_acc + cA, vA);
-                    tmem_ld32(t_acc + cB, vB);
-                    if (valid) apply_pairs<32>(p, p.mode, pt.seg, pt.t, k, tok, 0, vA, vB, ng);
+                    for (int k = 0; k < 4; ++k) {
+                        int cA, cB;
+                        chunk_cols(p.mode, k, cA, cB);
+                        float vA[32], vB[32];
+                        tmem_ld32(t_acc + cA, vA);
+                        tmem_ld32(t_acc + cB, vB);
+                        if (valid) apply_pairs<32>(p, p.mode, pt.seg, pt.t, k, tok, 0, vA, vB, ng);
+                    }
                 }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&tempty_bar[acc]));
+            if (lane == 0) mbar_arrive(smem_u32(tempty_bar));
         }
     }
     tc_fence_before();
@@ -1595,17 +1616,16 @@ size_t tc_acc_bytes(const TcParams& p, int n_tiles) {
 }
 
 // Prefill GEMM (pf_gemm_kernel): same operand layout as the decode GEMM, any
-// T; stages of 256 weight rows x 128 B plus one 128-token activation box (two
-// for the gate/up expand).
+// T; stages of 256 weight rows x 128 B plus two 128-token activation boxes.
 int pf_prepare(TcParams& p) {
     if (p.T <= 0 || p.n_sub < 1 || p.n_sub > 2 || p.n_seg < 0 || p.n_seg > kTcMaxSets ||
         p.n_seg * p.n_sub > kTcMaxSets || p.sh_nseg < 0 || p.sh_nseg > kTcMaxSets || p.kb < 1 ||
         (p.n_seg == 0 && p.sh_nseg == 0))
         return AOS_ERR_INVALID;
     p.T_box = kTcTok;
-    p.tb = 1;
+    p.tb = 2;
     p.act_off = (uint32_t)kTcBN * 128;
-    p.stage_bytes = p.act_off + (uint32_t)((p.n_sub == 2 && p.lora) ? 2 : 1) * kTcTok * 128;
+    p.stage_bytes = p.act_off + 2u * kTcTok * 128;  // 32 KB weights + two 128-token boxes
     const int budget = tc_max_dynamic_smem() - 1024 - (int)kTcTailBytes;
     p.n_stages = std::min(4, budget / (int)p.stage_bytes);
     return p.n_stages >= 2 ? AOS_OK : AOS_ERR_INVALID;

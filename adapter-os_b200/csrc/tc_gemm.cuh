@@ -104,7 +104,9 @@ constexpr int kMaxPiecesPerPool = 30;  // a slice is at least 1/30 of a tile
 // [160,192) drain piece ends, 192 kernel start, 193 kernel end, 194-199 grid
 // barrier events (arrive/complete of the three barriers), 200/201 final
 // reduction start/end, 202/203 producer wait for the shrink output, 204
-// producer's last shrink step issued, 205 MMA's last shrink step consumed.
+// producer's last shrink step issued, 205 MMA's last shrink step consumed,
+// 206/207 converter's shrink share done / drain share done, 208/209 drain's
+// shrink share start / end.
 constexpr int kTraceStride = 256;
 
 // Host helpers (tc_gemm.cu).
