@@ -454,13 +454,20 @@ __global__ void __launch_bounds__(512) attn_prefill_kernel(const __grid_constant
         }
         const int base_pos = pg * 16;
         float x[2][4];
+        if (base_pos + 15 <= p0) {  // every key of the page precedes every query of the block
 #pragma unroll
-        for (int nb = 0; nb < 2; ++nb)
+            for (int nb = 0; nb < 2; ++nb)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int kp = base_pos + nb * 8 + c2 + (e & 1);
-                x[nb][e] = kp <= (e < 2 ? qpos0 : qpos1) ? s[nb][e] * p.scale_log2 : -INFINITY;
-            }
+                for (int e = 0; e < 4; ++e) x[nb][e] = s[nb][e] * p.scale_log2;
+        } else {  // the diagonal page(s): causal mask
+#pragma unroll
+            for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int kp = base_pos + nb * 8 + c2 + (e & 1);
+                    x[nb][e] = kp <= (e < 2 ? qpos0 : qpos1) ? s[nb][e] * p.scale_log2 : -INFINITY;
+                }
+        }
         float mx0 = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
         float mx1 = fmaxf(fmaxf(x[0][2], x[0][3]), fmaxf(x[1][2], x[1][3]));
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
@@ -482,12 +489,15 @@ __global__ void __launch_bounds__(512) attn_prefill_kernel(const __grid_constant
         }
         l0 = l0 * a0 + (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
         l1 = l1 * a1 + (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
+        // rescale only when some row's running max moved (rare after the first pages)
+        if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            o[i][0] *= a0;
-            o[i][1] *= a0;
-            o[i][2] *= a1;
-            o[i][3] *= a1;
+            for (int i = 0; i < 16; ++i) {
+                o[i][0] *= a0;
+                o[i][1] *= a0;
+                o[i][2] *= a1;
+                o[i][3] *= a1;
+            }
         }
         const uint32_t pa0 = pack_bf16(pr[0][0], pr[0][1]), pa1 = pack_bf16(pr[0][2], pr[0][3]);
         const uint32_t pa2 = pack_bf16(pr[1][0], pr[1][1]), pa3 = pack_bf16(pr[1][2], pr[1][3]);

@@ -329,7 +329,10 @@ __device__ __forceinline__ void apply_pairs(const TcParams& p, int mode, int seg
 #pragma unroll
             for (int i = 0; i < N; ++i) {
                 const float g = vA[i], up = vB[i];
-                const float sg = 1.0f / (1.0f + expf(-g));  // gate * sigmoid(gate) * up
+                // gate * sigmoid(gate) * up with the hardware exp2 and a fast
+                // reciprocal: a few ulp of fp32 (the output is bf16); a very
+                // negative gate gives exp -> inf and sigmoid -> 0 exactly
+                const float sg = __fdividef(1.0f, 1.0f + __expf(-g));
                 s[i] = (g * sg) * up;
             }
             uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]) + (size_t)t * p.ld_out + f0;
@@ -416,7 +419,7 @@ struct Sched {
     int sh_per_seg;    // shrink tiles per shrink segment
     int n_sh, n_base;  // shrink tiles, base tiles
     int kbe, nge;      // K steps and expand steps per base tile in this launch
-    long long P[2];    // pool lengths: shrink K steps, base positions
+    int P[2];          // pool lengths: shrink K steps, base positions (< 2^31 / SMs)
     int G[2];          // CTAs that take part in each pool
     int len[2];        // steps (positions) per tile
 };
@@ -440,22 +443,23 @@ __device__ __forceinline__ Sched make_sched(const TcParams& p) {
     s.nge = (p.lora && (p.pools & 4)) ? s.ng : 0;
     s.len[0] = s.kb;
     s.len[1] = s.kbe + s.nge;
-    s.P[0] = (long long)s.n_sh * s.kb;
-    s.P[1] = (long long)s.n_base * s.len[1];
+    s.P[0] = s.n_sh * s.kb;
+    s.P[1] = s.n_base * s.len[1];
     // Every slice is at least len/kMaxPiecesPerPool steps long, so no tile is
     // cut into more than kMaxPiecesPerPool + 1 pieces.
     for (int q = 0; q < 2; ++q) {
-        const long long l = max(1, cdiv(max(s.len[q], 1), kMaxPiecesPerPool));
-        s.G[q] = s.P[q] > 0 ? (int)max(1ll, min((long long)gridDim.x, s.P[q] / l)) : 0;
+        const int l = max(1, cdiv(max(s.len[q], 1), kMaxPiecesPerPool));
+        s.G[q] = s.P[q] > 0 ? max(1, min((int)gridDim.x, s.P[q] / l)) : 0;
     }
     return s;
 }
-__device__ __forceinline__ long long pstart(int c, long long P, int G) { return (long long)c * P / G; }
+// Pool lengths times the grid stay below 2^31 (the host checks the plan).
+__device__ __forceinline__ int pstart(int c, int P, int G) { return c * P / G; }
 // CTA whose slice of a pool (length P, G CTAs) contains step s.
-__device__ __forceinline__ int cta_of(long long s, long long P, int G) { return (int)(((s + 1) * G - 1) / P); }
+__device__ __forceinline__ int cta_of(int s, int P, int G) { return ((s + 1) * G - 1) / P; }
 // K steps among the first `pos` positions of a base tile.
 __device__ __forceinline__ int bpos(const Sched& sc, int pos) {
-    return sc.len[1] ? (int)((long long)pos * sc.kbe / sc.len[1]) : 0;
+    return sc.len[1] ? pos * sc.kbe / sc.len[1] : 0;
 }
 
 __device__ __forceinline__ void tile_info(const TcParams& p, const Sched& sc, int tile, Piece& pc) {
@@ -480,7 +484,7 @@ __device__ __forceinline__ int tile_npieces(const Sched& sc, int tile) {
     const int q = tile < sc.n_sh ? 0 : 1;
     const int local = q ? tile - sc.n_sh : tile;
     if (sc.P[q] <= 0) return 0;
-    const long long a = (long long)local * sc.len[q];
+    const int a = local * sc.len[q];
     return cta_of(a + sc.len[q] - 1, sc.P[q], sc.G[q]) - cta_of(a, sc.P[q], sc.G[q]) + 1;
 }
 
@@ -510,12 +514,12 @@ __device__ bool build_work(const Sched& sc, int acc_stages, WorkTable& w) {
     int np = 0;
     for (int q = 0; q < 2; ++q) {
         if (c >= sc.G[q]) continue;
-        long long s = pstart(c, sc.P[q], sc.G[q]);
-        const long long e = pstart(c + 1, sc.P[q], sc.G[q]);
+        int s = pstart(c, sc.P[q], sc.G[q]);
+        const int e = pstart(c + 1, sc.P[q], sc.G[q]);
         const int L = sc.len[q];
         while (s < e) {
-            const int local = (int)(s / L);
-            const long long ts = (long long)local * L, te = min(ts + L, e);
+            const int local = s / L;
+            const int ts = local * L, te = min(ts + L, e);
             if (np == kMaxPieces) return false;
             PieceRec& r = w.pc[np++];
             const int p0 = (int)(s - ts), p1 = (int)(te - ts);
@@ -652,6 +656,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     const uint32_t tmem_base = *tmem_slot;
     unsigned long long* tr = p.trace ? p.trace + (size_t)blockIdx.x * kTraceStride : nullptr;
     if (tr && threadIdx.x == 0) {
+        tr[210] = tr[211] = tr[212] = tr[213] = 0;
         tr[192] = gtimer();
         uint32_t smid;
         asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
@@ -669,13 +674,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     // bound by L2 round trips, not bandwidth).
     constexpr int kConvItems = 2;
     auto convert = [&](int lo, int hi, int nthr, int ti) {
-        // item = (tile, pair chunk k, 8-column group g, token), token fastest
+        // item = (tile, pair chunk k, 8-column group g, token), token fastest.
+        // Three phases per batch of items, so that no store waits on a load of
+        // the same batch: every load is issued first (the accumulator words
+        // and, for shrink tiles, the group id), then the epilogues run, then
+        // the words are zeroed for the next launch.
         const int n_items = (hi - lo) * 16 * p.T;
         const int stride = (int)gridDim.x * nthr;
+        const bool tt = tr && ti == 128 && lo + hi > sc.n_sh;  // trace the converter's final pass
+        if (tt) tr[210] = gtimer();
+        bool first_it = true;
         for (int base = (int)blockIdx.x * nthr + ti; base < n_items; base += kConvItems * stride) {
             unsigned long long w[kConvItems][2][8];
+            unsigned long long* src[kConvItems][2];
             bool live[kConvItems];
-            int tile_[kConvItems], k_[kConvItems], tok_[kConvItems], g_[kConvItems];
+            int tile_[kConvItems], k_[kConvItems], tok_[kConvItems], g_[kConvItems], gid[kConvItems];
 #pragma unroll
             for (int e = 0; e < kConvItems; ++e) {
                 const int item = base + e * stride;
@@ -688,33 +701,60 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 tile_[e] = lo + r / 16;
                 live[e] = tile_npieces(sc, tile_[e]) > 1;  // else finished straight from TMEM
                 if (!live[e]) continue;
-                const int mode = tile_[e] < sc.n_sh ? TC_SHRINK_HM : p.mode;
+                const bool shrink = tile_[e] < sc.n_sh;
+                const int mode = shrink ? TC_SHRINK_HM : p.mode;
                 int cA, cB;
                 chunk_cols(mode, k_[e], cA, cB);
+                gid[e] = -1;
+                if (shrink) {  // the touched group this chunk belongs to
+                    const int slot = (tile_[e] % sc.sh_per_seg) * kShrinkGroupsPerTile + k_[e];
+                    if (slot < sc.ng) gid[e] = __ldg(p.groups + slot);
+                }
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    unsigned long long* src = reinterpret_cast<unsigned long long*>(p.acc) +
-                                              ((size_t)tile_[e] * kTcBN + (h ? cB : cA) + 8 * g_[e]) * p.acc_T + tok_[e];
+                    src[e][h] = reinterpret_cast<unsigned long long*>(p.acc) +
+                                ((size_t)tile_[e] * kTcBN + (h ? cB : cA) + 8 * g_[e]) * p.acc_T + tok_[e];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) w[e][h][j] = __ldcg(src + (size_t)j * p.acc_T);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) __stcg(src + (size_t)j * p.acc_T, 0ull);
+                    for (int j = 0; j < 8; ++j) w[e][h][j] = __ldcg(src[e][h] + (size_t)j * p.acc_T);
                 }
             }
+            if (tt && first_it) tr[211] = gtimer();
 #pragma unroll
             for (int e = 0; e < kConvItems; ++e) {
                 if (!live[e]) continue;
-                Piece pc;
-                tile_info(p, sc, tile_[e], pc);
-                const int mode = pc.shrink ? TC_SHRINK_HM : p.mode;
+                if (tt && first_it && e == 0) {
+                    volatile unsigned long long sink = w[e][0][0];
+                    (void)sink;
+                    tr[212] = gtimer();
+                }
                 float a[8], b[8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     a[j] = __ll2float_rn((long long)w[e][0][j]) * kFixInv;
                     b[j] = __ll2float_rn((long long)w[e][1][j]) * kFixInv;
                 }
-                apply_pairs<8>(p, mode, pc.seg, pc.t, k_[e], tok_[e], 8 * g_[e], a, b, sc.ng);
+                if (tile_[e] < sc.n_sh) {  // gated hm of shrink segment tile / per-segment tiles
+                    if (gid[e] >= 0) {
+                        const int seg = tile_[e] / sc.sh_per_seg;
+                        shrink_run<8>(p, seg, tok_[e], gid[e] * kGroup, 8 * g_[e], a);
+                        shrink_run<8>(p, seg, tok_[e], gid[e] * kGroup, 32 + 8 * g_[e], b);
+                    }
+                } else {
+                    Piece pc;
+                    tile_info(p, sc, tile_[e], pc);
+                    apply_pairs<8>(p, p.mode, pc.seg, pc.t, k_[e], tok_[e], 8 * g_[e], a, b, sc.ng);
+                }
             }
+#pragma unroll
+            for (int e = 0; e < kConvItems; ++e) {
+                if (!live[e]) continue;
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) __stcg(src[e][h] + (size_t)j * p.acc_T, 0ull);
+            }
+            if (tt && first_it) tr[213] = gtimer();
+            first_it = false;
         }
     };
     volatile int* go_final = flag + 1;  // converter -> drain: 1 = every CTA's pieces are in, -1 = failed
@@ -1068,6 +1108,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                         }
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
+                            // A shrink column whose adapter this token did not
+                            // select is gated to exactly zero: adding it would
+                            // change nothing, and skipping it keeps the L2
+                            // atomic traffic to the token's own adapters.
+                            if (pc.shrink && cf[4 * c + i / 8] == 0.f) continue;
                             const long long x = __float2ll_rn(v[i] * kFix);
                             asm volatile("red.global.add.u64 [%0], %1;" ::"l"(dst + (size_t)(c * 32 + i) * p.acc_T),
                                          "l"((unsigned long long)x)
@@ -1557,6 +1602,11 @@ int tc_prepare(TcParams& p, int smem_budget) {
     if (p.T <= 0 || p.T > 256 || p.n_sub < 1 || p.n_sub > 2 || p.n_seg < 1 || p.n_seg > kTcMaxSets ||
         p.n_seg * p.n_sub > kTcMaxSets || p.sh_nseg < 0 || p.sh_nseg > kTcMaxSets || p.kb < 1)
         return AOS_ERR_INVALID;
+    {  // the device schedule computes pool positions x grid in 32 bits
+        long long tiles = p.sh_nseg * ((long long)p.n_rgroups / kShrinkGroupsPerTile + 1);
+        for (int g = 0; g < p.n_seg; ++g) tiles += p.seg_tiles[g];
+        if (tiles * (p.kb + (long long)p.n_rgroups + 1) * tc_num_sms() >= (1ll << 31)) return AOS_ERR_INVALID;
+    }
     p.T_pad = tc_t_pad(p.T);
     p.T_box = tc_t_box(p.T);
     p.tb = (p.T_pad + kTcTok - 1) / kTcTok;
