@@ -150,6 +150,7 @@ struct aos_ctx {
     size_t stage_bytes = 0;
     long long* d_acc = nullptr;   // GEMM fixed-point accumulators of split tiles (kept zero)
     size_t acc_bytes = 0;
+    float* d_part = nullptr;      // GEMM fp32 partials of split base tiles (steps with T > 128)
     int* d_sync = nullptr;        // [4] GEMM grid-barrier counters
     int* d_err = nullptr;
     unsigned long long* d_trace = nullptr;  // AOS_TC_TRACE diagnostics
@@ -252,6 +253,7 @@ int build_owner_plan(aos_ctx* c, int layer, int g, int T, TcParams& p) {
     p.n_groups = c->d_n_groups;
     p.acc = c->d_acc;
     p.acc_T = c->T_cap;
+    p.part = T > kTcTok ? c->d_part : nullptr;
     p.sync = c->d_sync;
     p.err = c->d_err;
     p.R = c->R;
@@ -312,6 +314,7 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp, bool sharded =
         p.n_groups = c->d_n_groups;
         p.acc = c->d_acc;
         p.acc_T = c->T_cap;
+        p.part = T > kTcTok ? c->d_part : nullptr;
         p.sync = c->d_sync;
         p.err = c->d_err;
         p.R = c->R;
@@ -479,6 +482,7 @@ int get_plan(aos_ctx* c, int T, StepPlan** out, bool sharded = false) {
     p.err = c->d_err;
     p.acc = c->d_acc;
     p.acc_T = c->T_cap;
+    p.part = T > kTcTok ? c->d_part : nullptr;
     p.sync = c->d_sync;
     const uint32_t V = c->cfg.vocab;
     p.w_pk[0] = c->lm_head;
@@ -1074,6 +1078,8 @@ aos_ctx* aos_init(const aos_model_config* cfg) {
         const size_t tiles = max_launch_tiles(c.get());
         c->acc_bytes = tiles * kTcBN * (size_t)c->T_cap * sizeof(long long);
         INIT_CHECK(dalloc(&c->d_acc, c->acc_bytes / sizeof(long long)), "GEMM accumulators");
+        if (c->T_cap > kTcTok)  // one slot per (CTA, base tile) pair that can hold a piece
+            INIT_CHECK(dalloc(&c->d_part, (tc_num_sms() + tiles) * kTcBN * (size_t)c->T_cap), "GEMM partials");
         INIT_CHECK(dalloc(&c->d_sync, 4), "sync");
     }
     INIT_CHECK(dalloc(&c->d_err, 1), "err");
@@ -1140,7 +1146,7 @@ void aos_destroy(aos_ctx* c) {
     f(c->d_hidden); f(c->d_normed); f(c->d_q); f(c->d_attn); f(c->d_act);
     f(c->d_groups); f(c->d_n_groups); f(c->d_block_tables); f(c->d_ctx_lens);
     f(c->d_rings); f(c->d_tokens); f(c->d_logits); f(c->d_rope);
-    f(c->d_attn_part); f(c->d_attn_ml); f(c->d_stage); f(c->d_acc); f(c->d_sync); f(c->d_err); f(c->d_trace);
+    f(c->d_attn_part); f(c->d_attn_ml); f(c->d_stage); f(c->d_acc); f(c->d_part); f(c->d_sync); f(c->d_err); f(c->d_trace);
     for (int i = 0; i < aos_ctx::kStageSlots; ++i) {
         if (c->h_stage[i]) cudaFreeHost(c->h_stage[i]);
         if (c->stage_ev[i]) cudaEventDestroy(c->stage_ev[i]);

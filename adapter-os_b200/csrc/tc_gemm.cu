@@ -597,6 +597,9 @@ __device__ __noinline__ bool spin_ge(const int* ptr, int target, int* err) {
 }
 
 // ---------------------------------------------------------------- the kernel
+// kPart: split base tiles go through fp32 partials (p.part, T > 128); the
+// instance without it keeps the partials code out of the T <= 128 kernel.
+template <bool kPart>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-align the dynamic region (SWIZZLE_128B atoms).
@@ -684,6 +687,50 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         const bool tt = tr && ti == 128 && lo + hi > sc.n_sh;  // trace the converter's final pass
         if (tt) tr[210] = gtimer();
         bool first_it = true;
+        if (kPart && lo >= sc.n_sh) {
+            // base tiles from fp32 partials: sum the pieces in CTA order, two
+            // pieces' words in flight at a time
+            for (int item = (int)blockIdx.x * nthr + ti; item < n_items; item += stride) {
+                const int tok = item % p.T;
+                const int r = item / p.T;
+                const int g = r % 4, k = (r / 4) % 4, tile = lo + r / 16;
+                const int local = tile - sc.n_sh;
+                const int s0 = local * sc.len[1];
+                const int c0 = cta_of(s0, sc.P[1], sc.G[1]), c1 = cta_of(s0 + sc.len[1] - 1, sc.P[1], sc.G[1]);
+                if (c1 == c0) continue;  // finished straight from TMEM
+                int cA, cB;
+                chunk_cols(p.mode, k, cA, cB);
+                float a[8], b[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) a[j] = b[j] = 0.f;
+                for (int c = c0; c <= c1; c += 2) {
+                    float x[2][2][8];
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        if (c + e > c1) continue;
+                        const float* src = p.part + (size_t)(c + e + local) * kTcBN * p.acc_T + tok;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            x[e][0][j] = __ldcg(src + (size_t)(cA + 8 * g + j) * p.acc_T);
+                            x[e][1][j] = __ldcg(src + (size_t)(cB + 8 * g + j) * p.acc_T);
+                        }
+                    }
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        if (c + e > c1) continue;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            a[j] += x[e][0][j];
+                            b[j] += x[e][1][j];
+                        }
+                    }
+                }
+                Piece pc;
+                tile_info(p, sc, tile, pc);
+                apply_pairs<8>(p, p.mode, pc.seg, pc.t, k, tok, 8 * g, a, b, sc.ng);
+            }
+            return;
+        }
         for (int base = (int)blockIdx.x * nthr + ti; base < n_items; base += kConvItems * stride) {
             unsigned long long w[kConvItems][2][8];
             unsigned long long* src[kConvItems][2];
@@ -1091,7 +1138,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 // is order-independent, so the sum is exact and the same on every
                 // run); shrink pieces are gated first.  Layout [tile][column][token]:
                 // one red instruction adds a column for 32 consecutive tokens.
-                for (int b = 0; b < p.tb; ++b) {
+                const bool to_part = kPart && !pc.shrink;
+                for (int b = 0; b < p.tb && to_part; ++b) {  // fp32 partials, plain stores
+                    const int tok = token_of(b);
+                    const bool valid = tok >= 0 && tok < p.T;
+                    float* dst = p.part + (size_t)(blockIdx.x + pc.tile - sc.n_sh) * kTcBN * p.acc_T + (valid ? tok : 0);
+#pragma unroll
+                    for (int c = 0; c < kTcBN / 32; ++c) {
+                        float v[32];
+                        tmem_ld32(t_acc + b * kTcBN + c * 32, v);
+                        if (!valid) continue;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) __stcg(dst + (size_t)(c * 32 + i) * p.acc_T, v[i]);
+                    }
+                }
+                for (int b = 0; b < p.tb && !to_part; ++b) {
                     const int tok = token_of(b);
                     if (b > 0 && pc.shrink) gate_coefs(pc.t, tok < 0 ? 0 : tok, cf);
                     const bool valid = tok >= 0 && tok < p.T;
@@ -1143,7 +1204,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 if (clock64() - t0 > 2 * kSpinLimitCycles) break;  // the converter's own waits are bounded
             if (go == 1) {
                 __threadfence();
-                convert(handoff ? sc.n_sh : 0, sc.n_sh + sc.n_base, 192, tid);
+                if (!handoff) convert(0, sc.n_sh, 192, tid);  // else converted at the hand-off
+                convert(sc.n_sh, sc.n_sh + sc.n_base, 192, tid);
             }
         }
     } else {
@@ -1203,7 +1265,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         if (cid == 0) *go_final = ok ? 1 : -1;  // the drain warps join the final conversion
         if (ok) {
             if (tr && cid == 0) tr[200] = gtimer();
-            convert(handoff ? sc.n_sh : 0, sc.n_sh + sc.n_base, 192, 128 + cid);  // handoff: shrink done above
+            if (!handoff) convert(0, sc.n_sh, 192, 128 + cid);  // else converted at the hand-off
+            convert(sc.n_sh, sc.n_sh + sc.n_base, 192, 128 + cid);
             if (tr && cid == 0) tr[201] = gtimer();
         }
     }
@@ -1652,10 +1715,12 @@ cudaError_t tc_configure() {
     cudaFuncAttributes fa{};
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, tc_gemm_kernel);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, tc_gemm_kernel<false>);
     if (e != cudaSuccess) return e;
     g_tc_max_dyn = optin - (int)fa.sharedSizeBytes;
-    e = cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, g_tc_max_dyn);
+    e = cudaFuncSetAttribute(tc_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, g_tc_max_dyn);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(tc_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, g_tc_max_dyn);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(pf_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, g_tc_max_dyn);
 }
@@ -1690,7 +1755,8 @@ cudaError_t pf_launch(const TcParams& p, cudaStream_t stream) {
 cudaError_t tc_launch(const TcParams& p, int grid, cudaStream_t stream) {
     const size_t smem = tc_smem_bytes(p);
     if ((int)smem > tc_max_dynamic_smem()) return cudaErrorInvalidValue;
-    return launch_k(tc_gemm_kernel, dim3(grid), dim3(kTcThreads), smem, stream, p);
+    if (p.part) return launch_k(tc_gemm_kernel<true>, dim3(grid), dim3(kTcThreads), smem, stream, p);
+    return launch_k(tc_gemm_kernel<false>, dim3(grid), dim3(kTcThreads), smem, stream, p);
 }
 
 }  // namespace aos

@@ -114,6 +114,24 @@ def test_decode_step_small(with_lora):
     s2.gpu.close()
 
 
+def test_decode_step_two_token_blocks():
+    """T > 128: two MMA token blocks per tile, one TMEM accumulator, split base
+    tiles summed from fp32 partials."""
+    rng = np.random.default_rng(9)
+    ctx = tuple(int(x) for x in rng.integers(0, 90, size=160))
+    outs = []
+    for _ in range(2):
+        s = Setup(seed=4, ctx_lens=ctx, max_seq=128)
+        logits, hidden = s.gpu.run_step_batch(s.rings, s.tokens.astype(np.uint32), s.seq_ids, want_hidden=True)
+        outs.append((logits.tobytes(), hidden.tobytes()))
+        if len(outs) == 1:
+            ref_logits, ref_hidden = O.decode_step(s.m, s.ad, s.rings, s.tokens, s.kv)
+            assert_close(O.bf16_bits_to_f32(hidden), O.bf16_bits_to_f32(ref_hidden), "hidden (T=160)")
+            assert_close(logits, ref_logits, "logits (T=160)")
+        s.gpu.close()
+    assert outs[0] == outs[1], "T=160 step differs run to run"
+
+
 def test_decode_bit_identical_run_to_run():
     outs = []
     for _ in range(2):
