@@ -153,6 +153,30 @@ class CudaKernels final : public FusedKernels {
                       ctx_);
     }
 
+    // Prompt pass on device buffers (aos_prefill_dev): sequence i takes
+    // n_tok[i] tokens from its current length on; rings / tokens are device
+    // arrays concatenated over the sequences, logits device [n_seq][vocab].
+    AosError prefill_dev(const std::vector<uint64_t>& seqs, const std::vector<uint32_t>& n_tok,
+                         const aos_router_ring* rings_dev, const uint32_t* tokens_dev, float* logits_dev,
+                         void* stream = nullptr) {
+        if (seqs.size() != n_tok.size()) return AosError{AOS_ERR_INVALID, "seqs and n_tok differ in length"};
+        return status(aos_prefill_dev(ctx_, (uint32_t)seqs.size(), seqs.data(), n_tok.data(), rings_dev, tokens_dev,
+                                      logits_dev, stream),
+                      ctx_);
+    }
+
+    // Adapter-sharded decode: join the group once (collective), then every
+    // rank calls run_step_sharded_dev with the same number of home tokens.
+    AosError shard_init(uint32_t rank, uint32_t world, const void* unique_id) {
+        return status(aos_shard_init(ctx_, rank, world, unique_id), ctx_);
+    }
+    AosError run_step_sharded_dev(const aos_router_ring* rings_dev, const uint32_t* tokens_dev,
+                                  const std::vector<uint64_t>& seqs, float* logits_dev, void* stream = nullptr) {
+        return status(aos_run_step_sharded_dev(ctx_, rings_dev, tokens_dev, seqs.data(), (uint32_t)seqs.size(),
+                                               logits_dev, nullptr, stream),
+                      ctx_);
+    }
+
     // FusedKernels::run_step: decode io.input_ids in order at io.position for
     // the io.session_id sequence; logits of the last token; position advances
     // by input_ids.size() (mlx-ffi/src/backend.rs:1212-1310).
