@@ -19,6 +19,7 @@ cudaError_t launch_lora_op_f32(const float* x, int T, int in_dim, int out_dim, c
                                const float* A, const float* B, int n_adapters, int rank,
                                const float* alpha, const aos_router_ring* rings, float* y,
                                float* h_scratch, cudaStream_t stream);
+size_t lora_op_scratch_floats(int T, int out_dim, int rank);
 int lora_op_max_rank();
 
 namespace {
@@ -216,7 +217,8 @@ int aos_lora_op_f32_dev(const float* x, uint32_t T, uint32_t in_dim, uint32_t ou
     if (T == 0) return AOS_OK;
     cudaStream_t s = (cudaStream_t)stream;
     float* h = nullptr;
-    AOS_RETURN_IF_CUDA(cudaMallocAsync((void**)&h, (size_t)T * AOS_MAX_K * rank * 4, s), set_global_error);
+    AOS_RETURN_IF_CUDA(cudaMallocAsync((void**)&h, lora_op_scratch_floats((int)T, (int)out_dim, (int)rank) * 4, s),
+                       set_global_error);
     cudaError_t e = launch_lora_op_f32(x, (int)T, (int)in_dim, (int)out_dim, W, A, B, (int)n_adapters,
                                        (int)rank, alpha, rings, y, h, s);
     cudaFreeAsync(h, s);

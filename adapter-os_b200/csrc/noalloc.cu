@@ -34,7 +34,7 @@
 #include "common.cuh"
 
 namespace aos {
-cudaError_t launch_lora_op_f32(const float* x, int T, int in_dim, int out_dim, const float* W, const float* A,
+cudaError_t launch_lora_op_f32_small(const float* x, int T, int in_dim, int out_dim, const float* W, const float* A,
                                const float* B, int n_adapters, int rank, const float* alpha,
                                const aos_router_ring* rings, float* y, float* h_scratch, cudaStream_t stream);
 int lora_op_max_rank();
@@ -96,7 +96,7 @@ extern "C" int aos_lora_op_f32_noalloc_dev(const float* x, uint32_t T, uint32_t 
     if (T == 0) return AOS_OK;
     float* h = nullptr;
     if ((rc = scratch_address(&h))) return rc;
-    cudaError_t e = aos::launch_lora_op_f32(x, (int)T, (int)in_dim, (int)out_dim, W, A, B, (int)n_adapters, (int)rank,
+    cudaError_t e = aos::launch_lora_op_f32_small(x, (int)T, (int)in_dim, (int)out_dim, W, A, B, (int)n_adapters, (int)rank,
                                             alpha, rings, y, h, (cudaStream_t)stream);
     if (e != cudaSuccess) {
         aos::set_global_error(std::string("aos_lora_op_f32_noalloc_dev launch: ") + cudaGetErrorString(e));

@@ -323,6 +323,206 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ configs 1 and 2
+def _flush_l2(torch, dev, buf=[]):
+    """Write a buffer larger than L2 (126 MB) so the next launch reads from HBM."""
+    if not buf:
+        buf.append(torch.empty(64 << 20, dtype=torch.float32, device=dev))  # 256 MB
+    buf[0].fill_(1.0)
+
+
+def run_config1(args, rank, world, local):
+    """router + fp32 LoRA op.  64 tokens, hidden 2048 fp32
+    x ~ N(0,1); W 2048x2048, N=8 adapters of rank 16 (A, B ~ N(0, 0.02));
+    gate logits N(0,1), K=2, tau 1, eps 0.02; no alpha/rank scale (alpha = r).
+    One step = aos_route_batch_dev + aos_lora_op_f32_dev.  The operands fit in
+    L2, so L2 is flushed before every timed step (outside the events)."""
+    import torch
+    aos = importlib.import_module("adapter-os_b200")
+    from oracle import oracle as O
+    T, H, N, R, K = 64, 2048, 8, 16, 2
+    dev = f"cuda:{local}"
+    rng = np.random.default_rng(SEED + 1)
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    W = (rng.standard_normal((H, H)) * 0.02).astype(np.float32)
+    A = (rng.standard_normal((N, R, H)) * 0.02).astype(np.float32)
+    B = (rng.standard_normal((N, H, R)) * 0.02).astype(np.float32)
+    pri = rng.standard_normal((T, N)).astype(np.float32)
+    dx, dW, dA, dB, dp = (torch.from_numpy(a).to(dev) for a in (x, W, A, B, pri))
+    sids = torch.arange(N, device=dev, dtype=torch.int64)
+    rings = torch.zeros((T, 40), dtype=torch.uint8, device=dev)
+    y = torch.empty((T, H), dtype=torch.float32, device=dev)
+
+    def step(stream=None):
+        aos.route_batch_dev(dp, sids, rings, k=K, tau=1.0, eps=0.02, stream=stream)
+        aos.lora_op_f32_dev(dx, dW, dA, dB, rings, y, stream=stream)
+
+    W_, K_ = max(3, args.warmup), args.steps
+    for _ in range(W_):
+        step()
+    torch.cuda.synchronize()
+    # The op is a few tens of microseconds: replay it from a CUDA graph so the
+    # timed region holds the device work, not the Python call overhead.
+    side = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        step(side.cuda_stream)  # warm the stream-ordered allocator on this stream
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=side):
+            step(side.cuda_stream)
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(K_):
+        _flush_l2(torch, dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        total += e0.elapsed_time(e1)
+    ms = total / K_
+    # the same op through the Python/C-ABI calls, host overhead included
+    t0 = time.perf_counter()
+    for _ in range(K_):
+        step()
+    torch.cuda.synchronize()
+    call_ms = (time.perf_counter() - t0) * 1000.0 / K_
+    rn = rings.cpu().numpy().view(aos.RING_DTYPE).reshape(T)
+    sel = {int(r["indices"][j]) for r in rn for j in range(int(r["top_k"])) if r["gates_q15"][j] > 0}
+    nbytes = W.nbytes + len(sel) * (A[0].nbytes + B[0].nbytes) + x.nbytes + T * H * 4 + pri.nbytes + T * 40
+    peak, kind = peaks()
+    gbs = nbytes / (ms / 1000.0) / 1e9
+    # CPU: the oracle's router + fp32 op on the same inputs, 1 thread and all threads
+    cpu = {}
+    for th in (1, os.cpu_count() or 1):
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 3.0:
+            rg, _, _, _ = O.route_batch(pri, None, k=K, n_threads=th)
+            O.lora_op_f32(x, W, A, B, rg, None, n_threads=th)
+            reps += 1
+        cpu[th] = (time.perf_counter() - t0) / reps
+    if rank == 0:
+        line = {"metric": "config 1: router + fp32 LoRA op, 64 tokens x 2048, N=8 r=16, K=2 (tokens/s)",
+                "value": T / (ms / 1000.0), "unit": "tok/s", "n_gpus": 1, "steps": K_, "warmup": W_,
+                "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic",
+                "config": {"workload": "config 1", "l2": "flushed before every timed step",
+                           "timing": "CUDA-graph replay of route + op between CUDA events"},
+                "host_call_ms_per_step": call_ms,
+                "roofline": {"bound": "hbm", "kernel": "route + lora_shrink_f32 + lora_base_f32 + lora_expand_f32",
+                             "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak, "peak_kind": kind,
+                             "bytes_per_step": nbytes},
+                "cpu_baseline": {"value": T / cpu[1], "unit": "tok/s", "cores": 1, "kind": "port",
+                                 "sample": "the whole op (oracle router + fp32 op)",
+                                 "all_cores": {"value": T / cpu[os.cpu_count() or 1], "cores": os.cpu_count()}}}
+        print(json.dumps(line), flush=True)
+
+
+def run_config2(args, rank, world, local):
+    """one decoder layer, bf16, hidden 3584, 28/4 heads,
+    intermediate 18944; 32 rank-16 adapters on q/k/v/o, K=4; decode batch 32
+    with 2048 cached positions each.  One step = router + aos_layer_step_dev
+    (RMSNorm, q/k/v + LoRA + RoPE + KV append, attention, o + LoRA, RMSNorm,
+    gate/up + SwiGLU, down).  466 MB of layer weights exceed L2."""
+    import torch
+    aos = importlib.import_module("adapter-os_b200")
+    from oracle import oracle as O
+    H, nh, nkv, I, T, ctx, NA, R, K = 3584, 28, 4, 18944, 32, 2048, 32, 16, 4
+    dev = f"cuda:{local}"
+    rng = np.random.default_rng(SEED + 2)
+    W_, K_ = max(3, args.warmup), args.steps
+    mb = (ctx + W_ + K_ + 32 + 15) // 16
+    gpu = aos.CudaKernels(H, nh, nkv, 128, I, 256, 1, max_batch=T, kv_num_blocks=T * mb + 8, max_seq_len=mb * 16,
+                          lora_rank_capacity=NA * R, lora_max_adapters=NA,
+                          lora_modules=["q_proj", "k_proj", "v_proj", "o_proj"], device=local)
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED + 2)
+
+    def randn(shape, std):
+        return (torch.randn(shape, generator=g, device=dev, dtype=torch.float32) * std).to(torch.bfloat16)
+
+    QD, KVD = nh * 128, nkv * 128
+    shapes = [(QD, H), (KVD, H), (KVD, H), (H, QD), (I, H), (I, H), (H, I)]
+    gpu.load_weight(aos.W_ATTN_NORM, (1 + randn((H,), 0.1).float()).to(torch.bfloat16), layer=0, on_device=True)
+    gpu.load_weight(aos.W_MLP_NORM, (1 + randn((H,), 0.1).float()).to(torch.bfloat16), layer=0, on_device=True)
+    for mod, shp in enumerate(shapes):
+        gpu.load_weight(aos.W_PROJ, randn(shp, 0.02), layer=0, module=mod, on_device=True)
+    L = gpu._L
+    for a in range(NA):
+        aos.check(L.aos_adapter_new(gpu.ctx, a, R, float(2 * R)), gpu.ctx)
+        for mod in range(4):
+            out, inn = shapes[mod]
+            Am, Bm = randn((R, inn), 0.02), randn((out, R), 0.02)
+            aos.check(L.aos_adapter_set_module(gpu.ctx, a, 0, mod, Am.data_ptr(), Bm.data_ptr(), 1), gpu.ctx)
+    torch.cuda.synchronize()
+    sids = np.arange(T, dtype=np.uint64)
+    for t in range(T):
+        gpu.kv_alloc(int(sids[t]), mb * 16)
+    gpu.kv_fill_synthetic(seed=SEED, std=1.0)
+    for t in range(T):
+        gpu.kv_set_len(int(sids[t]), ctx)
+    pri = torch.from_numpy(rng.standard_normal((T, NA)).astype(np.float32)).to(dev)
+    nsids = torch.arange(NA, device=dev, dtype=torch.int64)
+    rings = torch.zeros((T, 40), dtype=torch.uint8, device=dev)
+    hidden = randn((T, H), 1.0).view(torch.int16)
+    stream_ptr = gpu.stream()
+    stream = torch.cuda.ExternalStream(stream_ptr)
+
+    def step():
+        aos.route_batch_dev(pri, nsids, rings, k=K, tau=1.0, eps=0.02, stream=stream_ptr)
+        gpu.layer_step_dev(0, rings, sids, hidden, advance=False, stream=stream_ptr)
+
+    for _ in range(W_):
+        step()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(K_):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / K_
+    gpu.health_check()
+    rn = rings.cpu().numpy().view(aos.RING_DTYPE).reshape(T)
+    sel = {int(r["indices"][j]) for r in rn for j in range(int(r["top_k"])) if r["gates_q15"][j] > 0}
+    base = ((QD + 2 * KVD) * H + H * QD + 2 * I * H + H * I) * 2
+    kvb = T * (ctx + 1) * KVD * 2 * 2
+    lora = len(sel) * R * ((H + QD) + 2 * (H + KVD) + (QD + H)) * 2
+    acts = T * (4 * H + QD * 2 + 2 * KVD + I) * 2
+    nbytes = base + kvb + lora + acts
+    peak, kind = peaks()
+    gbs = nbytes / (ms / 1000.0) / 1e9
+    # CPU: the oracle layer (its own seeded weights of the same shapes) on the
+    # host cores for a sample of the tokens
+    th = os.cpu_count() or 1
+    n_cpu = 4
+    m = O.HostModel.random(rng, H, nh, nkv, 128, I, 256, 1, with_embed=False)
+    ad = O.HostAdapters.random(rng, m, [R] * NA, modules=[0, 1, 2, 3])
+    bt = np.arange(n_cpu * mb, dtype=np.int32).reshape(n_cpu, mb)
+    kv = O.HostKV(m, n_cpu * mb, 16, bt, np.full(n_cpu, ctx, np.int32))
+    kv.k_pool[...] = O.f32_to_bf16_bits(rng.standard_normal(kv.k_pool.shape, dtype=np.float32))
+    kv.v_pool[...] = O.f32_to_bf16_bits(rng.standard_normal(kv.v_pool.shape, dtype=np.float32))
+    rg, _, _, _ = O.route_batch(rng.standard_normal((n_cpu, NA)).astype(np.float32), None, k=K)
+    hs = O.f32_to_bf16_bits(rng.standard_normal((n_cpu, H), dtype=np.float32))
+    t0 = time.perf_counter()
+    O.layer_step(m, ad, 0, rg, kv, hs, n_threads=th)
+    cpu_s = time.perf_counter() - t0
+    if rank == 0:
+        line = {"metric": "config 2: one decoder layer, batch 32, KV 2048, 32 rank-16 LoRAs K=4 (tokens/s)",
+                "value": T / (ms / 1000.0), "unit": "tok/s", "n_gpus": 1, "steps": K_, "warmup": W_,
+                "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": "config 2: H 3584, 28/4 heads, I 18944, q/k/v/o LoRA",
+                           "l2": "inputs larger than L2 (466 MB of layer weights)"},
+                "roofline": {"bound": "hbm", "kernel": "whole layer step", "achieved": gbs, "peak": peak,
+                             "unit": "GB/s", "frac": gbs / peak, "peak_kind": kind, "bytes_per_step": nbytes,
+                             "unique_adapters": len(sel)},
+                "cpu_baseline": {"value": n_cpu / cpu_s, "unit": "tok/s", "cores": th, "kind": "port",
+                                 "sample": f"oracle layer for {n_cpu} tokens with 2048 cached positions each"}}
+        print(json.dumps(line), flush=True)
+    gpu.close()
+
+
 # ------------------------------------------------------------------ config 4
 CFG4 = dict(n_prompts=8, prompt_len=2048, n_adapters=64, rank=16, K=4)
 METRIC4 = "prefill tok/s, 8B-shape, 8 x 2048-token prompts, K=4 of 64 rank-16 LoRAs; % of bf16 tensor roofline"
@@ -630,8 +830,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=CFG["n_layers"], help="debug only: fewer layers is not a valid number")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", type=int, default=3, choices=[3, 4, 5],
-                    help="3: the headline decode workload; 4: prefill; 5: the adapter-sharded large pool")
+    ap.add_argument("--config", type=int, default=3, choices=[1, 2, 3, 4, 5],
+                    help="1: router + fp32 LoRA op; 2: one layer; 3: the headline decode workload; "
+                         "4: prefill; 5: the adapter-sharded large pool")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -653,9 +854,10 @@ def main():
 
         dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
         dist = dist_mod
-    if args.config in (4, 5):
-        if args.config == 4:
-            run_config4(args, rank, world, local)
+    if args.config != 3:
+        runner = {1: run_config1, 2: run_config2, 4: run_config4}.get(args.config)
+        if runner:
+            runner(args, rank, world, local)
         else:
             run_config5(args, rank, world, local, dist)
         if dist:
