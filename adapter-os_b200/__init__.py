@@ -131,6 +131,9 @@ def lib():
             "aos_run_step_batch_dev": (C.c_int, [vp, vp, vp, vp, u32, vp, vp, vp]),
             "aos_layer_step_dev": (C.c_int, [vp, u32, vp, vp, u32, vp, C.c_int, vp]),
             "aos_prefill_dev": (C.c_int, [vp, u32, vp, vp, vp, vp, vp, vp]),
+            "aos_adapter_probe_safetensors": (C.c_int, [vp, u64, vp, u32, vp, vp, vp]),
+            "aos_adapter_load_safetensors": (C.c_int, [vp, C.c_uint16, vp, u64, vp]),
+            "aos_load_model_safetensors": (C.c_int, [vp, vp, u64]),
             "aos_shard_get_unique_id": (C.c_int, [vp]),
             "aos_shard_init": (C.c_int, [vp, u32, u32, vp]),
             "aos_run_step_sharded_dev": (C.c_int, [vp, vp, vp, vp, u32, vp, vp, vp]),
@@ -151,6 +154,37 @@ def lib():
 
 
 SHARD_ID_BYTES = 128
+
+
+class AdapterMeta(C.Structure):
+    """aos_adapter_meta: AdapterLoadMetadata (kernel-mtl/src/lib.rs:186-220)."""
+    _fields_ = [("rank", C.c_uint32), ("alpha", C.c_float), ("target_modules", C.POINTER(C.c_char_p)),
+                ("n_targets", C.c_uint32)]
+
+
+def _adapter_meta(rank=0, alpha=0.0, target_modules=None):
+    m = AdapterMeta(int(rank), float(alpha), None, 0)
+    keep = None
+    if target_modules is not None:
+        keep = (C.c_char_p * max(1, len(target_modules)))(*[t.encode() for t in target_modules])
+        m.target_modules = C.cast(keep, C.POINTER(C.c_char_p))
+        m.n_targets = len(target_modules)
+    return m, keep
+
+
+def adapter_probe_safetensors(data: bytes, n_layers, rank=0, alpha=0.0, target_modules=None):
+    """What aos_adapter_load_safetensors would load: (rank, alpha, found) with
+    found[layer][module] bit 0 = lora_A, bit 1 = lora_B (no device needed)."""
+    meta, keep = _adapter_meta(rank, alpha, target_modules)
+    buf = C.create_string_buffer(bytes(data), len(data))
+    r, a = C.c_uint32(0), C.c_float(0.0)
+    found = np.zeros((n_layers, len(MODULES)), np.uint32)
+    rc = lib().aos_adapter_probe_safetensors(buf, len(data), C.byref(meta), n_layers, C.byref(r), C.byref(a),
+                                             _p(found))
+    del keep
+    if rc != 0:
+        raise AosError(rc, last_error())
+    return int(r.value), float(a.value), found
 
 
 def shard_unique_id() -> bytes:
@@ -506,6 +540,19 @@ class CudaKernels:
         sid = np.ascontiguousarray(seq_ids, np.uint64)
         self._check(self._L.aos_run_step_batch_dev(self.ctx, _p(rings), _p(token_ids), _p(sid), len(sid),
                                                   _p(logits), _p(hidden), stream))
+
+    # -- safetensors loading --------------------------------------------------
+    def load_adapter_safetensors(self, adapter_id, data: bytes, rank=0, alpha=0.0, target_modules=None):
+        """FusedKernels::load_adapter_with_metadata from safetensors bytes."""
+        meta, keep = _adapter_meta(rank, alpha, target_modules)
+        buf = C.create_string_buffer(bytes(data), len(data))
+        self._check(self._L.aos_adapter_load_safetensors(self.ctx, int(adapter_id), buf, len(data), C.byref(meta)))
+        del keep
+
+    def load_model_safetensors(self, data: bytes):
+        """Base weights under the Hugging Face LLaMA tensor names."""
+        buf = C.create_string_buffer(bytes(data), len(data))
+        self._check(self._L.aos_load_model_safetensors(self.ctx, buf, len(data)))
 
     # -- prefill ----------------------------------------------------------
     def prefill_dev(self, seq_ids, n_tok, rings, token_ids, logits=None, stream=None):

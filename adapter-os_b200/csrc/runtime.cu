@@ -947,6 +947,23 @@ int enqueue_prefill_layer(aos_ctx* c, int layer, int T, int n_qblk, cudaStream_t
 
 }  // namespace
 
+// Model dimensions and the context's error channel, for the loaders in
+// safetensors.cu.
+namespace aos {
+int ctx_model_dims(const aos_ctx* c, uint32_t* n_layers, uint32_t* in_dims, uint32_t* out_dims, uint32_t* hidden,
+                   uint32_t* vocab) {
+    *n_layers = c->cfg.n_layers;
+    for (int m = 0; m < AOS_NUM_MODULES; ++m) {
+        in_dims[m] = mod_in(c, m);
+        out_dims[m] = mod_out(c, m);
+    }
+    *hidden = c->cfg.hidden;
+    *vocab = c->cfg.vocab;
+    return AOS_OK;
+}
+int ctx_fail(aos_ctx* c, int code, const std::string& msg) { return c->fail(code, msg); }
+}  // namespace aos
+
 // ============================================================================ C ABI
 extern "C" {
 

@@ -255,6 +255,35 @@ int aos_layer_step_dev(aos_ctx* ctx, uint32_t layer, const aos_router_ring* ring
                        const uint64_t* seq_ids, uint32_t T, uint16_t* hidden, int advance,
                        void* stream);
 
+/* ---- loading from safetensors bytes ------------------------------------------
+ * Adapters (FusedKernels::load_adapter_with_metadata,
+ * kernel-mtl/src/lib.rs:1893-2046): for every target module, the first tensor
+ * name in sorted order that contains the module name and "lora_A" (resp.
+ * "lora_B"); a name with ".layers.<L>." belongs to layer L, one without to
+ * layer 0.  Target modules: meta->target_modules (trimmed, empty and repeated
+ * names dropped) or, when absent or matching nothing, q_proj, k_proj, v_proj,
+ * down_proj, up_proj.  Rank: meta->rank if > 0, else lora_A's first dimension,
+ * else 16; alpha: meta->alpha if finite and > 0, else 2 * rank.  F32, F16 and
+ * BF16 tensors are stored as bf16.  meta may be NULL. */
+typedef struct aos_adapter_meta {
+    uint32_t rank;
+    float alpha;
+    const char* const* target_modules;
+    uint32_t n_targets;
+} aos_adapter_meta;
+/* Context-free: the rank / alpha the load would use and, per layer and module
+ * (found[layer * 7 + module]), bit 0 = lora_A found, bit 1 = lora_B found. */
+int aos_adapter_probe_safetensors(const void* data, uint64_t len, const aos_adapter_meta* meta,
+                                  uint32_t n_layers, uint32_t* rank_out, float* alpha_out,
+                                  uint32_t* found);
+int aos_adapter_load_safetensors(aos_ctx* ctx, uint16_t id, const void* data, uint64_t len,
+                                 const aos_adapter_meta* meta);
+/* Base weights under the Hugging Face LLaMA names (kernel-mtl/src/lib.rs:660-1000):
+ * model.embed_tokens, lm_head (tied to the embedding when absent), model.norm,
+ * model.layers.<L>.{input_layernorm, post_attention_layernorm,
+ * self_attn.{q,k,v,o}_proj, mlp.{gate,up,down}_proj}.weight. */
+int aos_load_model_safetensors(aos_ctx* ctx, const void* data, uint64_t len);
+
 /* ---- prefill (the prompt path) ---------------------------------------------
  * InferencePipeline's prompt pass (inference_pipeline.rs:983-1154, MLX
  * forward over the prompt, mlx_cpp_wrapper_real.cpp:3338-3559 with T > 1):
