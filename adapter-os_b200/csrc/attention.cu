@@ -5,7 +5,7 @@
 // (mlx_cpp_wrapper_real.cpp:3284-3324; kv_cache.metal:101-183 for the decode
 // form).
 //
-// Split-KV: one CTA per (token, kv head, chunk of 16 pages = 256 positions);
+// Split-KV: one CTA per (token, kv head, chunk of 64 pages = 1024 positions);
 // its 4 warps take pages round-robin.  Pages (16 positions x 128 dims) arrive
 // by TMA (SWIZZLE_128B, two 64-dim boxes each for K and V) into per-warp
 // double buffers; QK^T and PV run on mma.sync m16n8k16 with the query heads
@@ -21,7 +21,7 @@
 namespace aos {
 namespace {
 
-constexpr int kPages = 16;          // pages per chunk
+constexpr int kPages = 64;          // pages per chunk
 constexpr int kWarps = 4;
 constexpr int kPageBytes = 16 * 128 * 2;  // one of K or V
 constexpr int kBufBytes = 2 * kPageBytes;  // K + V
