@@ -148,9 +148,9 @@ struct aos_ctx {
     int attn_chunks = 0;
     uint16_t* d_stage = nullptr;  // bounded staging for packing host or unaligned weights
     size_t stage_bytes = 0;
-    long long* d_acc = nullptr;   // GEMM fixed-point accumulators of split tiles (kept zero)
+    long long* d_acc = nullptr;   // GEMM fixed-point accumulators of split shrink tiles (kept zero)
     size_t acc_bytes = 0;
-    float* d_part = nullptr;      // GEMM fp32 partials of split base tiles (steps with T > 128)
+    float* d_part = nullptr;      // GEMM fp32 partials of split base tiles
     int* d_sync = nullptr;        // [4] GEMM grid-barrier counters
     int* d_err = nullptr;
     unsigned long long* d_trace = nullptr;  // AOS_TC_TRACE diagnostics
@@ -253,7 +253,7 @@ int build_owner_plan(aos_ctx* c, int layer, int g, int T, TcParams& p) {
     p.n_groups = c->d_n_groups;
     p.acc = c->d_acc;
     p.acc_T = c->T_cap;
-    p.part = T > kTcTok ? c->d_part : nullptr;
+    p.part = c->d_part;
     p.sync = c->d_sync;
     p.err = c->d_err;
     p.R = c->R;
@@ -314,7 +314,7 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp, bool sharded =
         p.n_groups = c->d_n_groups;
         p.acc = c->d_acc;
         p.acc_T = c->T_cap;
-        p.part = T > kTcTok ? c->d_part : nullptr;
+        p.part = c->d_part;
         p.sync = c->d_sync;
         p.err = c->d_err;
         p.R = c->R;
@@ -482,7 +482,7 @@ int get_plan(aos_ctx* c, int T, StepPlan** out, bool sharded = false) {
     p.err = c->d_err;
     p.acc = c->d_acc;
     p.acc_T = c->T_cap;
-    p.part = T > kTcTok ? c->d_part : nullptr;
+    p.part = c->d_part;
     p.sync = c->d_sync;
     const uint32_t V = c->cfg.vocab;
     p.w_pk[0] = c->lm_head;
@@ -1095,8 +1095,8 @@ aos_ctx* aos_init(const aos_model_config* cfg) {
         const size_t tiles = max_launch_tiles(c.get());
         c->acc_bytes = tiles * kTcBN * (size_t)c->T_cap * sizeof(long long);
         INIT_CHECK(dalloc(&c->d_acc, c->acc_bytes / sizeof(long long)), "GEMM accumulators");
-        if (c->T_cap > kTcTok)  // one slot per (CTA, base tile) pair that can hold a piece
-            INIT_CHECK(dalloc(&c->d_part, (tc_num_sms() + tiles) * kTcBN * (size_t)c->T_cap), "GEMM partials");
+        // one slot per (CTA, base tile) pair that can hold a piece
+        INIT_CHECK(dalloc(&c->d_part, (tc_num_sms() + tiles) * kTcBN * (size_t)c->T_cap), "GEMM partials");
         INIT_CHECK(dalloc(&c->d_sync, 4), "sync");
     }
     INIT_CHECK(dalloc(&c->d_err, 1), "err");

@@ -88,12 +88,12 @@ struct TcParams {
     // conversion re-zeroes what it reads).
     long long* acc;
     int acc_T;                      // token stride of the accumulator (T_cap)
-    // Optional (set for T > 128, where one piece holds 256 tokens x 256
-    // columns): split base tiles write fp32 partial sums here with plain
-    // stores instead of adding into acc, [slot][256 columns][acc_T tokens]
-    // with slot = CTA + base tile index (unique per piece), and the final
-    // conversion sums a tile's pieces in CTA order.  Shrink tiles keep the
-    // fixed-point adds (only a token's own adapters' columns are added).
+    // Split base tiles write fp32 partial sums here with plain stores,
+    // [slot][256 columns][acc_T tokens] with slot = CTA + base tile index
+    // (unique per piece), and the final conversion sums a tile's pieces in
+    // CTA order (fixed order: bit-identical run to run).  Shrink tiles keep
+    // the fixed-point adds into acc, which touch only a token's own adapters'
+    // columns.  Null selects fixed-point adds for base tiles too.
     float* part;
     // Token placement in the MMA's M (TMEM lanes): with spread (T <= 64) token
     // t sits in lane 32 * (t / 16) + t % 16, so all four lane quarters (drain
