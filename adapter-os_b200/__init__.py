@@ -142,6 +142,14 @@ def lib():
             "aos_profile_read": (C.c_int, [vp, vp, C.c_int]),
             "aos_health_check": (C.c_int, [vp]),
             "aos_attest_determinism": (C.c_int, [vp, vp]),
+            "aos_archive_parse": (C.c_int, [vp, u64, vp, vp, u32]),
+            "aos_blake3": (C.c_int, [vp, vp, u64, C.c_int, vp]),
+            "aos_archive_verify": (C.c_int, [vp, vp, u64, vp]),
+            "aos_adapter_load_aos": (C.c_int, [vp, C.c_uint16, vp, u64, C.c_char_p, vp]),
+            "aos_adapter_verify_buffers": (C.c_int, [vp, C.c_uint16, vp, vp, vp, vp, vp]),
+            "aos_adapter_fingerprint": (C.c_int, [vp, C.c_uint16, vp, vp]),
+            "aos_store_gpu_fingerprint": (C.c_int, [vp, C.c_uint16, u64, C.c_char_p]),
+            "aos_verify_gpu_fingerprint": (C.c_int, [vp, C.c_uint16, u64, C.c_char_p, vp]),
         }
         for name, (res, args) in sig.items():
             if not hasattr(L, name):
@@ -185,6 +193,45 @@ def adapter_probe_safetensors(data: bytes, n_layers, rank=0, alpha=0.0, target_m
     if rc != 0:
         raise AosError(rc, last_error())
     return int(r.value), float(a.value), found
+
+
+class ArchiveSegment(C.Structure):
+    """aos_archive_segment: one 80-byte .aos index entry (adapteros-aos/src/writer.rs:313-323)."""
+    _fields_ = [("segment_id", C.c_uint32), ("backend_tag", C.c_uint16), ("reserved", C.c_uint16),
+                ("offset", C.c_uint64), ("len", C.c_uint64), ("scope_hash", C.c_uint8 * 16),
+                ("weights_hash", C.c_uint8 * 32)]
+
+
+class ArchiveInfo(C.Structure):
+    _fields_ = [("flags", C.c_uint32), ("n_segments", C.c_uint32), ("manifest_offset", C.c_uint64),
+                ("manifest_size", C.c_uint64)]
+
+
+class ArchiveLoadInfo(C.Structure):
+    _fields_ = [("rank", C.c_uint32), ("tensor_rank", C.c_uint32), ("storage_rank", C.c_uint32),
+                ("alpha", C.c_float), ("module_mask", C.c_uint32), ("segment_id", C.c_uint32),
+                ("backend_tag", C.c_uint16), ("reserved", C.c_uint16), ("weights_hash", C.c_uint8 * 32),
+                ("scope_hash", C.c_uint8 * 16)]
+
+
+BACKEND_TAGS = ("canonical", "mlx", "metal", "coreml")
+
+
+def archive_parse(data: bytes):
+    """Layout of a .aos archive (AosWriter::parse_header_bytes + parse_segments
+    without the hash check; no device needed): (info dict, [segment dicts])."""
+    buf = C.create_string_buffer(bytes(data), max(1, len(data)))
+    info = ArchiveInfo()
+    rc = lib().aos_archive_parse(buf, len(data), C.byref(info), None, 0)
+    if rc != 0:
+        raise AosError(rc, last_error())
+    segs = (ArchiveSegment * max(1, info.n_segments))()
+    check(lib().aos_archive_parse(buf, len(data), C.byref(info), segs, info.n_segments))
+    out = [{"segment_id": s.segment_id, "backend": BACKEND_TAGS[s.backend_tag], "offset": s.offset, "len": s.len,
+            "scope_hash": bytes(s.scope_hash).hex(), "weights_hash": bytes(s.weights_hash).hex()}
+           for s in segs[:info.n_segments]]
+    return {"flags": info.flags, "n_segments": info.n_segments, "manifest_offset": info.manifest_offset,
+            "manifest_size": info.manifest_size}, out
 
 
 def shard_unique_id() -> bytes:
@@ -553,6 +600,59 @@ class CudaKernels:
         """Base weights under the Hugging Face LLaMA tensor names."""
         buf = C.create_string_buffer(bytes(data), len(data))
         self._check(self._L.aos_load_model_safetensors(self.ctx, buf, len(data)))
+
+    # -- .aos archives and GPU fingerprints ---------------------------------
+    def blake3(self, data) -> str:
+        """BLAKE3 hex digest computed on the GPU; data: bytes, or a CUDA tensor."""
+        out = C.create_string_buffer(32)
+        if hasattr(data, "data_ptr"):
+            n = data.numel() * data.element_size()
+            self._check(self._L.aos_blake3(self.ctx, data.data_ptr(), n, 1, out))
+        else:
+            buf = C.create_string_buffer(bytes(data), max(1, len(data)))
+            self._check(self._L.aos_blake3(self.ctx, buf, len(data), 0, out))
+        return out.raw.hex()
+
+    def archive_verify(self, data: bytes):
+        """open_aos: layout plus every segment hash (on the GPU); raises on a bad archive."""
+        buf = C.create_string_buffer(bytes(data), max(1, len(data)))
+        bad = C.c_int32(-1)
+        self._check(self._L.aos_archive_verify(self.ctx, buf, len(data), C.byref(bad)))
+
+    def load_adapter_aos(self, adapter_id, data: bytes, backend="canonical") -> dict:
+        """LifecycleLoader::load_from_aos_static into adapter slot adapter_id."""
+        buf = C.create_string_buffer(bytes(data), max(1, len(data)))
+        info = ArchiveLoadInfo()
+        self._check(self._L.aos_adapter_load_aos(self.ctx, int(adapter_id), buf, len(data),
+                                                 backend.encode() if backend else None, C.byref(info)))
+        return {"rank": info.rank, "tensor_rank": info.tensor_rank, "storage_rank": info.storage_rank,
+                "alpha": info.alpha, "modules": [MODULES[m] for m in range(len(MODULES)) if info.module_mask >> m & 1],
+                "segment_id": info.segment_id, "backend": BACKEND_TAGS[info.backend_tag],
+                "weights_hash": bytes(info.weights_hash).hex(), "scope_hash": bytes(info.scope_hash).hex()}
+
+    def verify_adapter_buffers(self, adapter_id):
+        """(buffer_bytes, first, last, mid) samples of the adapter's arena buffer."""
+        size, n = C.c_uint64(0), C.c_uint32(0)
+        bufs = [C.create_string_buffer(4096) for _ in range(3)]
+        self._check(self._L.aos_adapter_verify_buffers(self.ctx, int(adapter_id), C.byref(size), bufs[0], bufs[1],
+                                                       bufs[2], C.byref(n)))
+        return int(size.value), bufs[0].raw[:n.value], bufs[1].raw[:n.value], bufs[2].raw[:n.value]
+
+    def adapter_fingerprint(self, adapter_id):
+        """(buffer_bytes, BLAKE3 hex of first || last || mid), hashed on the GPU."""
+        size, h = C.c_uint64(0), C.create_string_buffer(32)
+        self._check(self._L.aos_adapter_fingerprint(self.ctx, int(adapter_id), C.byref(size), h))
+        return int(size.value), h.raw.hex()
+
+    def store_gpu_fingerprint(self, adapter_id, buffer_bytes, checkpoint_hash_hex):
+        self._check(self._L.aos_store_gpu_fingerprint(self.ctx, int(adapter_id), int(buffer_bytes),
+                                                      checkpoint_hash_hex.encode()))
+
+    def verify_gpu_fingerprint(self, adapter_id, buffer_bytes, checkpoint_hash_hex) -> bool:
+        m = C.c_int(0)
+        self._check(self._L.aos_verify_gpu_fingerprint(self.ctx, int(adapter_id), int(buffer_bytes),
+                                                       checkpoint_hash_hex.encode(), C.byref(m)))
+        return bool(m.value)
 
     # -- prefill ----------------------------------------------------------
     def prefill_dev(self, seq_ids, n_tok, rings, token_ids, logits=None, stream=None):

@@ -5,6 +5,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "loader.cuh"
 
 namespace aos {
 namespace {
@@ -203,7 +204,40 @@ __global__ void pack_blocks_kernel(const uint16_t* __restrict__ src, int rows, i
     }
 }
 
+// Reads elements of the canonical (row-major, unpacked) view of packed
+// matrices: element e of window w is starts[w] + k; the segment holding it is
+// found by binary search over segs[].e0 (ascending), and its packed address
+// is the one pack_blocks_kernel writes for (row0 + i, col0 + j).
+__global__ void unpack_samples_kernel(const UnpackSeg* __restrict__ segs, int n_segs,
+                                      const long long* __restrict__ starts, int n_per, uint16_t* __restrict__ out) {
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= 3 * n_per) return;
+    const long long e = starts[idx / n_per] + idx % n_per;
+    int lo = 0, hi = n_segs - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) / 2;
+        if (segs[mid].e0 <= e) lo = mid;
+        else hi = mid - 1;
+    }
+    const UnpackSeg sg = segs[lo];
+    const long long local = e - sg.e0;
+    const int dr = sg.row0 + (int)(local / sg.cols), dc = sg.col0 + (int)(local % sg.cols);
+    const long long blk = (long long)(dr / sg.br) * (sg.dst_cols / 64) + dc / 64;
+    const int rr = dr % sg.br, q = (dc % 64) / 8;
+    const uint8_t* p = reinterpret_cast<const uint8_t*>(sg.base) + blk * sg.br * 128 + rr * 128 +
+                       ((q ^ (rr & 7)) * 16) + (dc % 8) * 2;
+    out[idx] = *reinterpret_cast<const uint16_t*>(p);
+}
+
 }  // namespace
+
+cudaError_t launch_unpack_samples(const UnpackSeg* segs, int n_segs, const long long* starts, int n_per,
+                                  uint16_t* out, cudaStream_t s) {
+    const int n = 3 * n_per;
+    if (n <= 0) return cudaSuccess;
+    unpack_samples_kernel<<<(n + 255) / 256, 256, 0, s>>>(segs, n_segs, starts, n_per, out);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_embed(const uint16_t* table, const uint32_t* ids, int T, int H, int V, uint16_t* out,
                          cudaStream_t s) {

@@ -29,6 +29,7 @@
 
 #include <nccl.h>
 
+#include "loader.cuh"
 #include "tc_gemm.cuh"
 
 namespace aos {
@@ -116,6 +117,7 @@ struct aos_ctx {
     float* d_ucoef = nullptr; // [T_cap][R/64 touched-group slots][8 units] per-step unit coefficients
     std::vector<int> col_owner;  // host mirror, 8-column units
     std::unordered_map<uint16_t, AdapterEntry> adapters;
+    std::map<uint16_t, std::pair<uint64_t, std::string>> fingerprints;  // id -> (buffer bytes, checkpoint hash hex)
     uint64_t arena_bytes = 0;
 
     // KV cache
@@ -151,6 +153,7 @@ struct aos_ctx {
     long long* d_acc = nullptr;   // GEMM fixed-point accumulators of split shrink tiles (kept zero)
     size_t acc_bytes = 0;
     float* d_part = nullptr;      // GEMM fp32 partials of split base tiles
+    uint16_t* d_fp = nullptr;     // adapter buffer samples [3][2048] for fingerprints
     int* d_sync = nullptr;        // [4] GEMM grid-barrier counters
     int* d_err = nullptr;
     unsigned long long* d_trace = nullptr;  // AOS_TC_TRACE diagnostics
@@ -962,6 +965,11 @@ int ctx_model_dims(const aos_ctx* c, uint32_t* n_layers, uint32_t* in_dims, uint
     return AOS_OK;
 }
 int ctx_fail(aos_ctx* c, int code, const std::string& msg) { return c->fail(code, msg); }
+cudaStream_t ctx_stream(aos_ctx* c) { return c->stream; }
+int ctx_set_device(aos_ctx* c) {
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    return AOS_OK;
+}
 }  // namespace aos
 
 // ============================================================================ C ABI
@@ -1163,7 +1171,7 @@ void aos_destroy(aos_ctx* c) {
     f(c->d_hidden); f(c->d_normed); f(c->d_q); f(c->d_attn); f(c->d_act);
     f(c->d_groups); f(c->d_n_groups); f(c->d_block_tables); f(c->d_ctx_lens);
     f(c->d_rings); f(c->d_tokens); f(c->d_logits); f(c->d_rope);
-    f(c->d_attn_part); f(c->d_attn_ml); f(c->d_stage); f(c->d_acc); f(c->d_part); f(c->d_sync); f(c->d_err); f(c->d_trace);
+    f(c->d_attn_part); f(c->d_attn_ml); f(c->d_stage); f(c->d_acc); f(c->d_part); f(c->d_fp); f(c->d_sync); f(c->d_err); f(c->d_trace);
     for (int i = 0; i < aos_ctx::kStageSlots; ++i) {
         if (c->h_stage[i]) cudaFreeHost(c->h_stage[i]);
         if (c->stage_ev[i]) cudaEventDestroy(c->stage_ev[i]);
@@ -1238,6 +1246,12 @@ int aos_load_weight(aos_ctx* c, aos_weight_kind kind, uint32_t layer, aos_module
 // ------------------------------------------------------------------ adapters
 int aos_adapter_new(aos_ctx* c, uint16_t id, uint32_t rank, float alpha) {
     if (!c) return AOS_ERR_INVALID;
+    return aos::ctx_adapter_new(c, id, rank, alpha, alpha / (float)rank);
+}
+
+}  // extern "C"
+
+int aos::ctx_adapter_new(aos_ctx* c, uint16_t id, uint32_t rank, float alpha, float scale) {
     if (!c->module_mask) return c->fail(AOS_ERR_STATE, "this context has no LoRA arena");
     if (id >= c->cfg.lora_max_adapters) return c->fail(AOS_ERR_INVALID, "adapter id >= lora_max_adapters");
     if (rank < 8 || rank > 256 || rank % 8) return c->fail(AOS_ERR_INVALID, "rank must be a multiple of 8 in [8, 256]");
@@ -1273,7 +1287,6 @@ int aos_adapter_new(aos_ctx* c, uint16_t id, uint32_t rank, float alpha) {
     std::vector<int> owner((size_t)rank, (int)id);
     CTX_CUDA(c, cudaMemcpy(c->d_col_owner + off, owner.data(), rank * 4, cudaMemcpyHostToDevice));
     const int irank = (int)rank;
-    const float scale = alpha / (float)rank;
     CTX_CUDA(c, cudaMemcpy(c->d_col_off + id, &off, 4, cudaMemcpyHostToDevice));
     CTX_CUDA(c, cudaMemcpy(c->d_rank + id, &irank, 4, cudaMemcpyHostToDevice));
     CTX_CUDA(c, cudaMemcpy(c->d_scale + id, &scale, 4, cudaMemcpyHostToDevice));
@@ -1282,6 +1295,8 @@ int aos_adapter_new(aos_ctx* c, uint16_t id, uint32_t rank, float alpha) {
     c->m.arena_used_rank_cols += rank;
     return AOS_OK;
 }
+
+extern "C" {
 
 int aos_adapter_set_module(aos_ctx* c, uint16_t id, uint32_t layer, aos_module module, const uint16_t* A,
                            const uint16_t* B, int src_on_device) {
@@ -1322,6 +1337,107 @@ int aos_adapter_unload(aos_ctx* c, uint16_t id) {
 }
 
 int aos_adapter_is_loaded(const aos_ctx* c, uint16_t id) { return c && c->adapters.count(id) ? 1 : 0; }
+
+}  // extern "C"
+
+// The adapter's device buffer in canonical form: for every layer and every
+// LoRA-enabled module (aos_module order), its lora_A rows [rank][in] and then
+// its lora_B columns [out][rank], bf16 row-major, read out of the packed
+// arena.  Windows of 4 KB (or the whole buffer when smaller) at its start,
+// its end and its middle (start (size - window) / 2, in elements) are
+// gathered on the device into c->d_fp [first | last | mid].
+static int adapter_samples(aos_ctx* c, uint16_t id, uint64_t* size_bytes, int* n_per) {
+    auto it = c->adapters.find(id);
+    if (it == c->adapters.end()) return c->fail(AOS_ERR_NOT_FOUND, "adapter not loaded");
+    const int off = it->second.off, rank = it->second.rank;
+    std::vector<UnpackSeg> segs;
+    long long e = 0;
+    for (uint32_t l = 0; l < c->cfg.n_layers; ++l)
+        for (int m = 0; m < AOS_NUM_MODULES; ++m) {
+            if (!(c->module_mask & (1u << m))) continue;
+            const int in = (int)mod_in(c, m), out = (int)mod_out(c, m);
+            segs.push_back(UnpackSeg{e, c->A[m][l], rank, in, in, kGroup, off, 0});
+            e += (long long)rank * in;
+            segs.push_back(UnpackSeg{e, c->B[m][l], out, rank, c->R, 128, 0, off});
+            e += (long long)out * rank;
+        }
+    if (segs.empty()) return c->fail(AOS_ERR_STATE, "this context has no LoRA arena");
+    const int w = (int)std::min<long long>(2048, e);
+    const long long starts[3] = {0, e - w, (e - w) / 2};
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    cudaStream_t s = c->stream;
+    UnpackSeg* d_segs = nullptr;
+    long long* d_starts = nullptr;
+    CTX_CUDA(c, cudaMallocAsync((void**)&d_segs, segs.size() * sizeof(UnpackSeg), s));
+    CTX_CUDA(c, cudaMallocAsync((void**)&d_starts, sizeof starts, s));
+    if (!c->d_fp) CTX_CUDA(c, cudaMalloc((void**)&c->d_fp, 3 * 2048 * sizeof(uint16_t)));
+    CTX_CUDA(c, cudaMemcpyAsync(d_segs, segs.data(), segs.size() * sizeof(UnpackSeg), cudaMemcpyHostToDevice, s));
+    CTX_CUDA(c, cudaMemcpyAsync(d_starts, starts, sizeof starts, cudaMemcpyHostToDevice, s));
+    LAUNCH(c, launch_unpack_samples(d_segs, (int)segs.size(), d_starts, w, c->d_fp, s));
+    CTX_CUDA(c, cudaFreeAsync(d_segs, s));
+    CTX_CUDA(c, cudaFreeAsync(d_starts, s));
+    *size_bytes = (uint64_t)e * 2;
+    *n_per = w;
+    return AOS_OK;
+}
+
+static std::string hex_lower(const uint8_t* h, int n) {
+    static const char* d = "0123456789abcdef";
+    std::string s;
+    for (int i = 0; i < n; ++i) {
+        s += d[h[i] >> 4];
+        s += d[h[i] & 15];
+    }
+    return s;
+}
+
+extern "C" {
+
+int aos_adapter_verify_buffers(aos_ctx* c, uint16_t id, uint64_t* buffer_bytes, void* first, void* last, void* mid,
+                               uint32_t* sample_bytes) {
+    if (!c || !buffer_bytes) return AOS_ERR_INVALID;
+    int n_per = 0, rc = adapter_samples(c, id, buffer_bytes, &n_per);
+    if (rc) return rc;
+    void* dst[3] = {first, last, mid};
+    for (int k = 0; k < 3; ++k)
+        if (dst[k])
+            CTX_CUDA(c, cudaMemcpyAsync(dst[k], c->d_fp + (size_t)k * n_per, (size_t)n_per * 2, cudaMemcpyDeviceToHost,
+                                        c->stream));
+    CTX_CUDA(c, cudaStreamSynchronize(c->stream));
+    if (sample_bytes) *sample_bytes = (uint32_t)n_per * 2;
+    return AOS_OK;
+}
+
+int aos_adapter_fingerprint(aos_ctx* c, uint16_t id, uint64_t* buffer_bytes, uint8_t* hash) {
+    if (!c || !buffer_bytes || !hash) return AOS_ERR_INVALID;
+    int n_per = 0, rc = adapter_samples(c, id, buffer_bytes, &n_per);
+    if (rc) return rc;
+    const uint64_t off = 0, len = (uint64_t)n_per * 6;  // first || last || mid, contiguous
+    std::string err;
+    if ((rc = aos::blake3_many(reinterpret_cast<const uint8_t*>(c->d_fp), &off, &len, 1, hash, c->stream, err)))
+        return c->fail(rc, err);
+    return AOS_OK;
+}
+
+int aos_store_gpu_fingerprint(aos_ctx* c, uint16_t id, uint64_t buffer_bytes, const char* checkpoint_hash_hex) {
+    if (!c || !checkpoint_hash_hex) return AOS_ERR_INVALID;
+    const std::string h = checkpoint_hash_hex;
+    if (h.size() != 64 || h.find_first_not_of("0123456789abcdefABCDEF") != std::string::npos)
+        return c->fail(AOS_ERR_INVALID, "Invalid checkpoint hash hex: " + h);
+    std::string lower = h;
+    for (auto& ch : lower) ch = (char)tolower((unsigned char)ch);
+    c->fingerprints[id] = {buffer_bytes, lower};
+    return AOS_OK;
+}
+
+int aos_verify_gpu_fingerprint(aos_ctx* c, uint16_t id, uint64_t buffer_bytes, const char* checkpoint_hash_hex,
+                               int* matches) {
+    if (!c || !checkpoint_hash_hex || !matches) return AOS_ERR_INVALID;
+    auto it = c->fingerprints.find(id);
+    *matches = it != c->fingerprints.end() && it->second.first == buffer_bytes &&
+               it->second.second == checkpoint_hash_hex;
+    return AOS_OK;
+}
 
 // ------------------------------------------------------------------ KV cache
 int aos_kv_alloc(aos_ctx* c, uint64_t seq_id, uint32_t max_tokens) {

@@ -31,17 +31,10 @@
 #include <vector>
 
 #include "common.cuh"
-
-struct aos_ctx;
+#include "loader.cuh"
 
 namespace aos {
 namespace {
-
-struct StTensor {
-    std::string name, dtype;
-    std::vector<int64_t> shape;
-    uint64_t b = 0, e = 0;
-};
 
 // ---------------------------------------------------------------- JSON (header subset)
 struct Json {
@@ -349,6 +342,15 @@ int plan_adapter(const std::vector<StTensor>& ts, const aos_adapter_meta* meta, 
 }
 
 }  // namespace
+
+int parse_safetensors(const uint8_t* d, uint64_t len, std::vector<StTensor>& out, const uint8_t** base,
+                      std::string& err) {
+    return st_parse(d, len, out, base, err);
+}
+int tensor_to_bf16(const StTensor& t, const uint8_t* base, std::vector<uint16_t>& out, std::string& err) {
+    return st_to_bf16(t, base, out, err);
+}
+
 }  // namespace aos
 
 // context internals used here (runtime.cu)
@@ -360,12 +362,6 @@ int aos_adapter_unload(aos_ctx* ctx, uint16_t id);
 int aos_load_weight(aos_ctx* ctx, aos_weight_kind kind, uint32_t layer, aos_module module, const uint16_t* data,
                     uint64_t n, int src_on_device);
 }
-namespace aos {
-int ctx_model_dims(const aos_ctx* c, uint32_t* n_layers, uint32_t* in_dims, uint32_t* out_dims, uint32_t* hidden,
-                   uint32_t* vocab);
-int ctx_fail(aos_ctx* c, int code, const std::string& msg);
-}  // namespace aos
-
 using namespace aos;
 
 extern "C" {

@@ -284,6 +284,80 @@ int aos_adapter_load_safetensors(aos_ctx* ctx, uint16_t id, const void* data, ui
  * self_attn.{q,k,v,o}_proj, mlp.{gate,up,down}_proj}.weight. */
 int aos_load_model_safetensors(aos_ctx* ctx, const void* data, uint64_t len);
 
+/* ---- .aos adapter archives -------------------------------------------------
+ * Layout and validation of crates/adapteros-aos/src/writer.rs:118-135,
+ * 407-558: 64-byte header, 80-byte index entries, payloads, JSON manifest. */
+typedef struct aos_archive_segment {
+    uint32_t segment_id;
+    uint16_t backend_tag; /* 0 canonical, 1 mlx, 2 metal, 3 coreml (writer.rs:41-71) */
+    uint16_t reserved;
+    uint64_t offset;
+    uint64_t len;
+    uint8_t scope_hash[16];   /* first 16 bytes of BLAKE3(manifest metadata.scope_path) */
+    uint8_t weights_hash[32]; /* BLAKE3 of the payload */
+} aos_archive_segment;
+typedef struct aos_archive_info {
+    uint32_t flags;
+    uint32_t n_segments;
+    uint64_t manifest_offset;
+    uint64_t manifest_size;
+} aos_archive_info;
+/* Context-free layout check (AosWriter::parse_header_bytes + parse_segments
+ * without the hash check, same rules and messages); copies up to max_segs
+ * index entries.  AOS_ERR_INVALID with aos_last_error(NULL) on a bad layout. */
+int aos_archive_parse(const void* data, uint64_t len, aos_archive_info* info, aos_archive_segment* segs,
+                      uint32_t max_segs);
+/* BLAKE3 (B3Hash::hash, crates/adapteros-infra-common/src/hash.rs:22-27) of
+ * len bytes, computed on the GPU; data is host memory, or device memory when
+ * on_device != 0.  out: 32 bytes. */
+int aos_blake3(aos_ctx* ctx, const void* data, uint64_t len, int on_device, uint8_t* out);
+/* Layout check plus every segment's BLAKE3 against its index entry, on the
+ * GPU (open_aos, writer.rs:561-585).  bad_segment: index of the first
+ * mismatching entry, or -1. */
+int aos_archive_verify(aos_ctx* ctx, const void* data, uint64_t len, int32_t* bad_segment);
+typedef struct aos_archive_load_info {
+    uint32_t rank;         /* scaling rank: manifest rank / lora_rank, else 4 */
+    uint32_t tensor_rank;  /* rows of lora_A in the payload */
+    uint32_t storage_rank; /* arena columns: tensor_rank rounded up to a multiple of 8 */
+    float alpha;           /* manifest alpha / lora_alpha, else 16 */
+    uint32_t module_mask;  /* bit m: module m (aos_module order) loaded, at every layer */
+    uint32_t segment_id;
+    uint16_t backend_tag;
+    uint16_t reserved;
+    uint8_t weights_hash[32]; /* BLAKE3 of the selected payload */
+    uint8_t scope_hash[16];
+} aos_archive_load_info;
+/* LifecycleLoader::load_from_aos_static (crates/adapteros-lora-lifecycle/src/
+ * loader.rs:931-1070) into adapter slot id: layout, segment hashes (GPU),
+ * canonical segment present, scope_path required, segment chosen for
+ * `backend` ("mlx", "metal", "coreml", "canonical"; anything else or NULL =
+ * canonical), per_layer_hashes and weights_hash checked when present; the
+ * payload's lora_a.<m> / lora_b.<m> (or <m>.lora_A / <m>.lora_B) tensors load
+ * under the MLX backend's rules (mlx-ffi/src/backend.rs:1017-1200) and apply
+ * at every layer; LoRA scale = alpha / rank.  info may be NULL. */
+int aos_adapter_load_aos(aos_ctx* ctx, uint16_t id, const void* data, uint64_t len, const char* backend,
+                         aos_archive_load_info* info);
+
+/* ---- GPU buffer fingerprints (FusedKernels::verify_adapter_buffers /
+ * store_gpu_fingerprint / verify_gpu_fingerprint, crates/adapteros-lora-
+ * kernel-api/src/lib.rs:440-508; GpuBufferFingerprint, kernel-mtl/src/
+ * vram.rs:20-80).  An adapter's buffer is, for every layer and LoRA-enabled
+ * module (aos_module order), its lora_A [rank][in] then its lora_B
+ * [out][rank], bf16 row-major, as read back from the arena.  Samples are the
+ * first, last and middle 4 KB (the whole buffer when smaller; the middle
+ * window starts at (size - window) / 2). */
+int aos_adapter_verify_buffers(aos_ctx* ctx, uint16_t id, uint64_t* buffer_bytes, void* first, void* last,
+                               void* mid, uint32_t* sample_bytes);
+/* BLAKE3(first || last || mid) on the GPU: GpuBufferFingerprint::new's
+ * checkpoint hash.  hash: 32 bytes. */
+int aos_adapter_fingerprint(aos_ctx* ctx, uint16_t id, uint64_t* buffer_bytes, uint8_t* hash);
+/* Baseline per adapter id (64 hex digits; stored lower-case). */
+int aos_store_gpu_fingerprint(aos_ctx* ctx, uint16_t id, uint64_t buffer_bytes, const char* checkpoint_hash_hex);
+/* *matches = 1 when a baseline exists with the same size and the same hex
+ * string, else 0 (no baseline reads as 0, as in the reference). */
+int aos_verify_gpu_fingerprint(aos_ctx* ctx, uint16_t id, uint64_t buffer_bytes, const char* checkpoint_hash_hex,
+                               int* matches);
+
 /* ---- prefill (the prompt path) ---------------------------------------------
  * InferencePipeline's prompt pass (inference_pipeline.rs:983-1154, MLX
  * forward over the prompt, mlx_cpp_wrapper_real.cpp:3338-3559 with T > 1):

@@ -106,6 +106,9 @@ def lib():
         L.oracle_rope_table.argtypes = [C.c_uint32, C.c_float, C.c_uint32, C.c_uint32, C.c_void_p]
         L.oracle_bf16_to_f32.restype = C.c_float
         L.oracle_bf16_to_f32.argtypes = [C.c_uint16]
+        L.oracle_blake3.argtypes = [C.c_void_p, C.c_uint64, C.c_void_p]
+        L.oracle_blake3_incremental.argtypes = [C.c_void_p, C.c_uint64, C.c_void_p]
+        L.oracle_aos_validate.argtypes = [C.c_void_p, C.c_uint64, C.c_void_p]
         L.oracle_f32_to_bf16.restype = C.c_uint16
         L.oracle_f32_to_bf16.argtypes = [C.c_float]
         _lib = L
@@ -117,6 +120,29 @@ def _p(a):
 
 
 # ------------------------------------------------------------------ router
+def blake3(data: bytes, incremental=False) -> bytes:
+    """BLAKE3 digest (B3Hash::hash, adapteros-infra-common/src/hash.rs:22-27;
+    the `blake3` crate 1.8.3 restated in aos_archive_oracle.cpp)."""
+    buf = C.create_string_buffer(bytes(data), max(1, len(data)))
+    out = C.create_string_buffer(32)
+    (lib().oracle_blake3_incremental if incremental else lib().oracle_blake3)(buf, len(data), out)
+    return out.raw
+
+
+AOS_RULES = {0: "ok", 1: "too small", 2: "bad magic", 3: "index offset", 4: "reserved bytes", 5: "no index flag",
+             6: "index beyond file", 7: "index size", 8: "manifest beyond file", 9: "manifest overlaps index",
+             10: "backend tag", 11: "segment overlaps index", 12: "segment overlaps manifest",
+             13: "segment beyond file", 14: "segment hash"}
+
+
+def aos_validate(data: bytes):
+    """open_aos (adapteros-aos/src/writer.rs:407-558): (rule code, n_segments)."""
+    buf = C.create_string_buffer(bytes(data), max(1, len(data)))
+    n = C.c_uint32(0)
+    rc = lib().oracle_aos_validate(buf, len(data), C.byref(n))
+    return int(rc), int(n.value)
+
+
 def quantize_gate(g: float) -> int:
     """quantization.rs:172-175."""
     return int(lib().oracle_quantize_gate(float(g)))
