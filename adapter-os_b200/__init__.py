@@ -142,6 +142,7 @@ def lib():
             "aos_profile_read": (C.c_int, [vp, vp, C.c_int]),
             "aos_health_check": (C.c_int, [vp]),
             "aos_attest_determinism": (C.c_int, [vp, vp]),
+            "aos_sample_dev": (C.c_int, [vp, u32, u32, u64, vp, vp, vp, vp]),
             "aos_archive_parse": (C.c_int, [vp, u64, vp, vp, u32]),
             "aos_blake3": (C.c_int, [vp, vp, u64, C.c_int, vp]),
             "aos_archive_verify": (C.c_int, [vp, vp, u64, vp]),
@@ -232,6 +233,121 @@ def archive_parse(data: bytes):
            for s in segs[:info.n_segments]]
     return {"flags": info.flags, "n_segments": info.n_segments, "manifest_offset": info.manifest_offset,
             "manifest_size": info.manifest_size}, out
+
+
+class SampleParams(C.Structure):
+    """aos_sample_params: Generator's temperature / top_k / top_p (generation.rs:9-21)."""
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_uint32), ("top_p", C.c_float), ("flags", C.c_uint32)]
+
+
+SAMPLE_GREEDY, SAMPLE_TOP_K, SAMPLE_TOP_P = 1, 2, 4
+
+
+def sample_dev(logits, u=None, temperature=1.0, top_k=None, top_p=None, greedy=False, out=None, stream=None):
+    """Next token per row of device logits [T, V] (f32) on the GPU:
+    Generator::next_token (or greedy) of lora-worker/src/generation.rs:321-490
+    with u [T] (device f32) as each row's uniform draw.  Returns uint32 [T]."""
+    import torch
+    T, V = logits.shape
+    if out is None:
+        out = torch.empty(T, dtype=torch.int32, device=logits.device)
+    flags = (SAMPLE_GREEDY if greedy else 0) | (SAMPLE_TOP_K if top_k is not None else 0) | \
+            (SAMPLE_TOP_P if top_p is not None else 0)
+    prm = SampleParams(float(temperature), int(top_k or 0), float(top_p or 0.0), flags)
+    if stream is None:
+        stream = torch.cuda.current_stream(logits.device).cuda_stream
+    rc = lib().aos_sample_dev(logits.data_ptr(), T, V, logits.stride(0), C.byref(prm),
+                              u.data_ptr() if u is not None else None, out.data_ptr(), stream)
+    if rc != 0:
+        raise AosError(rc, last_error())
+    return out
+
+
+def _hkdf_sha256(ikm: bytes, info: bytes, n=32) -> bytes:
+    """HKDF-SHA256 with no salt (RFC 5869), as derive_seed uses it (adapteros-core/src/seed.rs:986-1016)."""
+    import hashlib
+    import hmac
+    prk = hmac.new(bytes(32), ikm, hashlib.sha256).digest()
+    okm, block, i = b"", b"", 1
+    while len(okm) < n:
+        block = hmac.new(prk, block + info + bytes([i]), hashlib.sha256).digest()
+        okm += block
+        i += 1
+    return okm[:n]
+
+
+class DeterministicRng:
+    """lora-worker/src/deterministic_rng.rs: ChaCha20Rng (rand_chacha 0.3) seeded
+    with derive_seed(seed, label); gen_f32 is rand 0.8's Standard f32
+    ((next_u32 >> 8) * 2^-24).  The keystream comes from the `cryptography`
+    package's ChaCha20 with a zero counter and nonce (rand_chacha's stream 0)."""
+
+    def __init__(self, seed32: bytes, label: str):
+        from cryptography.hazmat.primitives.ciphers import Cipher, algorithms
+        self.seed = _hkdf_sha256(bytes(seed32), label.encode())
+        self._enc = Cipher(algorithms.ChaCha20(self.seed, bytes(16)), mode=None).encryptor()
+        self._buf = b""
+
+    def next_u32(self) -> int:
+        if len(self._buf) < 4:
+            self._buf += self._enc.update(bytes(256))
+        v = int.from_bytes(self._buf[:4], "little")
+        self._buf = self._buf[4:]
+        return v
+
+    def gen_f32(self) -> float:
+        return float(np.float32(self.next_u32() >> 8) * np.float32(1.0 / (1 << 24)))
+
+
+class Generator:
+    """Generator (lora-worker/src/generation.rs): temperature, top-k, top-p and a
+    seeded RNG; the sampling itself runs on the GPU (sample_dev)."""
+
+    def __init__(self, seed: bytes = bytes(32), deterministic=False):
+        self.base_seed = bytes(seed)
+        self.rng = DeterministicRng(self.base_seed, "sampling")
+        self.temperature, self.top_k, self.top_p = 1.0, None, None
+        self.deterministic = deterministic
+
+    @staticmethod
+    def new_deterministic(seed_global: bytes, context: str):
+        if len(seed_global) != 32:
+            raise AosError(-1, "new_deterministic: a 32-byte global seed is required here")
+        g = Generator(_hkdf_sha256(seed_global, context.encode()), deterministic=True)
+        return g
+
+    def with_temperature(self, t):
+        self.temperature = max(float(np.float32(t)), 0.01)
+        return self
+
+    def with_top_k(self, k):
+        self.top_k = int(k)
+        return self
+
+    def with_top_p(self, p):
+        self.top_p = min(max(float(p), 0.0), 1.0)
+        return self
+
+    def reseed_for_step(self, step: int):
+        if self.deterministic:  # derive_seed_indexed(base, "sample", step)
+            self.rng = DeterministicRng(_hkdf_sha256(self.base_seed, f"sample:{step}".encode()), "sampling")
+
+    def next_tokens_dev(self, logits, generators=None):
+        """One token per row of device logits; row r draws from generators[r] (default: self)."""
+        import torch
+        gens = generators or [self] * logits.shape[0]
+        u = torch.tensor([g.rng.gen_f32() for g in gens], dtype=torch.float32, device=logits.device)
+        return sample_dev(logits, u, self.temperature, self.top_k, self.top_p)
+
+    def next_token(self, logits) -> int:
+        import torch
+        x = logits if hasattr(logits, "data_ptr") else torch.tensor(np.asarray(logits, np.float32), device="cuda")
+        return int(self.next_tokens_dev(x.reshape(1, -1).float().contiguous())[0].item())
+
+    def greedy(self, logits) -> int:
+        import torch
+        x = logits if hasattr(logits, "data_ptr") else torch.tensor(np.asarray(logits, np.float32), device="cuda")
+        return int(sample_dev(x.reshape(1, -1).float().contiguous(), greedy=True)[0].item())
 
 
 def shard_unique_id() -> bytes:
@@ -454,6 +570,22 @@ class CudaKernels:
             raise AosError(rc, last_error(self.ctx))
         return rc
 
+    def _ordered(self, stream, call):
+        """Runs call(stream).  With stream=None the call goes on the context's
+        own (non-blocking) stream, ordered after the work already queued on
+        torch's current stream and before the work queued on it later, so
+        tensors made and read by torch around the call are safe."""
+        if stream is not None:
+            return call(stream)
+        import torch
+        cur = torch.cuda.current_stream(self.cfg.device)
+        ext = torch.cuda.ExternalStream(self.stream(), device=cur.device)
+        ext.wait_stream(cur)
+        try:
+            return call(None)
+        finally:
+            cur.wait_stream(ext)
+
     # -- identity -------------------------------------------------------
     def device_name(self) -> str:
         return self._L.aos_device_name(self.ctx).decode()
@@ -585,8 +717,8 @@ class CudaKernels:
     def run_step_batch_dev(self, rings, token_ids, seq_ids, logits=None, hidden=None, stream=None):
         """Device form: rings/token_ids/logits/hidden are torch CUDA tensors; seq_ids a host array."""
         sid = np.ascontiguousarray(seq_ids, np.uint64)
-        self._check(self._L.aos_run_step_batch_dev(self.ctx, _p(rings), _p(token_ids), _p(sid), len(sid),
-                                                  _p(logits), _p(hidden), stream))
+        self._ordered(stream, lambda st: self._check(self._L.aos_run_step_batch_dev(
+            self.ctx, _p(rings), _p(token_ids), _p(sid), len(sid), _p(logits), _p(hidden), st)))
 
     # -- safetensors loading --------------------------------------------------
     def load_adapter_safetensors(self, adapter_id, data: bytes, rank=0, alpha=0.0, target_modules=None):
@@ -662,8 +794,78 @@ class CudaKernels:
         for each sequence's last token, optional); seq_ids/n_tok host arrays."""
         sid = np.ascontiguousarray(seq_ids, np.uint64)
         nt = np.ascontiguousarray(n_tok, np.uint32)
-        self._check(self._L.aos_prefill_dev(self.ctx, len(sid), _p(sid), _p(nt), _p(rings), _p(token_ids),
-                                           _p(logits), stream))
+        self._ordered(stream, lambda st: self._check(self._L.aos_prefill_dev(
+            self.ctx, len(sid), _p(sid), _p(nt), _p(rings), _p(token_ids), _p(logits), st)))
+
+    # -- the worker's generation loop ---------------------------------------
+    def generate_tokens(self, generators, stable_ids, initial_tokens, max_tokens, eos_token, seq_ids, k=4):
+        """Generator::generate_tokens (lora-worker/src/generation.rs:226-310),
+        batched over sequences: each step reseeds every live sequence's
+        generator for the step, routes with uniform priors 1/N over the
+        adapters (ring position = current length - 1), runs one decode step for
+        the live sequences' last tokens, samples on the GPU, and drops a
+        sequence when it draws eos_token.  The prompt up to its last token is
+        cached first (prefill), so a step's input sits at position len - 1 as
+        the reference's IoBuffers.position says.  Returns the token lists."""
+        import torch
+        dev = torch.device("cuda", self.cfg.device)
+        st = self.stream()  # routing, steps, sampling and torch's own copies all in the context's stream order
+        with torch.cuda.stream(torch.cuda.ExternalStream(st, device=dev)):
+            return self._generate(generators, stable_ids, initial_tokens, max_tokens, eos_token, seq_ids, k, dev, st)
+
+    def _generate(self, generators, stable_ids, initial_tokens, max_tokens, eos_token, seq_ids, k, dev, st):
+        import torch
+        n, N = len(initial_tokens), len(stable_ids)
+        toks = [list(map(int, t)) for t in initial_tokens]
+        if any(len(t) == 0 for t in toks):
+            raise AosError(-1, "Token sequence cannot be empty during generation")
+        sids = torch.tensor(np.asarray(stable_ids, np.uint64).view(np.int64), device=dev)
+        prior = float(np.float32(1.0) / np.float32(N))
+
+        def rings_for(positions):
+            T = len(positions)
+            rings = torch.zeros((T, 40), dtype=torch.uint8, device=dev)
+            route_batch_dev(torch.full((T, N), prior, dtype=torch.float32, device=dev), sids, rings, k=k,
+                            positions=torch.tensor(positions, dtype=torch.int32, device=dev), stream=st)
+            return rings
+
+        for s, t in zip(seq_ids, toks):
+            self.kv_alloc(int(s), len(t) + int(max_tokens))
+        pre = [i for i in range(n) if len(toks[i]) > 1]
+        if pre:
+            pos = [p for i in pre for p in range(len(toks[i]) - 1)]
+            ids = torch.tensor([x for i in pre for x in toks[i][:-1]], dtype=torch.int32, device=dev)
+            self.prefill_dev([seq_ids[i] for i in pre], [len(toks[i]) - 1 for i in pre], rings_for(pos), ids,
+                             stream=st)
+        logits = torch.empty((n, self.vocab), dtype=torch.float32, device=dev)
+        active = list(range(n))
+        for step in range(int(max_tokens)):
+            if not active:
+                break
+            for i in active:
+                generators[i].reseed_for_step(step)
+            T = len(active)
+            rings = rings_for([len(toks[i]) - 1 for i in active])
+            last = torch.tensor([toks[i][-1] for i in active], dtype=torch.int32, device=dev)
+            self.run_step_batch_dev(rings, last, [seq_ids[i] for i in active], logits=logits[:T], stream=st)
+            nxt = np.zeros(T, np.int64)
+            groups = {}
+            for j, i in enumerate(active):  # rows sharing sampling settings go in one launch
+                g = generators[i]
+                groups.setdefault((g.temperature, g.top_k, g.top_p), []).append(j)
+            for rows in groups.values():
+                sub = logits[torch.tensor(rows, device=dev)]
+                lead = generators[active[rows[0]]]
+                got = lead.next_tokens_dev(sub, [generators[active[j]] for j in rows]).cpu().numpy()
+                nxt[rows] = got
+            still = []
+            for j, i in enumerate(active):
+                if int(nxt[j]) == int(eos_token):
+                    continue
+                toks[i].append(int(nxt[j]))
+                still.append(i)
+            active = still
+        return toks
 
     # -- adapter-sharded step ---------------------------------------------
     def shard_init(self, rank, world, unique_id: bytes):
@@ -677,13 +879,13 @@ class CudaKernels:
         """Decode step of this rank's home tokens (collective; same T on every
         rank).  Arguments as run_step_batch_dev; rings carry global adapter ids."""
         sid = np.ascontiguousarray(seq_ids, np.uint64)
-        self._check(self._L.aos_run_step_sharded_dev(self.ctx, _p(rings), _p(token_ids), _p(sid), len(sid),
-                                                    _p(logits), _p(hidden), stream))
+        self._ordered(stream, lambda st: self._check(self._L.aos_run_step_sharded_dev(
+            self.ctx, _p(rings), _p(token_ids), _p(sid), len(sid), _p(logits), _p(hidden), st)))
 
     def layer_step_dev(self, layer, rings, seq_ids, hidden, advance=False, stream=None):
         sid = np.ascontiguousarray(seq_ids, np.uint64)
-        self._check(self._L.aos_layer_step_dev(self.ctx, layer, _p(rings), _p(sid), len(sid), _p(hidden),
-                                              int(advance), stream))
+        self._ordered(stream, lambda st: self._check(self._L.aos_layer_step_dev(
+            self.ctx, layer, _p(rings), _p(sid), len(sid), _p(hidden), int(advance), st)))
 
     def run_step(self, ring: RouterRing, io: IoBuffers):
         """FusedKernels::run_step for one sequence: every id in io.input_ids is

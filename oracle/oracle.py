@@ -109,6 +109,11 @@ def lib():
         L.oracle_blake3.argtypes = [C.c_void_p, C.c_uint64, C.c_void_p]
         L.oracle_blake3_incremental.argtypes = [C.c_void_p, C.c_uint64, C.c_void_p]
         L.oracle_aos_validate.argtypes = [C.c_void_p, C.c_uint64, C.c_void_p]
+        L.oracle_greedy.restype = C.c_uint32
+        L.oracle_greedy.argtypes = [C.c_void_p, C.c_uint32]
+        L.oracle_sample.restype = C.c_uint32
+        L.oracle_sample.argtypes = [C.c_void_p, C.c_uint32, C.c_float, C.c_int, C.c_uint32, C.c_int, C.c_float,
+                                    C.c_float]
         L.oracle_f32_to_bf16.restype = C.c_uint16
         L.oracle_f32_to_bf16.argtypes = [C.c_float]
         _lib = L
@@ -141,6 +146,25 @@ def aos_validate(data: bytes):
     n = C.c_uint32(0)
     rc = lib().oracle_aos_validate(buf, len(data), C.byref(n))
     return int(rc), int(n.value)
+
+
+def sample(logits, u=None, temperature=1.0, top_k=None, top_p=None, greedy=False):
+    """Generator::next_token / greedy (lora-worker/src/generation.rs:321-490)
+    per row of logits [T, V] f32; u [T] uniform draws.  Returns uint32 [T]."""
+    x = np.ascontiguousarray(logits, np.float32)
+    if x.ndim == 1:
+        x = x[None]
+    T, V = x.shape
+    out = np.zeros(T, np.uint32)
+    for t in range(T):
+        row = x[t]
+        if greedy:
+            out[t] = lib().oracle_greedy(_p(row), V)
+        else:
+            out[t] = lib().oracle_sample(_p(row), V, float(temperature), int(top_k is not None),
+                                         int(top_k or 0), int(top_p is not None), float(top_p or 0.0),
+                                         float(u[t]))
+    return out
 
 
 def quantize_gate(g: float) -> int:
