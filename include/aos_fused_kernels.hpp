@@ -165,6 +165,45 @@ class CudaKernels final : public FusedKernels {
                       ctx_);
     }
 
+    // .aos archive into adapter slot id (LifecycleLoader::load_from_aos_static
+    // + the MLX adapter rules); backend: "mlx", "metal", "coreml", "canonical".
+    AosError load_adapter_aos(uint16_t id, const std::vector<uint8_t>& archive, const char* backend = "canonical",
+                              aos_archive_load_info* info = nullptr) {
+        return status(aos_adapter_load_aos(ctx_, id, archive.data(), archive.size(), backend, info), ctx_);
+    }
+
+    // FusedKernels::verify_adapter_buffers / store_gpu_fingerprint /
+    // verify_gpu_fingerprint (kernel-api/src/lib.rs:440-508).
+    AosError verify_adapter_buffers(uint16_t id, uint64_t* bytes, std::vector<uint8_t>& first,
+                                    std::vector<uint8_t>& last, std::vector<uint8_t>& mid) {
+        first.assign(4096, 0);
+        last.assign(4096, 0);
+        mid.assign(4096, 0);
+        uint32_t n = 0;
+        AosError e = status(aos_adapter_verify_buffers(ctx_, id, bytes, first.data(), last.data(), mid.data(), &n),
+                            ctx_);
+        first.resize(n);
+        last.resize(n);
+        mid.resize(n);
+        return e;
+    }
+    AosError store_gpu_fingerprint(uint16_t id, uint64_t bytes, const std::string& hex) {
+        return status(aos_store_gpu_fingerprint(ctx_, id, bytes, hex.c_str()), ctx_);
+    }
+    AosError verify_gpu_fingerprint(uint16_t id, uint64_t bytes, const std::string& hex, bool* matches) const {
+        int m = 0;
+        AosError e = status(aos_verify_gpu_fingerprint(ctx_, id, bytes, hex.c_str(), &m), ctx_);
+        *matches = m != 0;
+        return e;
+    }
+
+    // Next tokens of device logits rows (Generator::next_token / greedy on the
+    // device); u: device uniform draws, one per row (the caller's RNG).
+    static AosError sample_dev(const float* logits_dev, uint32_t rows, uint32_t vocab, const aos_sample_params& p,
+                               const float* u_dev, uint32_t* tokens_dev, void* stream = nullptr) {
+        return status(aos_sample_dev(logits_dev, rows, vocab, vocab, &p, u_dev, tokens_dev, stream), nullptr);
+    }
+
     // Adapter-sharded decode: join the group once (collective), then every
     // rank calls run_step_sharded_dev with the same number of home tokens.
     AosError shard_init(uint32_t rank, uint32_t world, const void* unique_id) {
