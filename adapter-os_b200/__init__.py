@@ -88,8 +88,57 @@ class DeterminismReport(C.Structure):
     _fields_ = [
         ("backend", C.c_char * 32), ("device_name", C.c_char * 64), ("sm_major", C.c_uint32),
         ("sm_minor", C.c_uint32), ("fast_math", C.c_uint32), ("float_atomics", C.c_uint32),
-        ("fixed_reduction_order", C.c_uint32), ("kernel_build_id", C.c_char * 64),
+        ("fixed_reduction_order", C.c_uint32), ("kernel_build_id", C.c_char * 65),
+        ("compiler_flags", C.c_char * 512), ("runtime_version", C.c_char * 64), ("device_id", C.c_char * 64),
+        ("rng_seed_method", C.c_uint32), ("floating_point_mode", C.c_uint32), ("determinism_level", C.c_uint32),
+        ("deterministic", C.c_uint32),
     ]
+
+
+RNG_METHODS = ("HkdfSeeded", "FixedSeed", "SystemEntropy")
+FP_MODES = ("Deterministic", "FastMath", "Unknown")
+DET_LEVELS = ("none", "bounded_tolerance", "bit_exact")
+
+
+def validate_report(rep: dict):
+    """DeterminismReport::validate (kernel-api/src/attestation.rs:163-233):
+    the list of violations (empty = valid)."""
+    errors = []
+    if not rep["deterministic"]:
+        errors.append("Overall deterministic flag is false")
+    if rep["deterministic"] and rep["determinism_level"] == "none":
+        errors.append("Determinism level must be deterministic when deterministic=true")
+    if not rep["deterministic"] and rep["determinism_level"] != "none":
+        errors.append("Determinism level must be none when deterministic=false")
+    if rep["rng_seed_method"] == "SystemEntropy":
+        errors.append("RNG seeding method SystemEntropy is not deterministic")
+    if rep["floating_point_mode"] != "Deterministic":
+        errors.append(f"Floating-point mode {rep['floating_point_mode']} is not deterministic")
+    for flag in rep["compiler_flags"]:
+        for bad in ("-ffast-math", "-funsafe-math-optimizations"):
+            if bad in flag:
+                errors.append(f"Forbidden compiler flag: {flag}")
+    if not rep.get("kernel_hash"):
+        errors.append("the backend must provide a kernel hash")
+    return errors
+
+
+def attestation_hash_input(rep: dict) -> bytes:
+    """The bytes DeterminismReport::to_attestation_hash hashes
+    (attestation.rs:254-300): u32-LE length-prefixed components -- backend,
+    RNG method, FP mode, level, kernel hash bytes (the metallib_hash slot),
+    verified flag, runtime version, device id, then the compiler flags sorted."""
+    comps = [rep["backend_type"].encode(), rep["rng_seed_method"].encode(), rep["floating_point_mode"].encode(),
+             rep["determinism_level"].encode()]
+    if rep.get("kernel_hash"):
+        comps.append(bytes.fromhex(rep["kernel_hash"]))
+    comps.append(bytes([1 if rep.get("kernel_verified") else 0]))
+    if rep.get("runtime_version"):
+        comps.append(rep["runtime_version"].encode())
+    if rep.get("device_id"):
+        comps.append(rep["device_id"].encode())
+    comps += [f.encode() for f in sorted(rep["compiler_flags"])]
+    return b"".join(len(c).to_bytes(4, "little") + c for c in comps)
 
 
 def lib():
@@ -594,13 +643,32 @@ class CudaKernels:
         return self._L.aos_stream(self.ctx)
 
     def attest_determinism(self) -> dict:
+        """FusedKernels::attest_determinism (kernel-api/src/lib.rs:383): the
+        DeterminismReport fields, its validate() result and its attestation
+        hash (BLAKE3 on the GPU).  kernel_verified: the library's build stamp
+        equals the stamp of the kernel sources beside it (False where the
+        sources are not deployed)."""
         r = DeterminismReport()
         self._check(self._L.aos_attest_determinism(self.ctx, C.byref(r)))
-        return {"backend": r.backend.decode(), "device": r.device_name.decode(),
-                "sm": (r.sm_major, r.sm_minor), "fast_math": bool(r.fast_math),
-                "float_atomics": bool(r.float_atomics),
-                "fixed_reduction_order": bool(r.fixed_reduction_order),
-                "build": r.kernel_build_id.decode()}
+        stamp = r.kernel_build_id.decode()
+        try:
+            from . import build as _b
+            verified = _b.current_stamp() == stamp
+        except Exception:
+            verified = False
+        rep = {"backend": r.backend.decode(), "backend_type": "Cuda", "device": r.device_name.decode(),
+               "sm": (r.sm_major, r.sm_minor), "fast_math": bool(r.fast_math),
+               "float_atomics": bool(r.float_atomics),
+               "fixed_reduction_order": bool(r.fixed_reduction_order),
+               "build": stamp, "kernel_hash": stamp if len(stamp) == 64 else "", "kernel_verified": verified,
+               "compiler_flags": r.compiler_flags.decode().split(),
+               "runtime_version": r.runtime_version.decode(), "device_id": r.device_id.decode(),
+               "rng_seed_method": RNG_METHODS[r.rng_seed_method],
+               "floating_point_mode": FP_MODES[r.floating_point_mode],
+               "determinism_level": DET_LEVELS[r.determinism_level], "deterministic": bool(r.deterministic)}
+        rep["violations"] = validate_report(rep)
+        rep["attestation_hash"] = self.blake3(attestation_hash_input(rep))
+        return rep
 
     def get_metrics(self) -> dict:
         m = Metrics()

@@ -64,6 +64,12 @@ def _stamp(paths):
     return h.hexdigest()
 
 
+def current_stamp() -> str:
+    """Stamp of the kernel sources and flags as they are now (the value a fresh
+    build bakes into the library)."""
+    return _stamp(_sources() + _headers())
+
+
 def build(verbose: bool = False, force: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     srcs = _sources()
@@ -77,7 +83,10 @@ def build(verbose: bool = False, force: bool = False) -> str:
     procs = []
     for s in srcs:
         o = os.path.join(BUILD, os.path.basename(s) + ".o")
-        cmd = [NVCC, *NVCC_FLAGS, "-c", s, "-o", o]
+        # the build stamp (sources + flags) and the flags themselves go into
+        # the library for aos_attest_determinism
+        flags_str = " ".join(NVCC_FLAGS).replace('"', "")
+        cmd = [NVCC, *NVCC_FLAGS, f'-DAOS_BUILD_STAMP="{stamp}"', f'-DAOS_BUILD_FLAGS="{flags_str}"', "-c", s, "-o", o]
         if verbose:
             print(" ".join(cmd))
         procs.append((s, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT)))

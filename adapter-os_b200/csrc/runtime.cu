@@ -1800,7 +1800,26 @@ int aos_attest_determinism(const aos_ctx* c, aos_determinism_report* out) {
     out->fast_math = 0;
     out->float_atomics = 0;
     out->fixed_reduction_order = 1;
-    std::snprintf(out->kernel_build_id, sizeof(out->kernel_build_id), "%s", aos_version());
+#ifndef AOS_BUILD_STAMP
+#define AOS_BUILD_STAMP "unstamped"
+#endif
+#ifndef AOS_BUILD_FLAGS
+#define AOS_BUILD_FLAGS ""
+#endif
+    std::snprintf(out->kernel_build_id, sizeof(out->kernel_build_id), "%s", AOS_BUILD_STAMP);
+    std::snprintf(out->compiler_flags, sizeof(out->compiler_flags), "%s", AOS_BUILD_FLAGS);
+    int rt = 0, drv = 0;
+    cudaRuntimeGetVersion(&rt);
+    cudaDriverGetVersion(&drv);
+    std::snprintf(out->runtime_version, sizeof(out->runtime_version), "cuda runtime %d.%d, driver api %d.%d", rt / 1000,
+                  (rt % 1000) / 10, drv / 1000, (drv % 1000) / 10);
+    char bus[32] = {0};
+    cudaDeviceGetPCIBusId(bus, sizeof bus, c->device);
+    std::snprintf(out->device_id, sizeof(out->device_id), "cuda:%d %s", c->device, bus);
+    out->rng_seed_method = 0;       // the device path draws no random numbers; routing and sampling take the caller's
+    out->floating_point_mode = 0;   // IEEE division and square root, no flush-to-zero, no fast-math
+    out->determinism_level = 2;     // bit-identical run to run (fixed-order reductions, no float atomics)
+    out->deterministic = 1;
     return AOS_OK;
 }
 

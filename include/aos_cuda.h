@@ -105,14 +105,23 @@ typedef struct aos_metrics {           /* BackendMetrics (kernel-api/src/lib.rs:
     float last_step_ms;
 } aos_metrics;
 
-typedef struct aos_determinism_report { /* attestation.rs:130-460 (subset)            */
+typedef struct aos_determinism_report { /* DeterminismReport, attestation.rs:130-160 */
     char backend[32];
     char device_name[64];
     uint32_t sm_major, sm_minor;
     uint32_t fast_math;             /* 0: built without fast-math                     */
     uint32_t float_atomics;         /* 0: no floating-point atomics on any path       */
     uint32_t fixed_reduction_order; /* 1: every split reduction has a fixed order     */
-    char kernel_build_id[64];
+    char kernel_build_id[65];       /* kernel hash: SHA-256 (hex) of every kernel source and
+                                       header plus the compiler flags, fixed at build time
+                                       (the role of the Metal backend's metallib_hash) */
+    char compiler_flags[512];       /* the nvcc flags, space separated                */
+    char runtime_version[64];       /* CUDA runtime and driver versions               */
+    char device_id[64];             /* "cuda:<ordinal> <PCI bus id>"                  */
+    uint32_t rng_seed_method;       /* 0 HkdfSeeded (RngSeedingMethod)                */
+    uint32_t floating_point_mode;   /* 0 Deterministic (FloatingPointMode)            */
+    uint32_t determinism_level;     /* 2 BitExact (DeterminismLevel: 0 None, 1 Bounded) */
+    uint32_t deterministic;         /* 1                                              */
 } aos_determinism_report;
 
 typedef struct aos_ctx aos_ctx;
