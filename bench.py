@@ -38,9 +38,9 @@ CFG = dict(hidden=4096, n_heads=32, n_kv_heads=8, head_dim=128, intermediate=143
            n_adapters=128, ranks=(8, 16, 32, 64), K=4, batch=64, ctx_lo=512, ctx_hi=4096)
 METRIC = "decode tok/s, 8B-shape, K=4 of 128 LoRAs; LoRA+attn % of HBM roofline"
 # DRAM bytes (read + write) of one layer's four GEMM launches of this workload
-# (q/k/v 201.6 MB, o 101.8 MB, gate/up 534.5 MB, down 263.3 MB), from an ncu
-# capture of the 2-layer case: profiles/tc_gemm_kernel_decode_config3_2layer.md.
-GEMM_DRAM_BYTES_PER_LAYER = 1101.24e6
+# (q/k/v 199.0 MB, o 100.0 MB, gate/up 519.0 MB, down 261.9 MB), from an ncu
+# capture (dram__bytes_read.sum + dram__bytes_write.sum) of the 2-layer case.
+GEMM_DRAM_BYTES_PER_LAYER = 1079.93e6
 SEED = 20261201
 
 
