@@ -12,19 +12,19 @@
 // compression carries ROOT.
 //
 // Work decomposition (the host builds it, blake3_plan below):
-//   level 0  one CTA of 64 threads per 64 consecutive chunks of a message.
-//            The CTA stages its 64 KB in shared memory with coalesced 16-byte
-//            loads (a 257-word stride per chunk keeps thread t's word w in
-//            bank (t + w) mod 32), each thread compresses one chunk, and the
-//            64 chaining values are reduced pairwise to one subtree value.
-//   level k  one CTA per 64 consecutive nodes of the level below, reduced the
-//            same way, until a message has one task left: that task's top
+//   level 0  one CTA of 256 threads per 256 consecutive chunks of a message;
+//            each thread compresses one chunk, reading it with 16-byte loads
+//            (no shared-memory staging, so occupancy stays high for this
+//            integer-ALU-bound work), and the 256 chaining values are reduced
+//            pairwise to one subtree value in shared memory.
+//   level k  one CTA per 256 consecutive nodes of the level below, reduced
+//            the same way, until a message has one task left: that task's top
 //            compression is the root.
 // Pairing nodes (2i, 2i+1) and carrying an odd last node up unchanged at
 // every level builds exactly the specification's left-balanced tree, and a
-// 64-node group is an aligned subtree at every level, so CTAs never need to
+// 256-node group is an aligned subtree at every level, so CTAs never need to
 // see each other's nodes.  Every message of a batch advances one level per
-// launch; a batch of messages up to 64^L chunks long needs L + 1 launches.
+// launch; a batch of messages up to 256^L chunks long needs L + 1 launches.
 
 #include <algorithm>
 #include <cstring>
@@ -44,8 +44,7 @@ struct B3Task {
 
 namespace {
 
-constexpr int kB3Group = 64;   // chunks / nodes per CTA
-constexpr int kB3Stride = 257; // staged words per chunk
+constexpr int kB3Group = 256;  // chunks / nodes per CTA (one thread each)
 constexpr uint32_t kStart = 1, kEnd = 2, kParent = 4, kRoot = 8;
 
 __device__ __forceinline__ uint32_t rotr(uint32_t x, int n) { return __funnelshift_r(x, x, n); }
@@ -96,7 +95,7 @@ __device__ __forceinline__ void b3_iv(uint32_t h[8]) {
 }
 
 // Reduces cv[0..m) (shared memory) to cv[0]; the compression that leaves one
-// node carries ROOT when `root`.  All 64 threads call it.
+// node carries ROOT when `root`.  Every thread of the CTA calls it.
 __device__ void b3_reduce(uint32_t (*cv)[8], int m, bool root) {
     const int t = threadIdx.x;
     while (m > 1) {
@@ -134,46 +133,45 @@ __global__ void __launch_bounds__(kB3Group) b3_chunks_kernel(const uint8_t* __re
                                                               const B3Task* __restrict__ tasks,
                                                               uint32_t* __restrict__ nodes,
                                                               uint32_t* __restrict__ digests) {
-    extern __shared__ uint32_t sm[];  // [64][257] staged words, then [64][8] chaining values
-    uint32_t(*cv)[8] = reinterpret_cast<uint32_t(*)[8]>(sm + kB3Group * kB3Stride);
+    __shared__ uint32_t cv[kB3Group][8];
     const B3Task tk = tasks[blockIdx.x];
     const int t = threadIdx.x;
-    const uint64_t bytes = tk.len < (uint64_t)kB3Group * 1024 ? tk.len : (uint64_t)kB3Group * 1024;
+    const uint64_t cap = (uint64_t)kB3Group * 1024;
+    const uint64_t bytes = tk.len < cap ? tk.len : cap;
     const int nc = tk.len == 0 ? 1 : (int)((bytes + 1023) / 1024);
     const uint8_t* src = base + tk.src;
-    // stage the task's bytes; words past the message end are masked below
-    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-        const int n16 = (int)(bytes / 16);
-        for (int v = t; v < n16; v += kB3Group) {
-            const uint4 x = __ldg(reinterpret_cast<const uint4*>(src) + v);
-            uint32_t* d = sm + (v >> 6) * kB3Stride + (v & 63) * 4;
-            d[0] = x.x; d[1] = x.y; d[2] = x.z; d[3] = x.w;
-        }
-        uint8_t* sb = reinterpret_cast<uint8_t*>(sm);
-        for (int i = n16 * 16 + t; i < (int)bytes; i += kB3Group)
-            sb[(size_t)(i >> 10) * kB3Stride * 4 + (i & 1023)] = __ldg(src + i);
-    } else {
-        uint8_t* sb = reinterpret_cast<uint8_t*>(sm);
-        for (int i = t; i < (int)bytes; i += kB3Group)
-            sb[(size_t)(i >> 10) * kB3Stride * 4 + (i & 1023)] = __ldg(src + i);
-    }
-    __syncthreads();
     const bool single = tk.root && nc == 1;  // a one-chunk message: the chunk is the root
     if (t < nc) {
+        // each thread reads its own chunk straight from memory: 16-byte loads
+        // (the chunk's 64-byte blocks are consecutive, so the L1 line a load
+        // brings in serves the thread's next loads), bytes when unaligned
         const uint64_t left = bytes - (uint64_t)t * 1024;
         const uint32_t clen = left < 1024 ? (uint32_t)left : 1024u;
         const int nb = clen == 0 ? 1 : (int)((clen + 63) / 64);
-        const uint32_t* cw = sm + t * kB3Stride;
+        const uint8_t* cp = src + (size_t)t * 1024;
+        const bool vec = (reinterpret_cast<uintptr_t>(cp) & 15) == 0;
         uint32_t h[8];
         b3_iv(h);
         for (int b = 0; b < nb; ++b) {
             const uint32_t blen = min(64u, clen - 64u * b);
             uint32_t m[16];
+            if (vec && blen == 64) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int valid = (int)blen - 4 * i;  // bytes of word i inside the block
-                const uint32_t w = valid > 0 ? cw[16 * b + i] : 0u;
-                m[i] = valid >= 4 ? w : (valid > 0 ? w & ((1u << (8 * valid)) - 1u) : 0u);
+                for (int i = 0; i < 4; ++i) {
+                    const uint4 x = __ldg(reinterpret_cast<const uint4*>(cp + 64 * b) + i);
+                    m[4 * i] = x.x;
+                    m[4 * i + 1] = x.y;
+                    m[4 * i + 2] = x.z;
+                    m[4 * i + 3] = x.w;
+                }
+            } else {  // the message's last, partial block (zero padded), or an unaligned start
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    uint32_t w = 0;
+                    for (int k = 0; k < 4; ++k)
+                        if (4 * i + k < (int)blen) w |= (uint32_t)__ldg(cp + 64 * b + 4 * i + k) << (8 * k);
+                    m[i] = w;
+                }
             }
             uint32_t f = (b == 0 ? kStart : 0u) | (b + 1 == nb ? kEnd : 0u);
             if (single && b + 1 == nb) f |= kRoot;
@@ -260,11 +258,6 @@ static void blake3_plan(const uint64_t* offsets, const uint64_t* lens, int n_msg
     }
 }
 
-size_t blake3_smem_bytes() { return (size_t)kB3Group * kB3Stride * 4 + (size_t)kB3Group * 32; }
-
-cudaError_t blake3_configure() {
-    return cudaFuncSetAttribute(b3_chunks_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)blake3_smem_bytes());
-}
 
 // Digests of messages [base + offsets[i], + lens[i]) of device memory, into
 // host digests[i][32].  Synchronizes `s`.
@@ -288,13 +281,12 @@ int blake3_many(const uint8_t* d_base, const uint64_t* offsets, const uint64_t* 
     if (e == cudaSuccess) e = cudaMallocAsync((void**)&d_nodes, 2 * node_words * 4, s);
     if (e == cudaSuccess) e = cudaMallocAsync((void**)&d_dig, (size_t)n_msg * 32, s);
     if (e == cudaSuccess) e = cudaMemcpyAsync(d_tasks, all.data(), sizeof(B3Task) * n_tasks, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) e = blake3_configure();
     size_t t0 = 0;
     for (size_t l = 0; l < plan.levels.size() && e == cudaSuccess; ++l) {
         const unsigned grid = (unsigned)plan.levels[l].size();
         uint32_t* out = d_nodes + (l & 1) * node_words;
         if (l == 0) {
-            b3_chunks_kernel<<<grid, kB3Group, blake3_smem_bytes(), s>>>(d_base, d_tasks, out, d_dig);
+            b3_chunks_kernel<<<grid, kB3Group, 0, s>>>(d_base, d_tasks, out, d_dig);
         } else {
             const uint32_t* in = d_nodes + ((l - 1) & 1) * node_words;
             b3_level_kernel<<<grid, kB3Group, 0, s>>>(in, d_tasks + t0, out, d_dig);
