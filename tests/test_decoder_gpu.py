@@ -132,6 +132,29 @@ def test_decode_step_two_token_blocks():
     assert outs[0] == outs[1], "T=160 step differs run to run"
 
 
+@pytest.mark.parametrize("T", [1, 17, 64, 65, 127, 128, 129, 256])
+def test_decode_step_batch_sizes(T):
+    """Ragged batch sizes across the token-block and tile boundaries (one and
+    two MMA token blocks, T = 256 as the adapter owners run it): logits and
+    hidden states within tolerance of the oracle, and every appended K/V row
+    of the first and last token."""
+    rng = np.random.default_rng(100 + T)
+    ctx = tuple(int(x) for x in rng.integers(0, 40, size=T))
+    s = Setup(seed=T, ctx_lens=ctx, max_seq=64)
+    logits, hidden = s.gpu.run_step_batch(s.rings, s.tokens.astype(np.uint32), s.seq_ids, want_hidden=True)
+    ref_logits, ref_hidden = O.decode_step(s.m, s.ad, s.rings, s.tokens, s.kv)
+    assert_close(O.bf16_bits_to_f32(hidden), O.bf16_bits_to_f32(ref_hidden), f"hidden (T={T})")
+    assert_close(logits, ref_logits, f"logits (T={T})")
+    for t in {0, T - 1}:
+        pos = int(s.ctx_lens[t])
+        for l in range(s.m.n_layers):
+            gk, gv = s.gpu.kv_read(int(s.seq_ids[t]), l, pos, 1)
+            rk, rv = s.oracle_kv_row(t, l, pos)
+            assert_close(O.bf16_bits_to_f32(gk[0]), O.bf16_bits_to_f32(rk), f"k t={t} l={l} (T={T})")
+            assert_close(O.bf16_bits_to_f32(gv[0]), O.bf16_bits_to_f32(rv), f"v t={t} l={l} (T={T})")
+    s.gpu.close()
+
+
 def test_decode_bit_identical_run_to_run():
     outs = []
     for _ in range(2):
