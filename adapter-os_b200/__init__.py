@@ -192,6 +192,7 @@ def lib():
             "aos_health_check": (C.c_int, [vp]),
             "aos_attest_determinism": (C.c_int, [vp, vp]),
             "aos_sample_dev": (C.c_int, [vp, u32, u32, u64, vp, vp, vp, vp]),
+            "aos_debug_bounded_wait": (C.c_int, [vp, C.c_int]),
             "aos_archive_parse": (C.c_int, [vp, u64, vp, vp, u32]),
             "aos_blake3": (C.c_int, [vp, vp, u64, C.c_int, vp]),
             "aos_archive_verify": (C.c_int, [vp, vp, u64, vp]),

@@ -1753,6 +1753,23 @@ int aos_layer_step_dev(aos_ctx* c, uint32_t layer, const aos_router_ring* rings,
 }
 
 // ------------------------------------------------------------------ metrics etc.
+// Failure-path check: a kernel whose bounded wait can never be satisfied
+// (0: a global-counter spin, 1: an mbarrier wait) runs on the context's
+// stream; its time limit ends it, and the status comes back as a step's
+// would: AOS_ERR_TIMEOUT, with the context's device state cleared so the next
+// step runs normally.
+int aos_debug_bounded_wait(aos_ctx* c, int kind) {
+    if (!c || kind < 0 || kind > 1) return AOS_ERR_INVALID;
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    int* never = nullptr;
+    CTX_CUDA(c, cudaMallocAsync((void**)&never, sizeof(int), c->stream));
+    CTX_CUDA(c, cudaMemsetAsync(never, 0, sizeof(int), c->stream));
+    LAUNCH(c, tc_debug_wait(kind, never, c->d_err, c->stream));
+    CTX_CUDA(c, cudaFreeAsync(never, c->stream));
+    CTX_CUDA(c, cudaStreamSynchronize(c->stream));
+    return check_device_error(c);
+}
+
 int aos_debug_trace_read(aos_ctx* c, uint64_t* out, uint64_t n) {
     if (!c || !out) return AOS_ERR_INVALID;
     if (!c->d_trace) return c->fail(AOS_ERR_STATE, "tracing is off (set AOS_TC_TRACE before aos_init)");

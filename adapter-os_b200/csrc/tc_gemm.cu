@@ -1585,7 +1585,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
     if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(512));
 }
 
+// Runs one of the GEMM kernel's bounded waits against a condition that never
+// comes true, so that its time limit is what ends it: kind 0 spins on a
+// global counter that nothing increments (the grid barriers' spin_ge), kind 1
+// waits on a shared-memory mbarrier that nothing arrives on (the pipeline's
+// mbar_wait).  Either returns after kSpinLimitCycles with AOS_ERR_TIMEOUT in
+// *err, as a real stalled wait would.
+__global__ void debug_wait_kernel(int kind, const int* never, int* err) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    if (kind == 0) {
+        spin_ge(never, 1, err);
+    } else {
+        mbar_init(smem_u32(&bar), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_wait(smem_u32(&bar), 0, err);
+    }
+}
+
 }  // namespace
+
+cudaError_t tc_debug_wait(int kind, const int* never, int* err, cudaStream_t s) {
+    debug_wait_kernel<<<1, 32, 0, s>>>(kind, never, err);
+    return cudaGetLastError();
+}
 
 // ---------------------------------------------------------------- host side
 namespace {

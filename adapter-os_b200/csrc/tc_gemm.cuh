@@ -131,6 +131,8 @@ inline int tc_t_box(int T) { return tc_spread(T) ? 16 : (tc_t_pad(T) < kTcTok ? 
 int tc_prepare(TcParams& p, int smem_budget);
 // Launch on `grid` CTAs; every CTA must be resident at once (grid <= SM
 // count): the launch synchronises its CTAs through bounded grid barriers.
+// Failure-path check of the GEMM kernel's bounded waits (see tc_gemm.cu).
+cudaError_t tc_debug_wait(int kind, const int* never, int* err, cudaStream_t s);
 cudaError_t tc_launch(const TcParams& p, int grid, cudaStream_t stream);
 // Prefill GEMM: data-parallel tiles of 128 tokens over the whole K (no split),
 // for any T.  n_seg == 0 with sh_nseg > 0 is a shrink launch (gated hm out).

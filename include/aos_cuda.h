@@ -455,6 +455,11 @@ int aos_profile_read(aos_ctx* ctx, aos_profile* out, int reset);
  * qkv, o, gate/up, down; 4..7: their LoRA shrinks) of layer 0 writes per-CTA
  * %globaltimer stamps (256 slots per CTA); this copies n of them to host. */
 int aos_debug_trace_read(aos_ctx* ctx, uint64_t* out, uint64_t n);
+/* Failure-path check: runs one of the GEMM kernel's bounded waits against a
+ * condition nothing satisfies (kind 0: global-counter spin, 1: mbarrier wait);
+ * returns AOS_ERR_TIMEOUT after the wait's limit (about one second), with the
+ * context left usable. */
+int aos_debug_bounded_wait(aos_ctx* ctx, int kind);
 
 /* ---- metrics / health / attestation (lib.rs:383, 559-593) ---------------- */
 int aos_get_metrics(const aos_ctx* ctx, aos_metrics* out);
