@@ -31,166 +31,50 @@
 #include <vector>
 
 #include "common.cuh"
+#include "json.cuh"
 #include "loader.cuh"
 
 namespace aos {
 namespace {
-
-// ---------------------------------------------------------------- JSON (header subset)
-struct Json {
-    const char* p;
-    const char* end;
-    std::string err;
-    void ws() {
-        while (p < end && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) ++p;
-    }
-    bool expect(char c) {
-        ws();
-        if (p < end && *p == c) {
-            ++p;
-            return true;
-        }
-        err = std::string("expected '") + c + "'";
-        return false;
-    }
-    bool str(std::string& out) {
-        ws();
-        if (p >= end || *p != '"') {
-            err = "expected a string";
-            return false;
-        }
-        ++p;
-        out.clear();
-        while (p < end && *p != '"') {
-            if (*p == '\\') {
-                if (++p >= end) break;
-                const char c = *p++;
-                if (c == 'u') {
-                    if (end - p < 4) break;
-                    unsigned v = 0;
-                    for (int i = 0; i < 4; ++i) {
-                        const char h = *p++;
-                        v = v * 16 + (unsigned)(h >= '0' && h <= '9' ? h - '0' : (h | 32) - 'a' + 10);
-                    }
-                    if (v < 0x80) out += (char)v;
-                    else if (v < 0x800) { out += (char)(0xC0 | (v >> 6)); out += (char)(0x80 | (v & 63)); }
-                    else { out += (char)(0xE0 | (v >> 12)); out += (char)(0x80 | ((v >> 6) & 63)); out += (char)(0x80 | (v & 63)); }
-                } else {
-                    out += c == 'n' ? '\n' : c == 't' ? '\t' : c == 'r' ? '\r' : c == 'b' ? '\b' : c == 'f' ? '\f' : c;
-                }
-            } else {
-                out += *p++;
-            }
-        }
-        if (p >= end) {
-            err = "unterminated string";
-            return false;
-        }
-        ++p;
-        return true;
-    }
-    bool num(int64_t& v) {
-        ws();
-        const char* s = p;
-        bool neg = false;
-        if (p < end && *p == '-') { neg = true; ++p; }
-        uint64_t x = 0;
-        while (p < end && *p >= '0' && *p <= '9') x = x * 10 + (uint64_t)(*p++ - '0');
-        if (p == s || (neg && p == s + 1)) {
-            err = "expected an integer";
-            return false;
-        }
-        v = neg ? -(int64_t)x : (int64_t)x;
-        return true;
-    }
-    bool skip() {  // any value
-        ws();
-        if (p >= end) { err = "truncated"; return false; }
-        if (*p == '"') { std::string s; return str(s); }
-        if (*p == '{' || *p == '[') {
-            const char close = *p == '{' ? '}' : ']';
-            const bool obj = *p == '{';
-            ++p;
-            ws();
-            if (p < end && *p == close) { ++p; return true; }
-            while (true) {
-                if (obj) {
-                    std::string k;
-                    if (!str(k) || !expect(':')) return false;
-                }
-                if (!skip()) return false;
-                ws();
-                if (p < end && *p == ',') { ++p; continue; }
-                return expect(close);
-            }
-        }
-        while (p < end && *p != ',' && *p != '}' && *p != ']') ++p;  // number / true / false / null
-        return true;
-    }
-};
 
 int st_parse(const uint8_t* d, uint64_t len, std::vector<StTensor>& out, const uint8_t** base, std::string& err) {
     if (!d || len < 8) { err = "safetensors: shorter than its 8-byte header length"; return AOS_ERR_INVALID; }
     uint64_t n = 0;
     for (int i = 7; i >= 0; --i) n = (n << 8) | d[i];
     if (n > len - 8) { err = "safetensors: header length exceeds the buffer"; return AOS_ERR_INVALID; }
-    Json j{reinterpret_cast<const char*>(d + 8), reinterpret_cast<const char*>(d + 8 + n), {}};
     *base = d + 8 + n;
     const uint64_t data_len = len - 8 - n;
     out.clear();
-    if (!j.expect('{')) { err = "safetensors header: " + j.err; return AOS_ERR_INVALID; }
-    j.ws();
-    if (j.p < j.end && *j.p == '}') return AOS_OK;
-    while (true) {
-        std::string name;
-        if (!j.str(name) || !j.expect(':')) { err = "safetensors header: " + j.err; return AOS_ERR_INVALID; }
-        if (name == "__metadata__") {
-            if (!j.skip()) { err = "safetensors header: " + j.err; return AOS_ERR_INVALID; }
-        } else {
-            StTensor t;
-            t.name = name;
-            bool have_dtype = false, have_shape = false, have_off = false;
-            if (!j.expect('{')) { err = "safetensors header: " + j.err; return AOS_ERR_INVALID; }
-            while (true) {
-                std::string key;
-                if (!j.str(key) || !j.expect(':')) { err = "safetensors header: " + j.err; return AOS_ERR_INVALID; }
-                if (key == "dtype") {
-                    if (!j.str(t.dtype)) { err = "safetensors header: " + j.err; return AOS_ERR_INVALID; }
-                    have_dtype = true;
-                } else if (key == "shape" || key == "data_offsets") {
-                    std::vector<int64_t> v;
-                    if (!j.expect('[')) { err = "safetensors header: " + j.err; return AOS_ERR_INVALID; }
-                    j.ws();
-                    if (j.p < j.end && *j.p == ']') ++j.p;
-                    else
-                        while (true) {
-                            int64_t x;
-                            if (!j.num(x)) { err = "safetensors header: " + j.err; return AOS_ERR_INVALID; }
-                            v.push_back(x);
-                            j.ws();
-                            if (j.p < j.end && *j.p == ',') { ++j.p; continue; }
-                            if (!j.expect(']')) { err = "safetensors header: " + j.err; return AOS_ERR_INVALID; }
-                            break;
-                        }
-                    if (key == "shape") { t.shape = v; have_shape = true; }
-                    else if (v.size() == 2 && v[0] >= 0 && v[1] >= v[0]) { t.b = (uint64_t)v[0]; t.e = (uint64_t)v[1]; have_off = true; }
-                } else if (!j.skip()) {
-                    err = "safetensors header: " + j.err;
-                    return AOS_ERR_INVALID;
-                }
-                j.ws();
-                if (j.p < j.end && *j.p == ',') { ++j.p; continue; }
-                if (!j.expect('}')) { err = "safetensors header: " + j.err; return AOS_ERR_INVALID; }
-                break;
-            }
-            if (!have_dtype || !have_shape || !have_off) { err = "safetensors: tensor " + name + " lacks dtype, shape or data_offsets"; return AOS_ERR_INVALID; }
-            if (t.e > data_len) { err = "safetensors: tensor " + name + " runs past the buffer"; return AOS_ERR_INVALID; }
-            out.push_back(std::move(t));
+    JVal h;
+    if (!parse_json(d + 8, n, h, err, "safetensors header")) return AOS_ERR_INVALID;
+    if (h.k != JVal::OBJ) { err = "safetensors header: not an object"; return AOS_ERR_INVALID; }
+    for (const auto& kv : h.o) {
+        if (kv.first == "__metadata__") continue;
+        const JVal& t = kv.second;
+        const JVal *dt = t.get("dtype"), *sh = t.get("shape"), *of = t.get("data_offsets");
+        if (!dt || dt->k != JVal::STR || !sh || sh->k != JVal::ARR || !of || of->k != JVal::ARR) {
+            err = "safetensors: tensor " + kv.first + " lacks dtype, shape or data_offsets";
+            return AOS_ERR_INVALID;
         }
-        j.ws();
-        if (j.p < j.end && *j.p == ',') { ++j.p; continue; }
-        if (!j.expect('}')) { err = "safetensors header: " + j.err; return AOS_ERR_INVALID; }
-        break;
+        StTensor x;
+        x.name = kv.first;
+        x.dtype = dt->s;
+        for (const JVal& e : sh->a) {
+            if (e.k != JVal::NUM || !e.n_uint || e.u > (uint64_t)INT64_MAX) {
+                err = "safetensors: tensor " + kv.first + ": shape must list non-negative integers";
+                return AOS_ERR_INVALID;
+            }
+            x.shape.push_back((int64_t)e.u);
+        }
+        if (of->a.size() != 2 || of->a[0].k != JVal::NUM || !of->a[0].n_uint || of->a[1].k != JVal::NUM ||
+            !of->a[1].n_uint || of->a[1].u < of->a[0].u) {
+            err = "safetensors: tensor " + kv.first + " lacks dtype, shape or data_offsets";
+            return AOS_ERR_INVALID;
+        }
+        x.b = of->a[0].u;
+        x.e = of->a[1].u;
+        if (x.e > data_len) { err = "safetensors: tensor " + kv.first + " runs past the buffer"; return AOS_ERR_INVALID; }
+        out.push_back(std::move(x));
     }
     return AOS_OK;
 }
