@@ -59,18 +59,48 @@ def peaks():
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clock and throttle reasons sampled during the timed region: NVML
+    polled every 10 ms by a thread (reads only), or nvidia-smi -lms 50 where
+    NVML is missing."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
 
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.nvml = None
         self.lines = []
+        self.samples = []  # (sm MHz, max MHz, reason bits)
+        self.stop_ev = threading.Event()
 
     def start(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self.nvml = pynvml
+
+            def poll():
+                while not self.stop_ev.is_set():
+                    try:
+                        self.samples.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), mx, get_reasons(h)))
+                    except Exception:
+                        pass
+                    self.stop_ev.wait(0.01)
+
+            self.samples.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), mx, get_reasons(h)))
+            self.t = threading.Thread(target=poll, daemon=True)
+            self.t.start()
+            return
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                                           "-i", str(self.index), "-lms", "50"], stdout=subprocess.PIPE,
@@ -85,6 +115,18 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def stop(self):
+        if self.nvml is not None:
+            self.stop_ev.set()
+            self.t.join(timeout=2)
+            sm = [float(a) for a, _, _ in self.samples]
+            mx = max((float(b) for _, b, _ in self.samples), default=0.0)
+            reasons = {n for n, bit in self.REASONS for _, _, r in self.samples if r & bit}
+            try:
+                self.nvml.nvmlShutdown()
+            except Exception:
+                pass
+            return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None,
+                    "reasons": sorted(reasons), "samples": len(sm), "source": "nvml, 10 ms"}
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -107,7 +149,7 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi, 50 ms"}
 
 
 # ------------------------------------------------------------------ model setup
@@ -372,6 +414,8 @@ def run_config1(args, rank, world, local):
             step(side.cuda_stream)
     torch.cuda.synchronize()
     total = 0.0
+    clocks = ClockSampler(local)
+    clocks.start()
     for _ in range(K_):
         _flush_l2(torch, dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -380,6 +424,7 @@ def run_config1(args, rank, world, local):
         e1.record()
         torch.cuda.synchronize()
         total += e0.elapsed_time(e1)
+    clk = clocks.stop()
     ms = total / K_
     # the same op through the Python/C-ABI calls, host overhead included
     t0 = time.perf_counter()
@@ -408,7 +453,7 @@ def run_config1(args, rank, world, local):
                 "dtype": "f32", "data": "synthetic",
                 "config": {"workload": "config 1", "l2": "flushed before every timed step",
                            "timing": "CUDA-graph replay of route + op between CUDA events"},
-                "host_call_ms_per_step": call_ms,
+                "host_call_ms_per_step": call_ms, "clocks": clk,
                 "roofline": {"bound": "hbm", "kernel": "route + lora_shrink_f32 + lora_base_f32 + lora_expand_f32",
                              "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak, "peak_kind": kind,
                              "bytes_per_step": nbytes},
@@ -476,11 +521,14 @@ def run_config2(args, rank, world, local):
         step()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    clocks.start()
     ev0.record(stream)
     for _ in range(K_):
         step()
     ev1.record(stream)
     torch.cuda.synchronize()
+    clk = clocks.stop()
     ms = ev0.elapsed_time(ev1) / K_
     gpu.health_check()
     rn = rings.cpu().numpy().view(aos.RING_DTYPE).reshape(T)
@@ -514,6 +562,7 @@ def run_config2(args, rank, world, local):
                 "dtype": "bf16", "data": "synthetic",
                 "config": {"workload": "config 2: H 3584, 28/4 heads, I 18944, q/k/v/o LoRA",
                            "l2": "inputs larger than L2 (466 MB of layer weights)"},
+                "clocks": clk,
                 "roofline": {"bound": "hbm", "kernel": "whole layer step", "achieved": gbs, "peak": peak,
                              "unit": "GB/s", "frac": gbs / peak, "peak_kind": kind, "bytes_per_step": nbytes,
                              "unique_adapters": len(sel)},
