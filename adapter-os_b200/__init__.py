@@ -193,6 +193,14 @@ def lib():
             "aos_attest_determinism": (C.c_int, [vp, vp]),
             "aos_sample_dev": (C.c_int, [vp, u32, u32, u64, vp, vp, vp, vp]),
             "aos_debug_bounded_wait": (C.c_int, [vp, C.c_int]),
+            "aos_kv_set_generation": (C.c_int, [vp, u64]),
+            "aos_kv_generation": (u64, [vp]),
+            "aos_kv_ensure_coherence": (C.c_int, [vp, u64, vp]),
+            "aos_kv_alloc_guarded": (C.c_int, [vp, u64, u32, u64]),
+            "aos_kv_has_stale_guards": (C.c_int, [vp, u64]),
+            "aos_kv_drain_guarded": (C.c_int, [vp, vp]),
+            "aos_kv_zeroize": (C.c_int, [vp, u64]),
+            "aos_kv_zeroize_all": (C.c_int, [vp]),
             "aos_archive_parse": (C.c_int, [vp, u64, vp, vp, u32]),
             "aos_blake3": (C.c_int, [vp, vp, u64, C.c_int, vp]),
             "aos_archive_verify": (C.c_int, [vp, vp, u64, vp]),
@@ -763,6 +771,35 @@ class CudaKernels:
         sid = self._sessions.pop(session_id, None)
         if sid is not None:
             self.kv_free(sid)
+
+    # -- KvCache generation guards and zeroization (kvcache.rs:288-402, 586-733)
+    def set_generation(self, generation):
+        self._check(self._L.aos_kv_set_generation(self.ctx, int(generation)))
+
+    def generation(self) -> int:
+        return int(self._L.aos_kv_generation(self.ctx))
+
+    def ensure_cache_coherence(self, generation) -> bool:
+        r = C.c_int(0)
+        self._check(self._L.aos_kv_ensure_coherence(self.ctx, int(generation), C.byref(r)))
+        return bool(r.value)
+
+    def allocate_with_guard(self, seq_id, max_tokens, generation):
+        self._check(self._L.aos_kv_alloc_guarded(self.ctx, int(seq_id), int(max_tokens), int(generation)))
+
+    def has_active_sequences_with_generation(self, generation) -> bool:
+        return bool(self._L.aos_kv_has_stale_guards(self.ctx, int(generation)))
+
+    def drain_active_sequences(self) -> int:
+        n = C.c_uint32(0)
+        self._check(self._L.aos_kv_drain_guarded(self.ctx, C.byref(n)))
+        return int(n.value)
+
+    def zeroize_sequence(self, seq_id):
+        self._check(self._L.aos_kv_zeroize(self.ctx, int(seq_id)))
+
+    def zeroize_all(self):
+        self._check(self._L.aos_kv_zeroize_all(self.ctx))
 
     def clear_all_caches(self):
         self._check(self._L.aos_kv_clear_all(self.ctx))

@@ -229,7 +229,29 @@ __global__ void unpack_samples_kernel(const UnpackSeg* __restrict__ segs, int n_
     out[idx] = *reinterpret_cast<const uint16_t*>(p);
 }
 
+// Zeroes the K and V pages of blocks[0..n) in every layer: CTA (i, layer)
+// clears nkv pages of 16 x 128 bf16 in each pool (one contiguous run).
+__global__ void zero_kv_blocks_kernel(uint16_t* __restrict__ k_pool, uint16_t* __restrict__ v_pool,
+                                      const int* __restrict__ blocks, int num_blocks, int nkv) {
+    const int b = blocks[blockIdx.x], layer = blockIdx.y;
+    const size_t off = ((size_t)layer * num_blocks + b) * nkv * 16 * 128;
+    const int n16 = nkv * 16 * 128 / 8;  // uint4 per pool run
+    uint4* k = reinterpret_cast<uint4*>(k_pool + off);
+    uint4* v = reinterpret_cast<uint4*>(v_pool + off);
+    for (int i = threadIdx.x; i < n16; i += blockDim.x) {
+        k[i] = make_uint4(0, 0, 0, 0);
+        v[i] = make_uint4(0, 0, 0, 0);
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_zero_kv_blocks(uint16_t* k_pool, uint16_t* v_pool, const int* blocks, int n, int n_layers,
+                                  int num_blocks, int nkv, cudaStream_t s) {
+    if (n <= 0 || n_layers <= 0) return cudaSuccess;
+    zero_kv_blocks_kernel<<<dim3(n, n_layers), 256, 0, s>>>(k_pool, v_pool, blocks, num_blocks, nkv);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_unpack_samples(const UnpackSeg* segs, int n_segs, const long long* starts, int n_per,
                                   uint16_t* out, cudaStream_t s) {

@@ -33,6 +33,8 @@
 #include "tc_gemm.cuh"
 
 namespace aos {
+cudaError_t launch_zero_kv_blocks(uint16_t* k_pool, uint16_t* v_pool, const int* blocks, int n, int n_layers,
+                                  int num_blocks, int nkv, cudaStream_t s);
 cudaError_t launch_embed(const uint16_t*, const uint32_t*, int, int, int, uint16_t*, cudaStream_t);
 cudaError_t launch_rmsnorm(const uint16_t*, const uint16_t*, int, int, float, uint16_t*, cudaStream_t);
 cudaError_t launch_lora_prep(const aos_router_ring* rings, int T, const int* col_off, const int* rank,
@@ -118,6 +120,8 @@ struct aos_ctx {
     std::vector<int> col_owner;  // host mirror, 8-column units
     std::unordered_map<uint16_t, AdapterEntry> adapters;
     std::map<uint16_t, std::pair<uint64_t, std::string>> fingerprints;  // id -> (buffer bytes, checkpoint hash hex)
+    uint64_t kv_generation = 0;                  // KvCache::stack_generation
+    std::map<uint64_t, uint64_t> kv_guards;      // sequence -> generation it was allocated under
     uint64_t arena_bytes = 0;
 
     // KV cache
@@ -1464,6 +1468,7 @@ int aos_kv_free(aos_ctx* c, uint64_t seq_id) {
     if (it == c->seqs.end()) return c->fail(AOS_ERR_NOT_FOUND, "unknown sequence");
     for (int b : it->second.blocks) c->free_blocks.push_back(b);
     c->seqs.erase(it);
+    c->kv_guards.erase(seq_id);
     c->m.sequences = (uint32_t)c->seqs.size();
     c->m.kv_blocks_used = c->cfg.kv_num_blocks - (uint32_t)c->free_blocks.size();
     return AOS_OK;
@@ -1545,6 +1550,82 @@ int aos_kv_clear_all(aos_ctx* c) {
     std::vector<uint64_t> ids;
     for (auto& kv : c->seqs) ids.push_back(kv.first);
     for (auto id : ids) aos_kv_free(c, id);
+    return AOS_OK;
+}
+
+// ---- KvCache generation guards and zeroization (crates/adapteros-lora-worker/
+// src/kvcache.rs:288-402 and 586-733)
+int aos_kv_zeroize(aos_ctx* c, uint64_t seq_id) {
+    if (!c) return AOS_ERR_INVALID;
+    auto it = c->seqs.find(seq_id);
+    if (it == c->seqs.end()) return c->fail(AOS_ERR_NOT_FOUND, "Sequence ID " + std::to_string(seq_id) + " not found");
+    const std::vector<int>& bl = it->second.blocks;
+    if (bl.empty()) return AOS_OK;
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    int* d_bl = nullptr;
+    CTX_CUDA(c, cudaMallocAsync((void**)&d_bl, bl.size() * sizeof(int), c->stream));
+    CTX_CUDA(c, cudaMemcpyAsync(d_bl, bl.data(), bl.size() * sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    LAUNCH(c, launch_zero_kv_blocks(c->k_pool, c->v_pool, d_bl, (int)bl.size(), (int)c->cfg.n_layers,
+                                    (int)c->cfg.kv_num_blocks, (int)c->cfg.n_kv_heads, c->stream));
+    CTX_CUDA(c, cudaFreeAsync(d_bl, c->stream));
+    CTX_CUDA(c, cudaStreamSynchronize(c->stream));
+    return AOS_OK;
+}
+
+int aos_kv_zeroize_all(aos_ctx* c) {  // zeroize / reset_all: both pools to zero, every sequence released
+    if (!c) return AOS_ERR_INVALID;
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    CTX_CUDA(c, cudaStreamSynchronize(c->stream));
+    const size_t bytes = aos_kv_memory_bytes(c) / 2;
+    CTX_CUDA(c, cudaMemsetAsync(c->k_pool, 0, bytes, c->stream));
+    CTX_CUDA(c, cudaMemsetAsync(c->v_pool, 0, bytes, c->stream));
+    CTX_CUDA(c, cudaStreamSynchronize(c->stream));
+    aos_kv_clear_all(c);
+    c->kv_guards.clear();
+    return AOS_OK;
+}
+
+int aos_kv_set_generation(aos_ctx* c, uint64_t generation) {
+    if (!c) return AOS_ERR_INVALID;
+    c->kv_generation = generation;
+    return AOS_OK;
+}
+
+uint64_t aos_kv_generation(const aos_ctx* c) { return c ? c->kv_generation : 0; }
+
+int aos_kv_ensure_coherence(aos_ctx* c, uint64_t generation, int* reset) {
+    if (!c) return AOS_ERR_INVALID;
+    if (reset) *reset = 0;
+    if (generation == c->kv_generation) return AOS_OK;
+    int rc = aos_kv_zeroize_all(c);  // reset_all: release every sequence, zero the pools
+    if (rc) return rc;
+    c->kv_generation = generation;
+    if (reset) *reset = 1;
+    return AOS_OK;
+}
+
+int aos_kv_alloc_guarded(aos_ctx* c, uint64_t seq_id, uint32_t max_tokens, uint64_t generation) {
+    if (!c) return AOS_ERR_INVALID;
+    int rc = aos_kv_ensure_coherence(c, generation, nullptr);
+    if (!rc) rc = aos_kv_alloc(c, seq_id, max_tokens);
+    if (!rc) c->kv_guards[seq_id] = generation;
+    return rc;
+}
+
+int aos_kv_has_stale_guards(const aos_ctx* c, uint64_t generation) {
+    if (!c) return 0;
+    for (const auto& kv : c->kv_guards)
+        if (kv.second != generation) return 1;
+    return 0;
+}
+
+int aos_kv_drain_guarded(aos_ctx* c, uint32_t* n_drained) {
+    if (!c) return AOS_ERR_INVALID;
+    std::vector<uint64_t> ids;
+    for (const auto& kv : c->kv_guards) ids.push_back(kv.first);
+    for (uint64_t id : ids) aos_kv_free(c, id);
+    c->kv_guards.clear();
+    if (n_drained) *n_drained = (uint32_t)ids.size();
     return AOS_OK;
 }
 

@@ -239,6 +239,23 @@ int aos_kv_fill_synthetic(aos_ctx* ctx, uint64_t seed, float std);
 /* FusedKernels::clear_all_caches / cache_memory_bytes (lib.rs:536-554). */
 int aos_kv_clear_all(aos_ctx* ctx);
 uint64_t aos_kv_memory_bytes(const aos_ctx* ctx);
+/* KvCache's generation guards and zeroization (crates/adapteros-lora-worker/
+ * src/kvcache.rs:288-402, 586-733).  ensure_coherence: when the generation
+ * differs, every sequence is released and both pools are zeroed (reset_all),
+ * *reset = 1.  alloc_guarded: ensure_coherence, then aos_kv_alloc, recording
+ * the sequence's generation.  has_stale_guards: 1 when a guarded sequence was
+ * allocated under another generation.  drain_guarded: releases every guarded
+ * sequence.  zeroize: zeroes one sequence's K/V pages in every layer (the
+ * sequence stays allocated); zeroize_all: both pools to zero, every sequence
+ * released. */
+int aos_kv_set_generation(aos_ctx* ctx, uint64_t generation);
+uint64_t aos_kv_generation(const aos_ctx* ctx);
+int aos_kv_ensure_coherence(aos_ctx* ctx, uint64_t generation, int* reset);
+int aos_kv_alloc_guarded(aos_ctx* ctx, uint64_t seq_id, uint32_t max_tokens, uint64_t generation);
+int aos_kv_has_stale_guards(const aos_ctx* ctx, uint64_t generation);
+int aos_kv_drain_guarded(aos_ctx* ctx, uint32_t* n_drained);
+int aos_kv_zeroize(aos_ctx* ctx, uint64_t seq_id);
+int aos_kv_zeroize_all(aos_ctx* ctx);
 
 /* ---- the step (FusedKernels::run_step, batched; lib.rs:371) --------------
  * One decode token per entry: rings[t] selects the adapters for token t,
