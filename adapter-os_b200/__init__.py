@@ -193,6 +193,7 @@ def lib():
             "aos_attest_determinism": (C.c_int, [vp, vp]),
             "aos_sample_dev": (C.c_int, [vp, u32, u32, u64, vp, vp, vp, vp]),
             "aos_debug_bounded_wait": (C.c_int, [vp, C.c_int]),
+            "aos_memory_report": (C.c_int, [vp, vp, vp, u32, vp]),
             "aos_kv_set_generation": (C.c_int, [vp, u64]),
             "aos_kv_generation": (u64, [vp]),
             "aos_kv_ensure_coherence": (C.c_int, [vp, u64, vp]),
@@ -683,6 +684,23 @@ class CudaKernels:
         m = Metrics()
         self._check(self._L.aos_get_metrics(self.ctx, C.byref(m)))
         return {f: getattr(m, f) for f, _ in Metrics._fields_}
+
+    def memory_report(self) -> dict:
+        """FusedKernels::memory_report (kernel-api/src/lib.rs:588-593, GpuMemoryReportData)."""
+        class Rep(C.Structure):
+            _fields_ = [("total_gpu_bytes", C.c_uint64), ("used_gpu_bytes", C.c_uint64), ("adapter_count", C.c_uint32),
+                        ("adapter_vram_total", C.c_uint64), ("arena_bytes", C.c_uint64),
+                        ("arena_used_bytes", C.c_uint64), ("kv_pool_bytes", C.c_uint64), ("kv_used_bytes", C.c_uint64)]
+
+        class Alloc(C.Structure):
+            _fields_ = [("adapter_id", C.c_uint32), ("bytes", C.c_uint64)]
+
+        r, n = Rep(), C.c_uint32(0)
+        allocs = (Alloc * 1024)()
+        self._check(self._L.aos_memory_report(self.ctx, C.byref(r), allocs, 1024, C.byref(n)))
+        out = {f: getattr(r, f) for f, _ in Rep._fields_}
+        out["adapter_allocations"] = [(a.adapter_id, a.bytes) for a in allocs[:min(n.value, 1024)]]
+        return out
 
     def health_check(self):
         return self._check(self._L.aos_health_check(self.ctx))

@@ -1851,6 +1851,39 @@ int aos_debug_bounded_wait(aos_ctx* c, int kind) {
     return check_device_error(c);
 }
 
+int aos_memory_report(aos_ctx* c, aos_memory_report_data* out, aos_adapter_allocation* allocs, uint32_t max_allocs,
+                      uint32_t* n_allocs) {
+    if (!c || !out) return AOS_ERR_INVALID;
+    std::memset(out, 0, sizeof *out);
+    CTX_CUDA(c, cudaSetDevice(c->device));
+    size_t free_b = 0, total_b = 0;
+    CTX_CUDA(c, cudaMemGetInfo(&free_b, &total_b));
+    out->total_gpu_bytes = total_b;
+    out->used_gpu_bytes = total_b - free_b;
+    // bytes one rank column takes in every layer and LoRA module (lora_A row + lora_B column)
+    uint64_t per_col = 0;
+    for (int m = 0; m < AOS_NUM_MODULES; ++m)
+        if (c->module_mask & (1u << m)) per_col += (uint64_t)(mod_in(c, m) + mod_out(c, m)) * 2;
+    per_col *= c->cfg.n_layers;
+    std::vector<uint16_t> ids;
+    for (const auto& kv : c->adapters) ids.push_back(kv.first);
+    std::sort(ids.begin(), ids.end());
+    uint32_t k = 0;
+    for (uint16_t id : ids) {
+        const uint64_t b = per_col * (uint64_t)c->adapters[id].rank;
+        out->adapter_vram_total += b;
+        if (allocs && k < max_allocs) allocs[k++] = aos_adapter_allocation{id, b};
+    }
+    if (n_allocs) *n_allocs = (uint32_t)ids.size();
+    out->adapter_count = (uint32_t)ids.size();
+    out->arena_bytes = per_col * (uint64_t)c->R;
+    out->arena_used_bytes = per_col * (uint64_t)c->m.arena_used_rank_cols;
+    out->kv_pool_bytes = aos_kv_memory_bytes(c);
+    const uint64_t used_blocks = c->cfg.kv_num_blocks - (uint64_t)c->free_blocks.size();
+    out->kv_used_bytes = c->cfg.kv_num_blocks ? out->kv_pool_bytes / c->cfg.kv_num_blocks * used_blocks : 0;
+    return AOS_OK;
+}
+
 int aos_debug_trace_read(aos_ctx* c, uint64_t* out, uint64_t n) {
     if (!c || !out) return AOS_ERR_INVALID;
     if (!c->d_trace) return c->fail(AOS_ERR_STATE, "tracing is off (set AOS_TC_TRACE before aos_init)");

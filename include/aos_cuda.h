@@ -125,6 +125,15 @@ typedef struct aos_determinism_report { /* DeterminismReport, attestation.rs:130
 } aos_determinism_report;
 
 typedef struct aos_ctx aos_ctx;
+/* GpuMemoryReportData (kernel-api/src/lib.rs:732-758) */
+typedef struct aos_memory_report_data {
+    uint64_t total_gpu_bytes, used_gpu_bytes;      /* cudaMemGetInfo of the context's device  */
+    uint32_t adapter_count;
+    uint64_t adapter_vram_total;                   /* arena bytes held by the loaded adapters */
+    uint64_t arena_bytes, arena_used_bytes;        /* the LoRA arena (pool) and its used part */
+    uint64_t kv_pool_bytes, kv_used_bytes;         /* KV pages held by sequences              */
+} aos_memory_report_data;
+typedef struct aos_adapter_allocation { uint32_t adapter_id; uint64_t bytes; } aos_adapter_allocation;
 
 /* ---- library ------------------------------------------------------------ */
 const char* aos_version(void);
@@ -471,6 +480,11 @@ int aos_profile_read(aos_ctx* ctx, aos_profile* out, int reset);
 /* Diagnostics: with AOS_TC_TRACE=<g> set before aos_init, the GEMM (g = 0..3:
  * qkv, o, gate/up, down; 4..7: their LoRA shrinks) of layer 0 writes per-CTA
  * %globaltimer stamps (256 slots per CTA); this copies n of them to host. */
+/* FusedKernels::memory_report (kernel-api/src/lib.rs:588-593): totals, and up
+ * to max_allocs per-adapter allocations (id, bytes) in id order; *n_allocs
+ * receives the number of loaded adapters. */
+int aos_memory_report(aos_ctx* ctx, aos_memory_report_data* out, aos_adapter_allocation* allocs, uint32_t max_allocs,
+                      uint32_t* n_allocs);
 int aos_debug_trace_read(aos_ctx* ctx, uint64_t* out, uint64_t n);
 /* Failure-path check: runs one of the GEMM kernel's bounded waits against a
  * condition nothing satisfies (kind 0: global-counter spin, 1: mbarrier wait);

@@ -70,3 +70,24 @@ def test_generation_guards_and_zeroize():
             g.kv_len(9)
     finally:
         g.close()
+
+
+def test_memory_report():
+    rng = np.random.default_rng(1)
+    g = make()
+    try:
+        m = O.HostModel.random(rng, 256, 2, 1, 128, 384, 512, 2)
+        ad = O.HostAdapters.random(rng, m, [8, 16], modules=range(7))
+        for a in range(2):
+            g.load_adapter_with_metadata(a, ad.ranks[a], ad.alphas[a],
+                                         {(l, mod): (ad.A[a][l][mod], ad.B[a][l][mod]) for l in range(2) for mod in range(7)})
+        g.kv_alloc(5, 40)
+        rep = g.memory_report()
+        per_col = 2 * sum(i + o for o, i in (m.mod_shape(k) for k in range(7))) * 2
+        assert rep["adapter_count"] == 2
+        assert rep["adapter_allocations"] == [(0, 8 * per_col), (1, 16 * per_col)]
+        assert rep["adapter_vram_total"] == 24 * per_col == rep["arena_used_bytes"]
+        assert rep["kv_used_bytes"] == rep["kv_pool_bytes"] // 32 * 3  # 40 tokens -> 3 blocks of 16
+        assert 0 < rep["used_gpu_bytes"] <= rep["total_gpu_bytes"]
+    finally:
+        g.close()
