@@ -194,6 +194,8 @@ def lib():
             "aos_sample_dev": (C.c_int, [vp, u32, u32, u64, vp, vp, vp, vp]),
             "aos_debug_bounded_wait": (C.c_int, [vp, C.c_int]),
             "aos_memory_report": (C.c_int, [vp, vp, vp, u32, vp]),
+            "aos_check_memory_footprint": (C.c_int, [vp, C.c_uint16, u64, vp, vp, vp, vp, vp]),
+            "aos_get_gpu_fingerprints": (C.c_int, [vp, vp, vp, vp, u32, vp]),
             "aos_kv_set_generation": (C.c_int, [vp, u64]),
             "aos_kv_generation": (u64, [vp]),
             "aos_kv_ensure_coherence": (C.c_int, [vp, u64, vp]),
@@ -903,6 +905,22 @@ class CudaKernels:
     def store_gpu_fingerprint(self, adapter_id, buffer_bytes, checkpoint_hash_hex):
         self._check(self._L.aos_store_gpu_fingerprint(self.ctx, int(adapter_id), int(buffer_bytes),
                                                       checkpoint_hash_hex.encode()))
+
+    def check_memory_footprint(self, adapter_id, buffer_bytes):
+        """(within_tolerance, z_score, (mean, stddev, samples))."""
+        w, z, m, sd, n = C.c_int(0), C.c_double(0), C.c_double(0), C.c_double(0), C.c_uint32(0)
+        self._check(self._L.aos_check_memory_footprint(self.ctx, int(adapter_id), int(buffer_bytes), C.byref(w),
+                                                       C.byref(z), C.byref(m), C.byref(sd), C.byref(n)))
+        return bool(w.value), float(z.value), (float(m.value), float(sd.value), int(n.value))
+
+    def get_gpu_fingerprints(self) -> dict:
+        """{adapter id: (buffer bytes, checkpoint hash hex)} of the stored baselines."""
+        n = C.c_uint32(0)
+        self._check(self._L.aos_get_gpu_fingerprints(self.ctx, None, None, None, 0, C.byref(n)))
+        k = n.value
+        ids, nb, hx = (C.c_uint32 * max(1, k))(), (C.c_uint64 * max(1, k))(), C.create_string_buffer(65 * max(1, k))
+        self._check(self._L.aos_get_gpu_fingerprints(self.ctx, ids, nb, hx, k, C.byref(n)))
+        return {int(ids[i]): (int(nb[i]), hx.raw[65 * i:65 * i + 64].decode()) for i in range(k)}
 
     def verify_gpu_fingerprint(self, adapter_id, buffer_bytes, checkpoint_hash_hex) -> bool:
         m = C.c_int(0)

@@ -17,6 +17,7 @@
 // (one TMA box of 128 rows x 128 B per group and weight tile).
 
 #include <algorithm>
+#include <cfloat>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -120,6 +121,11 @@ struct aos_ctx {
     std::vector<int> col_owner;  // host mirror, 8-column units
     std::unordered_map<uint16_t, AdapterEntry> adapters;
     std::map<uint16_t, std::pair<uint64_t, std::string>> fingerprints;  // id -> (buffer bytes, checkpoint hash hex)
+    struct Footprint {  // MemoryFootprintBaseline (kernel-mtl/src/vram.rs:82-196)
+        std::vector<uint64_t> samples;
+        size_t max_samples = 0;
+    };
+    std::map<uint16_t, Footprint> footprints;
     uint64_t kv_generation = 0;                  // KvCache::stack_generation
     std::map<uint64_t, uint64_t> kv_guards;      // sequence -> generation it was allocated under
     uint64_t arena_bytes = 0;
@@ -1431,6 +1437,74 @@ int aos_store_gpu_fingerprint(aos_ctx* c, uint16_t id, uint64_t buffer_bytes, co
     std::string lower = h;
     for (auto& ch : lower) ch = (char)tolower((unsigned char)ch);
     c->fingerprints[id] = {buffer_bytes, lower};
+    // VramTracker::store_fingerprint also feeds the footprint baseline (window 10)
+    auto& fp = c->footprints[id];
+    if (!fp.max_samples) fp.max_samples = 10;
+    if (fp.samples.size() >= fp.max_samples) fp.samples.erase(fp.samples.begin());
+    fp.samples.push_back(buffer_bytes);
+    return AOS_OK;
+}
+
+// FusedKernels::check_memory_footprint (VramTracker, kernel-mtl/src/vram.rs:
+// 386-407, MemoryFootprintBaseline 82-196): with a baseline, |bytes - mean| /
+// stddev <= 2 (population stddev; an exact match when every sample is equal);
+// without one, a baseline of window 100 is started with this sample.
+int aos_check_memory_footprint(aos_ctx* c, uint16_t id, uint64_t bytes, int* within, double* z_score, double* mean,
+                               double* stddev, uint32_t* n_samples) {
+    if (!c || !within || !z_score) return AOS_ERR_INVALID;
+    auto it = c->footprints.find(id);
+    const bool fresh = it == c->footprints.end();
+    if (fresh) {
+        auto& fp = c->footprints[id];
+        fp.max_samples = 100;
+        fp.samples.push_back(bytes);
+        it = c->footprints.find(id);
+    }
+    const auto& v = it->second.samples;
+    double m = 0.0, sd = 0.0;
+    if (!v.empty()) {
+        uint64_t sum = 0;
+        for (uint64_t x : v) sum += x;
+        m = (double)sum / (double)v.size();
+    }
+    if (v.size() >= 2) {
+        double var = 0.0;
+        for (uint64_t x : v) {
+            const double d = (double)x - m;
+            var += d * d;
+        }
+        sd = std::sqrt(var / (double)v.size());
+    }
+    if (fresh || v.size() < 2) {
+        *within = 1;
+        *z_score = 0.0;
+    } else if (sd == 0.0) {
+        *within = (double)bytes == m;
+        *z_score = *within ? 0.0 : DBL_MAX;
+    } else {
+        *z_score = std::fabs((double)bytes - m) / sd;
+        *within = *z_score <= 2.0;
+    }
+    if (mean) *mean = m;
+    if (stddev) *stddev = sd;
+    if (n_samples) *n_samples = (uint32_t)v.size();
+    return AOS_OK;
+}
+
+// FusedKernels::get_gpu_fingerprints: the stored baselines in id order.
+int aos_get_gpu_fingerprints(const aos_ctx* c, uint32_t* ids, uint64_t* buffer_bytes, char* hex65, uint32_t max,
+                             uint32_t* n) {
+    if (!c || !n) return AOS_ERR_INVALID;
+    uint32_t k = 0;
+    for (const auto& kv : c->fingerprints) {
+        if (k < max) {
+            if (ids) ids[k] = kv.first;
+            if (buffer_bytes) buffer_bytes[k] = kv.second.first;
+            if (hex65) std::snprintf(hex65 + 65 * (size_t)k, 65, "%s", kv.second.second.c_str());
+        }
+        ++k;
+    }
+    *n = k;
     return AOS_OK;
 }
 

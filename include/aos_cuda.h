@@ -417,6 +417,16 @@ int aos_store_gpu_fingerprint(aos_ctx* ctx, uint16_t id, uint64_t buffer_bytes, 
  * string, else 0 (no baseline reads as 0, as in the reference). */
 int aos_verify_gpu_fingerprint(aos_ctx* ctx, uint16_t id, uint64_t buffer_bytes, const char* checkpoint_hash_hex,
                                int* matches);
+/* FusedKernels::check_memory_footprint (kernel-mtl/src/vram.rs:386-407): the
+ * adapter's footprint baseline (storing a fingerprint adds a sample, window 10;
+ * the first check starts a baseline of window 100) against bytes: within 2
+ * population standard deviations, or equal when every sample is. */
+int aos_check_memory_footprint(aos_ctx* ctx, uint16_t id, uint64_t bytes, int* within, double* z_score, double* mean,
+                               double* stddev, uint32_t* n_samples);
+/* FusedKernels::get_gpu_fingerprints: up to max stored baselines in id order
+ * (hex65: max x 65 chars); *n receives how many there are. */
+int aos_get_gpu_fingerprints(const aos_ctx* ctx, uint32_t* ids, uint64_t* buffer_bytes, char* hex65, uint32_t max,
+                             uint32_t* n);
 
 /* ---- prefill (the prompt path) ---------------------------------------------
  * InferencePipeline's prompt pass (inference_pipeline.rs:983-1154, MLX

@@ -286,5 +286,18 @@ def test_adapter_fingerprint(model):
         g.load_adapter_aos(2, write_aos([("canonical", payload(w2))], manifest(8, 16.0, ["q_proj", "down_proj"])))
         s2, h2 = g.adapter_fingerprint(2)
         assert s2 == size and h2 != fhash and not g.verify_gpu_fingerprint(2, s2, h2)
+        assert g.get_gpu_fingerprints() == {2: (size, fhash)}
+        # footprint baseline: the stored fingerprint gave one sample; fewer than two -> within
+        assert g.check_memory_footprint(2, size) == (True, 0.0, (float(size), 0.0, 1))
+        g.store_gpu_fingerprint(2, size, fhash)
+        within, z, (mean, sd, n) = g.check_memory_footprint(2, size)
+        assert within and z == 0.0 and n == 2 and sd == 0.0  # identical samples: exact match required
+        assert not g.check_memory_footprint(2, size + 1)[0]
+        g.store_gpu_fingerprint(2, size + 1000, fhash)
+        within, z, (mean, sd, n) = g.check_memory_footprint(2, size)
+        assert n == 3 and sd > 0 and within and abs(z - abs(size - mean) / sd) < 1e-12
+        assert not g.check_memory_footprint(2, size + 10 ** 6)[0]
+        # first check of an adapter without a baseline starts one
+        assert g.check_memory_footprint(7, 123) == (True, 0.0, (123.0, 0.0, 1))
     finally:
         g.close()
