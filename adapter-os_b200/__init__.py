@@ -750,7 +750,20 @@ class CudaKernels:
         self._check(self._L.aos_adapter_unload(self.ctx, adapter_id))
 
     def detach_adapter(self, adapter_id):
+        """FusedKernels::detach_adapter: forwards to unload_adapter (kernel-api/src/lib.rs:414-420)."""
         self.unload_adapter(adapter_id)
+
+    def attach_adapter(self, adapter_id):
+        """FusedKernels::attach_adapter: a no-op, as the trait default (lib.rs:410-412); every
+        loaded adapter is selectable by the router rings."""
+
+    def switch_adapter(self, adapter_id):
+        """FusedKernels::switch_adapter: a no-op, as the trait default (lib.rs:425-427)."""
+
+    def load_adapter(self, adapter_id, weights: bytes):
+        """FusedKernels::load_adapter (lib.rs:388): safetensors bytes with no metadata
+        (rank / alpha / target modules from the tensors and the defaults)."""
+        self.load_adapter_safetensors(adapter_id, weights)
 
     def is_loaded(self, adapter_id) -> bool:
         return bool(self._L.aos_adapter_is_loaded(self.ctx, adapter_id))
