@@ -413,19 +413,23 @@ def run_config1(args, rank, world, local):
         with torch.cuda.graph(graph, stream=side):
             step(side.cuda_stream)
     torch.cuda.synchronize()
-    total = 0.0
+    # Every step is enqueued before any is waited for: the L2 flush that runs on
+    # the GPU ahead of each start event gives the host time to enqueue the
+    # replay, so host-side delays (the clock sampler's thread among them) do
+    # not open a gap inside a timed interval.
     clocks = ClockSampler(local)
     clocks.start()
+    evs = []
     for _ in range(K_):
         _flush_l2(torch, dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         graph.replay()
         e1.record()
-        torch.cuda.synchronize()
-        total += e0.elapsed_time(e1)
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
     clk = clocks.stop()
-    ms = total / K_
+    ms = sum(a.elapsed_time(b) for a, b in evs) / K_
     # the same op through the Python/C-ABI calls, host overhead included
     t0 = time.perf_counter()
     for _ in range(K_):
