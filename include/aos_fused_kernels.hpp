@@ -197,6 +197,33 @@ class CudaKernels final : public FusedKernels {
         return e;
     }
 
+    // FusedKernels::check_memory_footprint: within 2 sigma of the adapter's
+    // footprint baseline (kernel-mtl/src/vram.rs:386-407).
+    AosError check_memory_footprint(uint16_t id, uint64_t bytes, bool* within, double* z_score) {
+        int w = 0;
+        AosError e = status(aos_check_memory_footprint(ctx_, id, bytes, &w, z_score, nullptr, nullptr, nullptr), ctx_);
+        *within = w != 0;
+        return e;
+    }
+    // FusedKernels::memory_report (kernel-api/src/lib.rs:588-593).
+    AosError memory_report(aos_memory_report_data* out, std::vector<aos_adapter_allocation>* allocs = nullptr) {
+        uint32_t n = 0;
+        AosError e = status(aos_memory_report(ctx_, out, nullptr, 0, &n), ctx_);
+        if (e.ok() && allocs) {
+            allocs->resize(n);
+            e = status(aos_memory_report(ctx_, out, allocs->data(), n, &n), ctx_);
+        }
+        return e;
+    }
+    // KvCache generation guards (crates/adapteros-lora-worker/src/kvcache.rs:288-402).
+    AosError ensure_cache_coherence(uint64_t generation, bool* reset) {
+        int r = 0;
+        AosError e = status(aos_kv_ensure_coherence(ctx_, generation, &r), ctx_);
+        if (reset) *reset = r != 0;
+        return e;
+    }
+    AosError zeroize_sequence(uint64_t seq) { return status(aos_kv_zeroize(ctx_, seq), ctx_); }
+
     // Next tokens of device logits rows (Generator::next_token / greedy on the
     // device); u: device uniform draws, one per row (the caller's RNG).
     static AosError sample_dev(const float* logits_dev, uint32_t rows, uint32_t vocab, const aos_sample_params& p,
