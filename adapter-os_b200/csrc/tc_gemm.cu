@@ -597,8 +597,9 @@ __device__ __noinline__ bool spin_ge(const int* ptr, int target, int* err) {
 }
 
 // ---------------------------------------------------------------- the kernel
-// kPart: split base tiles go through fp32 partials (p.part, T > 128); the
-// instance without it keeps the partials code out of the T <= 128 kernel.
+// kPart: split base tiles go through fp32 partials (p.part; the runtime sets
+// it for every launch); the instance without it (p.part null) adds base
+// pieces in fixed point like the shrink pieces.
 template <bool kPart>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
