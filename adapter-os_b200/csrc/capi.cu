@@ -212,6 +212,12 @@ int aos_lora_op_f32_dev(const float* x, uint32_t T, uint32_t in_dim, uint32_t ou
         set_global_error("aos_lora_op_f32: invalid arguments (rank in [1,64], in_dim % 4 == 0)");
         return AOS_ERR_INVALID;
     }
+    // The shrink reads x and A rows with 16-byte loads (in_dim % 4 == 0 keeps
+    // every row on a 16-byte boundary once the base pointer is).
+    if (((uintptr_t)x | (uintptr_t)A) & 15u) {
+        set_global_error("aos_lora_op_f32: x and A must be 16-byte aligned");
+        return AOS_ERR_INVALID;
+    }
     int rc = require_device();
     if (rc) return rc;
     if (T == 0) return AOS_OK;

@@ -143,6 +143,7 @@ struct aos_ctx {
     uint16_t* d_hm[AOS_NUM_MODULES] = {};
     int *d_groups = nullptr, *d_n_groups = nullptr;
     int *d_block_tables = nullptr, *d_ctx_lens = nullptr;
+    int* d_zero_blocks = nullptr;  // [kv_num_blocks]: block list of aos_kv_zeroize
     // Pinned staging of the per-step block tables and lengths.  A ring of
     // kStageSlots buffers, each reused only after the event recorded behind
     // its last copy has completed, so the host may run steps ahead of the GPU
@@ -1094,6 +1095,7 @@ aos_ctx* aos_init(const aos_model_config* cfg) {
     INIT_CHECK(dalloc(&c->d_groups, (size_t)c->R / kGroup + 1), "groups");
     INIT_CHECK(dalloc(&c->d_n_groups, 1), "n_groups");
     INIT_CHECK(dalloc(&c->d_block_tables, TC * c->max_blocks), "block tables");
+    INIT_CHECK(dalloc(&c->d_zero_blocks, (size_t)c->cfg.kv_num_blocks), "zeroization block list");
     INIT_CHECK(dalloc(&c->d_ctx_lens, TC), "ctx lens");
     for (int i = 0; i < aos_ctx::kStageSlots; ++i) {
         INIT_CHECK(cudaMallocHost((void**)&c->h_stage[i], (TC * c->max_blocks + TC) * 4), "pinned tables");
@@ -1179,7 +1181,7 @@ void aos_destroy(aos_ctx* c) {
     f(c->d_col_owner); f(c->d_col_off); f(c->d_rank); f(c->d_scale); f(c->d_coef); f(c->d_ucoef);
     f(c->k_pool); f(c->v_pool);
     f(c->d_hidden); f(c->d_normed); f(c->d_q); f(c->d_attn); f(c->d_act);
-    f(c->d_groups); f(c->d_n_groups); f(c->d_block_tables); f(c->d_ctx_lens);
+    f(c->d_groups); f(c->d_n_groups); f(c->d_block_tables); f(c->d_ctx_lens); f(c->d_zero_blocks);
     f(c->d_rings); f(c->d_tokens); f(c->d_logits); f(c->d_rope);
     f(c->d_attn_part); f(c->d_attn_ml); f(c->d_stage); f(c->d_acc); f(c->d_part); f(c->d_fp); f(c->d_sync); f(c->d_err); f(c->d_trace);
     for (int i = 0; i < aos_ctx::kStageSlots; ++i) {
@@ -1636,12 +1638,13 @@ int aos_kv_zeroize(aos_ctx* c, uint64_t seq_id) {
     const std::vector<int>& bl = it->second.blocks;
     if (bl.empty()) return AOS_OK;
     CTX_CUDA(c, cudaSetDevice(c->device));
-    int* d_bl = nullptr;
-    CTX_CUDA(c, cudaMallocAsync((void**)&d_bl, bl.size() * sizeof(int), c->stream));
-    CTX_CUDA(c, cudaMemcpyAsync(d_bl, bl.data(), bl.size() * sizeof(int), cudaMemcpyHostToDevice, c->stream));
-    LAUNCH(c, launch_zero_kv_blocks(c->k_pool, c->v_pool, d_bl, (int)bl.size(), (int)c->cfg.n_layers,
+    // a sequence holds at most kv_num_blocks blocks: the list goes into the
+    // context's preallocated buffer (the synchronize below keeps it from
+    // being overwritten by the next call while the kernel still reads it)
+    CTX_CUDA(c, cudaMemcpyAsync(c->d_zero_blocks, bl.data(), bl.size() * sizeof(int), cudaMemcpyHostToDevice,
+                                c->stream));
+    LAUNCH(c, launch_zero_kv_blocks(c->k_pool, c->v_pool, c->d_zero_blocks, (int)bl.size(), (int)c->cfg.n_layers,
                                     (int)c->cfg.kv_num_blocks, (int)c->cfg.n_kv_heads, c->stream));
-    CTX_CUDA(c, cudaFreeAsync(d_bl, c->stream));
     CTX_CUDA(c, cudaStreamSynchronize(c->stream));
     return AOS_OK;
 }

@@ -172,7 +172,8 @@ int aos_route_batch_dev(const float* priors, const uint64_t* stable_ids,
  * (kernel_testing.rs:220-257 cpu_lora_forward; liquid.rs:222-250 blend loop;
  *  gate dequant mlx-ffi/src/backend.rs:405-418).  x: [T, in]; W: [out, in];
  * A: [n_adapters, rank, in]; B: [n_adapters, out, rank]; alpha: [n_adapters]
- * or NULL (alpha = rank); rings: [T]; y: [T, out].  rank <= 64, in % 4 == 0. */
+ * or NULL (alpha = rank); rings: [T]; y: [T, out].  rank <= 64, in % 4 == 0;
+ * on device, x and A must be 16-byte aligned (AOS_ERR_INVALID otherwise). */
 int aos_lora_op_f32(const float* x, uint32_t T, uint32_t in_dim, uint32_t out_dim,
                     const float* W, const float* A, const float* B, uint32_t n_adapters,
                     uint32_t rank, const float* alpha, const aos_router_ring* rings, float* y);
@@ -181,18 +182,22 @@ int aos_lora_op_f32_dev(const float* x, uint32_t T, uint32_t in_dim, uint32_t ou
                         uint32_t rank, const float* alpha, const aos_router_ring* rings, float* y,
                         void* stream);
 
-/* Same op as aos_lora_op_f32_dev, for callers that must not allocate device
+/* The op of aos_lora_op_f32_dev, for callers that must not allocate device
  * memory (no counterpart in the reference).  Hosts with a device-memory budget
  * fixed at start-up, code sharing a device with an open CUDA graph capture
  * (cudaMalloc/cudaFree synchronise the device and are illegal while a capture
  * is open) and latency-critical loops can call this one: its scratch is a
  * fixed 512 KiB device array in the library (131072 floats, held on every
  * device that loads the library until exit), not an allocation.  Requires
- * T * 8 * rank <= 131072, otherwise AOS_ERR_INVALID.  The first call on a
- * device looks up the array's address (cudaGetSymbolAddress) and should be
- * made before any stream capture on that device.  All calls share the array:
- * calls that overlap on the GPU race, so serialise them (one stream).  It
- * calls no cudaMalloc, cudaFree or allocating library routine. */
+ * T * 8 * rank <= 131072, otherwise AOS_ERR_INVALID; same argument rules as
+ * aos_lora_op_f32_dev.  Its base GEMM is one single-pass kernel over all of K
+ * (aos_lora_op_f32_dev sums four K-quarter partials), so the two agree within
+ * fp32 tolerance, not bit for bit; each is bit-identical run to run.  The
+ * first call in each CUDA context on a device looks up the array's address
+ * (cudaGetSymbolAddress) and should be made before any stream capture on that
+ * device.  All calls share the array: calls that overlap on the GPU race, so
+ * serialise them (one stream).  It calls no cudaMalloc, cudaFree or
+ * allocating library routine. */
 int aos_lora_op_f32_noalloc_dev(const float* x, uint32_t T, uint32_t in_dim, uint32_t out_dim,
                                 const float* W, const float* A, const float* B, uint32_t n_adapters,
                                 uint32_t rank, const float* alpha, const aos_router_ring* rings,

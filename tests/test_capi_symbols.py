@@ -43,3 +43,20 @@ def test_no_cpu_fallback_without_device():
 
 def test_ring_layout_is_40_bytes():
     assert ctypes.sizeof(aos.RouterRingC) == 40 and aos.RING_DTYPE.itemsize == 40
+
+
+@pytest.mark.parametrize("name", ["aos_lora_op_f32_dev", "aos_lora_op_f32_noalloc_dev"])
+def test_fp32_op_rejects_misaligned_vector_operands(name):
+    """The fp32 LoRA op reads x and A with 16-byte loads: a pointer off a
+    16-byte boundary is refused with AOS_ERR_INVALID before any device work
+    (the addresses are only checked, never dereferenced, so no GPU is needed)."""
+    lib = aos.lib()
+    f = getattr(lib, name)
+    vp, u32 = ctypes.c_void_p, ctypes.c_uint32
+    f.restype = ctypes.c_int
+    f.argtypes = [vp, u32, u32, u32, vp, vp, vp, u32, u32, vp, vp, vp, vp]
+    good, bad = 0x10000, 0x10004
+    for x, a in ((bad, good), (good, bad)):
+        rc = f(x, 4, 64, 64, good, a, good, 2, 16, None, good, good, None)
+        assert rc == -1  # AOS_ERR_INVALID
+        assert "16-byte aligned" in aos.last_error()

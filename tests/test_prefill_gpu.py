@@ -2,10 +2,16 @@
 time (oracle/aos_oracle.cpp: the decode step of mlx_cpp_wrapper_real.cpp:3338-3559
 at consecutive positions is the causal prompt pass).
 
-Three prompts (37 tokens from an empty cache, 50 tokens after 20 cached ones,
-a single token) with LoRA on all seven modules.  Checked: each sequence's
-last-token logits, every K/V row the prompt appends (all layers), the new
-sequence lengths, and bit-identical results run to run.
+Small case: three prompts (37 tokens from an empty cache, 50 tokens after 20
+cached ones, a single token) in one 256-token tile.  Multi-tile case: prompts
+of 300 tokens, 2100 tokens after 24 cached ones, and 5 tokens (2405 tokens:
+ten 256-token tiles, so the two-accumulator M=256 tiles, the band schedule of
+eight token tiles per weight tile and a partial last tile all run; causal
+attention over up to 133 pages).  LoRA on all seven modules.  Checked: each
+sequence's last-token logits, every K/V row the prompt appends (all layers,
+which also checks every prompt token's attention output of the first layer
+through the second layer's K/V), the new sequence lengths, and bit-identical
+results run to run.
 Tolerance (bf16 path): relative L2 <= 2e-2 and max-abs <= 2e-2 * max|ref|."""
 import numpy as np
 import pytest
@@ -58,9 +64,9 @@ def _gpu(m, ad, kv, bt, prompts, max_seq, sids):
     return gpu
 
 
-def test_prefill_matches_oracle():
+def _check_prefill(**case):
     import torch
-    m, ad, kv, bt, rings, tokens, prompts, max_seq = _case()
+    m, ad, kv, bt, rings, tokens, prompts, max_seq = _case(**case)
     S = len(prompts)
     sids = np.arange(500, 500 + S, dtype=np.uint64)
     n_tok = np.array([p[1] for p in prompts], np.uint32)
@@ -96,3 +102,11 @@ def test_prefill_matches_oracle():
             rv = np.stack([kv.v_pool[l, bt[i, p // 16], :, p % 16] for p in range(n0, n0 + n)])
             assert_close(O.bf16_bits_to_f32(gk), O.bf16_bits_to_f32(rk), f"sequence {i} layer {l} k rows")
             assert_close(O.bf16_bits_to_f32(gv), O.bf16_bits_to_f32(rv), f"sequence {i} layer {l} v rows")
+
+
+def test_prefill_matches_oracle():
+    _check_prefill()
+
+
+def test_prefill_multi_tile_matches_oracle():
+    _check_prefill(seed=11, prompts=((0, 300), (24, 2100), (0, 5)), max_seq=2144)

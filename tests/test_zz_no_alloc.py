@@ -1,23 +1,37 @@
 """aos_lora_op_f32_noalloc_dev: the fp32 LoRA op for callers that cannot
-allocate device memory (a fixed device-memory budget, an open CUDA graph
-capture on the same device, or a latency-critical loop).  Its scratch is a
+allocate device memory -- a host that fixes its device-memory budget at
+start-up, code that shares the device with an open CUDA graph capture
+(cudaMalloc and cudaFree are not allowed while one is open), or a
+latency-critical loop that must not stall on an allocator.  Its scratch is a
 fixed device array inside the library instead of a per-call allocation.
 
-Checked through the C ABI against aos_lora_op_f32_dev, the entry point that
-allocates its scratch, on two calls in a row, with the same 1e-5 relative
-tolerance as the other fp32 LoRA tests.  This file is named so that pytest
+Checked through the C ABI, on two calls in a row with different shapes (the
+second reuses more of the scratch than the first left in it):
+  - against the CPU oracle (kernel_testing.rs:220-257, liquid.rs:222-250
+    restated in oracle/) with the 1e-5 relative bound of the other fp32 LoRA
+    tests;
+  - against aos_lora_op_f32_dev, the entry point that allocates its scratch,
+    within the same bound (the two use different base kernels, so they are
+    not bit-identical);
+  - that the calls allocate nothing: the device's default memory pool (where
+    the allocating entry point's cudaMallocAsync draws from) reaches no new
+    high-water mark, and the device's free memory is unchanged.
+Sizes beyond the scratch are refused.  This file is named so that pytest
 collects it last."""
 import ctypes as C
 
 import numpy as np
 import pytest
 
+from oracle import oracle as O
 from tests.aos_import import aos
 
 pytestmark = pytest.mark.gpu
 
 TOL = 1e-5  # fp32 op tolerance, as in tests/test_lora_f32_gpu.py
 SCRATCH_FLOATS = 131072  # fixed scratch of the no-allocation entry point
+CU_MEMPOOL_ATTR_USED_MEM_CURRENT = 7
+CU_MEMPOOL_ATTR_USED_MEM_HIGH = 8
 
 
 def _bind():
@@ -29,52 +43,99 @@ def _bind():
     return lib, f
 
 
-def _inputs(torch, seed, T, H, O, N, r):
-    g = torch.Generator(device="cuda")
-    g.manual_seed(seed)
-    x = torch.randn(T, H, generator=g, device="cuda")
-    W = torch.randn(O, H, generator=g, device="cuda") * 0.02
-    A = torch.randn(N, r, H, generator=g, device="cuda") * 0.02
-    B = torch.randn(N, O, r, generator=g, device="cuda") * 0.02
-    alpha = torch.linspace(1.0, 2.0 * r, N, device="cuda")
-    logits = np.random.default_rng(seed).standard_normal((T, N)).astype(np.float32)
-    rings, _, _ = aos.route_batch(logits, k=min(4, N))
-    rings_d = torch.from_numpy(rings.view(np.uint8).copy()).cuda()
-    return x, W, A, B, alpha, rings_d
+class _DefaultPool:
+    """The current device's default memory pool, read through the driver API."""
+
+    def __init__(self, device):
+        self.cu = C.CDLL("libcuda.so.1")
+        dev = C.c_int()
+        assert self.cu.cuDeviceGet(C.byref(dev), device) == 0
+        self.pool = C.c_void_p()
+        assert self.cu.cuDeviceGetDefaultMemPool(C.byref(self.pool), dev) == 0
+
+    def get(self, attr):
+        v = C.c_uint64()
+        assert self.cu.cuMemPoolGetAttribute(self.pool, attr, C.byref(v)) == 0
+        return v.value
+
+    def reset_high(self):
+        zero = C.c_uint64(0)  # resets the high-water mark to the current use
+        assert self.cu.cuMemPoolSetAttribute(self.pool, CU_MEMPOOL_ATTR_USED_MEM_HIGH, C.byref(zero)) == 0
 
 
-def _run(fn, torch, x, W, A, B, alpha, rings_d):
+def _inputs(seed, T, H, Od, N, r):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((T, H), dtype=np.float32)
+    W = rng.standard_normal((Od, H), dtype=np.float32) * 0.02
+    A = rng.standard_normal((N, r, H), dtype=np.float32) * 0.02
+    B = rng.standard_normal((N, Od, r), dtype=np.float32) * 0.02
+    alpha = np.linspace(1.0, 2.0 * r, N).astype(np.float32)
+    rings, _, _, _ = O.route_batch(rng.standard_normal((T, N), dtype=np.float32), None, k=min(4, N))
+    return x, W, A, B, alpha, rings
+
+
+def _call(fn, torch, dev, x, W, A, B, alpha, rings, y):
     T, H = x.shape
-    O = W.shape[0]
+    Od = W.shape[0]
     N, r, _ = A.shape
-    y = torch.full((T, O), float("nan"), device="cuda")
-    rc = fn(x.data_ptr(), T, H, O, W.data_ptr(), A.data_ptr(), B.data_ptr(), N, r, alpha.data_ptr(),
-            rings_d.data_ptr(), y.data_ptr(), None)
+    rc = fn(dev["x"].data_ptr(), T, H, Od, dev["W"].data_ptr(), dev["A"].data_ptr(), dev["B"].data_ptr(), N, r,
+            dev["alpha"].data_ptr(), dev["rings"].data_ptr(), y.data_ptr(), None)
     assert rc == 0, aos.last_error()
-    torch.cuda.synchronize()
-    return y
 
 
-def test_no_alloc_matches_allocating_entry_point_twice():
+def _rel(got, ref):
+    return float(np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+def test_no_alloc_matches_oracle_twice_and_allocates_nothing():
     torch = pytest.importorskip("torch")
     lib, noalloc = _bind()
-    # two calls in a row, the second with a different shape that reuses more of the scratch
-    for seed, (T, H, O, N, r) in ((1, (64, 2048, 2048, 8, 16)), (2, (200, 512, 384, 5, 64))):
+    shapes = ((1, (64, 2048, 2048, 8, 16)), (2, (200, 512, 384, 5, 64)))
+    cases = []
+    for seed, (T, H, Od, N, r) in shapes:
         assert T * 8 * r <= SCRATCH_FLOATS
-        x, W, A, B, alpha, rings_d = _inputs(torch, seed, T, H, O, N, r)
-        ref = _run(lib.aos_lora_op_f32_dev, torch, x, W, A, B, alpha, rings_d)
-        got = _run(noalloc, torch, x, W, A, B, alpha, rings_d)
-        err = (got - ref).abs().max().item() / max(ref.abs().max().item(), 1e-30)
-        assert err <= TOL, f"call with seed {seed}: rel max error {err:.3e}"
+        x, W, A, B, alpha, rings = _inputs(seed, T, H, Od, N, r)
+        dev = {k: torch.from_numpy(v).cuda() for k, v in (("x", x), ("W", W), ("A", A), ("B", B), ("alpha", alpha))}
+        dev["rings"] = torch.from_numpy(rings.view(np.uint8).copy()).cuda()
+        ref = O.lora_op_f32(x, W, A, B, rings, alpha)
+        y = torch.full((T, Od), float("nan"), device="cuda")
+        cases.append((x, W, A, B, alpha, rings, dev, ref, y))
+    # warm-up: the first call in the context looks up the scratch array's
+    # address and loads the kernels (lazy module loading takes device memory)
+    for x, W, A, B, alpha, rings, dev, ref, y in cases:
+        _call(noalloc, torch, dev, x, W, A, B, alpha, rings, y)
+        y.fill_(float("nan"))
+    torch.cuda.synchronize()
+    pool = _DefaultPool(torch.cuda.current_device())
+    pool.reset_high()
+    free0, _ = torch.cuda.mem_get_info()
+    for x, W, A, B, alpha, rings, dev, ref, y in cases:  # two calls in a row
+        _call(noalloc, torch, dev, x, W, A, B, alpha, rings, y)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert pool.get(CU_MEMPOOL_ATTR_USED_MEM_HIGH) == pool.get(CU_MEMPOOL_ATTR_USED_MEM_CURRENT), \
+        "the no-allocation entry point drew memory from the device pool"
+    assert free1 == free0, "device free memory changed across the no-allocation calls"
+    for i, (x, W, A, B, alpha, rings, dev, ref, y) in enumerate(cases):
+        got = y.cpu().numpy()
+        err = _rel(got, ref)
+        assert err <= TOL, f"call {i + 1} vs the oracle: rel max error {err:.3e}"
+        y2 = torch.full_like(y, float("nan"))
+        _call(lib.aos_lora_op_f32_dev, torch, dev, x, W, A, B, alpha, rings, y2)
+        torch.cuda.synchronize()
+        err2 = _rel(got, y2.cpu().numpy())
+        assert err2 <= TOL, f"call {i + 1} vs aos_lora_op_f32_dev: rel max error {err2:.3e}"
 
 
 def test_no_alloc_rejects_sizes_beyond_its_scratch():
     torch = pytest.importorskip("torch")
     _, noalloc = _bind()
-    T, H, O, N, r = 300, 64, 64, 4, 64  # 300 * 8 * 64 = 153600 > 131072
-    x, W, A, B, alpha, rings_d = _inputs(torch, 3, T, H, O, N, r)
-    y = torch.zeros((T, O), device="cuda")
-    rc = noalloc(x.data_ptr(), T, H, O, W.data_ptr(), A.data_ptr(), B.data_ptr(), N, r, alpha.data_ptr(),
-                 rings_d.data_ptr(), y.data_ptr(), None)
+    T, H, Od, N, r = 300, 64, 64, 4, 64  # 300 * 8 * 64 = 153600 > 131072
+    x, W, A, B, alpha, rings = _inputs(3, T, H, Od, N, r)
+    dev = {k: torch.from_numpy(v).cuda() for k, v in (("x", x), ("W", W), ("A", A), ("B", B), ("alpha", alpha))}
+    dev["rings"] = torch.from_numpy(rings.view(np.uint8).copy()).cuda()
+    y = torch.zeros((T, Od), device="cuda")
+    rc = noalloc(dev["x"].data_ptr(), T, H, Od, dev["W"].data_ptr(), dev["A"].data_ptr(), dev["B"].data_ptr(), N, r,
+                 dev["alpha"].data_ptr(), dev["rings"].data_ptr(), y.data_ptr(), None)
     assert rc == -1  # AOS_ERR_INVALID
     assert "exceeds the fixed scratch" in aos.last_error()
