@@ -212,6 +212,13 @@ def lib():
             "aos_adapter_fingerprint": (C.c_int, [vp, C.c_uint16, vp, vp]),
             "aos_store_gpu_fingerprint": (C.c_int, [vp, C.c_uint16, u64, C.c_char_p]),
             "aos_verify_gpu_fingerprint": (C.c_int, [vp, C.c_uint16, u64, C.c_char_p, vp]),
+            "aos_plan_config_parse": (C.c_int, [C.c_char_p, u64, vp]),
+            "aos_plan_config_validate": (C.c_int, [vp]),
+            "aos_plan_config_validate_gqa": (C.c_int, [vp]),
+            "aos_plan_validate_lora_targets": (C.c_int, [vp, u32]),
+            "aos_plan_lora_size": (C.c_int, [vp, u32, vp, u32, vp]),
+            "aos_model_config_from_plan": (C.c_int, [vp, u64, vp, vp]),
+            "aos_init_from_plan": (vp, [vp, u64, vp, vp]),
         }
         for name, (res, args) in sig.items():
             if not hasattr(L, name):
@@ -224,6 +231,76 @@ def lib():
 
 
 SHARD_ID_BYTES = 128
+
+
+# ------------------------------------------------------------------ model plan
+class PlanConfig(C.Structure):
+    """aos_plan_config: the plan crate's ModelConfig with its derived values
+    (crates/adapteros-lora-plan/src/config.rs:9-62, 171-208)."""
+
+    _fields_ = [
+        ("name", C.c_char * 128), ("architecture", C.c_char * 128),
+        ("hidden_size", C.c_uint32), ("intermediate_size", C.c_uint32), ("num_hidden_layers", C.c_uint32),
+        ("num_attention_heads", C.c_uint32), ("num_key_value_heads", C.c_uint32),
+        ("max_position_embeddings", C.c_uint32), ("vocab_size", C.c_uint32), ("rope_theta", C.c_float),
+        ("has_rope_scaling_factor", C.c_uint32), ("rope_scaling_factor", C.c_float),
+        ("has_rope_scaling", C.c_uint32), ("scaling_factor", C.c_float),
+        ("scaling_original_max_position_embeddings", C.c_uint32), ("scaling_type", C.c_char * 64),
+        ("rms_norm_eps", C.c_float), ("head_dim", C.c_uint32), ("kv_width", C.c_uint32),
+        ("total_params", C.c_uint64), ("effective_context_length", C.c_uint32), ("is_qwen2_5", C.c_uint32),
+    ]
+
+    def to_dict(self):
+        return {k: (v.decode() if isinstance(v, bytes) else v)
+                for k, v in ((f[0], getattr(self, f[0])) for f in self._fields_)}
+
+
+def plan_config_parse(json_text, validate=True) -> PlanConfig:
+    """ModelConfig::from_json (config.rs:80-86), then ModelConfig::validate
+    (:127-167) unless validate is False; AosError with the reference's message."""
+    raw = json_text.encode() if isinstance(json_text, str) else bytes(json_text)
+    cfg = PlanConfig()
+    check(lib().aos_plan_config_parse(raw, len(raw), C.byref(cfg)))
+    if validate:
+        check(lib().aos_plan_config_validate(C.byref(cfg)))
+    return cfg
+
+
+def plan_config_validate(cfg: PlanConfig, gqa_only=False):
+    fn = lib().aos_plan_config_validate_gqa if gqa_only else lib().aos_plan_config_validate
+    check(fn(C.byref(cfg)))
+
+
+def _c_strings(names):
+    arr = (C.c_char_p * max(1, len(names)))(*[n.encode() for n in names])
+    return C.cast(arr, C.c_void_p), arr
+
+
+def plan_validate_lora_targets(targets):
+    """validate_lora_targets (config.rs:256-277)."""
+    p, keep = _c_strings(list(targets))
+    check(lib().aos_plan_validate_lora_targets(p, len(targets)))
+    del keep
+
+
+def plan_lora_size(cfg: PlanConfig, rank, targets) -> int:
+    """calculate_lora_size (config.rs:212-253): fp16 bytes over every layer."""
+    p, keep = _c_strings(list(targets))
+    out = C.c_uint64()
+    check(lib().aos_plan_lora_size(C.byref(cfg), int(rank), p, len(targets), C.byref(out)))
+    del keep
+    return out.value
+
+
+def model_config_from_plan(plan_bytes: bytes, plan_cfg: PlanConfig = None) -> dict:
+    """The model dimensions FusedKernels::load infers from a plan's tensor
+    shapes (kernel-mtl/src/lib.rs:790-839; aos_model_config_from_plan)."""
+    buf = C.create_string_buffer(bytes(plan_bytes), max(1, len(plan_bytes)))
+    mc = ModelConfig()
+    check(lib().aos_model_config_from_plan(buf, len(plan_bytes), C.byref(plan_cfg) if plan_cfg else None,
+                                           C.byref(mc)))
+    return {k: getattr(mc, k) for k in ("hidden", "n_heads", "n_kv_heads", "head_dim", "intermediate", "vocab",
+                                        "n_layers", "rms_eps", "rope_theta")}
 
 
 class AdapterMeta(C.Structure):
@@ -614,6 +691,38 @@ class CudaKernels:
         self.vocab, self.hidden, self.n_layers = vocab, hidden, n_layers
         self.n_kv_heads, self.head_dim = n_kv_heads, head_dim
         self._sessions = {}
+
+    @classmethod
+    def from_plan(cls, plan_bytes: bytes, plan_config=None, rope_mlx_as_written=False, max_batch=64,
+                  kv_block_size=16, kv_num_blocks=1024, max_seq_len=4096, lora_rank_capacity=1024,
+                  lora_max_adapters=128, lora_modules=MODULES, device=0):
+        """FusedKernels::load(plan_bytes) (kernel-api/src/lib.rs:350): the model's
+        dimensions come from the plan (safetensors base weights) and, when
+        given, its model config (a PlanConfig or the config JSON); the keyword
+        arguments are the runtime sizes.  aos_init_from_plan."""
+        if plan_config is not None and not isinstance(plan_config, PlanConfig):
+            plan_config = plan_config_parse(plan_config)
+        mask = 0
+        for m in lora_modules:
+            mask |= 1 << MOD_INDEX[m]
+        rt = ModelConfig(0, 0, 0, 0, 0, 0, 0, 0.0, 0.0, int(bool(rope_mlx_as_written)), max_batch, kv_block_size,
+                         kv_num_blocks, max_seq_len, lora_rank_capacity, lora_max_adapters, mask, device)
+        L = lib()
+        buf = C.create_string_buffer(bytes(plan_bytes), max(1, len(plan_bytes)))
+        ctx = L.aos_init_from_plan(buf, len(plan_bytes), C.byref(plan_config) if plan_config else None, C.byref(rt))
+        if not ctx:
+            raise AosError(-1, last_error())
+        self = cls.__new__(cls)
+        dims = model_config_from_plan(plan_bytes, plan_config)
+        for k, v in dims.items():
+            setattr(rt, k, v)
+        self.cfg = rt
+        self._L = L
+        self.ctx = ctx
+        self.vocab, self.hidden, self.n_layers = dims["vocab"], dims["hidden"], dims["n_layers"]
+        self.n_kv_heads, self.head_dim = dims["n_kv_heads"], dims["head_dim"]
+        self._sessions = {}
+        return self
 
     def close(self):
         if getattr(self, "ctx", None):

@@ -1755,8 +1755,12 @@ int aos_run_step_batch(aos_ctx* c, const aos_router_ring* rings, const uint32_t*
 }
 
 // ------------------------------------------------------------------ prefill
-int aos_prefill_dev(aos_ctx* c, uint32_t n_seq, const uint64_t* seq_ids, const uint32_t* n_tok,
-                    const aos_router_ring* rings, const uint32_t* token_ids, float* logits, void* stream) {
+namespace {
+// The prefill step; `in_kind` says where rings and token_ids live
+// (cudaMemcpyDeviceToDevice for aos_prefill_dev, HostToDevice for aos_prefill).
+int prefill_run(aos_ctx* c, uint32_t n_seq, const uint64_t* seq_ids, const uint32_t* n_tok,
+                const aos_router_ring* rings, const uint32_t* token_ids, float* logits, void* stream,
+                cudaMemcpyKind in_kind) {
     if (!c || !seq_ids || !n_tok || !rings || !token_ids || n_seq == 0) return AOS_ERR_INVALID;
     if (n_seq > c->cfg.max_batch) return c->fail(AOS_ERR_INVALID, "more sequences than max_batch");
     cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
@@ -1792,8 +1796,8 @@ int aos_prefill_dev(aos_ctx* c, uint32_t n_seq, const uint64_t* seq_ids, const u
     CTX_CUDA(c, cudaMemcpyAsync(b.pos, pos.data(), T * 4, cudaMemcpyHostToDevice, s));
     CTX_CUDA(c, cudaMemcpyAsync(b.block_tables, bt.data(), bt.size() * 4, cudaMemcpyHostToDevice, s));
     CTX_CUDA(c, cudaMemcpyAsync(b.qblk, qblk.data(), qblk.size() * sizeof(int2), cudaMemcpyHostToDevice, s));
-    CTX_CUDA(c, cudaMemcpyAsync(b.rings, rings, T * sizeof(aos_router_ring), cudaMemcpyDeviceToDevice, s));
-    CTX_CUDA(c, cudaMemcpyAsync(b.tokens, token_ids, T * 4, cudaMemcpyDeviceToDevice, s));
+    CTX_CUDA(c, cudaMemcpyAsync(b.rings, rings, T * sizeof(aos_router_ring), in_kind, s));
+    CTX_CUDA(c, cudaMemcpyAsync(b.tokens, token_ids, T * 4, in_kind, s));
     PLAUNCH(c, AOS_K_PREP, s,
             launch_lora_prep(b.rings, (int)T, c->d_col_off, c->d_rank, c->d_scale, (int)c->cfg.lora_max_adapters,
                              c->R / kGroup, c->d_groups, c->d_n_groups, b.coef, c->d_col_owner, b.ucoef, s));
@@ -1825,6 +1829,25 @@ int aos_prefill_dev(aos_ctx* c, uint32_t n_seq, const uint64_t* seq_ids, const u
         c->prof_used = 0;
     }
     return AOS_OK;
+}
+}  // namespace
+
+int aos_prefill_dev(aos_ctx* c, uint32_t n_seq, const uint64_t* seq_ids, const uint32_t* n_tok,
+                    const aos_router_ring* rings, const uint32_t* token_ids, float* logits, void* stream) {
+    return prefill_run(c, n_seq, seq_ids, n_tok, rings, token_ids, logits, stream, cudaMemcpyDeviceToDevice);
+}
+
+int aos_prefill(aos_ctx* c, uint32_t n_seq, const uint64_t* seq_ids, const uint32_t* n_tok,
+                const aos_router_ring* rings, const uint32_t* token_ids, float* logits) {
+    if (!c) return AOS_ERR_INVALID;
+    int rc = prefill_run(c, n_seq, seq_ids, n_tok, rings, token_ids, logits ? c->d_logits : nullptr, nullptr,
+                         cudaMemcpyHostToDevice);
+    if (rc) return rc;
+    if (logits)
+        CTX_CUDA(c, cudaMemcpyAsync(logits, c->d_logits, (size_t)n_seq * c->cfg.vocab * 4, cudaMemcpyDeviceToHost,
+                                    c->stream));
+    CTX_CUDA(c, cudaStreamSynchronize(c->stream));
+    return check_device_error(c);
 }
 
 // ------------------------------------------------------------------ adapter-sharded step

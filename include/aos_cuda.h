@@ -324,6 +324,62 @@ int aos_adapter_load_safetensors(aos_ctx* ctx, uint16_t id, const void* data, ui
  * self_attn.{q,k,v,o}_proj, mlp.{gate,up,down}_proj}.weight. */
 int aos_load_model_safetensors(aos_ctx* ctx, const void* data, uint64_t len);
 
+/* ---- model plan: FusedKernels::load(plan_bytes) ---------------------------
+ * The plan crate's ModelConfig (crates/adapteros-lora-plan/src/config.rs:9-62)
+ * as ModelConfig::from_json reads it (required: name, architecture,
+ * hidden_size, intermediate_size, num_hidden_layers, num_attention_heads,
+ * num_key_value_heads, max_position_embeddings, rope_theta, vocab_size;
+ * optional: rope_scaling_factor, rope_scaling {factor,
+ * original_max_position_embeddings, scaling_type}; other fields ignored),
+ * plus its derived values: dimensions() (:171-193), effective_context_length()
+ * (:201-208) and is_qwen2_5() (:196-198). */
+typedef struct aos_plan_config {
+    char name[128];
+    char architecture[128];
+    uint32_t hidden_size, intermediate_size, num_hidden_layers;
+    uint32_t num_attention_heads, num_key_value_heads, max_position_embeddings, vocab_size;
+    float rope_theta;
+    uint32_t has_rope_scaling_factor; /* Option<f32> rope_scaling_factor               */
+    float rope_scaling_factor;
+    uint32_t has_rope_scaling;        /* Option<RopeScaling> rope_scaling              */
+    float scaling_factor;
+    uint32_t scaling_original_max_position_embeddings;
+    char scaling_type[64];
+    float rms_norm_eps;               /* "rms_norm_eps" when the JSON carries it, else 0 */
+    uint32_t head_dim, kv_width;      /* hidden / heads (0 when heads == 0), kv_heads * head_dim */
+    uint64_t total_params;            /* dimensions().total_params                     */
+    uint32_t effective_context_length;
+    uint32_t is_qwen2_5;
+} aos_plan_config;
+/* ModelConfig::from_json (config.rs:80-86): AOS_ERR_INVALID with
+ * aos_last_error(NULL) = "Failed to parse model config: ..." (missing field,
+ * wrong type, malformed JSON). */
+int aos_plan_config_parse(const char* json, uint64_t len, aos_plan_config* out);
+/* ModelConfig::validate (config.rs:127-167) and validate_gqa (:101-124), with
+ * the reference's messages in aos_last_error(NULL). */
+int aos_plan_config_validate(const aos_plan_config* cfg);
+int aos_plan_config_validate_gqa(const aos_plan_config* cfg);
+/* validate_lora_targets (config.rs:256-277) and calculate_lora_size
+ * (:212-253): fp16 bytes of a rank-`rank` adapter on `targets` over every layer. */
+int aos_plan_validate_lora_targets(const char* const* targets, uint32_t n);
+int aos_plan_lora_size(const aos_plan_config* cfg, uint32_t rank, const char* const* targets, uint32_t n,
+                       uint64_t* bytes);
+/* Dimension inference of FusedKernels::load (kernel-mtl/src/lib.rs:1476-1537,
+ * validate_embedding_dimensions :790-839): vocab and hidden from the plan's
+ * embedding tensor [vocab, hidden] (first of model.embed_tokens.weight,
+ * transformer.wte.weight, embeddings.word_embeddings.weight,
+ * embed_tokens.weight, wte.weight); layers from model.layers.<l>.*; the MLP
+ * width from mlp.gate_proj; heads, KV heads, head_dim, rope_theta and
+ * rms_norm_eps from `pc` when given (checked against the tensor shapes), else
+ * GqaConfig::default() (head_dim 128, rope_theta 10000; fused_qkv.rs:41-54).
+ * Fills those fields of *cfg and leaves its runtime fields (batch, KV pool,
+ * adapter arena, device) as the caller set them.  Context-free, no device. */
+int aos_model_config_from_plan(const void* plan, uint64_t len, const aos_plan_config* pc, aos_model_config* cfg);
+/* FusedKernels::load(plan_bytes): the dimensions above with the runtime
+ * fields of *runtime, aos_init, then aos_load_model_safetensors of the plan.
+ * NULL on failure (aos_last_error(NULL)). */
+aos_ctx* aos_init_from_plan(const void* plan, uint64_t len, const aos_plan_config* pc, const aos_model_config* runtime);
+
 /* ---- .aos adapter archives -------------------------------------------------
  * Layout and validation of crates/adapteros-aos/src/writer.rs:118-135,
  * 407-558: 64-byte header, 80-byte index entries, payloads, JSON manifest. */
@@ -444,6 +500,12 @@ int aos_get_gpu_fingerprints(const aos_ctx* ctx, uint32_t* ids, uint64_t* buffer
  * n_seq <= max_batch. */
 int aos_prefill_dev(aos_ctx* ctx, uint32_t n_seq, const uint64_t* seq_ids, const uint32_t* n_tok,
                     const aos_router_ring* rings, const uint32_t* token_ids, float* logits, void* stream);
+/* The same prompt pass with host arrays (FusedKernels::run_step with several
+ * input ids, kernel-api/src/lib.rs:371): rings / token_ids are host arrays,
+ * logits a host [n_seq][vocab] f32 array or NULL; returns when the step is
+ * done. */
+int aos_prefill(aos_ctx* ctx, uint32_t n_seq, const uint64_t* seq_ids, const uint32_t* n_tok,
+                const aos_router_ring* rings, const uint32_t* token_ids, float* logits);
 
 /* ---- adapter-sharded decode (the large-pool config) -------------------------
  * No reference counterpart: the reference keeps every adapter on one device

@@ -15,6 +15,7 @@
 
 #include <cstdint>
 #include <cstring>
+#include <memory>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -116,6 +117,19 @@ class CudaKernels final : public FusedKernels {
    public:
     explicit CudaKernels(const aos_model_config& cfg) : cfg_(cfg), ctx_(aos_init(&cfg)) {
         if (!ctx_) throw std::runtime_error(std::string("aos_init: ") + aos_last_error(nullptr));
+    }
+    // FusedKernels::load(plan_bytes) (kernel-api/src/lib.rs:350): the model's
+    // dimensions from the plan's tensor shapes (and `pc`, the plan crate's
+    // model config, when given), the runtime sizes from `runtime`, then the
+    // plan's base weights (aos_init_from_plan).  Throws with the reason.
+    static std::unique_ptr<CudaKernels> from_plan(const std::vector<uint8_t>& plan, const aos_plan_config* pc,
+                                                  const aos_model_config& runtime) {
+        aos_model_config cfg = runtime;
+        if (aos_model_config_from_plan(plan.data(), plan.size(), pc, &cfg) != AOS_OK)
+            throw std::runtime_error(std::string("load: ") + aos_last_error(nullptr));
+        aos_ctx* ctx = aos_init_from_plan(plan.data(), plan.size(), pc, &cfg);
+        if (!ctx) throw std::runtime_error(std::string("load: ") + aos_last_error(nullptr));
+        return std::unique_ptr<CudaKernels>(new CudaKernels(cfg, ctx));
     }
     ~CudaKernels() override { aos_destroy(ctx_); }
     CudaKernels(const CudaKernels&) = delete;
@@ -243,9 +257,11 @@ class CudaKernels final : public FusedKernels {
                       ctx_);
     }
 
-    // FusedKernels::run_step: decode io.input_ids in order at io.position for
-    // the io.session_id sequence; logits of the last token; position advances
-    // by input_ids.size() (mlx-ffi/src/backend.rs:1212-1310).
+    // FusedKernels::run_step: io.input_ids at io.position of the
+    // io.session_id sequence -- one id is a decode token (aos_run_step_batch),
+    // several are a prompt pass with causal attention (aos_prefill), the ring
+    // applying to each; logits of the last token; position advances by
+    // input_ids.size() (mlx-ffi/src/backend.rs:1212-1310).
     AosError run_step(const RouterRing& ring, IoBuffers& io) override {
         if (io.input_ids.empty()) return AosError{AOS_ERR_INVALID, "Input token IDs cannot be empty"};
         uint64_t seq = session(io.session_id);
@@ -253,10 +269,14 @@ class CudaKernels final : public FusedKernels {
         if (!e.ok()) return e;
         std::vector<float> logits(cfg_.vocab);
         const aos_router_ring r = ring.device_layout();
-        for (uint32_t tok : io.input_ids) {
-            e = status(aos_run_step_batch(ctx_, &r, &tok, &seq, 1, logits.data(), nullptr), ctx_);
-            if (!e.ok()) return e;
+        if (io.input_ids.size() == 1) {
+            e = status(aos_run_step_batch(ctx_, &r, io.input_ids.data(), &seq, 1, logits.data(), nullptr), ctx_);
+        } else {
+            const std::vector<aos_router_ring> rings(io.input_ids.size(), r);
+            const uint32_t n = (uint32_t)io.input_ids.size();
+            e = status(aos_prefill(ctx_, 1, &seq, &n, rings.data(), io.input_ids.data(), logits.data()), ctx_);
         }
+        if (!e.ok()) return e;
         const size_t n = io.output_logits.size() < logits.size() ? io.output_logits.size() : logits.size();
         std::memcpy(io.output_logits.data(), logits.data(), n * sizeof(float));
         io.position += io.input_ids.size();
@@ -284,6 +304,7 @@ class CudaKernels final : public FusedKernels {
     AosError health_check() override { return status(aos_health_check(ctx_), ctx_); }
 
    private:
+    CudaKernels(const aos_model_config& cfg, aos_ctx* ctx) : cfg_(cfg), ctx_(ctx) {}
     uint64_t session(const std::string& sid) {
         for (auto& kv : sessions_)
             if (kv.first == sid) return kv.second;
