@@ -28,13 +28,6 @@ thread_local std::string g_error;
 
 void set_global_error(const std::string& msg) { g_error = msg; }
 
-bool pdl_enabled() {
-    static const bool on = [] {
-        const char* e = getenv("AOS_PDL");  // AOS_PDL=0 turns programmatic dependent launch off
-        return !(e && e[0] == '0');
-    }();
-    return on;
-}
 const char* global_error() { return g_error.c_str(); }
 
 int require_device(int device) {

@@ -74,10 +74,8 @@ struct Sequence {
 };
 
 struct LayerPlan {
-    TcParams gemm[4];    // per input group: shrink + base (+ expand when fused) in one launch
-    TcParams expand[4];  // q/k/v and o: the LoRA expand as a launch of its own
+    TcParams gemm[4];    // per input group: LoRA shrink + base + LoRA expand in one launch
     TcParams owner[4];   // adapter-sharded step: this rank's LoRA (shrink + expand) for every rank's rows
-    bool split[4];
     int gemm_grid[4];
 };
 
@@ -438,31 +436,12 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp, bool sharded =
             }
             if ((rc = build_owner_plan(c, layer, g, T * c->shard_world, lp.owner[g]))) return rc;
         }
-        // Tuning knob AOS_SPLIT_EXPAND=1: run the q/k/v and o LoRA expand as a
-        // launch of its own (RoPE is linear, and the o epilogue adds into the
-        // residual anyway).  Off by default: measured slower than the fused launch.
         p.pools = 7;
-        static const bool split_expand = [] {
-            const char* e = getenv("AOS_SPLIT_EXPAND");
-            return e && e[0] == '1';
-        }();
-        lp.split[g] = split_expand && p.lora && !sharded && (g == kGroupQKV || g == kGroupO);
-        if (lp.split[g]) {
-            TcParams& e = lp.expand[g];
-            e = p;
-            e.pools = 4;
-            e.sh_nseg = 0;
-            e.add_out = g == kGroupQKV ? 1 : 0;
-            if ((rc = tc_prepare(e, smem_budget))) return rc;
-            p.pools = 3;
-        }
         if ((rc = tc_prepare(p, smem_budget))) return rc;
         lp.gemm_grid[g] = tc_num_sms();
         // Diagnostics: AOS_TC_TRACE=<0..3> traces layer 0's GEMM g.
-        if (const char* tv = getenv("AOS_TC_TRACE")) {  // 0-3: layer 0's GEMM g; 4-7: its expand launch
+        if (const char* tv = getenv("AOS_TC_TRACE"))
             if (layer == 0 && c->d_trace && atoi(tv) == g) p.trace = c->d_trace;
-            if (layer == 0 && c->d_trace && atoi(tv) == g + 4 && lp.split[g]) lp.expand[g].trace = c->d_trace;
-        }
     }
     return AOS_OK;
 }
@@ -595,13 +574,11 @@ int enqueue_layer(aos_ctx* c, const StepPlan& plan, int layer, cudaStream_t s) {
     }
     PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(c->d_hidden, c->attn_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
     PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupQKV], lp.gemm_grid[kGroupQKV], s));
-    if (lp.split[kGroupQKV]) PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.expand[kGroupQKV], lp.gemm_grid[kGroupQKV], s));
     PLAUNCH(c, AOS_K_ATTN, s,
             launch_attention(c->tm_k, c->tm_v, c->d_q, c->d_block_tables, c->d_ctx_lens, c->d_attn_part, c->d_attn_ml, T,
                              (int)c->cfg.n_heads, (int)c->cfg.n_kv_heads, layer, (int)c->cfg.kv_num_blocks, c->max_blocks,
                              c->attn_chunks, c->d_err, c->d_attn, s));
     PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupO], lp.gemm_grid[kGroupO], s));
-    if (lp.split[kGroupO]) PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.expand[kGroupO], lp.gemm_grid[kGroupO], s));
     PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(c->d_hidden, c->mlp_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
     PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupGU], lp.gemm_grid[kGroupGU], s));
     PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupD], lp.gemm_grid[kGroupD], s));
@@ -664,11 +641,6 @@ void prof_end(aos_ctx* c, int slot, cudaStream_t s) {
     if (slot >= 0) cudaEventRecord(c->prof_ev[slot + 1], s);
 }
 
-bool use_graphs() {
-    const char* e = getenv("AOS_NO_GRAPH");
-    return !(e && e[0] == '1');
-}
-
 int run_step_device(aos_ctx* c, int T, bool with_logits, cudaStream_t s, bool sharded = false) {
     StepPlan* plan = nullptr;
     int rc = get_plan(c, T, &plan, sharded);
@@ -690,7 +662,6 @@ int run_step_device(aos_ctx* c, int T, bool with_logits, cudaStream_t s, bool sh
         c->prof.last_touched_groups = (uint32_t)ns;
         return AOS_OK;
     }
-    if (!use_graphs()) return enqueue_step(c, *plan, with_logits, s);
     if (plan->sharded && !plan->eager_done) {
         plan->eager_done = true;
         return enqueue_step(c, *plan, with_logits, s);

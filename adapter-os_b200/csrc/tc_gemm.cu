@@ -376,13 +376,6 @@ __device__ __forceinline__ void apply_pairs(const TcParams& p, int mode, int seg
                 const int blk = __ldg(p.block_tables + (size_t)t * p.max_blocks + (pos >> 4));
                 dst = pool + ((((size_t)p.layer * p.num_blocks + blk) * p.nkv + head) * 16 + (pos & 15)) * 128 + d;
             }
-            if (p.add_out) {  // expand-only launch: add the rotated LoRA term to the stored value
-#pragma unroll
-                for (int i = 0; i < N; ++i) {
-                    a[i] += bf2f(dst[i]);
-                    b[i] += bf2f(dst[64 + i]);
-                }
-            }
             store_bf16_run<N>(dst, a);
             store_bf16_run<N>(dst + 64, b);
             break;
@@ -862,16 +855,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             };
             auto act_bytes = [&](bool ex) -> uint32_t {
                 const int nh = (ex && p.n_sub == 2) ? 2 : 1;
-                return (uint32_t)(nh * (p.spread ? p.n_xbox * 16 : p.tb * p.T_box) * 128);
+                return (uint32_t)(nh * p.tb * p.T_box * 128);
             };
             auto issue_x = [&](const Piece& pc, bool ex, int st, uint32_t sbase, uint32_t fb) -> bool {
                 const uint32_t act = sbase + p.act_off;
                 if (!ex) {
-                    if (p.spread) {  // 16-token groups to lane quarters: rows 32j .. 32j + 15
-                        for (int j = 0; j < p.n_xbox; ++j) tma_2d(&p.tm_x, act + j * 4096, fb, st * kTcBK, 16 * j, pol_x);
-                    } else {
-                        for (int b = 0; b < p.tb; ++b) tma_2d(&p.tm_x, act + b * kActBox, fb, st * kTcBK, b * kTcTok, pol_x);
-                    }
+                    for (int b = 0; b < p.tb; ++b) tma_2d(&p.tm_x, act + b * kActBox, fb, st * kTcBK, b * kTcTok, pol_x);
                     return true;
                 }
                 if (!shrink_ready) {  // hm is written by this launch's shrink tiles and reduction
@@ -884,13 +873,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 const int gcol = __ldg(p.groups + st) * kGroup;
                 const int nh = p.n_sub == 2 ? 2 : 1;
                 for (int h = 0; h < nh; ++h) {
-                    if (p.spread) {
-                        for (int j = 0; j < p.n_xbox; ++j)
-                            tma_2d(&p.tm_lh[pc.seg * p.n_sub + h], act + h * kActBox + j * 4096, fb, gcol, 16 * j, pol_x);
-                    } else {
-                        for (int b = 0; b < p.tb; ++b)
-                            tma_2d(&p.tm_lh[pc.seg * p.n_sub + h], act + (h * p.tb + b) * kActBox, fb, gcol, b * kTcTok, pol_x);
-                    }
+                    for (int b = 0; b < p.tb; ++b)
+                        tma_2d(&p.tm_lh[pc.seg * p.n_sub + h], act + (h * p.tb + b) * kActBox, fb, gcol, b * kTcTok, pol_x);
                 }
                 return true;
             };
@@ -1063,7 +1047,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             const uint32_t tphase = (uint32_t)((it / acc_stages) & 1);
             float cf[32];
             if (pc.shrink)  // loads overlap the MMAs of this piece
-                gate_coefs(pc.t, p.spread ? (lane < 16 ? 16 * q + lane : 0) : tok_lane, cf);
+                gate_coefs(pc.t, tok_lane, cf);
             // Wait for this piece's accumulator; meanwhile take a share of the
             // shrink conversion as soon as the converter opens it (the expand
             // steps of every CTA wait for it).
@@ -1099,10 +1083,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             const uint32_t t_acc = tmem_base + lane_off + (uint32_t)(acc * cols_per_acc);
             const int mode = pc.shrink ? TC_SHRINK_HM : p.mode;
             // token held by this thread's TMEM lane in token block b (-1: none)
-            auto token_of = [&](int b) -> int {
-                if (p.spread) return lane < 16 ? 16 * q + lane : -1;
-                return b * kTcTok + tok_lane;
-            };
+            auto token_of = [&](int b) -> int { return b * kTcTok + tok_lane; };
             if (pc.n == 1 && pc.shrink) {  // whole shrink tile: gate and store hm from TMEM
                 for (int b = 0; b < p.tb; ++b) {
                     const int tok = token_of(b);
@@ -1673,13 +1654,6 @@ int tc_encode_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uin
 size_t tc_tail_bytes(const TcParams&) { return kTcTailBytes; }  // mbarriers and flags
 int tc_max_dynamic_smem();
 
-bool tc_spread(int T) {
-    static const bool on = [] {  // tuning knob, off by default (measured slower on config 3)
-        const char* e = getenv("AOS_SPREAD");
-        return e && e[0] == '1';
-    }();
-    return on && tc_t_pad(T) <= 64;
-}
 
 size_t tc_smem_bytes(const TcParams& p) {
     return 1024 + (size_t)p.n_stages * p.stage_bytes + tc_tail_bytes(p);
@@ -1697,8 +1671,6 @@ int tc_prepare(TcParams& p, int smem_budget) {
     p.T_pad = tc_t_pad(p.T);
     p.T_box = tc_t_box(p.T);
     p.tb = (p.T_pad + kTcTok - 1) / kTcTok;
-    p.spread = tc_spread(p.T) ? 1 : 0;
-    p.n_xbox = p.spread ? p.T_pad / 16 : 0;
     // stage: 256 weight rows x 128 B, then one 128-row activation box per
     // token block (two for the gate/up expand, whose halves read different hm)
     const int n_act = p.tb * ((p.n_sub == 2 && p.lora) ? 2 : 1);

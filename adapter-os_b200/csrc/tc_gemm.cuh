@@ -46,7 +46,6 @@ struct TcParams {
     CUtensorMap tm_lh[kTcMaxSets];     // gated shrink output hm [T, R], SW128 box 64 x T_box
     int mode, n_sub, n_seg, T, T_pad, T_box, tb, kb, n_stages, lora;
     int pools;                      // work pools: 1 shrink K steps, 2 base K steps, 4 expand steps
-    int add_out;                    // TC_QKV_ROPE: add to the stored q / K / V (expand-only launch)
     int sh_nseg;                    // shrink segments (LoRA modules that read X), 0 = none
     int n_rgroups;                  // rank groups of the arena (R / 64)
     int seg_tiles[kTcMaxSets];      // tiles per segment (256 rows; gate/up: 128 features)
@@ -95,10 +94,7 @@ struct TcParams {
     // the fixed-point adds into acc, which touch only a token's own adapters'
     // columns.  Null selects fixed-point adds for base tiles too.
     float* part;
-    // Token placement in the MMA's M (TMEM lanes): with spread (T <= 64) token
-    // t sits in lane 32 * (t / 16) + t % 16, so all four lane quarters (drain
-    // warps) hold tokens; otherwise token t sits in lane t % 128 of block t / 128.
-    int spread, n_xbox;             // spread mode; 16-row activation boxes per step (spread)
+    // Token t sits in TMEM lane t % 128 of MMA token block t / 128.
     int* sync;                      // [4] grid barriers (shrink drained, shrink reduced, all drained, exit)
     int* err;                       // device error word (0 = ok)
     unsigned long long* trace;      // optional per-CTA %globaltimer trace (null = off)
@@ -123,10 +119,9 @@ int tc_encode_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uin
                  uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1, uint32_t b2,
                  int swizzle_bytes);
 // Token padding of a batch of T (T_pad: multiple of 16) and the activation box
-// height: 16-row boxes when T <= 64 (spread placement), else up to 128 rows.
+// height: T_pad rows, at most 128 (one MMA token block).
 inline int tc_t_pad(int T) { return ((T + 15) / 16) * 16; }
-bool tc_spread(int T);  // spread placement for this batch (T <= 64 and AOS_SPREAD=1)
-inline int tc_t_box(int T) { return tc_spread(T) ? 16 : (tc_t_pad(T) < kTcTok ? tc_t_pad(T) : kTcTok); }
+inline int tc_t_box(int T) { return tc_t_pad(T) < kTcTok ? tc_t_pad(T) : kTcTok; }
 // Fills T_pad, tb, T_box, stage sizes; returns 0 or an aos_status.
 int tc_prepare(TcParams& p, int smem_budget);
 // Launch on `grid` CTAs; every CTA must be resident at once (grid <= SM

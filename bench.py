@@ -355,6 +355,8 @@ def run_reference(args, rank, world):
     value = float(np.median(vals))
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * CFG["batch"] / value,
+            "ms_per_step_kind": "extrapolated from each step's bounded sample (1 of 32 layers x 16 tokens + an "
+                                "lm_head slice), not a timed full step",
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "config 3: 32-layer 8B-shape decode, batch 64, K=4 of 128 LoRAs (ranks 8-64), "
                                    "paged KV block 16, ctx U[512,4096]", "parallelism": "cpu",
@@ -1043,6 +1045,9 @@ def main():
         # launch the step enqueues (the LoRA prep and the attention enqueue two
         # kernels each: prep + coefficient table, decode + combine)
         lc = prof["launches"]
+        # whole step: projections (base + selected LoRA + activations), attention
+        # (KV + q/out) and the lm_head weights, per step of the instrumented pass
+        step_bytes = proj_bytes / PS + abytes / PS + c["vocab"] * c["hidden"] * 2
         launches_per_step = 1 + (sum(lc.values()) + lc["prep"] + lc["attention"]) / PS
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
@@ -1056,14 +1061,20 @@ def main():
             "roofline": {"bound": "hbm", "kernel": "tc_gemm_kernel (base + fused LoRA shrink/expand)",
                          "achieved": proj_gbs, "peak": peak, "unit": "GB/s", "frac": proj_gbs / peak,
                          "traffic": GEMM_DRAM_BYTES_PER_LAYER * args.layers, "traffic_unit": "bytes per step",
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one layer's GEMM "
-                                           "launches (2-layer case), times the layers",
+                         "traffic_source": "a separate ncu capture, not this run: dram__bytes_read.sum + "
+                                           "dram__bytes_write.sum of one layer's four GEMM launches on the 2-layer "
+                                           "case (its own routing draw), times the layers",
                          "peak_kind": peak_kind,
                          "bytes_per_step": proj_bytes / PS, "ms_per_step": proj_ms / PS,
                          "launches_per_step": n_gemm_launches / PS, "unique_adapters_per_step": n_sel / PS},
             "roofline_attention": {"bound": "hbm", "kernel": "attn_decode_kernel + attn_combine_kernel",
                                    "achieved": attn_gbs, "peak": peak, "unit": "GB/s", "frac": attn_gbs / peak,
                                    "bytes_per_step": abytes / PS, "ms_per_step": prof["ms"]["attention"] / PS},
+            "roofline_step": {"bound": "hbm", "what": "whole decode step: projections + attention + lm_head "
+                                                      "algorithmic bytes over the timed (graphed) step",
+                              "bytes_per_step": step_bytes, "ms_per_step": ms / K,
+                              "achieved": step_bytes / (ms / K / 1000.0) / 1e9, "peak": peak, "unit": "GB/s",
+                              "frac": step_bytes / (ms / K / 1000.0) / 1e9 / peak},
             "kernel_ms_per_step": {k: v / PS for k, v in prof["ms"].items()},
             "instrumented_step_ms": step_ms_prof,
             "cpu_baseline": cpu,

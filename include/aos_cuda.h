@@ -554,9 +554,9 @@ typedef struct aos_profile {
 
 int aos_profile_enable(aos_ctx* ctx, int enable);
 int aos_profile_read(aos_ctx* ctx, aos_profile* out, int reset);
-/* Diagnostics: with AOS_TC_TRACE=<g> set before aos_init, the GEMM (g = 0..3:
- * qkv, o, gate/up, down; 4..7: their LoRA shrinks) of layer 0 writes per-CTA
- * %globaltimer stamps (256 slots per CTA); this copies n of them to host. */
+/* Diagnostics: with AOS_TC_TRACE=<g> set before aos_init, the GEMM launch g
+ * (0..3: qkv, o, gate/up, down) of layer 0 writes per-CTA %globaltimer stamps
+ * (256 slots per CTA); this copies n of them to host. */
 /* FusedKernels::memory_report (kernel-api/src/lib.rs:588-593): totals, and up
  * to max_allocs per-adapter allocations (id, bytes) in id order; *n_allocs
  * receives the number of loaded adapters. */
