@@ -53,6 +53,13 @@ cudaError_t launch_attention_prefill(const CUtensorMap& tm_k, const CUtensorMap&
                                      int nkv, int layer, int num_blocks, int max_blocks, int* err, uint16_t* out,
                                      cudaStream_t s);
 cudaError_t attn_configure();
+bool attn_prefill_tc_supported(int nq, int nkv);
+int attn_prefill_tc_block(int nq, int nkv);
+cudaError_t attn_tc_configure();
+cudaError_t launch_attention_prefill_tc(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                                        const int* block_tables, const int* pos, const int2* qblk, int n_qblk, int nq,
+                                        int nkv, int layer, int num_blocks, int max_blocks, int* err, uint16_t* out,
+                                        cudaStream_t s);
 }  // namespace aos
 
 using namespace aos;
@@ -902,7 +909,7 @@ int prefill_gemm_params(aos_ctx* c, int layer, int g, int T, bool shrink, TcPara
 
 // One prefill layer: per input group, the LoRA shrink launch then the base +
 // expand launch (data-parallel prefill GEMM), with causal attention between.
-int enqueue_prefill_layer(aos_ctx* c, int layer, int T, int n_qblk, cudaStream_t s) {
+int enqueue_prefill_layer(aos_ctx* c, int layer, int T, int n_qblk, const CUtensorMap* tm_q, cudaStream_t s) {
     auto& b = c->pf;
     const uint32_t H = c->cfg.hidden;
     const int gmod[4] = {AOS_MOD_Q, AOS_MOD_O, AOS_MOD_GATE, AOS_MOD_DOWN};
@@ -920,10 +927,16 @@ int enqueue_prefill_layer(aos_ctx* c, int layer, int T, int n_qblk, cudaStream_t
     int rc;
     PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(b.hidden, c->attn_norm[layer], T, (int)H, c->cfg.rms_eps, b.normed, s));
     if ((rc = gemm(kGroupQKV))) return rc;
-    PLAUNCH(c, AOS_K_ATTN, s,
-            launch_attention_prefill(c->tm_k, c->tm_v, b.q, b.block_tables, b.pos, b.qblk, n_qblk, (int)c->cfg.n_heads,
-                                     (int)c->cfg.n_kv_heads, layer, (int)c->cfg.kv_num_blocks, c->max_blocks, c->d_err,
-                                     b.attn, s));
+    if (tm_q)  // tensor-core kernel: query blocks of 128 / G tokens
+        PLAUNCH(c, AOS_K_ATTN, s,
+                launch_attention_prefill_tc(*tm_q, c->tm_k, c->tm_v, b.block_tables, b.pos, b.qblk, n_qblk,
+                                            (int)c->cfg.n_heads, (int)c->cfg.n_kv_heads, layer,
+                                            (int)c->cfg.kv_num_blocks, c->max_blocks, c->d_err, b.attn, s));
+    else  // GQA groups that do not divide 128 rows: query blocks of 16 tokens on mma.sync
+        PLAUNCH(c, AOS_K_ATTN, s,
+                launch_attention_prefill(c->tm_k, c->tm_v, b.q, b.block_tables, b.pos, b.qblk, n_qblk,
+                                         (int)c->cfg.n_heads, (int)c->cfg.n_kv_heads, layer,
+                                         (int)c->cfg.kv_num_blocks, c->max_blocks, c->d_err, b.attn, s));
     if ((rc = gemm(kGroupO))) return rc;
     PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(b.hidden, c->mlp_norm[layer], T, (int)H, c->cfg.rms_eps, b.normed, s));
     if ((rc = gemm(kGroupGU))) return rc;
@@ -1111,6 +1124,7 @@ aos_ctx* aos_init(const aos_model_config* cfg) {
     }
     INIT_CHECK(tc_configure(), "GEMM smem attribute");
     INIT_CHECK(attn_configure(), "attention smem attribute");
+    INIT_CHECK(attn_tc_configure(), "tensor-core prefill attention smem attribute");
     INIT_CHECK(cudaEventCreate(&c->ev0), "event");
     INIT_CHECK(cudaEventCreate(&c->ev1), "event");
     INIT_CHECK(cudaDeviceSynchronize(), "init sync");
@@ -1745,6 +1759,10 @@ int prefill_run(aos_ctx* c, uint32_t n_seq, const uint64_t* seq_ids, const uint3
     if (T > (1u << 24)) return c->fail(AOS_ERR_INVALID, "prompt batch too large");
     std::vector<int> pos(T), bt(T * (size_t)c->max_blocks, 0);
     std::vector<int2> qblk;
+    // query blocks of the prompt attention: 128 / G tokens (the tensor-core
+    // kernel's 128 MMA rows hold the GQA group's heads for each token), else 16
+    const bool attn_tc = attn_prefill_tc_supported((int)c->cfg.n_heads, (int)c->cfg.n_kv_heads);
+    const uint32_t qb_size = attn_tc ? (uint32_t)attn_prefill_tc_block((int)c->cfg.n_heads, (int)c->cfg.n_kv_heads) : 16u;
     std::vector<size_t> last(n_seq);
     size_t t = 0;
     for (uint32_t i = 0; i < n_seq; ++i) {
@@ -1757,7 +1775,7 @@ int prefill_run(aos_ctx* c, uint32_t n_seq, const uint64_t* seq_ids, const uint3
         for (uint32_t j = 0; j < n_tok[i]; ++j, ++t) {
             pos[t] = (int)(sq.len + j);
             std::copy(sq.blocks.begin(), sq.blocks.end(), bt.begin() + t * c->max_blocks);
-            if (j % 16 == 0) qblk.push_back(make_int2((int)t, (int)std::min<uint32_t>(16, n_tok[i] - j)));
+            if (j % qb_size == 0) qblk.push_back(make_int2((int)t, (int)std::min<uint32_t>(qb_size, n_tok[i] - j)));
         }
         last[i] = t - 1;
     }
@@ -1773,8 +1791,11 @@ int prefill_run(aos_ctx* c, uint32_t n_seq, const uint64_t* seq_ids, const uint3
             launch_lora_prep(b.rings, (int)T, c->d_col_off, c->d_rank, c->d_scale, (int)c->cfg.lora_max_adapters,
                              c->R / kGroup, c->d_groups, c->d_n_groups, b.coef, c->d_col_owner, b.ucoef, s));
     PLAUNCH(c, AOS_K_EMBED, s, launch_embed(c->embed, b.tokens, (int)T, (int)c->cfg.hidden, (int)c->cfg.vocab, b.hidden, s));
+    CUtensorMap tm_q{};  // the q buffer [cap][n_heads * 128], boxes of 64 dims x qb_size tokens
+    if (attn_tc && tc_encode_2d(&tm_q, b.q, (uint64_t)c->QD, (uint64_t)b.cap, (uint64_t)c->QD * 2, 64, qb_size, 128))
+        return c->fail(AOS_ERR_CUDA, "prefill q tensor map encode failed");
     for (uint32_t l = 0; l < c->cfg.n_layers; ++l)
-        if ((rc = enqueue_prefill_layer(c, (int)l, (int)T, (int)qblk.size(), s))) return rc;
+        if ((rc = enqueue_prefill_layer(c, (int)l, (int)T, (int)qblk.size(), attn_tc ? &tm_q : nullptr, s))) return rc;
     // every sequence's last token: final norm and lm_head on the decode buffers
     const size_t H = c->cfg.hidden;
     for (uint32_t i = 0; i < n_seq; ++i)

@@ -689,7 +689,7 @@ def run_config4(args, rank, world, local):
             "roofline_gemm": {"bound": "tensor", "kernel": "pf_gemm_kernel (base + LoRA shrink/expand)",
                               "achieved": gemm_tf, "peak": peak, "unit": "TFLOP/s", "frac": gemm_tf / peak,
                               "ms_per_step": gemm_ms},
-            "roofline_attention": {"bound": "tensor", "kernel": "attn_prefill_kernel (mma.sync)",
+            "roofline_attention": {"bound": "tensor", "kernel": "attn_prefill_tc_kernel (tcgen05, TMEM)",
                                    "achieved": attn_tf, "peak": peak, "unit": "TFLOP/s", "frac": attn_tf / peak,
                                    "ms_per_step": prof["ms"]["attention"]},
             "lora_flop_executed_per_step": lora_exec_flop,

@@ -2,6 +2,9 @@
 time (oracle/aos_oracle.cpp: the decode step of mlx_cpp_wrapper_real.cpp:3338-3559
 at consecutive positions is the causal prompt pass).
 
+The prompt attention runs on the tensor-core kernel (attention_tc.cu) when the
+GQA group size divides 128, else on the mma.sync kernel; both are checked.
+
 Small case: three prompts (37 tokens from an empty cache, 50 tokens after 20
 cached ones, a single token) in one 256-token tile.  Multi-tile case: prompts
 of 300 tokens, 2100 tokens after 24 cached ones, and 5 tokens (2405 tokens:
@@ -108,5 +111,14 @@ def test_prefill_matches_oracle():
     _check_prefill()
 
 
-def test_prefill_multi_tile_matches_oracle():
-    _check_prefill(seed=11, prompts=((0, 300), (24, 2100), (0, 5)), max_seq=2144)
+@pytest.mark.parametrize("nh,nkv", [(4, 2), (8, 2)])
+def test_prefill_multi_tile_matches_oracle(nh, nkv):
+    """GQA groups of 2 and 4 (config 4's group): the tensor-core attention with
+    query blocks of 64 and 32 tokens, 128-key tiles up to 2124 positions."""
+    _check_prefill(seed=11, nh=nh, nkv=nkv, prompts=((0, 300), (24, 2100), (0, 5)), max_seq=2144)
+
+
+def test_prefill_gqa3_mma_sync_path():
+    """A GQA group of 3 does not divide the tensor-core kernel's 128 rows: the
+    prompt attention runs on the mma.sync kernel (16-token query blocks)."""
+    _check_prefill(seed=13, nh=6, nkv=2, prompts=((0, 70), (33, 150), (0, 1)), max_seq=256)
