@@ -7,10 +7,11 @@
 // (mlx_cpp_wrapper_real.cpp:3284-3324 with the causal mask;
 // flash_attention.metal:23-97 for the tiled online softmax).
 //
-// One CTA per (block of TB = 128 / G consecutive prompt tokens of one
-// sequence, KV head).  The MMA's 128 rows are the group's G query heads times
-// the block's tokens (row r = head r / TB, token r % TB), so each K/V tile is
-// loaded once for the whole GQA group.
+// A unit of work is (block of TB = 128 / G consecutive prompt tokens of one
+// sequence, KV head); persistent CTAs walk the units, longest first.  The
+// MMA's 128 rows are the group's G query heads times the block's tokens
+// (row r = head r / TB, token r % TB), so each K/V tile is loaded once for the
+// whole GQA group.
 //   warp 0    : TMA producer -- the Q block once, then K and V tiles of 128
 //               keys (8 pages of 16, each page two SWIZZLE_128B boxes of 64
 //               dims)
@@ -223,6 +224,32 @@ __device__ __forceinline__ uint32_t idesc_128(bool b_mn) {
            ((uint32_t)(128 >> 4) << 24);
 }
 
+// One attention unit: a query block of one sequence and a KV head.
+struct AtUnit {
+    int t0, nt, kvh, p_first, last_page, n_tiles;
+    const int* bt;
+};
+__device__ __forceinline__ AtUnit at_unit(const PfAttnTcParams& p, int u) {
+    AtUnit a;
+    const int qb = p.n_qblk - 1 - u / p.nkv;  // longest blocks (latest in each prompt) first
+    a.kvh = u % p.nkv;
+    const int2 blk = __ldg(p.qblk + qb);
+    a.t0 = blk.x;
+    a.nt = blk.y;
+    a.p_first = __ldg(p.pos + a.t0);
+    const int p_last = a.p_first + a.nt - 1;
+    a.last_page = p_last >> 4;
+    a.n_tiles = p_last / kAtKeys + 1;
+    a.bt = p.block_tables + (size_t)a.t0 * p.max_blocks;
+    return a;
+}
+
+// Persistent: CTA c takes units c, c + grid, c + 2 grid, ... (longest first).
+// Barriers complete once per key tile across all units (parity = the CTA's
+// running tile count J), q_full and o_free once per unit (parity = the CTA's
+// unit count U).  The producer loads a unit's Q as soon as the previous unit's
+// last S has read its Q, so the next unit's first copies overlap the previous
+// unit's last softmax, PV and output.
 __global__ void __launch_bounds__(kAtThreads, 2) attn_prefill_tc_kernel(const __grid_constant__ PfAttnTcParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -230,26 +257,19 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_prefill_tc_kernel(const __
     const uint32_t k_s = q_s + kAtQBytes;
     const uint32_t v_s = k_s + kAtTileBytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kAtQBytes + 2 * kAtTileBytes);
-    uint64_t* q_full = bars;       // Q block landed
-    uint64_t* k_full = bars + 1;   // K_j landed
-    uint64_t* v_full = bars + 2;   // V_j landed
-    uint64_t* k_empty = bars + 3;  // MMA: S_j done (K stage free)
-    uint64_t* s_full = bars + 4;   // MMA: S_j in TMEM
-    uint64_t* p_full = bars + 5;   // softmax: P_j written over S_j, O rescaled (4 warps)
-    uint64_t* pv_done = bars + 6;  // MMA: PV_j done (V stage, S/P columns and O free)
-    uint64_t* drain = bars + 7;    // MMA error path
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+    uint64_t* q_full = bars;       // a unit's Q block landed
+    uint64_t* k_full = bars + 1;   // K_J landed
+    uint64_t* v_full = bars + 2;   // V_J landed
+    uint64_t* k_empty = bars + 3;  // MMA: S_J done (K stage free; after a unit's last S, its Q too)
+    uint64_t* s_full = bars + 4;   // MMA: S_J in TMEM
+    uint64_t* p_full = bars + 5;   // softmax: P_J written over S_J, O rescaled (4 warps)
+    uint64_t* pv_done = bars + 6;  // MMA: PV_J done (V stage, S/P columns and O free)
+    uint64_t* o_free = bars + 7;   // softmax: a unit's O read out (4 warps)
+    uint64_t* drain = bars + 8;    // MMA error path
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // longest blocks (latest in each prompt) first
-    const int qb = p.n_qblk - 1 - (int)(blockIdx.x / p.nkv);
-    const int kvh = (int)(blockIdx.x % p.nkv);
-    const int2 blk = __ldg(p.qblk + qb);
-    const int t0 = blk.x, nt = blk.y;
-    const int p_first = __ldg(p.pos + t0);
-    const int p_last = p_first + nt - 1;
-    const int last_page = p_last >> 4;
-    const int n_tiles = p_last / kAtKeys + 1;
+    const int n_units = p.n_qblk * p.nkv;
 
     if (threadIdx.x == 0) {
         mbar_init(smem_u32(q_full), 1);
@@ -259,6 +279,7 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_prefill_tc_kernel(const __
         mbar_init(smem_u32(s_full), 1);
         mbar_init(smem_u32(p_full), 4);
         mbar_init(smem_u32(pv_done), 1);
+        mbar_init(smem_u32(o_free), 4);
         mbar_init(smem_u32(drain), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -275,38 +296,43 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_prefill_tc_kernel(const __
 
     if (warp == 0) {
         // ============================ TMA producer ============================
-        // Tile j's K goes in once S_{j-1} is done, its V once PV_{j-1} is done.
         if (lane == 0) {
             pdl_wait();  // q and the prompt's own K/V rows come from the previous launches
             pdl_trigger();
-            const int* bt = p.block_tables + (size_t)t0 * p.max_blocks;
-            mbar_expect_tx(smem_u32(q_full), (uint32_t)(p.G * p.TB) * 256u);
-            for (int g = 0; g < p.G; ++g)
-                for (int c = 0; c < 2; ++c)
-                    tma_2d(&p.tm_q, q_s + c * kAtHalf + g * p.TB * 128, smem_u32(q_full), (kvh * p.G + g) * 128 + 64 * c,
-                           t0);
-            auto load = [&](const CUtensorMap* m, uint32_t base, uint64_t* full, int j) {
+            int J = 0, q_issued = 0, k_issued = 0, v_issued = 0;
+            bool ok = true;
+            auto load = [&](const CUtensorMap* m, uint32_t base, uint64_t* full, const AtUnit& a, int j) {
                 mbar_expect_tx(smem_u32(full), kAtTileBytes);
                 for (int pg = 0; pg < kAtPages; ++pg) {
                     // pages past the block's last position repeat that page (masked; finite values)
-                    const int page = min(j * kAtPages + pg, last_page);
-                    const int row = ((p.layer * p.num_blocks + __ldg(bt + page)) * p.nkv + kvh) * 16;
+                    const int page = min(j * kAtPages + pg, a.last_page);
+                    const int row = ((p.layer * p.num_blocks + __ldg(a.bt + page)) * p.nkv + a.kvh) * 16;
                     for (int h = 0; h < 2; ++h) tma_2d(m, base + h * kAtHalf + pg * 2048, smem_u32(full), 64 * h, row);
                 }
             };
-            int k_issued = 0, v_issued = 0;
-            for (int j = 0; j < n_tiles; ++j) {
-                const uint32_t prev = ((uint32_t)j & 1u) ^ 1u;  // completion j - 1 (a fresh barrier passes)
-                if (!mbar_wait(smem_u32(k_empty), prev, p.err)) break;
-                load(&p.tm_k, k_s, k_full, j);
-                ++k_issued;
-                if (!mbar_wait(smem_u32(pv_done), prev, p.err)) break;
-                load(&p.tm_v, v_s, v_full, j);
-                ++v_issued;
+            for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+                const AtUnit a = at_unit(p, u);
+                for (int j = 0; j < a.n_tiles; ++j, ++J) {
+                    const uint32_t prev = ((uint32_t)J & 1u) ^ 1u;  // completion J - 1 (a fresh barrier passes)
+                    if (!mbar_wait(smem_u32(k_empty), prev, p.err)) { ok = false; break; }
+                    if (j == 0) {  // the previous unit's last S has read its Q
+                        ++q_issued;
+                        mbar_expect_tx(smem_u32(q_full), (uint32_t)(p.G * p.TB) * 256u);
+                        for (int g = 0; g < p.G; ++g)
+                            for (int c = 0; c < 2; ++c)
+                                tma_2d(&p.tm_q, q_s + c * kAtHalf + g * p.TB * 128, smem_u32(q_full),
+                                       (a.kvh * p.G + g) * 128 + 64 * c, a.t0);
+                    }
+                    load(&p.tm_k, k_s, k_full, a, j);
+                    ++k_issued;
+                    if (!mbar_wait(smem_u32(pv_done), prev, p.err)) { ok = false; break; }
+                    load(&p.tm_v, v_s, v_full, a, j);
+                    ++v_issued;
+                }
             }
             // every issued copy lands before the CTA may exit (the older ones
-            // were consumed before their stage was refilled)
-            mbar_wait_drain(smem_u32(q_full), 0);
+            // were consumed before their buffer was refilled)
+            if (q_issued) mbar_wait_drain(smem_u32(q_full), (uint32_t)(q_issued - 1) & 1u);
             if (k_issued) mbar_wait_drain(smem_u32(k_full), (uint32_t)(k_issued - 1) & 1u);
             if (v_issued) mbar_wait_drain(smem_u32(v_full), (uint32_t)(v_issued - 1) & 1u);
         }
@@ -314,35 +340,38 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_prefill_tc_kernel(const __
         // ============================ MMA issuer ==============================
         if (lane == 0) {
             const uint32_t id_s = idesc_128(false), id_pv = idesc_128(true);
-            bool ok = mbar_wait(smem_u32(q_full), 0, p.err);
-            bool any = false;
-            for (int j = 0; ok && j < n_tiles; ++j) {
-                const uint32_t par = (uint32_t)j & 1u;
-                // S_j overwrites the S/P columns: PV_{j-1} must have read P_{j-1}
-                if (!mbar_wait(smem_u32(k_full), par, p.err) ||
-                    (j > 0 && !mbar_wait(smem_u32(pv_done), par ^ 1u, p.err))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
+            bool ok = true, any = false;
+            int J = 0, U = 0;
+            for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++U) {
+                const AtUnit a = at_unit(p, u);
+                if (!mbar_wait(smem_u32(q_full), (uint32_t)U & 1u, p.err)) { ok = false; break; }
+                for (int j = 0; j < a.n_tiles; ++j, ++J) {
+                    const uint32_t par = (uint32_t)J & 1u;
+                    // S_J overwrites the S/P columns that PV_{J-1} reads as its A
+                    // operand; MMAs issued by one thread run in issue order, so
+                    // S_J's accumulator writes come after PV_{J-1}'s operand reads
+                    if (!mbar_wait(smem_u32(k_full), par, p.err)) { ok = false; break; }
+                    tc_fence_after();
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t off = (uint32_t)(kk >> 2) * kAtHalf + (uint32_t)(kk & 3) * 32;
-                    umma_ss(tmem + kColS, desc_k(q_s + off), desc_k(k_s + off), id_s, kk > 0 ? 1u : 0u);
-                }
-                any = true;
-                umma_commit(smem_u32(k_empty));
-                umma_commit(smem_u32(s_full));
-                if (!mbar_wait(smem_u32(p_full), par, p.err) || !mbar_wait(smem_u32(v_full), par, p.err)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t off = (uint32_t)(kk >> 2) * kAtHalf + (uint32_t)(kk & 3) * 32;
+                        umma_ss(tmem + kColS, desc_k(q_s + off), desc_k(k_s + off), id_s, kk > 0 ? 1u : 0u);
+                    }
+                    any = true;
+                    umma_commit(smem_u32(k_empty));
+                    umma_commit(smem_u32(s_full));
+                    if (!mbar_wait(smem_u32(p_full), par, p.err) || !mbar_wait(smem_u32(v_full), par, p.err) ||
+                        (j == 0 && U > 0 && !mbar_wait(smem_u32(o_free), (uint32_t)(U - 1) & 1u, p.err))) {
+                        ok = false;  // (a unit's first PV overwrites O: the previous unit's O is read out)
+                        break;
+                    }
+                    tc_fence_after();
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk)  // 16 keys per step: 8 TMEM columns of P, 2048 bytes of V
-                    umma_ts(tmem + kColO, tmem + kColS + 8 * kk, desc_mn(v_s + kk * 2048), id_pv,
-                            (j > 0 || kk > 0) ? 1u : 0u);
-                umma_commit(smem_u32(pv_done));
+                    for (int kk = 0; kk < 8; ++kk)  // 16 keys per step: 8 TMEM columns of P, 2048 bytes of V
+                        umma_ts(tmem + kColO, tmem + kColS + 8 * kk, desc_mn(v_s + kk * 2048), id_pv,
+                                (j > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit(smem_u32(pv_done));
+                }
             }
             if (!ok && any) {  // the MMAs already issued finish before TMEM is freed
                 umma_commit(smem_u32(drain));
@@ -354,103 +383,109 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_prefill_tc_kernel(const __
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         const int r = q * 32 + lane;
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-        const int g = r / p.TB, i = r % p.TB;
-        const bool valid = g < p.G && i < nt;
-        const int qpos = valid ? p_first + i : -1;  // a row that is no query masks every key
         const uint32_t sb = tmem + lane_off + kColS, ob = tmem + lane_off + kColO;
-        float m_used = -INFINITY, l = 0.f;
+        const int g = r / p.TB, i = r % p.TB;
         bool ok = true;
-        for (int j = 0; j < n_tiles; ++j) {
-            const uint32_t par = (uint32_t)j & 1u;
-            const bool got = mbar_wait(smem_u32(s_full), par, p.err);
-            if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
-            tc_fence_after();
-            const int k0 = j * kAtKeys;
-            // the row's 128 scores in registers (two TMEM round trips); a tile
-            // whose keys all precede the block's first query needs no mask
-            float v[kAtKeys];
-            tmem_ld64(sb, v);
-            tmem_ld64(sb + 64, v + 64);
-            if (k0 + kAtKeys - 1 > p_first) {
-#pragma unroll
-                for (int e = 0; e < kAtKeys; ++e)
-                    if (k0 + e > qpos) v[e] = -INFINITY;
-            }
-            // tile maximum from eight partial maxima (the scale is positive, so
-            // max(v) * scale = max(v * scale))
-            float mx[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) mx[e] = v[e];
-#pragma unroll
-            for (int e = 8; e < kAtKeys; ++e) mx[e & 7] = fmaxf(mx[e & 7], v[e]);
-            const float tmax =
-                fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
-                p.scale_log2;
-            const bool raise = tmax > -INFINITY && (m_used == -INFINITY || tmax > m_used + kLazyMax);
-            const float m_new = raise ? tmax : m_used;
-            const float m_sub = m_new > -INFINITY ? m_new : 0.f;  // a row with no key yet: every score is -inf
-            // a raised maximum rescales O once PV_{j-1} is done, and l
-            const float alpha = (raise && m_used > -INFINITY) ? ex2(m_used - m_new) : 1.f;
-            if (__any_sync(0xffffffffu, alpha != 1.f)) {
-                const bool got_o = mbar_wait(smem_u32(pv_done), par ^ 1u, p.err);
-                if (!__all_sync(0xffffffffu, got_o)) { ok = false; break; }
+        int J = 0;
+        for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+            const AtUnit a = at_unit(p, u);
+            const bool valid = g < p.G && i < a.nt;
+            const int qpos = valid ? a.p_first + i : -1;  // a row that is no query masks every key
+            float m_used = -INFINITY, l = 0.f;
+            for (int j = 0; j < a.n_tiles; ++j, ++J) {
+                const uint32_t par = (uint32_t)J & 1u;
+                const bool got = mbar_wait(smem_u32(s_full), par, p.err);
+                if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
                 tc_fence_after();
+                const int k0 = j * kAtKeys;
+                // the row's 128 scores in registers (two TMEM round trips); a tile
+                // whose keys all precede the block's first query needs no mask
+                float v[kAtKeys];
+                tmem_ld64(sb, v);
+                tmem_ld64(sb + 64, v + 64);
+                if (k0 + kAtKeys - 1 > a.p_first) {
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    float o[32];
-                    tmem_ld32(ob + 32 * c, o);
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) o[e] *= alpha;
-                    tmem_st32(ob + 32 * c, o);
+                    for (int e = 0; e < kAtKeys; ++e)
+                        if (k0 + e > qpos) v[e] = -INFINITY;
                 }
-            }
-            // probabilities as bf16 pairs over the S columns (every score of the
-            // row is already in registers); their sum from eight partial sums
-            // in a fixed order
-            float sp[8];
+                // tile maximum from eight partial maxima (the scale is positive, so
+                // max(v) * scale = max(v * scale))
+                float mx[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) sp[e] = 0.f;
+                for (int e = 0; e < 8; ++e) mx[e] = v[e];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t u[16];
+                for (int e = 8; e < kAtKeys; ++e) mx[e & 7] = fmaxf(mx[e & 7], v[e]);
+                const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                         fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
+                                   p.scale_log2;
+                const bool raise = tmax > -INFINITY && (m_used == -INFINITY || tmax > m_used + kLazyMax);
+                const float m_new = raise ? tmax : m_used;
+                const float m_sub = m_new > -INFINITY ? m_new : 0.f;  // a row with no key yet: every score is -inf
+                // a raised maximum rescales O once PV_{J-1} is done, and l
+                const float alpha = (raise && m_used > -INFINITY) ? ex2(m_used - m_new) : 1.f;
+                if (__any_sync(0xffffffffu, alpha != 1.f)) {
+                    const bool got_o = mbar_wait(smem_u32(pv_done), par ^ 1u, p.err);
+                    if (!__all_sync(0xffffffffu, got_o)) { ok = false; break; }
+                    tc_fence_after();
 #pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    const float p0 = ex2(fmaf(v[32 * c + e], p.scale_log2, -m_sub));
-                    const float p1 = ex2(fmaf(v[32 * c + e + 1], p.scale_log2, -m_sub));
-                    sp[(e >> 1) & 7] += p0 + p1;
-                    u[e >> 1] = bf16x2(p0, p1);
-                }
-                tmem_st16(sb + 16 * c, u);
-            }
-            l = l * alpha + (((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7])));
-            m_used = m_new;
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(p_full));  // P_j written, O rescaled: PV_j may run
-        }
-        if (ok) {  // O / l once the last PV is done
-            const bool got = mbar_wait(smem_u32(pv_done), (uint32_t)(n_tiles - 1) & 1u, p.err);
-            if (__all_sync(0xffffffffu, got)) {
-                tc_fence_after();
-                const float inv = l > 0.f ? 1.f / l : 0.f;
-                uint16_t* dst = p.out + (size_t)(t0 + i) * p.nq * 128 + (size_t)(kvh * p.G + g) * 128;
+                    for (int c = 0; c < 4; ++c) {
+                        float o[32];
+                        tmem_ld32(ob + 32 * c, o);
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    float o[32];
-                    tmem_ld32(ob + 32 * c, o);
-                    if (!valid) continue;
-#pragma unroll
-                    for (int e = 0; e < 32; e += 8) {
-                        uint4 w;
-                        w.x = bf16x2(o[e] * inv, o[e + 1] * inv);
-                        w.y = bf16x2(o[e + 2] * inv, o[e + 3] * inv);
-                        w.z = bf16x2(o[e + 4] * inv, o[e + 5] * inv);
-                        w.w = bf16x2(o[e + 6] * inv, o[e + 7] * inv);
-                        *reinterpret_cast<uint4*>(dst + 32 * c + e) = w;
+                        for (int e = 0; e < 32; ++e) o[e] *= alpha;
+                        tmem_st32(ob + 32 * c, o);
                     }
                 }
+                // probabilities as bf16 pairs over the S columns (every score of the
+                // row is already in registers); their sum from eight partial sums
+                // in a fixed order
+                float sp[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) sp[e] = 0.f;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t w[16];
+#pragma unroll
+                    for (int e = 0; e < 32; e += 2) {
+                        const float p0 = ex2(fmaf(v[32 * c + e], p.scale_log2, -m_sub));
+                        const float p1 = ex2(fmaf(v[32 * c + e + 1], p.scale_log2, -m_sub));
+                        sp[(e >> 1) & 7] += p0 + p1;
+                        w[e >> 1] = bf16x2(p0, p1);
+                    }
+                    tmem_st16(sb + 16 * c, w);
+                }
+                l = l * alpha + (((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7])));
+                m_used = m_new;
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(p_full));  // P_J written, O rescaled: PV_J may run
             }
+            if (!ok) break;
+            // O / l once the unit's last PV is done; then O is free for the next unit
+            const bool got = mbar_wait(smem_u32(pv_done), (uint32_t)(J - 1) & 1u, p.err);
+            if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+            tc_fence_after();
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            uint16_t* dst = p.out + (size_t)(a.t0 + i) * p.nq * 128 + (size_t)(a.kvh * p.G + g) * 128;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                float o[32];
+                tmem_ld32(ob + 32 * c, o);
+                if (!valid) continue;
+#pragma unroll
+                for (int e = 0; e < 32; e += 8) {
+                    uint4 w;
+                    w.x = bf16x2(o[e] * inv, o[e + 1] * inv);
+                    w.y = bf16x2(o[e + 2] * inv, o[e + 3] * inv);
+                    w.z = bf16x2(o[e + 4] * inv, o[e + 5] * inv);
+                    w.w = bf16x2(o[e + 6] * inv, o[e + 7] * inv);
+                    *reinterpret_cast<uint4*>(dst + 32 * c + e) = w;
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(o_free));
         }
         tmem_wait_st();
     }
@@ -500,7 +535,11 @@ cudaError_t launch_attention_prefill_tc(const CUtensorMap& tm_q, const CUtensorM
     p.max_blocks = max_blocks;
     p.scale_log2 = 1.4426950408889634f / sqrtf(128.0f);
     p.err = err;
-    return launch_k(attn_prefill_tc_kernel, dim3(n_qblk * nkv), dim3(kAtThreads), kAtSmem, s, p);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int units = n_qblk * nkv, grid = units < 2 * sms ? units : 2 * sms;  // two CTAs per SM, persistent
+    return launch_k(attn_prefill_tc_kernel, dim3(grid), dim3(kAtThreads), kAtSmem, s, p);
 }
 
 }  // namespace aos
