@@ -171,6 +171,7 @@ struct aos_ctx {
     float* d_part = nullptr;      // GEMM fp32 partials of split base tiles
     uint16_t* d_fp = nullptr;     // adapter buffer samples [3][2048] for fingerprints
     int* d_sync = nullptr;        // [4] GEMM grid-barrier counters
+    int gemm_coop = 0;            // AOS_GEMM_COOPERATIVE=1: cooperative GEMM launches (shared device)
     int* d_err = nullptr;
     unsigned long long* d_trace = nullptr;  // AOS_TC_TRACE diagnostics
 
@@ -274,6 +275,7 @@ int build_owner_plan(aos_ctx* c, int layer, int g, int T, TcParams& p) {
     p.acc_T = c->T_cap;
     p.part = c->d_part;
     p.sync = c->d_sync;
+    p.cooperative = c->gemm_coop;
     p.err = c->d_err;
     p.R = c->R;
     p.n_rgroups = c->R / kGroup;
@@ -335,6 +337,7 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp, bool sharded =
         p.acc_T = c->T_cap;
         p.part = c->d_part;
         p.sync = c->d_sync;
+        p.cooperative = c->gemm_coop;
         p.err = c->d_err;
         p.R = c->R;
         p.n_rgroups = c->R / kGroup;
@@ -484,6 +487,7 @@ int get_plan(aos_ctx* c, int T, StepPlan** out, bool sharded = false) {
     p.acc_T = c->T_cap;
     p.part = c->d_part;
     p.sync = c->d_sync;
+    p.cooperative = c->gemm_coop;
     const uint32_t V = c->cfg.vocab;
     p.w_pk[0] = c->lm_head;
     int rc = tc_encode_2d(&p.tm_x, c->d_normed, c->cfg.hidden, (uint64_t)c->T_cap, (uint64_t)c->cfg.hidden * 2, 64,
@@ -1105,6 +1109,7 @@ aos_ctx* aos_init(const aos_model_config* cfg) {
     }
     INIT_CHECK(dalloc(&c->d_err, 1), "err");
     if (getenv("AOS_TC_TRACE")) INIT_CHECK(dalloc(&c->d_trace, (size_t)tc_num_sms() * kTraceStride), "trace");
+    if (const char* e = getenv("AOS_GEMM_COOPERATIVE")) c->gemm_coop = atoi(e) != 0 ? 1 : 0;
     // RoPE table, angles as the reference computes them (mlx_cpp_wrapper_real.cpp:3249-3268)
     {
         const uint32_t half = 64, P = k.max_seq_len + 1;

@@ -1718,7 +1718,17 @@ cudaError_t tc_configure() {
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(tc_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, g_tc_max_dyn);
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(pf_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, g_tc_max_dyn);
+    e = cudaFuncSetAttribute(pf_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, g_tc_max_dyn);
+    if (e != cudaSuccess) return e;
+    // The decode GEMM's grid (one CTA per SM) waits on itself at its grid
+    // barriers: every SM must hold one CTA at the largest shared-memory size.
+    for (auto* k : {tc_gemm_kernel<false>, tc_gemm_kernel<true>}) {
+        int per_sm = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kTcThreads, (size_t)g_tc_max_dyn);
+        if (e != cudaSuccess) return e;
+        if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
+    }
+    return cudaSuccess;
 }
 int tc_max_dynamic_smem() { return g_tc_max_dyn > 0 ? g_tc_max_dyn : 227 * 1024 - 4096; }
 
@@ -1751,8 +1761,13 @@ cudaError_t pf_launch(const TcParams& p, cudaStream_t stream) {
 cudaError_t tc_launch(const TcParams& p, int grid, cudaStream_t stream) {
     const size_t smem = tc_smem_bytes(p);
     if ((int)smem > tc_max_dynamic_smem()) return cudaErrorInvalidValue;
-    if (p.part) return launch_k(tc_gemm_kernel<true>, dim3(grid), dim3(kTcThreads), smem, stream, p);
-    return launch_k(tc_gemm_kernel<false>, dim3(grid), dim3(kTcThreads), smem, stream, p);
+    // The grid barriers need every CTA resident (one per SM).  On a device
+    // the context has to itself that holds by construction; in shared-device
+    // mode (p.cooperative) the launch asks for it, at the cost of the overlap
+    // with the neighbouring launches.
+    const bool coop = p.cooperative != 0;
+    if (p.part) return launch_k_ex(coop, tc_gemm_kernel<true>, dim3(grid), dim3(kTcThreads), smem, stream, p);
+    return launch_k_ex(coop, tc_gemm_kernel<false>, dim3(grid), dim3(kTcThreads), smem, stream, p);
 }
 
 }  // namespace aos

@@ -96,6 +96,7 @@ struct TcParams {
     float* part;
     // Token t sits in TMEM lane t % 128 of MMA token block t / 128.
     int* sync;                      // [4] grid barriers (shrink drained, shrink reduced, all drained, exit)
+    int cooperative;                // host side: launch as a cooperative grid (shared-device mode)
     int* err;                       // device error word (0 = ok)
     unsigned long long* trace;      // optional per-CTA %globaltimer trace (null = off)
 };

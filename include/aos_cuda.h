@@ -205,7 +205,16 @@ int aos_lora_op_f32_noalloc_dev(const float* x, uint32_t T, uint32_t in_dim, uin
 
 /* ---- context: FusedKernels::load + hot-swap arena + KV cache ------------- */
 /* Create a backend on cfg->device; allocates the KV pool, adapter arena and
- * step scratch up front (kernel-mtl/src/lib.rs:1476-1537 load). */
+ * step scratch up front (kernel-mtl/src/lib.rs:1476-1537 load).
+ * The decode projection GEMMs run one CTA per SM and wait on one another
+ * inside the launch; init checks that every SM can hold one such CTA.  By
+ * default they are plain launches, which assumes no other kernel occupies the
+ * device's SMs during a step (otherwise a step ends with AOS_ERR_TIMEOUT after
+ * about a second).  With AOS_GEMM_COOPERATIVE=1 in the environment at init
+ * they are cooperative launches, which the driver starts only with the whole
+ * grid resident (shared-device mode, about 3% slower per step: they give up
+ * the overlap with the neighbouring launches).  Results are bit-identical in
+ * both modes. */
 aos_ctx* aos_init(const aos_model_config* cfg);
 void aos_destroy(aos_ctx* ctx);
 /* FusedKernels::device_name (lib.rs:374). */

@@ -165,6 +165,20 @@ def test_decode_bit_identical_run_to_run():
     assert outs[0] == outs[1]
 
 
+def test_cooperative_gemm_mode_matches_default(monkeypatch):
+    """Shared-device mode (AOS_GEMM_COOPERATIVE=1 at init) launches the same
+    GEMMs as cooperative grids: the step's logits and hidden state are
+    bit-identical to the default launches."""
+    outs = []
+    for coop in ("0", "1"):
+        monkeypatch.setenv("AOS_GEMM_COOPERATIVE", coop)
+        s = Setup(seed=2)
+        logits, hidden = s.gpu.run_step_batch(s.rings, s.tokens.astype(np.uint32), s.seq_ids, want_hidden=True)
+        outs.append((logits.tobytes(), hidden.tobytes()))
+        s.gpu.close()
+    assert outs[0] == outs[1]
+
+
 def test_two_steps_and_unload():
     s = Setup(seed=3, ctx_lens=(5, 40, 64, 200, 17, 33, 1, 250), ranks=(16, 16, 8, 8, 32))
     toks = s.tokens.astype(np.uint32)
