@@ -174,6 +174,7 @@ def lib():
             "aos_kv_write": (C.c_int, [vp, u64, u32, u32, u32, vp, vp, C.c_int]),
             "aos_kv_read": (C.c_int, [vp, u64, u32, u32, u32, vp, vp]),
             "aos_kv_fill_synthetic": (C.c_int, [vp, u64, f32]),
+            "aos_kv_rotate": (C.c_int, [vp, u64, u32]),
             "aos_kv_clear_all": (C.c_int, [vp]),
             "aos_kv_memory_bytes": (u64, [vp]),
             "aos_run_step_batch": (C.c_int, [vp, vp, vp, vp, u32, vp, vp]),
@@ -889,6 +890,11 @@ class CudaKernels:
 
     def kv_set_len(self, seq_id, n):
         self._check(self._L.aos_kv_set_len(self.ctx, seq_id, n))
+
+    def kv_rotate(self, seq_id, shift):
+        """Sliding-window rotate (kv_cache.metal:200-236): drop the oldest
+        `shift` positions of the sequence in every layer."""
+        self._check(self._L.aos_kv_rotate(self.ctx, seq_id, shift))
 
     def kv_len(self, seq_id):
         v = C.c_uint32()

@@ -244,7 +244,46 @@ __global__ void zero_kv_blocks_kernel(uint16_t* __restrict__ k_pool, uint16_t* _
     }
 }
 
+// Sliding-window rotate, the part inside pages: position i of the sequence
+// takes the row of position i + r (0 < r < 16) for i < new_len, over the
+// sequence's pages blocks[0..n) in order.  CTA (layer, kv head, pool) walks
+// the pages in order, one thread per head dimension: it reads page b's rows
+// r..15 and page b+1's rows 0..r-1 (rows needed only below new_len), waits
+// for every thread, then writes page b.  Page b+1 is overwritten only in the
+// next iteration, after its first rows were read, so the in-place shift
+// never reads a row it has already moved.
+__global__ void kv_shift_rows_kernel(uint16_t* __restrict__ k_pool, uint16_t* __restrict__ v_pool,
+                                     const int* __restrict__ blocks, int n, int r, int new_len, int num_blocks, int nkv) {
+    const int layer = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+    uint16_t* pool = blockIdx.z ? v_pool : k_pool;
+    auto row = [&](int blk, int j) -> uint16_t* {
+        return pool + ((((size_t)layer * num_blocks + blk) * nkv + h) * 16 + j) * 128 + d;
+    };
+    const int n_dst = (new_len + 15) / 16;
+    for (int b = 0; b < n_dst && b < n; ++b) {
+        uint16_t val[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int src = j + r;  // row of page b (< 16) or of page b + 1
+            val[j] = 0;
+            if (b * 16 + j < new_len) val[j] = src < 16 ? *row(blocks[b], src) : *row(blocks[b + 1], src - 16);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            if (b * 16 + j < new_len) *row(blocks[b], j) = val[j];
+        __syncthreads();
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_kv_shift_rows(uint16_t* k_pool, uint16_t* v_pool, const int* blocks, int n, int r, int new_len,
+                                 int n_layers, int num_blocks, int nkv, cudaStream_t s) {
+    if (n <= 0 || n_layers <= 0 || new_len <= 0 || r <= 0 || r >= 16) return cudaSuccess;
+    kv_shift_rows_kernel<<<dim3(n_layers, nkv, 2), 128, 0, s>>>(k_pool, v_pool, blocks, n, r, new_len, num_blocks, nkv);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_zero_kv_blocks(uint16_t* k_pool, uint16_t* v_pool, const int* blocks, int n, int n_layers,
                                   int num_blocks, int nkv, cudaStream_t s) {

@@ -34,6 +34,8 @@
 #include "tc_gemm.cuh"
 
 namespace aos {
+cudaError_t launch_kv_shift_rows(uint16_t* k_pool, uint16_t* v_pool, const int* blocks, int n, int r, int new_len,
+                                 int n_layers, int num_blocks, int nkv, cudaStream_t s);
 cudaError_t launch_zero_kv_blocks(uint16_t* k_pool, uint16_t* v_pool, const int* blocks, int n, int n_layers,
                                   int num_blocks, int nkv, cudaStream_t s);
 cudaError_t launch_embed(const uint16_t*, const uint32_t*, int, int, int, uint16_t*, cudaStream_t);
@@ -1599,6 +1601,36 @@ int aos_kv_read(aos_ctx* c, uint64_t seq_id, uint32_t layer, uint32_t pos0, uint
     if (!c || !k || !v) return AOS_ERR_INVALID;
     CTX_CUDA(c, cudaStreamSynchronize(c->stream));
     return kv_copy(c, seq_id, layer, pos0, n, nullptr, nullptr, k, v, 0);
+}
+
+// Sliding-window rotate (kv_cache.metal:200-236, kv_cache_rotate): drop the
+// sequence's oldest `shift` positions; position i takes the K/V rows of
+// position i + shift in every layer and KV head, and the length becomes
+// len - shift.  On the paged pool the whole pages of the shift are a
+// rotation of the sequence's page list (the dropped pages move to its end
+// and keep serving its capacity); only the remainder shift % 16 moves rows,
+// in place, page by page.  The reference's Rust code never dispatches that
+// shader; this is its semantics on this cache.
+int aos_kv_rotate(aos_ctx* c, uint64_t seq_id, uint32_t shift) {
+    if (!c) return AOS_ERR_INVALID;
+    auto it = c->seqs.find(seq_id);
+    if (it == c->seqs.end()) return c->fail(AOS_ERR_NOT_FOUND, "unknown sequence");
+    Sequence& sq = it->second;
+    if (shift > sq.len) return c->fail(AOS_ERR_INVALID, "rotate shift beyond the sequence length");
+    if (shift == 0) return AOS_OK;
+    const uint32_t new_len = sq.len - shift, whole = shift / 16, r = shift % 16;
+    std::rotate(sq.blocks.begin(), sq.blocks.begin() + whole, sq.blocks.end());
+    if (r && new_len) {
+        CTX_CUDA(c, cudaSetDevice(c->device));
+        CTX_CUDA(c, cudaMemcpyAsync(c->d_zero_blocks, sq.blocks.data(), sq.blocks.size() * sizeof(int),
+                                    cudaMemcpyHostToDevice, c->stream));
+        LAUNCH(c, launch_kv_shift_rows(c->k_pool, c->v_pool, c->d_zero_blocks, (int)sq.blocks.size(), (int)r,
+                                       (int)new_len, (int)c->cfg.n_layers, (int)c->cfg.kv_num_blocks,
+                                       (int)c->cfg.n_kv_heads, c->stream));
+        CTX_CUDA(c, cudaStreamSynchronize(c->stream));  // the page list buffer is reused by the next call
+    }
+    sq.len = new_len;
+    return AOS_OK;
 }
 
 int aos_kv_fill_synthetic(aos_ctx* c, uint64_t seed, float std) {

@@ -259,6 +259,13 @@ int aos_kv_read(aos_ctx* ctx, uint64_t seq_id, uint32_t layer, uint32_t pos0, ui
                 uint16_t* k, uint16_t* v);
 /* Fill every page of the pool with seeded synthetic bf16 values ~N(0, std). */
 int aos_kv_fill_synthetic(aos_ctx* ctx, uint64_t seed, float std);
+/* Sliding-window rotate (kv_cache.metal:200-236 kv_cache_rotate): drops the
+ * sequence's oldest `shift` positions; position i then holds the K/V rows of
+ * old position i + shift in every layer, and the length is len - shift (the
+ * capacity is kept).  Rows are moved as stored: the keys keep the rotary
+ * angle of their old positions, as in the shader.  shift > len is
+ * AOS_ERR_INVALID; shift 0 does nothing. */
+int aos_kv_rotate(aos_ctx* ctx, uint64_t seq_id, uint32_t shift);
 /* FusedKernels::clear_all_caches / cache_memory_bytes (lib.rs:536-554). */
 int aos_kv_clear_all(aos_ctx* ctx);
 uint64_t aos_kv_memory_bytes(const aos_ctx* ctx);

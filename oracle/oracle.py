@@ -402,6 +402,21 @@ class HostKV:
         return s
 
 
+def kv_rotate_rows(rows, length, shift):
+    """kv_cache_rotate (crates/adapteros-lora-kernel-mtl/shaders/kv_cache.metal:
+    200-236) on one sequence's rows [positions, n_kv, head_dim] of one layer:
+    for seq_idx < length - shift, dst[seq_idx] = src[seq_idx + shift] (every
+    head and dimension); rows past the new length are left as they were.
+    Returns the new rows and the new length."""
+    if shift > length:
+        raise ValueError("shift beyond the sequence length")
+    new_len = length - shift
+    out = np.array(rows, copy=True)
+    for seq_idx in range(new_len):  # the shader's grid x, one position at a time
+        out[seq_idx] = rows[seq_idx + shift]
+    return out, new_len
+
+
 def layer_step(model: HostModel, adapters, layer, rings, kv: HostKV, hidden, rounding_mode=0,
                n_threads=0):
     """One decoder layer (mlx_cpp_wrapper_real.cpp:3437-3531); updates hidden
