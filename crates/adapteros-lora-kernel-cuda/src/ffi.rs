@@ -182,6 +182,7 @@ extern "C" {
     pub fn aos_kv_free(ctx: *mut AosCtx, seq_id: u64) -> c_int;
     pub fn aos_kv_set_len(ctx: *mut AosCtx, seq_id: u64, len: u32) -> c_int;
     pub fn aos_kv_clear_all(ctx: *mut AosCtx) -> c_int;
+    pub fn aos_kv_rotate(ctx: *mut AosCtx, seq_id: u64, shift: u32) -> c_int;
     pub fn aos_kv_memory_bytes(ctx: *const AosCtx) -> u64;
 
     // GPU buffer verification and fingerprints

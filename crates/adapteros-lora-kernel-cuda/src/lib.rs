@@ -172,6 +172,18 @@ impl CudaKernels {
         Ok(seq)
     }
 
+    /// Sliding-window rotate of a session's KV cache (kv_cache.metal:200-236):
+    /// drops its oldest `shift` positions in every layer.  Not part of
+    /// FusedKernels; a worker that wants a fixed-memory window calls it
+    /// between steps.
+    pub fn rotate_session_cache(&mut self, session_id: &str, shift: u32) -> Result<()> {
+        let ctx = self.ctx()?;
+        let Some(&seq) = self.sessions.get(session_id) else {
+            return Err(AosError::Validation(format!("unknown session {session_id}")));
+        };
+        check(unsafe { ffi::aos_kv_rotate(ctx, seq, shift) }, ctx)
+    }
+
     fn pc_ptr(&self) -> *const ffi::AosPlanConfig {
         self.plan_config.as_ref().map_or(ptr::null(), |p| p as *const _)
     }
