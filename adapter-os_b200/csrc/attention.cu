@@ -10,9 +10,10 @@
 // by TMA (SWIZZLE_128B, two 64-dim boxes each for K and V) into per-warp
 // double buffers; QK^T and PV run on mma.sync m16n8k16 with the query heads
 // of the group as the 16 rows (FA2 register layout, so P never leaves
-// registers).  Each CTA writes (m, l, O) for its chunk; attn_combine merges
-// the chunks of a (token, head) in chunk order.  Every order is fixed, so
-// results are bit-identical run to run.
+// registers).  Each CTA writes (m, l, O) for its chunk and counts itself in;
+// the CTA that writes the last chunk of a (token, kv head) merges the chunks
+// of its query heads in chunk order (no separate combine launch).  Every
+// order is fixed, so results are bit-identical run to run.
 
 #include <cuda.h>
 
@@ -113,10 +114,51 @@ struct AttnParams {
     const int* ctx_lens;      // [T] tokens cached before this step (new token at that position)
     float* part;              // [T][nkv][max_chunks][G][128] O, then m, l
     float* part_ml;           // [T][nkv][max_chunks][G][2]
+    int* chunk_cnt;           // [T][nkv] chunks written so far (zero between launches)
+    uint16_t* out;            // [T][nq*128] bf16
     int T, nq, nkv, G, layer, num_blocks, max_blocks, max_chunks;
     float scale_log2;         // log2(e) / sqrt(hd)
     int* err;
 };
+
+// Merges the chunk partials of query head row r of (token t, kv head) in
+// chunk order, one warp: lane i owns dims 4i .. 4i+3; lane c holds chunk c's
+// (m, l), and the running sums of l and of O are taken in chunk order, so the
+// result is the same on every run whichever chunk finished last.  The
+// partials were written by other CTAs of this launch: plain (coherent) loads.
+__device__ __forceinline__ void combine_row(const float* __restrict__ part, const float* __restrict__ part_ml,
+                                            size_t base, int G, int r, int n_chunks, int lane, uint16_t* dst) {
+    float m = -INFINITY;
+    for (int c = lane; c < n_chunks; c += 32) m = fmaxf(m, __ldcg(part_ml + ((base + c) * G + r) * 2));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float l = 0.f;
+    for (int c0 = 0; c0 < n_chunks; c0 += 32) {
+        const int c = c0 + lane;
+        float sc = 0.f, lc = 0.f;
+        if (c < n_chunks) {
+            const float2 ml = __ldcg(reinterpret_cast<const float2*>(part_ml) + (base + c) * G + r);
+            sc = ml.x == -INFINITY ? 0.f : exp2f(ml.x - m);
+            lc = ml.y;
+        }
+        const int nc = min(32, n_chunks - c0);
+#pragma unroll 4
+        for (int j = 0; j < nc; ++j) {
+            const float scj = __shfl_sync(0xffffffffu, sc, j);
+            l += __shfl_sync(0xffffffffu, lc, j) * scj;
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(part + ((base + c0 + j) * G + r) * 128) + lane);
+            acc.x += v.x * scj;
+            acc.y += v.y * scj;
+            acc.z += v.z * scj;
+            acc.w += v.w * scj;
+        }
+    }
+    uint2 w;
+    w.x = (uint32_t)f2bf(acc.x / l) | ((uint32_t)f2bf(acc.y / l) << 16);
+    w.y = (uint32_t)f2bf(acc.z / l) | ((uint32_t)f2bf(acc.w / l) << 16);
+    *reinterpret_cast<uint2*>(dst + lane * 4) = w;
+}
 
 __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant__ AttnParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -310,54 +352,24 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
             p.part_ml[(slot * p.G + r) * 2 + 1] = l;
         }
     }
-}
-
-// Merge the chunk partials of one (token, kv head, query head) in chunk
-// order: one warp per head row, lane i owning dims 4i .. 4i+3.  Lane c holds
-// chunk c's (m, l); the running sums of l and of O are taken in chunk order,
-// so the result is the same on every run.  bf16 output attn[t][head*128 + d].
-__global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restrict__ part, const float* __restrict__ part_ml,
-                                                           const int* __restrict__ ctx_lens, int T, int nkv, int G,
-                                                           int max_chunks, uint16_t* __restrict__ out) {
-    pdl_wait();
-    pdl_trigger();
-    const int wg = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
-    const int r = wg % G, rest = wg / G;
-    const int kvh = rest % nkv, t = rest / nkv;
-    if (t >= T) return;
-    const int L = __ldg(ctx_lens + t) + 1;
-    const int n_chunks = ((L + 15) / 16 + kPages - 1) / kPages;
-    const size_t base = ((size_t)t * nkv + kvh) * max_chunks;
-    float m = -INFINITY;
-    for (int c = lane; c < n_chunks; c += 32) m = fmaxf(m, __ldg(part_ml + ((base + c) * G + r) * 2));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float l = 0.f;
-    for (int c0 = 0; c0 < n_chunks; c0 += 32) {
-        const int c = c0 + lane;
-        float sc = 0.f, lc = 0.f;
-        if (c < n_chunks) {
-            const float2 ml = __ldg(reinterpret_cast<const float2*>(part_ml) + (base + c) * G + r);
-            sc = ml.x == -INFINITY ? 0.f : exp2f(ml.x - m);
-            lc = ml.y;
-        }
-        const int nc = min(32, n_chunks - c0);
-#pragma unroll 4
-        for (int j = 0; j < nc; ++j) {
-            const float scj = __shfl_sync(0xffffffffu, sc, j);
-            l += __shfl_sync(0xffffffffu, lc, j) * scj;
-            const float4 v = __ldg(reinterpret_cast<const float4*>(part + ((base + c0 + j) * G + r) * 128) + lane);
-            acc.x += v.x * scj;
-            acc.y += v.y * scj;
-            acc.z += v.z * scj;
-            acc.w += v.w * scj;
-        }
+    // ---- the CTA that writes the last chunk of (t, kv head) merges all of them
+    const int n_chunks = (n_pages + kPages - 1) / kPages;
+    __threadfence();  // this CTA's partial is visible before it is counted
+    __syncthreads();
+    int* last = reinterpret_cast<int*>(rml);  // scratch no longer read
+    if (threadIdx.x == 0) {
+        int* cnt = p.chunk_cnt + (size_t)t * p.nkv + kvh;
+        const bool is_last = atomicAdd(cnt, 1) == n_chunks - 1;
+        if (is_last) *cnt = 0;  // every chunk has counted: clear for the next launch
+        *last = is_last ? 1 : 0;
     }
-    uint2 w;
-    w.x = (uint32_t)f2bf(acc.x / l) | ((uint32_t)f2bf(acc.y / l) << 16);
-    w.y = (uint32_t)f2bf(acc.z / l) | ((uint32_t)f2bf(acc.w / l) << 16);
-    *reinterpret_cast<uint2*>(out + (size_t)t * nkv * G * 128 + (size_t)(kvh * G + r) * 128 + lane * 4) = w;
+    __syncthreads();
+    if (!*last) return;
+    __threadfence();  // the other chunks' partials, counted before this one
+    const size_t base = ((size_t)t * p.nkv + kvh) * p.max_chunks;
+    for (int r = warp; r < p.G; r += kWarps)
+        combine_row(p.part, p.part_ml, base, p.G, r, n_chunks, lane,
+                    p.out + (size_t)t * p.nq * 128 + (size_t)(kvh * p.G + r) * 128);
 }
 
 // ---------------------------------------------------------------- prefill
@@ -585,8 +597,9 @@ cudaError_t attn_configure() {
 int attn_max_chunks(int max_seq_len) { return ((max_seq_len + 15) / 16 + kPages - 1) / kPages; }
 
 cudaError_t launch_attention(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const uint16_t* q, const int* block_tables,
-                             const int* ctx_lens, float* part, float* part_ml, int T, int nq, int nkv, int layer,
-                             int num_blocks, int max_blocks, int max_chunks, int* err, uint16_t* out, cudaStream_t s) {
+                             const int* ctx_lens, float* part, float* part_ml, int* chunk_cnt, int T, int nq, int nkv,
+                             int layer, int num_blocks, int max_blocks, int max_chunks, int* err, uint16_t* out,
+                             cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
     AttnParams p;
     p.tm_k = tm_k;
@@ -596,6 +609,8 @@ cudaError_t launch_attention(const CUtensorMap& tm_k, const CUtensorMap& tm_v, c
     p.ctx_lens = ctx_lens;
     p.part = part;
     p.part_ml = part_ml;
+    p.chunk_cnt = chunk_cnt;
+    p.out = out;
     p.T = T;
     p.nq = nq;
     p.nkv = nkv;
@@ -607,13 +622,7 @@ cudaError_t launch_attention(const CUtensorMap& tm_k, const CUtensorMap& tm_v, c
     p.scale_log2 = 1.4426950408889634f / sqrtf(128.0f);
     p.err = err;
     const size_t smem = attn_smem_bytes();
-    cudaError_t e = launch_k(attn_decode_kernel, dim3(T * nkv * max_chunks), dim3(128), smem, s, p);
-    if (e != cudaSuccess) return e;
-    const float* cpart = part;
-    const float* cml = part_ml;
-    const int rows = T * nkv * (nq / nkv);  // one warp per (token, kv head, query head)
-    return launch_k(attn_combine_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, cpart, cml, ctx_lens, T, nkv, nq / nkv,
-                    max_chunks, out);
+    return launch_k(attn_decode_kernel, dim3(T * nkv * max_chunks), dim3(128), smem, s, p);
 }
 
 }  // namespace aos

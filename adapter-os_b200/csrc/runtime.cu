@@ -48,7 +48,7 @@ cudaError_t launch_zero_if_no_groups(const int* n_groups, uint16_t* p, size_t n,
 cudaError_t launch_pack_blocks(const uint16_t* src, int rows, int cols, long long src_ld, uint16_t* dst, int row0,
                                int col0, int dst_cols, int br, cudaStream_t s);
 cudaError_t launch_attention(const CUtensorMap&, const CUtensorMap&, const uint16_t*, const int*, const int*, float*,
-                             float*, int, int, int, int, int, int, int, int*, uint16_t*, cudaStream_t);
+                             float*, int*, int, int, int, int, int, int, int, int*, uint16_t*, cudaStream_t);
 int attn_max_chunks(int max_seq_len);
 cudaError_t launch_attention_prefill(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const uint16_t* q,
                                      const int* block_tables, const int* pos, const int2* qblk, int n_qblk, int nq,
@@ -165,6 +165,7 @@ struct aos_ctx {
     float* d_logits = nullptr;
     float *d_rope = nullptr;
     float *d_attn_part = nullptr, *d_attn_ml = nullptr;
+    int* d_attn_cnt = nullptr;  // [T_cap][n_kv] decode attention chunks counted, zero between launches
     int attn_chunks = 0;
     uint16_t* d_stage = nullptr;  // bounded staging for packing host or unaligned weights
     size_t stage_bytes = 0;
@@ -574,7 +575,7 @@ int enqueue_layer(aos_ctx* c, const StepPlan& plan, int layer, cudaStream_t s) {
         PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupQKV], lp.gemm_grid[kGroupQKV], s));
         PLAUNCH(c, AOS_K_ATTN, s,
                 launch_attention(c->tm_k, c->tm_v, c->d_q, c->d_block_tables, c->d_ctx_lens, c->d_attn_part, c->d_attn_ml,
-                                 T, (int)c->cfg.n_heads, (int)c->cfg.n_kv_heads, layer, (int)c->cfg.kv_num_blocks,
+                                 c->d_attn_cnt, T, (int)c->cfg.n_heads, (int)c->cfg.n_kv_heads, layer, (int)c->cfg.kv_num_blocks,
                                  c->max_blocks, c->attn_chunks, c->d_err, c->d_attn, s));
         if (lora[kGroupO] && (rc = shard_site(c, plan, lp, kGroupO, c->d_attn, c->QD, s))) return rc;
         PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupO], lp.gemm_grid[kGroupO], s));
@@ -588,7 +589,8 @@ int enqueue_layer(aos_ctx* c, const StepPlan& plan, int layer, cudaStream_t s) {
     PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(c->d_hidden, c->attn_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
     PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupQKV], lp.gemm_grid[kGroupQKV], s));
     PLAUNCH(c, AOS_K_ATTN, s,
-            launch_attention(c->tm_k, c->tm_v, c->d_q, c->d_block_tables, c->d_ctx_lens, c->d_attn_part, c->d_attn_ml, T,
+            launch_attention(c->tm_k, c->tm_v, c->d_q, c->d_block_tables, c->d_ctx_lens, c->d_attn_part, c->d_attn_ml,
+                             c->d_attn_cnt, T,
                              (int)c->cfg.n_heads, (int)c->cfg.n_kv_heads, layer, (int)c->cfg.kv_num_blocks, c->max_blocks,
                              c->attn_chunks, c->d_err, c->d_attn, s));
     PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupO], lp.gemm_grid[kGroupO], s));
@@ -775,6 +777,7 @@ int check_device_error(aos_ctx* c) {
         // counter part-way: clear them so the next step starts clean.
         cudaDeviceSynchronize();  // nothing of this context may still be running
         cudaMemset(c->d_sync, 0, 4 * sizeof(int));
+        cudaMemset(c->d_attn_cnt, 0, (size_t)c->T_cap * c->cfg.n_kv_heads * sizeof(int));
         cudaMemset(c->d_acc, 0, c->acc_bytes);
         cudaMemset(c->d_err, 0, sizeof(int));
         cudaDeviceSynchronize();
@@ -1101,6 +1104,7 @@ aos_ctx* aos_init(const aos_model_config* cfg) {
     c->attn_chunks = attn_max_chunks((int)k.max_seq_len);
     INIT_CHECK(dalloc(&c->d_attn_part, TC * k.n_kv_heads * c->attn_chunks * c->G * 128), "attn part");
     INIT_CHECK(dalloc(&c->d_attn_ml, TC * k.n_kv_heads * c->attn_chunks * c->G * 2), "attn ml");
+    INIT_CHECK(dalloc(&c->d_attn_cnt, TC * k.n_kv_heads), "attn chunk counts");
     {  // tiles of the largest launch: base tiles plus up to three shrink segments
         const size_t tiles = max_launch_tiles(c.get());
         c->acc_bytes = tiles * kTcBN * (size_t)c->T_cap * sizeof(long long);
@@ -1175,7 +1179,7 @@ void aos_destroy(aos_ctx* c) {
     f(c->d_hidden); f(c->d_normed); f(c->d_q); f(c->d_attn); f(c->d_act);
     f(c->d_groups); f(c->d_n_groups); f(c->d_block_tables); f(c->d_ctx_lens); f(c->d_zero_blocks);
     f(c->d_rings); f(c->d_tokens); f(c->d_logits); f(c->d_rope);
-    f(c->d_attn_part); f(c->d_attn_ml); f(c->d_stage); f(c->d_acc); f(c->d_part); f(c->d_fp); f(c->d_sync); f(c->d_err); f(c->d_trace);
+    f(c->d_attn_part); f(c->d_attn_ml); f(c->d_attn_cnt); f(c->d_stage); f(c->d_acc); f(c->d_part); f(c->d_fp); f(c->d_sync); f(c->d_err); f(c->d_trace);
     for (int i = 0; i < aos_ctx::kStageSlots; ++i) {
         if (c->h_stage[i]) cudaFreeHost(c->h_stage[i]);
         if (c->stage_ev[i]) cudaEventDestroy(c->stage_ev[i]);

@@ -1042,13 +1042,13 @@ def main():
 
     if rank == 0:
         # kernels per step, from the instrumented pass: one route kernel, plus every
-        # launch the step enqueues (the LoRA prep and the attention enqueue two
-        # kernels each: prep + coefficient table, decode + combine)
+        # launch the step enqueues (the LoRA prep enqueues two kernels: prep +
+        # coefficient table)
         lc = prof["launches"]
         # whole step: projections (base + selected LoRA + activations), attention
         # (KV + q/out) and the lm_head weights, per step of the instrumented pass
         step_bytes = proj_bytes / PS + abytes / PS + c["vocab"] * c["hidden"] * 2
-        launches_per_step = 1 + (sum(lc.values()) + lc["prep"] + lc["attention"]) / PS
+        launches_per_step = 1 + (sum(lc.values()) + lc["prep"]) / PS
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -1067,7 +1067,7 @@ def main():
                          "peak_kind": peak_kind,
                          "bytes_per_step": proj_bytes / PS, "ms_per_step": proj_ms / PS,
                          "launches_per_step": n_gemm_launches / PS, "unique_adapters_per_step": n_sel / PS},
-            "roofline_attention": {"bound": "hbm", "kernel": "attn_decode_kernel + attn_combine_kernel",
+            "roofline_attention": {"bound": "hbm", "kernel": "attn_decode_kernel (split-KV; the last chunk's CTA merges the chunks)",
                                    "achieved": attn_gbs, "peak": peak, "unit": "GB/s", "frac": attn_gbs / peak,
                                    "bytes_per_step": abytes / PS, "ms_per_step": prof["ms"]["attention"] / PS},
             "roofline_step": {"bound": "hbm", "what": "whole decode step: projections + attention + lm_head "
