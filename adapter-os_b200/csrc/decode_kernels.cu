@@ -69,6 +69,48 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* __restrict
     }
 }
 
+// First half of a folded RMSNorm (the decode GEMMs apply the second): per
+// token, hw = bf16(x * w) and the sum of x^2 in fixed point (each thread's
+// fp32 partial * 2^32 rounded, then an integer sum: order-independent, so
+// the result is the same on every run).  One CTA of 256 threads per token.
+__global__ void __launch_bounds__(256) norm_prep_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
+                                                        int T, int H, uint16_t* __restrict__ hw,
+                                                        unsigned long long* __restrict__ ss) {
+    pdl_wait();
+    pdl_trigger();
+    const int t = blockIdx.x;
+    if (t >= T) return;
+    const uint16_t* xt = x + (size_t)t * H;
+    float sq = 0.0f;
+    for (int i = threadIdx.x * 8; i < H; i += 256 * 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(xt + i);
+        const uint4 ww = *reinterpret_cast<const uint4*>(w + i);
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+        const uint32_t g[4] = {ww.x, ww.y, ww.z, ww.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float a = __uint_as_float(u[j] << 16), b = __uint_as_float(u[j] & 0xffff0000u);
+            const float wa = __uint_as_float(g[j] << 16), wb = __uint_as_float(g[j] & 0xffff0000u);
+            sq = fmaf(a, a, sq);
+            sq = fmaf(b, b, sq);
+            o[j] = (uint32_t)f2bf(a * wa) | ((uint32_t)f2bf(b * wb) << 16);
+        }
+        *reinterpret_cast<uint4*>(hw + (size_t)t * H + i) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    unsigned long long q = (unsigned long long)__float2ll_rn(sq * 4294967296.0f);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) q += __shfl_xor_sync(0xffffffffu, q, off);
+    __shared__ unsigned long long part[8];
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = q;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long tot = 0;
+        for (int i = 0; i < 8; ++i) tot += part[i];
+        ss[t] = tot;
+    }
+}
+
 // Routing prep for the LoRA GEMMs: mark every 64-column rank group of the
 // arena that holds a column of an adapter selected (q15 > 0) by any token,
 // then compact the marks in ascending group order.  One CTA of 1024 threads.
@@ -310,6 +352,12 @@ cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* w, int T, int H, f
                            cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
     return launch_k(rmsnorm_kernel, dim3(T), dim3(256), 0, s, x, w, T, H, eps, y);
+}
+
+cudaError_t launch_norm_prep(const uint16_t* x, const uint16_t* w, int T, int H, uint16_t* hw,
+                             unsigned long long* ss, cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    return launch_k(norm_prep_kernel, dim3(T), dim3(256), 0, s, x, w, T, H, hw, ss);
 }
 
 cudaError_t launch_lora_prep(const aos_router_ring* rings, int T, const int* col_off, const int* rank,

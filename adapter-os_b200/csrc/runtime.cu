@@ -40,6 +40,7 @@ cudaError_t launch_zero_kv_blocks(uint16_t* k_pool, uint16_t* v_pool, const int*
                                   int num_blocks, int nkv, cudaStream_t s);
 cudaError_t launch_embed(const uint16_t*, const uint32_t*, int, int, int, uint16_t*, cudaStream_t);
 cudaError_t launch_rmsnorm(const uint16_t*, const uint16_t*, int, int, float, uint16_t*, cudaStream_t);
+cudaError_t launch_norm_prep(const uint16_t*, const uint16_t*, int, int, uint16_t*, unsigned long long*, cudaStream_t);
 cudaError_t launch_lora_prep(const aos_router_ring* rings, int T, const int* col_off, const int* rank,
                              const float* scale, int max_adapters, int n_slab_total, int* slabs, int* n_slabs,
                              float* coef, const int* col_owner, float* ucoef, cudaStream_t s);
@@ -166,6 +167,7 @@ struct aos_ctx {
     float *d_rope = nullptr;
     float *d_attn_part = nullptr, *d_attn_ml = nullptr;
     int* d_attn_cnt = nullptr;  // [T_cap][n_kv] decode attention chunks counted, zero between launches
+    unsigned long long* d_ss = nullptr;  // [T_cap] folded RMSNorm: sum of squares of each token's hidden row
     int attn_chunks = 0;
     uint16_t* d_stage = nullptr;  // bounded staging for packing host or unaligned weights
     size_t stage_bytes = 0;
@@ -449,6 +451,19 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp, bool sharded =
             }
             if ((rc = build_owner_plan(c, layer, g, T * c->shard_world, lp.owner[g]))) return rc;
         }
+        // RMSNorm folded into the neighbouring launches: o and down write the
+        // next norm's hw = h * w (into d_normed) and each token's sum of h^2;
+        // q/k/v and gate/up read hw and scale by 1 / rms in their epilogue
+        if (g == kGroupQKV || g == kGroupGU) {
+            p.ss_in = c->d_ss;
+            p.ss_scale = (float)(1.0 / 4294967296.0 / (double)H);
+            p.norm_eps = c->cfg.rms_eps;
+        } else {
+            p.ss_out = c->d_ss;
+            p.hw_out = c->d_normed;
+            p.norm_w = g == kGroupO ? c->mlp_norm[layer]
+                                    : (layer + 1 < (int)c->cfg.n_layers ? c->attn_norm[layer + 1] : c->final_norm);
+        }
         p.pools = 7;
         if ((rc = tc_prepare(p, smem_budget))) return rc;
         lp.gemm_grid[g] = tc_num_sms();
@@ -500,6 +515,9 @@ int get_plan(aos_ctx* c, int T, StepPlan** out, bool sharded = false) {
     p.seg_rows[0] = (int)V;
     p.out[0] = c->d_logits;
     p.ld_out = (int)V;
+    p.ss_in = c->d_ss;  // the final norm, folded: hw from the last down launch, 1 / rms here
+    p.ss_scale = (float)(1.0 / 4294967296.0 / (double)c->cfg.hidden);
+    p.norm_eps = c->cfg.rms_eps;
     if ((rc = tc_prepare(p, 227 * 1024))) return c->fail(rc, "lm_head plan");
     plan->lm_grid = tc_num_sms();
     *out = plan.get();
@@ -570,7 +588,7 @@ int enqueue_layer(aos_ctx* c, const StepPlan& plan, int layer, cudaStream_t s) {
         const bool lora[4] = {lp.gemm[kGroupQKV].delta != nullptr, lp.gemm[kGroupO].delta != nullptr,
                               lp.gemm[kGroupGU].delta != nullptr, lp.gemm[kGroupD].delta != nullptr};
         int rc;
-        PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(c->d_hidden, c->attn_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
+        // d_normed holds hw (the norms are folded into the GEMMs)
         if (lora[kGroupQKV] && (rc = shard_site(c, plan, lp, kGroupQKV, c->d_normed, H, s))) return rc;
         PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupQKV], lp.gemm_grid[kGroupQKV], s));
         PLAUNCH(c, AOS_K_ATTN, s,
@@ -579,22 +597,21 @@ int enqueue_layer(aos_ctx* c, const StepPlan& plan, int layer, cudaStream_t s) {
                                  c->max_blocks, c->attn_chunks, c->d_err, c->d_attn, s));
         if (lora[kGroupO] && (rc = shard_site(c, plan, lp, kGroupO, c->d_attn, c->QD, s))) return rc;
         PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupO], lp.gemm_grid[kGroupO], s));
-        PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(c->d_hidden, c->mlp_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
         if (lora[kGroupGU] && (rc = shard_site(c, plan, lp, kGroupGU, c->d_normed, H, s))) return rc;
         PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupGU], lp.gemm_grid[kGroupGU], s));
         if (lora[kGroupD] && (rc = shard_site(c, plan, lp, kGroupD, c->d_act, c->cfg.intermediate, s))) return rc;
         PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupD], lp.gemm_grid[kGroupD], s));
         return AOS_OK;
     }
-    PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(c->d_hidden, c->attn_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
+    // the attention norm arrives folded: hw in d_normed and the sums in d_ss,
+    // from the previous layer's down launch (or the step's norm prep)
     PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupQKV], lp.gemm_grid[kGroupQKV], s));
     PLAUNCH(c, AOS_K_ATTN, s,
             launch_attention(c->tm_k, c->tm_v, c->d_q, c->d_block_tables, c->d_ctx_lens, c->d_attn_part, c->d_attn_ml,
                              c->d_attn_cnt, T,
                              (int)c->cfg.n_heads, (int)c->cfg.n_kv_heads, layer, (int)c->cfg.kv_num_blocks, c->max_blocks,
                              c->attn_chunks, c->d_err, c->d_attn, s));
-    PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupO], lp.gemm_grid[kGroupO], s));
-    PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(c->d_hidden, c->mlp_norm[layer], T, (int)H, c->cfg.rms_eps, c->d_normed, s));
+    PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupO], lp.gemm_grid[kGroupO], s));  // + the MLP norm's first half
     PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupGU], lp.gemm_grid[kGroupGU], s));
     PLAUNCH(c, AOS_K_GEMM, s, tc_launch(lp.gemm[kGroupD], lp.gemm_grid[kGroupD], s));
     return AOS_OK;
@@ -623,15 +640,16 @@ int enqueue_step(aos_ctx* c, StepPlan& plan, bool with_logits, cudaStream_t s) {
                                  c->R / kGroup, c->d_groups, c->d_n_groups, c->d_coef, c->d_col_owner, c->d_ucoef, s));
     }
     PLAUNCH(c, AOS_K_EMBED, s, launch_embed(c->embed, c->d_tokens, T, (int)c->cfg.hidden, (int)c->cfg.vocab, c->d_hidden, s));
+    // layer 0's attention norm, first half (every later norm is folded into
+    // the launch that writes the residual)
+    PLAUNCH(c, AOS_K_NORM, s,
+            launch_norm_prep(c->d_hidden, c->attn_norm[0], T, (int)c->cfg.hidden, c->d_normed, c->d_ss, s));
     for (uint32_t l = 0; l < c->cfg.n_layers; ++l) {
         int rc = enqueue_layer(c, plan, (int)l, s);
         if (rc) return rc;
     }
-    if (with_logits) {
-        PLAUNCH(c, AOS_K_NORM, s,
-                launch_rmsnorm(c->d_hidden, c->final_norm, T, (int)c->cfg.hidden, c->cfg.rms_eps, c->d_normed, s));
+    if (with_logits)  // the final norm: hw and sums from the last down launch
         PLAUNCH(c, AOS_K_LM_HEAD, s, tc_launch(plan.lm_head, plan.lm_grid, s));
-    }
     return AOS_OK;
 }
 
@@ -778,6 +796,7 @@ int check_device_error(aos_ctx* c) {
         cudaDeviceSynchronize();  // nothing of this context may still be running
         cudaMemset(c->d_sync, 0, 4 * sizeof(int));
         cudaMemset(c->d_attn_cnt, 0, (size_t)c->T_cap * c->cfg.n_kv_heads * sizeof(int));
+        cudaMemset(c->d_ss, 0, (size_t)c->T_cap * sizeof(unsigned long long));
         cudaMemset(c->d_acc, 0, c->acc_bytes);
         cudaMemset(c->d_err, 0, sizeof(int));
         cudaDeviceSynchronize();
@@ -1105,6 +1124,7 @@ aos_ctx* aos_init(const aos_model_config* cfg) {
     INIT_CHECK(dalloc(&c->d_attn_part, TC * k.n_kv_heads * c->attn_chunks * c->G * 128), "attn part");
     INIT_CHECK(dalloc(&c->d_attn_ml, TC * k.n_kv_heads * c->attn_chunks * c->G * 2), "attn ml");
     INIT_CHECK(dalloc(&c->d_attn_cnt, TC * k.n_kv_heads), "attn chunk counts");
+    INIT_CHECK(dalloc(&c->d_ss, TC), "norm sums");
     {  // tiles of the largest launch: base tiles plus up to three shrink segments
         const size_t tiles = max_launch_tiles(c.get());
         c->acc_bytes = tiles * kTcBN * (size_t)c->T_cap * sizeof(long long);
@@ -1179,7 +1199,7 @@ void aos_destroy(aos_ctx* c) {
     f(c->d_hidden); f(c->d_normed); f(c->d_q); f(c->d_attn); f(c->d_act);
     f(c->d_groups); f(c->d_n_groups); f(c->d_block_tables); f(c->d_ctx_lens); f(c->d_zero_blocks);
     f(c->d_rings); f(c->d_tokens); f(c->d_logits); f(c->d_rope);
-    f(c->d_attn_part); f(c->d_attn_ml); f(c->d_attn_cnt); f(c->d_stage); f(c->d_acc); f(c->d_part); f(c->d_fp); f(c->d_sync); f(c->d_err); f(c->d_trace);
+    f(c->d_attn_part); f(c->d_attn_ml); f(c->d_attn_cnt); f(c->d_ss); f(c->d_stage); f(c->d_acc); f(c->d_part); f(c->d_fp); f(c->d_sync); f(c->d_err); f(c->d_trace);
     for (int i = 0; i < aos_ctx::kStageSlots; ++i) {
         if (c->h_stage[i]) cudaFreeHost(c->h_stage[i]);
         if (c->stage_ev[i]) cudaEventDestroy(c->stage_ev[i]);
@@ -1844,7 +1864,8 @@ int prefill_run(aos_ctx* c, uint32_t n_seq, const uint64_t* seq_ids, const uint3
     if (logits) {
         StepPlan* plan = nullptr;
         if ((rc = get_plan(c, (int)n_seq, &plan))) return rc;
-        PLAUNCH(c, AOS_K_NORM, s, launch_rmsnorm(c->d_hidden, c->final_norm, (int)n_seq, (int)H, c->cfg.rms_eps, c->d_normed, s));
+        // the final norm's first half; the decode lm_head plan applies 1 / rms
+        PLAUNCH(c, AOS_K_NORM, s, launch_norm_prep(c->d_hidden, c->final_norm, (int)n_seq, (int)H, c->d_normed, c->d_ss, s));
         PLAUNCH(c, AOS_K_LM_HEAD, s, tc_launch(plan->lm_head, plan->lm_grid, s));
         if (logits != c->d_logits)
             CTX_CUDA(c, cudaMemcpyAsync(logits, c->d_logits, (size_t)n_seq * c->cfg.vocab * 4, cudaMemcpyDeviceToDevice, s));
@@ -1960,6 +1981,7 @@ int aos_layer_step_dev(aos_ctx* c, uint32_t layer, const aos_router_ring* rings,
     CTX_CUDA(c, cudaMemcpyAsync(c->d_hidden, hidden, (size_t)T * c->cfg.hidden * 2, cudaMemcpyDeviceToDevice, s));
     LAUNCH(c, launch_lora_prep(c->d_rings, (int)T, c->d_col_off, c->d_rank, c->d_scale, (int)c->cfg.lora_max_adapters,
                                c->R / kGroup, c->d_groups, c->d_n_groups, c->d_coef, c->d_col_owner, c->d_ucoef, s));
+    LAUNCH(c, launch_norm_prep(c->d_hidden, c->attn_norm[layer], (int)T, (int)c->cfg.hidden, c->d_normed, c->d_ss, s));
     if ((rc = enqueue_layer(c, *plan, (int)layer, s))) return rc;
     CTX_CUDA(c, cudaMemcpyAsync(hidden, c->d_hidden, (size_t)T * c->cfg.hidden * 2, cudaMemcpyDeviceToDevice, s));
     if (adv) advance(c, seq_ids, T);

@@ -228,23 +228,51 @@ __device__ __forceinline__ void store_run(const TcParams& p, int mode, int seg, 
                 if (r0 + i < lim) o[i] = v[i];
         }
     } else if (mode == TC_RESID_BF16) {
+        // h += v, eight columns at a time; with a folded norm also the next
+        // norm's input hw = h * w and this run's share of sum(h^2), from the
+        // same registers
         uint16_t* h = p.resid + off;
-        float s[N];
+        float sq = 0.f;
         if (full) {
 #pragma unroll
-            for (int i = 0; i < N; i += 4) {
-                const uint2 w = *reinterpret_cast<const uint2*>(h + i);
-                s[i] = bf2f((uint16_t)(w.x & 0xFFFFu)) + v[i];
-                s[i + 1] = bf2f((uint16_t)(w.x >> 16)) + v[i + 1];
-                s[i + 2] = bf2f((uint16_t)(w.y & 0xFFFFu)) + v[i + 2];
-                s[i + 3] = bf2f((uint16_t)(w.y >> 16)) + v[i + 3];
+            for (int i0 = 0; i0 < N; i0 += 8) {
+                const uint4 hv = *reinterpret_cast<const uint4*>(h + i0);
+                const uint32_t hu[4] = {hv.x, hv.y, hv.z, hv.w};
+                uint32_t nu[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    nu[j] = (uint32_t)f2bf(bf2f((uint16_t)(hu[j] & 0xFFFFu)) + v[i0 + 2 * j]) |
+                            ((uint32_t)f2bf(bf2f((uint16_t)(hu[j] >> 16)) + v[i0 + 2 * j + 1]) << 16);
+                *reinterpret_cast<uint4*>(h + i0) = make_uint4(nu[0], nu[1], nu[2], nu[3]);
+                if (p.ss_out) {
+                    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(p.norm_w + r0 + i0));
+                    const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+                    uint32_t ou[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float a = bf2f((uint16_t)(nu[j] & 0xFFFFu)), b = bf2f((uint16_t)(nu[j] >> 16));
+                        sq = fmaf(a, a, sq);
+                        sq = fmaf(b, b, sq);
+                        ou[j] = (uint32_t)f2bf(a * bf2f((uint16_t)(wu[j] & 0xFFFFu))) |
+                                ((uint32_t)f2bf(b * bf2f((uint16_t)(wu[j] >> 16))) << 16);
+                    }
+                    *reinterpret_cast<uint4*>(p.hw_out + off + i0) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
+                }
             }
-            store_bf16_run<N>(h, s);
         } else {
 #pragma unroll
             for (int i = 0; i < N; ++i)
-                if (r0 + i < lim) h[i] = f2bf(bf2f(h[i]) + v[i]);
+                if (r0 + i < lim) {
+                    const uint16_t nb = f2bf(bf2f(h[i]) + v[i]);
+                    h[i] = nb;
+                    if (p.ss_out) {
+                        const float a = bf2f(nb);
+                        sq = fmaf(a, a, sq);
+                        p.hw_out[off + i] = f2bf(a * bf2f(__ldg(p.norm_w + r0 + i)));
+                    }
+                }
         }
+        if (p.ss_out) atomicAdd(p.ss_out + t, (unsigned long long)__float2ll_rn(sq * kFix));
     } else {  // TC_STORE_BF16
         uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]) + off;
         if (full) {
@@ -291,13 +319,24 @@ __device__ __forceinline__ void add_delta_run(const TcParams& p, int t, int col,
     }
 }
 
+// Per-token scale of a launch that reads a folded norm's hw: 1 / rms of the
+// token's hidden row, from the fixed-point sum of squares the previous
+// launch accumulated; 1 without one.
+__device__ __noinline__ float token_scale_of(const unsigned long long* ss_in, int t, float ss_scale, float eps) {
+    const double ss = (double)(long long)__ldcg(ss_in + t);
+    return 1.0f / sqrtf((float)(ss * (double)ss_scale) + eps);
+}
+__device__ __forceinline__ float token_scale(const TcParams& p, int t) {
+    return p.ss_in ? token_scale_of(p.ss_in, t, p.ss_scale, p.norm_eps) : 1.f;
+}
+
 // Applies the epilogue of `mode` to pairs [pr0, pr0 + N) of chunk k of tile
 // `tile` (segment `seg`) for token t (t < T).  vA/vB: accumulator values of
 // the pairs' first and second columns (the owners' deltas, if any, are added
 // in place).
 template <int N>
 __device__ __forceinline__ void apply_pairs(const TcParams& p, int mode, int seg, int tile, int k, int t, int pr0,
-                                            float (&vA)[N], float (&vB)[N], int ng) {
+                                            float (&vA)[N], float (&vB)[N], int ng, float st = 1.f) {
     int cA, cB;
     chunk_cols(mode, k, cA, cB);
     cA += pr0;
@@ -313,6 +352,15 @@ __device__ __forceinline__ void apply_pairs(const TcParams& p, int mode, int seg
             const int rA = tile * kTcBN + cA, rB = tile * kTcBN + cB, lim = p.seg_rows[seg];
             if (rA < lim) add_delta_run<N>(p, t, p.dseg0[seg] + rA, lim - rA, vA);
             if (rB < lim) add_delta_run<N>(p, t, p.dseg0[seg] + rB, lim - rB, vB);
+        }
+    }
+    // a folded norm's 1 / rms scales the whole sum (base, expand and owners'
+    // deltas all read the unscaled hw); the shrink output stays unscaled
+    if (st != 1.f && mode != TC_SHRINK_HM) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            vA[i] *= st;
+            vB[i] *= st;
         }
     }
     switch (mode) {
@@ -721,7 +769,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 }
                 Piece pc;
                 tile_info(p, sc, tile, pc);
-                apply_pairs<8>(p, p.mode, pc.seg, pc.t, k, tok, 8 * g, a, b, sc.ng);
+                apply_pairs<8>(p, p.mode, pc.seg, pc.t, k, tok, 8 * g, a, b, sc.ng, token_scale(p, tok));
             }
             return;
         }
@@ -783,7 +831,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                 } else {
                     Piece pc;
                     tile_info(p, sc, tile_[e], pc);
-                    apply_pairs<8>(p, p.mode, pc.seg, pc.t, k_[e], tok_[e], 8 * g_[e], a, b, sc.ng);
+                    apply_pairs<8>(p, p.mode, pc.seg, pc.t, k_[e], tok_[e], 8 * g_[e], a, b, sc.ng,
+                                   token_scale(p, tok_[e]));
                 }
             }
 #pragma unroll
@@ -1104,6 +1153,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             } else if (pc.n == 1) {  // the whole tile is here: epilogue straight from TMEM
                 for (int b = 0; b < p.tb; ++b) {
                     const int tok = token_of(b);
+                    const float st = (tok >= 0 && tok < p.T) ? token_scale(p, tok) : 1.f;
 #pragma unroll 1
                     for (int k = 0; k < 4; ++k) {
                         int cA, cB;
@@ -1111,7 +1161,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
                         float vA[32], vB[32];
                         tmem_ld32(t_acc + b * kTcBN + cA, vA);
                         tmem_ld32(t_acc + b * kTcBN + cB, vB);
-                        if (tok >= 0 && tok < p.T) apply_pairs<32>(p, mode, pc.seg, pc.t, k, tok, 0, vA, vB, sc.ng);
+                        if (tok >= 0 && tok < p.T) apply_pairs<32>(p, mode, pc.seg, pc.t, k, tok, 0, vA, vB, sc.ng, st);
                     }
                 }
             } else {
@@ -1266,6 +1316,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             p.sync[1] = 0;
             p.sync[2] = 0;
             p.sync[3] = 0;
+            // every CTA has read the folded norm's sums: clear them for the
+            // launch that accumulates the next ones
+            if (p.ss_in)
+                for (int i = 0; i < p.T; ++i) p.ss_in[i] = 0ull;
             __threadfence();
         }
     }
