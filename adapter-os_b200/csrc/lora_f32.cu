@@ -7,9 +7,10 @@
 //
 // Three launches, all with fixed reduction orders (bit-identical run to run):
 //   1. shrink: one warp per (token, slot, rank row): h = A_a[r] . x[t]
-//   2. base: CTA tiles of 64 outputs x 64 tokens x one quarter of K, register
-//      tiles of 4 x 8, fp32 partials per quarter;
-//   3. expand: the quarters summed in order, then the slots' expand terms in
+//   2. base: CTA tiles of 64 outputs x 64 tokens x one eighth of K (enough CTAs
+//      to occupy the SMs at config 1's 64 tokens), register tiles of 4 x 8,
+//      fp32 partials per eighth;
+//   3. expand: the eighths summed in order, then the slots' expand terms in
 //      ring order.
 // fp32 in, fp32 FMA accumulation; W is read once per token tile.
 
@@ -48,12 +49,12 @@ __global__ void __launch_bounds__(256) lora_shrink_f32(const float* __restrict__
     if (lane == 0) h[gw] = acc;
 }
 
-// Base GEMM: CTA tile of 64 outputs x 64 tokens over one quarter of K
+// Base GEMM: CTA tile of 64 outputs x 64 tokens over one eighth of K
 // (blockIdx.z), 128 threads with a 4-output x 8-token register tile each; K
 // is staged through shared memory 32 at a time, the next chunk's global loads
-// in flight while the current one is multiplied.  The four K quarters are
-// written as fp32 partials and summed in quarter order by the expand kernel.
-constexpr int kBO = 64, kBT = 64, kBK = 32, kSplit = 4;
+// in flight while the current one is multiplied.  The eight K eighths are
+// written as fp32 partials and summed in order by the expand kernel.
+constexpr int kBO = 64, kBT = 64, kBK = 32, kSplit = 8;
 
 __global__ void __launch_bounds__(128) lora_base_f32(const float* __restrict__ x, int T, int in_dim, int out_dim,
                                                      const float* __restrict__ W, float* __restrict__ part) {
@@ -126,7 +127,7 @@ __global__ void __launch_bounds__(128) lora_base_f32(const float* __restrict__ x
     }
 }
 
-// y[t][o] = sum of the K-quarter partials (in quarter order) + the ring
+// y[t][o] = sum of the K-eighth partials (in order) + the ring
 // slots' expand terms in ring order: coeff * (B_a[o] . h[t][slot]) * scale.
 __global__ void __launch_bounds__(256) lora_expand_f32(int T, int out_dim, const float* __restrict__ part,
                                                        const float* __restrict__ B, int n_adapters, int rank,
@@ -250,7 +251,7 @@ cudaError_t launch_lora_op_f32_small(const float* x, int T, int in_dim, int out_
     return cudaGetLastError();
 }
 
-// Scratch floats launch_lora_op_f32 needs: shrink outputs + K-quarter partials.
+// Scratch floats launch_lora_op_f32 needs: shrink outputs + K-eighth partials.
 size_t lora_op_scratch_floats(int T, int out_dim, int rank) {
     return (size_t)T * AOS_MAX_K * rank + (size_t)kSplit * T * out_dim;
 }

@@ -1,7 +1,7 @@
 // noalloc.cu — aos_lora_op_f32_noalloc_dev: the fp32 base + K-sparse LoRA op
 // of aos_lora_op_f32_dev for callers that must not allocate device memory.
 // It runs the same shrink kernel and then one single-pass base + expand
-// kernel over all of K, where aos_lora_op_f32_dev sums four fp32 K-quarter
+// kernel over all of K, where aos_lora_op_f32_dev sums eight fp32 K-eighth
 // partials; the two entry points therefore round differently and agree
 // within fp32 tolerance, not bit for bit (each is bit-identical run to run).
 //

@@ -191,7 +191,7 @@ int aos_lora_op_f32_dev(const float* x, uint32_t T, uint32_t in_dim, uint32_t ou
  * device that loads the library until exit), not an allocation.  Requires
  * T * 8 * rank <= 131072, otherwise AOS_ERR_INVALID; same argument rules as
  * aos_lora_op_f32_dev.  Its base GEMM is one single-pass kernel over all of K
- * (aos_lora_op_f32_dev sums four K-quarter partials), so the two agree within
+ * (aos_lora_op_f32_dev sums eight K-eighth partials), so the two agree within
  * fp32 tolerance, not bit for bit; each is bit-identical run to run.  The
  * first call in each CUDA context on a device looks up the array's address
  * (cudaGetSymbolAddress) and should be made before any stream capture on that
