@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* __restrict
 
 // First half of a folded RMSNorm (the decode GEMMs apply the second): per
 // token, hw = bf16(x * w) and the sum of x^2 in fixed point (each thread's
-// fp32 partial * 2^32 rounded, then an integer sum: order-independent, so
+// fp32 partial * 2^16 rounded, then an integer sum: order-independent, so
 // the result is the same on every run).  One CTA of 256 threads per token.
 __global__ void __launch_bounds__(256) norm_prep_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
                                                         int T, int H, uint16_t* __restrict__ hw,
@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(256) norm_prep_kernel(const uint16_t* __restri
         }
         *reinterpret_cast<uint4*>(hw + (size_t)t * H + i) = make_uint4(o[0], o[1], o[2], o[3]);
     }
-    unsigned long long q = (unsigned long long)__float2ll_rn(sq * 4294967296.0f);
+    unsigned long long q = (unsigned long long)__float2ll_rn(sq * 65536.0f);  // the GEMMs' norm scale, 2^16
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) q += __shfl_xor_sync(0xffffffffu, q, off);
     __shared__ unsigned long long part[8];

@@ -456,7 +456,7 @@ int build_layer_plan(aos_ctx* c, int layer, int T, LayerPlan& lp, bool sharded =
         // q/k/v and gate/up read hw and scale by 1 / rms in their epilogue
         if (g == kGroupQKV || g == kGroupGU) {
             p.ss_in = c->d_ss;
-            p.ss_scale = (float)(1.0 / 4294967296.0 / (double)H);
+            p.ss_scale = (float)(1.0 / 65536.0 / (double)H);
             p.norm_eps = c->cfg.rms_eps;
         } else {
             p.ss_out = c->d_ss;
@@ -516,7 +516,7 @@ int get_plan(aos_ctx* c, int T, StepPlan** out, bool sharded = false) {
     p.out[0] = c->d_logits;
     p.ld_out = (int)V;
     p.ss_in = c->d_ss;  // the final norm, folded: hw from the last down launch, 1 / rms here
-    p.ss_scale = (float)(1.0 / 4294967296.0 / (double)c->cfg.hidden);
+    p.ss_scale = (float)(1.0 / 65536.0 / (double)c->cfg.hidden);
     p.norm_eps = c->cfg.rms_eps;
     if ((rc = tc_prepare(p, 227 * 1024))) return c->fail(rc, "lm_head plan");
     plan->lm_grid = tc_num_sms();

@@ -165,6 +165,10 @@ __device__ __forceinline__ unsigned long long gtimer() {
 // Fixed-point scale of the split-tile accumulators (value * 2^32 in int64).
 constexpr float kFix = 4294967296.0f;
 constexpr float kFixInv = 2.3283064365386963e-10f;
+// Fixed-point scale of the folded norms' sums of squares (value * 2^16):
+// finer than fp32 for any row, and room for hidden values in the thousands
+// across the whole row before int64 overflows.
+constexpr float kNormFix = 65536.0f;
 constexpr uint32_t kTcTailBytes = 512;  // mbarriers and flags after the stages
 
 // ---------------------------------------------------------------- epilogue
@@ -272,7 +276,7 @@ __device__ __forceinline__ void store_run(const TcParams& p, int mode, int seg, 
                     }
                 }
         }
-        if (p.ss_out) atomicAdd(p.ss_out + t, (unsigned long long)__float2ll_rn(sq * kFix));
+        if (p.ss_out) atomicAdd(p.ss_out + t, (unsigned long long)__float2ll_rn(sq * kNormFix));
     } else {  // TC_STORE_BF16
         uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]) + off;
         if (full) {

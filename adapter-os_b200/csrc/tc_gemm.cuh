@@ -98,9 +98,9 @@ struct TcParams {
     // RMSNorm folded into the neighbouring launches (decode).  A launch that
     // adds into the residual (o, down) also writes hw = bf16(h * w) with the
     // next norm's weight w and adds each token's sum of squares of h, in
-    // fixed point (value * 2^32), into ss_out.  A launch that reads hw (q/k/v,
+    // fixed point (value * 2^16), into ss_out.  A launch that reads hw (q/k/v,
     // gate/up, lm_head) scales its outputs by 1 / sqrt(ss * ss_scale + eps)
-    // per token (ss_scale = 2^-32 / H) and clears ss_in when it ends.
+    // per token (ss_scale = 2^-16 / H) and clears ss_in when it ends.
     unsigned long long* ss_out;
     uint16_t* hw_out;               // [T][ld_out] bf16
     const uint16_t* norm_w;         // [ld_out] bf16

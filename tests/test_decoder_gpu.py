@@ -165,6 +165,25 @@ def test_decode_bit_identical_run_to_run():
     assert outs[0] == outs[1]
 
 
+def test_decode_step_large_hidden_values():
+    """Hidden values in the thousands (embedding rows scaled to |x| ~ 3000):
+    the folded RMSNorm's fixed-point sums of squares keep their headroom (a
+    row of such values overflows int64 at a 2^32 scale), and the step still
+    matches the oracle."""
+    s = Setup(seed=11)
+    try:
+        big = O.f32_to_bf16_bits(O.bf16_bits_to_f32(s.m.embed) * 3000.0)
+        s.m.embed = big
+        s.gpu.load_weight(aos.W_EMBED, big)
+        logits, hidden = s.gpu.run_step_batch(s.rings, s.tokens.astype(np.uint32), s.seq_ids, want_hidden=True)
+        ref_logits, ref_hidden = O.decode_step(s.m, s.ad, s.rings, s.tokens, s.kv)
+        assert np.abs(O.bf16_bits_to_f32(ref_hidden)).max() > 1000.0
+        assert_close(O.bf16_bits_to_f32(hidden), O.bf16_bits_to_f32(ref_hidden), "hidden (large values)")
+        assert_close(logits, ref_logits, "logits (large hidden values)")
+    finally:
+        s.gpu.close()
+
+
 def test_cooperative_gemm_mode_matches_default(monkeypatch):
     """Shared-device mode (AOS_GEMM_COOPERATIVE=1 at init) launches the same
     GEMMs as cooperative grids: the step's logits and hidden state are
