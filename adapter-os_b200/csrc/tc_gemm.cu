@@ -1378,7 +1378,10 @@ __device__ __forceinline__ void pf_tile(const TcParams& p, int n_m, int n_n, int
     }
 }
 
-__global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_constant__ TcParams p) {
+// Warps: 0 producer, 1 MMA issuer, 2-9 drain (two per TMEM lane quarter: warps
+// 2-5 take a tile's first 128 tokens, warps 6-9 its second), 10-11 idle.
+constexpr int kPfThreads = 384;
+__global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_constant__ TcParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int NS = p.n_stages;
@@ -1409,7 +1412,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
             mbar_init(smem_u32(&empty_bar[s]), 1);
         }
         mbar_init(smem_u32(tfull_bar), 1);
-        mbar_init(smem_u32(tempty_bar), 4);
+        mbar_init(smem_u32(tempty_bar), 8);
         mbar_init(smem_u32(drain_bar), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -1563,9 +1566,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
                 mbar_wait_drain(smem_u32(drain_bar), 0);
             }
         }
-    } else if (warp < 6) {
-        // ---------------- drain + epilogue from TMEM (warps 2-5)
-        const int q = warp & 3;
+    } else if (warp < 10) {
+        // ---------------- drain + epilogue from TMEM (warps 2-9): token block b
+        const int q = warp & 3, b = (warp - 2) >> 2;
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
         pdl_wait();
         int local = 0;
@@ -1574,7 +1577,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
             pf_tile(p, n_m, n_n, ng, it, pt);
             if (!mbar_wait(smem_u32(tfull_bar), (uint32_t)(local & 1), p.err)) break;
             tc_fence_after();
-            for (int b = 0; b < 2; ++b) {
+            {
                 const uint32_t t_acc = tmem_base + lane_off + (uint32_t)(b * kTcBN);
                 const int tok = pt.m * kPfTok + b * kTcTok + q * 32 + lane;
                 const bool valid = tok < p.T;
@@ -1813,7 +1816,7 @@ int pf_prepare(TcParams& p) {
 cudaError_t pf_launch(const TcParams& p, cudaStream_t stream) {
     const size_t smem = tc_smem_bytes(p);
     if ((int)smem > tc_max_dynamic_smem()) return cudaErrorInvalidValue;
-    return launch_k(pf_gemm_kernel, dim3(tc_num_sms()), dim3(kTcThreads), smem, stream, p);
+    return launch_k(pf_gemm_kernel, dim3(tc_num_sms()), dim3(kPfThreads), smem, stream, p);
 }
 
 cudaError_t tc_launch(const TcParams& p, int grid, cudaStream_t stream) {
