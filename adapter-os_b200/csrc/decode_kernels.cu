@@ -24,8 +24,13 @@ __global__ void embed_kernel(const uint16_t* __restrict__ table, const uint32_t*
     for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = id < (uint32_t)V ? src[i] : make_uint4(0, 0, 0, 0);
 }
 
-// RMSNorm (mlx_cpp_wrapper_real.cpp:3384-3390): y = x * (w / sqrt(mean(x^2) + eps)).
-// One CTA (256 threads) per token; fixed-order tree reduction; bf16 in/out.
+// RMSNorm (mlx_cpp_wrapper_real.cpp:3384-3390): y = x * (w / sqrt(mean(x^2) + eps)),
+// computed as x * (w * r) with r = 1 / sqrt(mean(x^2) + eps) taken once per
+// row (one fp32 rounding more than w / denom; the output is bf16).
+// One CTA (256 threads) per token; thread i owns columns [8 (i + 256 c), +8)
+// for chunks c and keeps the first kCached chunks in registers between the
+// sum of squares and the scaling; fixed-order reduction; bf16 in/out.
+template <int kCached>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
                                                       int T, int H, float eps, uint16_t* __restrict__ y) {
     pdl_wait();
@@ -33,9 +38,20 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* __restrict
     const int t = blockIdx.x;
     if (t >= T) return;
     const uint16_t* xt = x + (size_t)t * H;
+    uint4 xc[kCached];
     float ss = 0.0f;
-    for (int i = threadIdx.x * 8; i < H; i += 256 * 8) {
-        const uint4 v = *reinterpret_cast<const uint4*>(xt + i);
+    for (int c = 0, i = threadIdx.x * 8; i < H; ++c, i += 256 * 8) {
+        uint4 v;
+        if (c < kCached) {
+#pragma unroll
+            for (int k = 0; k < kCached; ++k)
+                if (k == c) xc[k] = *reinterpret_cast<const uint4*>(xt + i);
+#pragma unroll
+            for (int k = 0; k < kCached; ++k)
+                if (k == c) v = xc[k];
+        } else {
+            v = *reinterpret_cast<const uint4*>(xt + i);
+        }
         const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -51,10 +67,17 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* __restrict
     __syncthreads();
     float tot = 0.0f;
     for (int i = 0; i < 8; ++i) tot += part[i];
-    const float denom = sqrtf(tot / (float)H + eps);
-    for (int i = threadIdx.x * 8; i < H; i += 256 * 8) {
-        const uint4 v = *reinterpret_cast<const uint4*>(xt + i);
-        const uint4 ww = *reinterpret_cast<const uint4*>(w + i);
+    const float r = 1.0f / sqrtf(tot / (float)H + eps);
+    for (int c = 0, i = threadIdx.x * 8; i < H; ++c, i += 256 * 8) {
+        uint4 v;
+        if (c < kCached) {
+#pragma unroll
+            for (int k = 0; k < kCached; ++k)
+                if (k == c) v = xc[k];
+        } else {
+            v = *reinterpret_cast<const uint4*>(xt + i);
+        }
+        const uint4 ww = __ldg(reinterpret_cast<const uint4*>(w + i));
         const uint32_t u[4] = {v.x, v.y, v.z, v.w};
         const uint32_t g[4] = {ww.x, ww.y, ww.z, ww.w};
         uint32_t o[4];
@@ -62,8 +85,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* __restrict
         for (int j = 0; j < 4; ++j) {
             const float a = __uint_as_float(u[j] << 16), b = __uint_as_float(u[j] & 0xffff0000u);
             const float wa = __uint_as_float(g[j] << 16), wb = __uint_as_float(g[j] & 0xffff0000u);
-            const float ra = a * __fdiv_rn(wa, denom), rb = b * __fdiv_rn(wb, denom);
-            o[j] = (uint32_t)f2bf(ra) | ((uint32_t)f2bf(rb) << 16);
+            o[j] = (uint32_t)f2bf(a * (wa * r)) | ((uint32_t)f2bf(b * (wb * r)) << 16);
         }
         *reinterpret_cast<uint4*>(y + (size_t)t * H + i) = make_uint4(o[0], o[1], o[2], o[3]);
     }
@@ -351,7 +373,11 @@ cudaError_t launch_embed(const uint16_t* table, const uint32_t* ids, int T, int 
 cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* w, int T, int H, float eps, uint16_t* y,
                            cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
-    return launch_k(rmsnorm_kernel, dim3(T), dim3(256), 0, s, x, w, T, H, eps, y);
+    // rows of up to 2048 / 4096 / 8192 columns stay in registers; longer rows
+    // re-read the columns past 8192
+    if (H <= 2048) return launch_k(rmsnorm_kernel<1>, dim3(T), dim3(256), 0, s, x, w, T, H, eps, y);
+    if (H <= 4096) return launch_k(rmsnorm_kernel<2>, dim3(T), dim3(256), 0, s, x, w, T, H, eps, y);
+    return launch_k(rmsnorm_kernel<4>, dim3(T), dim3(256), 0, s, x, w, T, H, eps, y);
 }
 
 cudaError_t launch_norm_prep(const uint16_t* x, const uint16_t* w, int T, int H, uint16_t* hw,
