@@ -1440,6 +1440,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
             uint32_t last_phase[16];
             uint32_t used = 0;
             bool ok = true, waited = false;
+            // A base launch with LoRA runs right after its own shrink launch,
+            // which waited for the launch that wrote X before it let this one
+            // start: X can be read at once, and only the expand steps' hm
+            // (the shrink's output) waits for the previous grid.  The base
+            // K steps then start on the SMs the shrink's last wave leaves.
+            const bool x_ready = p.n_seg > 0 && p.lora;
             for (int it = blockIdx.x; ok && it < n_tiles; it += gridDim.x) {
                 PfTile pt;
                 pf_tile(p, n_m, n_n, ng, it, pt);
@@ -1492,7 +1498,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                             bulk_g2s(sb + h * (kBlkW * 2), src, kBlkW * 2, fb, pol_w);
                         }
                     }
-                    if (!waited) {  // activations come from the previous launch
+                    if (!waited && (!x_ready || ex)) {  // this step reads the previous launch's output
                         pdl_wait();
                         pdl_trigger();
                         waited = true;
