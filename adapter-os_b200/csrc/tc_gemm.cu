@@ -323,6 +323,18 @@ __device__ __forceinline__ void add_delta_run(const TcParams& p, int t, int col,
     }
 }
 
+// s[i] = gate[i] * sigmoid(gate[i]) * up[i] with the hardware exp2 and a
+// fast reciprocal: a few ulp of fp32 (the output is bf16); a very negative
+// gate gives exp -> inf and sigmoid -> 0 exactly.
+template <int N>
+__device__ __forceinline__ void swiglu_run(const float (&gate)[N], const float (&up)[N], float (&s)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        const float sg = __fdividef(1.0f, 1.0f + __expf(-gate[i]));
+        s[i] = (gate[i] * sg) * up[i];
+    }
+}
+
 // Per-token scale of a launch that reads a folded norm's hw: 1 / rms of the
 // token's hidden row, from the fixed-point sum of squares the previous
 // launch accumulated; 1 without one.
@@ -378,15 +390,7 @@ __device__ __forceinline__ void apply_pairs(const TcParams& p, int mode, int seg
             const int f0 = tile * (kTcBN / 2) + cA;
             if (f0 >= p.seg_rows[seg]) break;
             float s[N];
-#pragma unroll
-            for (int i = 0; i < N; ++i) {
-                const float g = vA[i], up = vB[i];
-                // gate * sigmoid(gate) * up with the hardware exp2 and a fast
-                // reciprocal: a few ulp of fp32 (the output is bf16); a very
-                // negative gate gives exp -> inf and sigmoid -> 0 exactly
-                const float sg = __fdividef(1.0f, 1.0f + __expf(-g));
-                s[i] = (g * sg) * up;
-            }
+            swiglu_run<N>(vA, vB, s);
             uint16_t* o = reinterpret_cast<uint16_t*>(p.out[seg]) + (size_t)t * p.ld_out + f0;
             if (f0 + N <= p.seg_rows[seg]) {
                 store_bf16_run<N>(o, s);
@@ -1378,6 +1382,61 @@ __device__ __forceinline__ void pf_tile(const TcParams& p, int n_m, int n_n, int
     }
 }
 
+// Prefill epilogue rows through a per-warp shared-memory slab of 32 rows x 64
+// bytes.  A drain lane holds one token's run of 32 bf16 (64 bytes); stored by
+// its own lane, one warp instruction would touch 32 rows.  Transposed through
+// the slab, lane (j, c) = (lane / 4, lane % 4) moves 16-byte chunk c of row
+// 8 r + j, so one instruction covers 8 rows x 64 contiguous bytes.  Chunk i of
+// slab row r sits at chunk i ^ ((r / 2) % 4): both directions are free of bank
+// conflicts.  row_of(r) is row r's destination (or source), null to skip it.
+constexpr int kPfSlabBytes = 32 * 64;
+constexpr int kPfEpiBytes = 8 * kPfSlabBytes;  // one slab per drain warp
+__device__ __forceinline__ uint32_t slab_off(int row, int chunk) {
+    return (uint32_t)(row * 64 + ((chunk ^ ((row >> 1) & 3)) * 16));
+}
+template <class RowFn>
+__device__ __forceinline__ void warp_store_runs(uint8_t* slab, const uint32_t (&w)[16], int lane, RowFn row_of) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        *reinterpret_cast<uint4*>(slab + slab_off(lane, i)) = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    __syncwarp();
+    const int j = lane >> 2, c = lane & 3;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const int row = 8 * r + j;
+        const uint4 v = *reinterpret_cast<const uint4*>(slab + slab_off(row, c));
+        uint16_t* dst = row_of(row);
+        if (dst) *reinterpret_cast<uint4*>(dst + 8 * c) = v;
+    }
+    __syncwarp();
+}
+// The inverse: lane L receives row L's run (zeros for a skipped row).
+template <class RowFn>
+__device__ __forceinline__ void warp_load_runs(uint8_t* slab, uint32_t (&w)[16], int lane, RowFn row_of) {
+    const int j = lane >> 2, c = lane & 3;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const int row = 8 * r + j;
+        const uint16_t* src = row_of(row);
+        const uint4 v = src ? *reinterpret_cast<const uint4*>(src + 8 * c) : make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(slab + slab_off(row, c)) = v;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 v = *reinterpret_cast<const uint4*>(slab + slab_off(lane, i));
+        w[4 * i] = v.x;
+        w[4 * i + 1] = v.y;
+        w[4 * i + 2] = v.z;
+        w[4 * i + 3] = v.w;
+    }
+    __syncwarp();
+}
+__device__ __forceinline__ void pack_bf16_run(const float (&v)[32], uint32_t (&w)[16]) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) w[i] = (uint32_t)f2bf(v[2 * i]) | ((uint32_t)f2bf(v[2 * i + 1]) << 16);
+}
+
 // Warps: 0 producer, 1 MMA issuer, 2-9 drain (two per TMEM lane quarter: warps
 // 2-5 take a tile's first 128 tokens, warps 6-9 its second), 10-11 idle.
 constexpr int kPfThreads = 384;
@@ -1392,6 +1451,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
     uint64_t* tempty_bar = tfull_bar + 1;  // [1]
     uint64_t* drain_bar = tempty_bar + 1;  // [1]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+    // after the barriers: the drain warps' slabs (kPfSlabBytes each, warps 2-9)
+    uint8_t* epi = smem + (size_t)NS * p.stage_bytes + kTcTailBytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ng = (p.lora || p.sh_nseg) ? __ldg(p.n_groups) : 0;
     const int n_m = cdiv(p.T, kPfTok);
@@ -1581,12 +1642,19 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
         for (int it = blockIdx.x; it < n_tiles; it += gridDim.x, ++local) {
             PfTile pt;
             pf_tile(p, n_m, n_n, ng, it, pt);
-            if (!mbar_wait(smem_u32(tfull_bar), (uint32_t)(local & 1), p.err)) break;
+            // warp-uniform: the epilogue's slab transposes need all 32 lanes
+            const bool got = mbar_wait(smem_u32(tfull_bar), (uint32_t)(local & 1), p.err);
+            if (!__all_sync(0xffffffffu, got)) break;
             tc_fence_after();
             {
                 const uint32_t t_acc = tmem_base + lane_off + (uint32_t)(b * kTcBN);
                 const int tok = pt.m * kPfTok + b * kTcTok + q * 32 + lane;
                 const bool valid = tok < p.T;
+                // rows [tok0, tok0 + 32) of the tile are this warp's; the staged
+                // stores (and the residual's loads) skip rows at or past T
+                const int tok0 = tok - lane;
+                uint8_t* slab = epi + (warp - 2) * kPfSlabBytes;
+                const bool staged = !p.delta && !p.ss_out && !p.ss_in;
                 if (pt.shrink) {
                     float cf[32];
                     const float4* src = reinterpret_cast<const float4*>(
@@ -1609,7 +1677,19 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                             vA[i] *= cf[8 * k + i / 8];
                             vB[i] *= cf[8 * k + 4 + i / 8];
                         }
-                        if (valid) apply_pairs<32>(p, TC_SHRINK_HM, pt.seg, pt.t, k, tok, 0, vA, vB, ng);
+                        const int slot = pt.t * kShrinkGroupsPerTile + k;
+                        if (slot >= ng) continue;
+                        // hm[t][group column + 0..63]: two runs of 32 (see shrink_run)
+                        uint16_t* hm = reinterpret_cast<uint16_t*>(p.sh_out[pt.seg]) + __ldg(p.groups + slot) * kGroup;
+                        uint32_t w[16];
+                        pack_bf16_run(vA, w);
+                        warp_store_runs(slab, w, lane, [&](int r) -> uint16_t* {
+                            return tok0 + r < p.T ? hm + (size_t)(tok0 + r) * p.R : nullptr;
+                        });
+                        pack_bf16_run(vB, w);
+                        warp_store_runs(slab, w, lane, [&](int r) -> uint16_t* {
+                            return tok0 + r < p.T ? hm + (size_t)(tok0 + r) * p.R + 32 : nullptr;
+                        });
                     }
                 } else {
 #pragma unroll 1
@@ -1619,7 +1699,43 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                         float vA[32], vB[32];
                         tmem_ld32(t_acc + cA, vA);
                         tmem_ld32(t_acc + cB, vB);
-                        if (valid) apply_pairs<32>(p, p.mode, pt.seg, pt.t, k, tok, 0, vA, vB, ng);
+                        const int lim = p.seg_rows[pt.seg];
+                        if (staged && p.mode == TC_SWIGLU && pt.t * (kTcBN / 2) + cA + 32 <= lim) {
+                            // act[t][f0 + 0..31] = silu(gate) * up
+                            uint16_t* o = reinterpret_cast<uint16_t*>(p.out[pt.seg]) + pt.t * (kTcBN / 2) + cA;
+                            float sv[32];
+                            swiglu_run<32>(vA, vB, sv);
+                            uint32_t w[16];
+                            pack_bf16_run(sv, w);
+                            warp_store_runs(slab, w, lane, [&](int r) -> uint16_t* {
+                                return tok0 + r < p.T ? o + (size_t)(tok0 + r) * p.ld_out : nullptr;
+                            });
+                        } else if (staged && p.mode == TC_RESID_BF16) {
+                            // h[t][r0 + 0..31] += v for the two runs, h read and written
+                            // through the slab; rows that end past the segment go per lane
+#pragma unroll
+                            for (int hh = 0; hh < 2; ++hh) {
+                                const int r0 = pt.t * kTcBN + (hh ? cB : cA);
+                                const float(&v)[32] = hh ? vB : vA;
+                                if (r0 + 32 <= lim) {
+                                    uint16_t* h = p.resid + p.seg_out0[pt.seg] + r0;
+                                    auto row_of = [&](int r) -> uint16_t* {
+                                        return tok0 + r < p.T ? h + (size_t)(tok0 + r) * p.ld_out : nullptr;
+                                    };
+                                    uint32_t w[16];
+                                    warp_load_runs(slab, w, lane, row_of);
+#pragma unroll
+                                    for (int i = 0; i < 16; ++i)
+                                        w[i] = (uint32_t)f2bf(bf2f((uint16_t)(w[i] & 0xFFFFu)) + v[2 * i]) |
+                                               ((uint32_t)f2bf(bf2f((uint16_t)(w[i] >> 16)) + v[2 * i + 1]) << 16);
+                                    warp_store_runs(slab, w, lane, row_of);
+                                } else if (valid && r0 < lim) {
+                                    store_run<32>(p, TC_RESID_BF16, pt.seg, tok, r0, v);
+                                }
+                            }
+                        } else if (valid) {
+                            apply_pairs<32>(p, p.mode, pt.seg, pt.t, k, tok, 0, vA, vB, ng);
+                        }
                     }
                 }
             }
@@ -1814,13 +1930,13 @@ int pf_prepare(TcParams& p) {
     p.tb = 2;
     p.act_off = (uint32_t)kTcBN * 128;
     p.stage_bytes = p.act_off + 2u * kTcTok * 128;  // 32 KB weights + two 128-token boxes
-    const int budget = tc_max_dynamic_smem() - 1024 - (int)kTcTailBytes;
+    const int budget = tc_max_dynamic_smem() - 1024 - (int)kTcTailBytes - kPfEpiBytes;
     p.n_stages = std::min(4, budget / (int)p.stage_bytes);
     return p.n_stages >= 2 ? AOS_OK : AOS_ERR_INVALID;
 }
 
 cudaError_t pf_launch(const TcParams& p, cudaStream_t stream) {
-    const size_t smem = tc_smem_bytes(p);
+    const size_t smem = tc_smem_bytes(p) + kPfEpiBytes;
     if ((int)smem > tc_max_dynamic_smem()) return cudaErrorInvalidValue;
     return launch_k(pf_gemm_kernel, dim3(tc_num_sms()), dim3(kPfThreads), smem, stream, p);
 }
