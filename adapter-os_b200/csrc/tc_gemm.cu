@@ -335,6 +335,19 @@ __device__ __forceinline__ void swiglu_run(const float (&gate)[N], const float (
     }
 }
 
+// Half-split RoPE of N dimension pairs (x_d, x_{d+64}) -> (x_d c - x_{d+64} s,
+// x_d s + x_{d+64} c), cs = the position's (cos, sin) from dimension d on.
+template <int N>
+__device__ __forceinline__ void rope_run(const float (&x0)[N], const float (&x1)[N], const float2* cs, float (&a)[N],
+                                         float (&b)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        const float2 c = __ldg(cs + i);
+        a[i] = x0[i] * c.x - x1[i] * c.y;
+        b[i] = x1[i] * c.x + x0[i] * c.y;
+    }
+}
+
 // Per-token scale of a launch that reads a folded norm's hw: 1 / rms of the
 // token's hidden row, from the fixed-point sum of squares the previous
 // launch accumulated; 1 without one.
@@ -410,13 +423,7 @@ __device__ __forceinline__ void apply_pairs(const TcParams& p, int mode, int seg
             float a[N], b[N];
             if (module != AOS_MOD_V) {
                 // half-split RoPE: (x_d, x_{d+64}) -> (x_d c - x_{d+64} s, x_d s + x_{d+64} c)
-                const float2* cs = reinterpret_cast<const float2*>(p.rope) + (size_t)pos * 64 + d;
-#pragma unroll
-                for (int i = 0; i < N; ++i) {
-                    const float2 c = __ldg(cs + i);
-                    a[i] = vA[i] * c.x - vB[i] * c.y;
-                    b[i] = vB[i] * c.x + vA[i] * c.y;
-                }
+                rope_run<N>(vA, vB, reinterpret_cast<const float2*>(p.rope) + (size_t)pos * 64 + d, a, b);
             } else {
 #pragma unroll
                 for (int i = 0; i < N; ++i) {
@@ -1733,6 +1740,42 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                                     store_run<32>(p, TC_RESID_BF16, pt.seg, tok, r0, v);
                                 }
                             }
+                        } else if (staged && p.mode == TC_QKV_ROPE) {
+                            // RoPE of dims d, d + 64 of one head (see apply_pairs); the
+                            // two runs go to q, or to the token's paged K/V row
+                            const int module = p.seg_module[pt.seg];
+                            const int head = pt.t * 2 + (cA >> 7);
+                            if (head * 128 >= lim) continue;
+                            const int d = cA & 127;
+                            float a[32], bv[32];
+                            if (module != AOS_MOD_V) {
+                                const int pos = valid ? __ldg(p.ctx_lens + tok) : 0;
+                                rope_run<32>(vA, vB, reinterpret_cast<const float2*>(p.rope) + (size_t)pos * 64 + d, a, bv);
+                            } else {
+#pragma unroll
+                                for (int i = 0; i < 32; ++i) {
+                                    a[i] = vA[i];
+                                    bv[i] = vB[i];
+                                }
+                            }
+                            auto row_of = [&](int r) -> uint16_t* {
+                                const int tk = tok0 + r;
+                                if (tk >= p.T) return nullptr;
+                                if (module == AOS_MOD_Q)
+                                    return reinterpret_cast<uint16_t*>(p.out[pt.seg]) + (size_t)tk * p.ld_out + head * 128 + d;
+                                const int pos = __ldg(p.ctx_lens + tk);
+                                const int blk = __ldg(p.block_tables + (size_t)tk * p.max_blocks + (pos >> 4));
+                                uint16_t* pool = module == AOS_MOD_K ? p.k_pool : p.v_pool;
+                                return pool + ((((size_t)p.layer * p.num_blocks + blk) * p.nkv + head) * 16 + (pos & 15)) * 128 + d;
+                            };
+                            uint32_t w[16];
+                            pack_bf16_run(a, w);
+                            warp_store_runs(slab, w, lane, row_of);
+                            pack_bf16_run(bv, w);
+                            warp_store_runs(slab, w, lane, [&](int r) -> uint16_t* {
+                                uint16_t* dst = row_of(r);
+                                return dst ? dst + 64 : nullptr;
+                            });
                         } else if (valid) {
                             apply_pairs<32>(p, p.mode, pt.seg, pt.t, k, tok, 0, vA, vB, ng);
                         }
