@@ -1351,7 +1351,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
 // token blocks share each weight box: a step is 32 KB of weights plus 32 KB of
 // activations for eight MMAs, which halves the L2 bytes per MMA of a
 // 128-token tile.  The 256 x 256 fp32 accumulator takes all 512 TMEM columns,
-// so the MMA waits while a tile drains (a few percent of a tile's time).
+// so the MMA waits while a tile drains (about a tenth of the launch time at
+// 8B shapes).  The drain is kept short by eight drain warps (one per lane
+// quarter and 128-token block) and by stores staged through a per-warp slab.
 // Persistent CTAs walk the tiles in bands of kPfBand token tiles per weight
 // tile, so the tiles running at the same time share boxes in L2.
 // Gate/up expand steps come in halves (gate rows, then up rows, N = 128 each),
